@@ -1,0 +1,386 @@
+#!/usr/bin/env python
+"""Benchmark of the Gaussian render path: fwd+bwd Mpix/s on the C2 workload
+(1M Gaussians, SH degree 3, one 1920x1080 pinhole per GPU).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
+
+One step = SH colour forward -> ut_gs_render (UT projection, tile
+intersection + sort + offsets, rays, forward compositing) -> backward
+(compositing backward, SH backward) through the public API and autograd, and
+with N > 1 ranks the NCCL all-reduce (sum) of all Gaussian gradients
+(views are sharded one per rank; weak scaling).  Rank r renders the C2 view;
+every rank holds the full scene.
+
+value  : whole-job Mpix/s with inputs resident in HBM, device-timed with CUDA
+         events (max over ranks).
+e2e    : the same step through the same public API with the upstream
+         gradient images copied in from pinned host memory and the loss read
+         back each step.
+--impl reference : the CPU oracle restatement of the reference (the
+         reference itself cannot be built here), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+W_C2, H_C2, N_C2, DEG_C2 = 1920, 1080, 1_000_000, 3
+METRIC = "Gaussian-render fwd+bwd Mpix/s (1M Gaussians, 1080p)"
+L2_BYTES = 126 * 2**20
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--gaussians", type=int, default=N_C2)
+    return p.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_count():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------ CPU oracle --
+def oracle_view(sc, spec, rows=None):
+    """One fwd+bwd view of the C2 workload on the CPU oracle; `rows` limits
+    compositing to a band of tile rows (projection and tiling always cover
+    the whole view).  Returns (seconds, pixels composited)."""
+    import numpy as np
+    from oracle import oracle as O
+    from xsimgs_b200 import scenes
+    cam = spec.make("cpu")
+    pack = cam.pack.numpy().reshape(-1)
+    W, H = spec.width, spec.height
+    m, q, s, o, sh = (t.numpy() for t in (sc.means, sc.quats, sc.scales, sc.opacities, sc.sh))
+    vr, vd, va = (t.numpy() for t in scenes.upstream_grads(H, W, 3))
+    t0 = time.perf_counter()
+    flags, radii, m2, dep = O.projection_utgs("pinhole", pack, m, None, s, q, o, W, H)
+    tpg, ids, flat = O.isect_regular(m2, radii, dep, W, H, 16, 16)
+    tw, th = (W + 15) // 16, (H + 15) // 16
+    off = O.isect_offset_encode(ids, tw, th)
+    ro, rd, _ = O.camera_rays("pinhole", pack, W, H)
+    cols = O.sh_fwd(DEG_C2, pack[4:7], m, sh)
+    y0, y1 = (0, th) if rows is None else rows
+    band = slice(y0 * 16, min(H, y1 * 16))
+    start = int(off[y0, 0])
+    end = int(off[y1, 0]) if y1 < th else len(flat)
+    offb = off[y0:y1] - start
+    flb = flat[start:end]
+    Hb = band.stop - band.start
+    rgb, d, a, last, _ = O.rasterize_fwd(m, q, s, cols, o, W, Hb, 16, 16, ro[band], rd[band], offb, flb)
+    g = O.rasterize_bwd(m, q, s, cols, o, W, Hb, 16, 16, ro[band], rd[band], offb, flb, a, last,
+                        vr[band], vd[band], va[band])
+    O.sh_bwd(DEG_C2, pack[4:7], m, sh, g["v_colors"])
+    return time.perf_counter() - t0, W * Hb
+
+
+def reference_arm(args, world, rank):
+    """--impl reference: the CPU oracle on the box's host cores."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    from xsimgs_b200 import scenes
+    sc = scenes.street_scene(args.gaussians)
+    spec = scenes.c2_camera()
+    th = (spec.height + 15) // 16
+    cores = O.num_threads()
+    # calibrate: a full view; bound the whole run to about three minutes
+    t_full, px_full = oracle_view(sc, spec)
+    steps = args.steps + args.warmup
+    rows = None
+    per_step_budget = 170.0 / max(1, steps)
+    if t_full > per_step_budget:
+        frac = max(1.0 / th, per_step_budget / t_full)
+        nrows = max(1, int(th * frac))
+        y0 = max(0, th // 2 - nrows // 2)
+        rows = (y0, y0 + nrows)
+    for _ in range(args.warmup):
+        oracle_view(sc, spec, rows)
+    tot_t, tot_px = 0.0, 0
+    for _ in range(args.steps):
+        t, px = oracle_view(sc, spec, rows)
+        tot_t += t
+        tot_px += px
+    value = tot_px / tot_t / 1e6
+    sample = ("full C2 view per step" if rows is None else
+              f"C2 projection+tiling of all {args.gaussians} Gaussians and fwd+bwd compositing of "
+              f"tile rows {rows[0]}-{rows[1] - 1} ({spec.width}x{min(spec.height, rows[1] * 16) - rows[0] * 16} px) "
+              f"per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "Mpix/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * tot_t / args.steps, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded C2 scene)",
+        "config": {"workload": "C2: 1M Gaussians, SH deg 3, pinhole 1920x1080, fwd+bwd",
+                   "implementation": "CPU oracle restatement (reference not buildable here)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "Mpix/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "Mpix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ GPU arm ----
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while a timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for ln in open(self.path):
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        mx = max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def gpu_arm(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import xsimgs_b200 as X
+    from xsimgs_b200 import capi, scenes, roofline
+
+    sc = scenes.street_scene(args.gaussians).to(dev)
+    spec = scenes.c2_camera()
+    cam = spec.make(dev)
+    W, H = spec.width, spec.height
+    leaves = {k: v.clone().requires_grad_(True) for k, v in sc.params().items()}
+    # all gradients live in one flat buffer so one all-reduce covers them
+    sizes = [v.numel() for v in leaves.values()]
+    flat_grad = torch.zeros(sum(sizes), device=dev)
+    off = 0
+    for v, n in zip(leaves.values(), sizes):
+        v.grad = flat_grad[off:off + n].view_as(v)
+        off += n
+    origin = cam.t0
+    g_rgb, g_d, g_a = (t.to(dev) for t in scenes.upstream_grads(H, W, 3, seed=1 + rank))
+
+    def step(gr, gd, ga):
+        flat_grad.zero_()
+        colors = X.spherical_harmonics_fused(leaves["sh"], leaves["means"], origin, DEG_C2)
+        color, depth, alpha, _ = X.ut_gs_render(cam, leaves["means"], leaves["scales"], leaves["quats"],
+                                                leaves["opacities"], W, H, colors=colors)
+        loss = (color * gr).sum() + (depth * gd).sum() + (alpha * ga).sum()
+        loss.backward()
+        if world > 1:
+            dist.all_reduce(flat_grad)
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(g_rgb, g_d, g_a)
+    barrier()
+
+    # -------------------------------------------------- timed: value ----
+    clocks = ClockSampler(local)
+    clocks.start()
+    capi.timing_reset()
+    capi.timing_enable(True)
+    launches0 = capi.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record()
+    for _ in range(args.steps):
+        step(g_rgb, g_d, g_a)
+    ev1.record()
+    barrier()
+    launches = capi.launch_count() - launches0
+    capi.timing_enable(False)
+    t_ms = ev0.elapsed_time(ev1)
+    bwd_ms, bwd_n = capi.timing_query("rasterize_bwd")
+    fwd_ms, fwd_n = capi.timing_query("rasterize_fwd")
+    capi.timing_reset()
+
+    # ---------------------------------------------------- timed: e2e ----
+    host = [t.cpu().pin_memory() for t in (g_rgb, g_d, g_a)]
+    dbuf = [torch.empty_like(t) for t in (g_rgb, g_d, g_a)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    for _ in range(max(1, args.warmup // 2)):
+        for d, h in zip(dbuf, host):
+            d.copy_(h, non_blocking=True)
+        step(*dbuf).item()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        for d, h in zip(dbuf, host):
+            d.copy_(h, non_blocking=True)
+        step(*dbuf).item()
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+
+    # max over ranks
+    tt = torch.tensor([t_ms, e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms = tt.tolist()
+
+    # ------------------------------------------------ roofline inputs ----
+    roof = None
+    if rank == 0:
+        cnt = torch.zeros(2, dtype=torch.int64, device=dev)
+        capi.set_pair_counters(cnt.data_ptr())
+        with torch.no_grad():
+            colors = X.spherical_harmonics_fused(sc.sh, sc.means, origin, DEG_C2)
+            td = X.ut_gs_tiling(cam, sc.means, sc.scales, sc.quats, W, H, opacity=sc.opacities)
+            ro, rd = cam.camera_rays(W, H)
+            _, _, alpha, last = X._C.rasterize_eval3d_fwd(
+                means=sc.means, quats=sc.quats, scales=sc.scales, colors=colors.unsqueeze(0),
+                opacities=sc.opacities.view(1, -1), image_width=W, image_height=H, tile_size_width=16,
+                tile_size_height=16, ray_origs=ro, ray_dirs=rd, tile_offsets=td["isect_offsets"],
+                flatten_ids=td["flatten_ids"])
+        torch.cuda.synchronize()
+        capi.set_pair_counters(None)
+        n_eval_f, n_contrib = (int(x) for x in cnt.tolist())
+        # backward replays every pair up to each pixel's last contributor
+        tw = (W + 15) // 16
+        ty = torch.arange(H, device=dev) // 16
+        tx = torch.arange(W, device=dev) // 16
+        start = td["isect_offsets"].view(-1)[(ty[:, None] * tw + tx[None, :])]
+        n_eval_b = int(torch.where(alpha > 0, last - start + 1, torch.zeros_like(last)).sum())
+        peak_flops = fp32_peak(dev)
+        bwd_avg = bwd_ms / max(1, bwd_n)
+        fwd_avg = fwd_ms / max(1, fwd_n)
+        fl_b = roofline.bwd_flops(n_eval_b, n_contrib, 3)
+        fl_f = roofline.fwd_flops(n_eval_f, n_contrib, 3)
+        ach_b = fl_b / (bwd_avg * 1e-3) / 1e12
+        ach_f = fl_f / (fwd_avg * 1e-3) / 1e12
+        roof = {"kernel": "rasterize_bwd (raster_bwd_kernel<3,false>)", "bound": "fp32",
+                "achieved": round(ach_b, 2), "peak": round(peak_flops / 1e12, 2), "unit": "TFLOP/s",
+                "frac": round(ach_b / (peak_flops / 1e12), 3), "traffic": None,
+                "peak_source": "measured: FP32 FMA probe in this run (MEASURED_PEAKS.json has only HBM and bf16)",
+                "avg_launch_ms": round(bwd_avg, 4), "flops_per_launch": fl_b,
+                "pairs": {"evaluated_fwd": n_eval_f, "evaluated_bwd": n_eval_b, "contributing": n_contrib},
+                "fwd": {"achieved": round(ach_f, 2), "avg_launch_ms": round(fwd_avg, 4),
+                        "frac": round(ach_f / (peak_flops / 1e12), 3)},
+                "step_share": round((bwd_avg + fwd_avg) / (t_ms / args.steps), 3)}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        t, px = oracle_view(scenes.street_scene(args.gaussians), spec)
+        from oracle import oracle as O
+        cpu = {"value": round(px / t / 1e6, 4), "unit": "Mpix/s", "cores": O.num_threads(), "kind": "port",
+               "sample": "one full C2 view (projection, tiling, SH, fwd+bwd compositing) on the CPU oracle"}
+
+    px_total = world * W * H * args.steps
+    value = px_total / (t_ms * 1e-3) / 1e6
+    e2e = px_total / (e2e_ms * 1e-3) / 1e6
+    gbytes = sum(v.numel() * 4 for v in leaves.values())
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "Mpix/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded C2 scene)",
+        "config": {"workload": "C2: 1M Gaussians, SH deg 3, pinhole 1920x1080, fwd+bwd per view",
+                   "views_per_gpu": 1, "parallelism": f"view-sharded dp{world} + NCCL all-reduce of grads",
+                   "gaussians": args.gaussians, "width": W, "height": H, "tile": 16,
+                   "l2": f"inputs larger than L2: Gaussian params {gbytes / 1e6:.0f} MB > 126 MB L2"},
+        "e2e": {"value": round(e2e, 2), "unit": "Mpix/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": int(launches), "gpu_launches_per_step": round(launches / args.steps, 1),
+        "clocks": clk, "roofline": roof, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def fp32_peak(dev) -> float:
+    """FLOP/s of the FMA probe kernel (8 x 148 SM-filling blocks), best of 3."""
+    import torch
+    from xsimgs_b200 import capi
+    scratch = torch.empty(512, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    best = 0.0
+    for _ in range(4):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fl = capi.fp32_probe(scratch.data_ptr(), 4096, sms * 4, stream)
+        e1.record()
+        torch.cuda.synchronize()
+        best = max(best, fl / (e0.elapsed_time(e1) * 1e-3))
+    return best
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        return
+    gpu_arm(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,240 @@
+/*
+ * xsimgs-b200 C ABI — the boundary between host code (the PyTorch extension
+ * xsimgs_b200._C, or any C/ctypes/cffi caller) and the sm_100a kernels in
+ * libxsimgs_b200.so.
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer unless its name ends in
+ *     `_host`.  Arrays are dense, row-major, float32 unless stated.
+ *   - Every entry point enqueues work on `stream` and returns without
+ *     synchronising, except where a count must come back to the host (the
+ *     `*_count` tiling calls), which synchronise `stream` once.
+ *   - Return value: XSG_OK (0) or an XSG_ERR_* code; xsg_last_error() gives a
+ *     message (thread-local, valid until the next call on that thread).
+ *   - Scratch memory is never allocated inside the library: entry points that
+ *     need it take `workspace` + `workspace_bytes`, and a matching
+ *     *_workspace_size() call says how much.
+ *
+ * Each declaration cites the reference (whesense/xsimgs) function it replaces,
+ * as path:line within that project.
+ */
+#ifndef XSIMGS_B200_H
+#define XSIMGS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* xsg_stream_t; /* == cudaStream_t */
+
+enum xsg_status {
+    XSG_OK = 0,
+    XSG_ERR_INVALID_ARGUMENT = 1,
+    XSG_ERR_UNSUPPORTED = 2,
+    XSG_ERR_CUDA = 3,
+    XSG_ERR_WORKSPACE = 4,
+};
+
+/* Camera models; the pack layout (float32 words) is
+ *   [0:4) q0 (w,x,y,z) camera->world rotation   [4:7) t0   [7:10) v   [10:13) w
+ *   [13] padding   [14:16) rolling_time   [16] trigger_time   [17] pose_time
+ *   [18:...) intrinsics:
+ *     PINHOLE   f.x f.y c.x c.y (normalised by image size)         -> 22 words
+ *     FISHEYE   f.x f.y c.x c.y k1 k2 k3 k4                         -> 26 words
+ *     SPHERICAL phi_min phi_range theta_min theta_range             -> 22 words
+ *     LIDAR     the same 4 limits + 2 words holding the 64-bit device
+ *               address of the per-row elevation table (beam_v)      -> 24 words
+ * Reference: Camera<Impl> (include/cameras/camera.h:67-183) with the impls in
+ * csrc/cameras/perspective.cu:7-71, fisheye_opencv.cu:5-188 and
+ * spherical.h:34-100.  The lidar address words follow
+ * src/xsimgs/cameras/ext/lidar.py:14-19. */
+enum xsg_camera_type {
+    XSG_CAM_PINHOLE = 0,
+    XSG_CAM_FISHEYE = 1,
+    XSG_CAM_SPHERICAL = 2,
+    XSG_CAM_LIDAR = 3,
+};
+int xsg_camera_pack_words(int camera_type);
+
+const char* xsg_last_error(void);
+const char* xsg_version(void);
+
+/* Instrumentation (no counterpart in the reference; used by the benchmark):
+ * the number of kernels this library has launched in the process, and
+ * optional CUDA-event timing of the main kernels by name ("rasterize_fwd",
+ * "rasterize_bwd", ...).  xsg_timing_query synchronises the recorded events
+ * and returns their summed duration and count. */
+long long xsg_launch_count(void);
+void xsg_timing_enable(int on);
+void xsg_timing_reset(void);
+int xsg_timing_query(const char* name, double* total_ms, long long* launches);
+/* FP32 FMA peak probe: launches `blocks` x 512 threads of iters x 128
+ * independent FMAs, writes the FLOP count to *flops (time it with events). */
+int xsg_fp32_probe(float* scratch, int iters, int blocks, xsg_stream_t stream, double* flops);
+/* Pair counters of the forward compositing kernel: when `counters` (2 x u64,
+ * device, zeroed by the caller) is set, every xsg_rasterize_fwd adds the
+ * number of evaluated and of contributing (pixel, Gaussian) pairs to it.
+ * NULL (the default) turns counting off. */
+void xsg_set_pair_counters(unsigned long long* counters);
+
+/* Camera rays: ray_o/ray_d [H, W, 3] (ray_o and valid may be NULL).
+ * Replaces launch_camera_ray_fwd, include/cameras/ray_kernels.h:8-59. */
+int xsg_camera_rays(int camera_type, const float* pack, int width, int height,
+                    int world_space, int normalized, float* ray_o, float* ray_d,
+                    uint8_t* valid, xsg_stream_t stream);
+
+/* Per-pixel capture time (delta=0) or time relative to pose_time (delta=1),
+ * out [H, W].  Replaces pixel_time_fwd / pixel_time_delta_fwd,
+ * include/cameras/time_kernels.h:5-82. */
+int xsg_pixel_time(int camera_type, const float* pack, int width, int height, int delta,
+                   float* out, xsg_stream_t stream);
+/* The same from normalised uv [n, 2]; time_kernels.h:30-112. */
+int xsg_pixel_time_from_uv(int camera_type, const float* pack, const float* uv, int64_t n,
+                           int delta, float* out, xsg_stream_t stream);
+
+/* Rolling-shutter point projection, out uvdt [n, 4] and mask [n] (u8).
+ * force_no_jacobian selects the fixed-point iteration (projection_nojac).
+ * Replaces camera_projection_fwd, include/cameras/projection_kernels.h:259-309. */
+int xsg_projection(int camera_type, const float* pack, const float* points,
+                   const float* points_velocity, int64_t n, float residual_thr,
+                   float max_residual, float max_margin, int projection_mode,
+                   int force_no_jacobian, float* uvdt, uint8_t* mask, xsg_stream_t stream);
+
+/* Unscented-transform Gaussian projection.  Outputs flags u8[n], radii [n,2],
+ * means2d [n,2], depths [n] are fully written (zero where not visible).
+ * phm != 0 selects the phase-modelling variant (spherical / lidar only).
+ * Replaces launch_unscented_transform, include/cameras/ut_kernels.h:255-305,
+ * and launch_unscented_transform_phm, include/cameras/ut_phm_kernels.h:123-173. */
+int xsg_projection_utgs(int camera_type, const float* pack, const float* points,
+                        const float* points_velocity, const float* scales,
+                        const float* quats, const float* opacity, int64_t n, float width,
+                        float height, float ut_alpha, float ut_beta, float ut_kappa,
+                        float residual_thr, float max_residual, float max_margin, int phm,
+                        uint8_t* flags, float* radii, float* means2d, float* depths,
+                        xsg_stream_t stream);
+
+/* Zero radii of masked-out Gaussians, in place.  mask u8[n] (bool) or
+ * packed_mask u32[ceil(n/32)]; exactly one must be non-NULL.
+ * Replaces mask_radii / mask_radii_packed, csrc/tiling/mask_radii.cu:10-88. */
+int xsg_mask_radii(const uint8_t* mask, const uint32_t* packed_mask, int64_t n, float* radii,
+                   xsg_stream_t stream);
+
+/* Tile intersection, two phases.
+ *   1. *_count fills tiles_per_gauss i32[n] and returns the intersection
+ *      total in *n_isects_host (synchronises `stream`).
+ *   2. *_emit writes isect_ids i64[n_isects] (tile << 32 | depth bits) and
+ *      flatten_ids i32[n_isects], sorted by (tile, depth, Gaussian index) when
+ *      sort != 0, else in emission order.
+ * Workspace: xsg_isect_workspace_size(n, 0) bytes for *_count, and
+ * xsg_isect_workspace_size(n, sort ? n_isects : 0) for *_emit.
+ * Regular tiles replace isect_regular_tiles, csrc/tiling/regular_tiling.cu:72-135,
+ * with sort_intersections, tiling_common.cu:102-162. */
+size_t xsg_isect_workspace_size(int64_t n_gauss, int64_t max_isects);
+int xsg_isect_regular_count(const float* means2d, const float* radii, int64_t n, int width,
+                            int height, int tile_size_x, int tile_size_y,
+                            int32_t* tiles_per_gauss, int64_t* n_isects_host, void* workspace,
+                            size_t workspace_bytes, xsg_stream_t stream);
+int xsg_isect_regular_emit(const float* means2d, const float* radii, const float* depths,
+                           int64_t n, int width, int height, int tile_size_x, int tile_size_y,
+                           int sort, const int32_t* tiles_per_gauss, int64_t n_isects,
+                           int64_t* isect_ids, int32_t* flatten_ids, void* workspace,
+                           size_t workspace_bytes, xsg_stream_t stream);
+
+/* Azimuth/elevation tiling for range images.  lidar != 0: irregular
+ * elevation tiles bounded by elev_bounds[n_elev] (every tile_size_y-th beam
+ * value); else regular tiles of tile_size_x x tile_size_y.  Gaussians with
+ * flag 2 (wrap-around) are projected a second time.
+ * Replaces isect_lidar_tiles, csrc/tiling/phm_lidar_tiling.cu:239-351, and
+ * isect_spherical_tiles, csrc/tiling/phm_spherical_tiling.cu:179-291. */
+int xsg_isect_spherical_count(int lidar, const float* pack, const float* points,
+                              const float* points_velocity, const float* scales,
+                              const float* quats, const float* opacity, const uint8_t* flags,
+                              const float* means2d, const float* radii, const float* depths,
+                              const float* elev_bounds, int n_elev, int64_t n, int tile_size_x,
+                              int tile_size_y, float width, float height, float ut_alpha,
+                              float ut_beta, float ut_kappa, int32_t* tiles_per_gauss,
+                              int64_t* n_isects_host, void* workspace, size_t workspace_bytes,
+                              xsg_stream_t stream);
+int xsg_isect_spherical_emit(int lidar, const float* pack, const float* points,
+                             const float* points_velocity, const float* scales,
+                             const float* quats, const float* opacity, const uint8_t* flags,
+                             const float* means2d, const float* radii, const float* depths,
+                             const float* elev_bounds, int n_elev, int64_t n, int tile_size_x,
+                             int tile_size_y, float width, float height, float ut_alpha,
+                             float ut_beta, float ut_kappa, int sort,
+                             const int32_t* tiles_per_gauss, int64_t n_isects,
+                             int64_t* isect_ids, int32_t* flatten_ids, void* workspace,
+                             size_t workspace_bytes, xsg_stream_t stream);
+
+/* Per-tile start offsets i32[tile_height, tile_width] from sorted isect_ids.
+ * Replaces isect_offset_encode, csrc/tiling/tiling_common.cu:25-99. */
+int xsg_isect_offset_encode(const int64_t* isect_ids, int64_t n_isects, int tile_width,
+                            int tile_height, int32_t* offsets, xsg_stream_t stream);
+
+/* Channel counts the compositing kernels are built for (the reference's
+ * ndim_cases, csrc/rasterization/common.h:5-25).  Writes up to `cap` values
+ * and returns how many there are. */
+int xsg_raster_supported_channels(int* out, int cap);
+
+/* Forward compositing.  velocity/ray_time_delta non-NULL selects the dynamic
+ * variant.  colors [N, cdim] may be NULL with cdim = 0.  Outputs renders
+ * [H, W, cdim], depths/alphas [H, W], last_ids i32[H, W].
+ * Workspace: xsg_rasterize_workspace_size(n_gauss, cdim).
+ * Replaces rasterize_eval3d_fwd, csrc/rasterization/eval3d_fwd.cu:248-308,
+ * and rasterize_eval3d_dynamic_fwd, eval3d_dynamic_fwd.cu:259-323. */
+size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim);
+int xsg_rasterize_fwd(const float* means, const float* velocity, const float* quats,
+                      const float* scales, const float* colors, int cdim,
+                      const float* opacities, int64_t n_gauss, int width, int height,
+                      int tile_size_x, int tile_size_y, const float* ray_o,
+                      const float* ray_d, const float* ray_time_delta,
+                      const int32_t* tile_offsets, int tiles_w, int tiles_h,
+                      const int32_t* flatten_ids, int64_t n_isects, float* renders,
+                      float* depths, float* alphas, int32_t* last_ids, void* workspace,
+                      size_t workspace_bytes, xsg_stream_t stream);
+
+/* Backward compositing.  Gradient outputs are overwritten (zeroed first):
+ * v_means/v_velocity [N,3], v_quats [N,4], v_scales [N,3], v_opacities [N],
+ * v_colors [N, cdim] (NULL when cdim = 0), v_ray_o/v_ray_d [H, W, 3],
+ * v_ray_time_delta [H, W] (dynamic only).  v_renders may be NULL.
+ * Replaces rasterize_eval3d_bwd, csrc/rasterization/eval3d_bwd.cu:297-403,
+ * and rasterize_eval3d_dynamic_bwd, eval3d_dynamic_bwd.cu:312-429. */
+int xsg_rasterize_bwd(const float* means, const float* velocity, const float* quats,
+                      const float* scales, const float* colors, int cdim,
+                      const float* opacities, int64_t n_gauss, int width, int height,
+                      int tile_size_x, int tile_size_y, const float* ray_o,
+                      const float* ray_d, const float* ray_time_delta,
+                      const int32_t* tile_offsets, int tiles_w, int tiles_h,
+                      const int32_t* flatten_ids, int64_t n_isects,
+                      const float* render_alphas, const int32_t* last_ids,
+                      const float* v_renders, const float* v_depths, const float* v_alphas,
+                      float* v_means, float* v_velocity, float* v_quats, float* v_scales,
+                      float* v_colors, float* v_opacities, float* v_ray_o, float* v_ray_d,
+                      float* v_ray_time_delta, void* workspace, size_t workspace_bytes,
+                      xsg_stream_t stream);
+
+/* Spherical-harmonics colour, degree 0..4; layout_3kn selects [3, K, N]
+ * coefficients (else [N, K, 3]); coeffs_dc optionally holds band 0 apart;
+ * mask is a packed u32 bitmask or NULL.  out [N, 3] (masked rows untouched).
+ * Replaces spherical_harmonics_fused_fwd, csrc/color/sh_fwd.cu:162-245. */
+int xsg_sh_fwd(int degree, const float* origin, const float* positions, const float* coeffs,
+               const float* coeffs_dc, const uint32_t* mask, int layout_3kn, int64_t n,
+               int dim, float* out, xsg_stream_t stream);
+/* Backward: d_coeffs (shape of coeffs), d_coeffs_dc (shape of coeffs_dc or
+ * NULL), d_positions [N, 3], d_origin [3] — all overwritten.
+ * Replaces spherical_harmonics_fused_bwd, csrc/color/sh_bwd.cu:317-376. */
+size_t xsg_sh_bwd_workspace_size(int64_t n);
+int xsg_sh_bwd(int degree, const float* origin, const float* positions, const float* coeffs,
+               const float* coeffs_dc, const uint32_t* mask, int layout_3kn, int64_t n,
+               int dim, const float* d_out, float* d_coeffs, float* d_coeffs_dc,
+               float* d_positions, float* d_origin, void* workspace, size_t workspace_bytes,
+               xsg_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XSIMGS_B200_H */

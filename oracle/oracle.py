@@ -1,0 +1,228 @@
+"""ctypes front end of the CPU oracle (test infrastructure, never a product
+path).  Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg
+use it, as the checker / the timed CPU restatement.  Parity status: unpinned
+(see oracle/xsg_oracle.cpp).
+
+All functions take and return numpy arrays (float32 unless stated).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = _build.OUT
+        if not os.path.exists(path):
+            path = _build.build()
+        _lib = C.CDLL(path)
+        _lib.xsgo_isect_regular.restype = C.c_int64
+        _lib.xsgo_isect_spherical.restype = C.c_int64
+        _lib.xsgo_num_threads.restype = C.c_int
+    return _lib
+
+
+CAM = {"pinhole": 0, "fisheye": 1, "spherical": 2, "lidar": 3}
+
+
+def _p(a):
+    if a is None:
+        return None
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def _f32(a):
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+def set_threads(n: int):
+    lib().xsgo_set_num_threads(C.c_int(n))
+
+
+def num_threads() -> int:
+    return int(lib().xsgo_num_threads())
+
+
+def camera_rays(cam, pack, W, H, world_space=True, normalized=True, elev=None):
+    pack = _f32(pack).reshape(-1)
+    elev = _f32(elev)
+    ro = np.zeros((H, W, 3), np.float32)
+    rd = np.zeros((H, W, 3), np.float32)
+    valid = np.zeros((H, W), np.uint8)
+    lib().xsgo_camera_rays(C.c_int(CAM[cam]), _p(pack), _p(elev), C.c_int(W), C.c_int(H), C.c_int(int(world_space)),
+                           C.c_int(int(normalized)), _p(ro), _p(rd), _p(valid))
+    return ro, rd, valid.astype(bool)
+
+
+def pixel_time(cam, pack, W, H, delta, elev=None):
+    pack = _f32(pack).reshape(-1)
+    out = np.zeros((H, W), np.float32)
+    lib().xsgo_pixel_time(C.c_int(CAM[cam]), _p(pack), _p(_f32(elev)), C.c_int(W), C.c_int(H), C.c_int(int(delta)),
+                          _p(out))
+    return out
+
+
+def projection(cam, pack, pts, vel=None, thr=1e-4, max_res=0.002, margin=1.0, mode=0, nojac=False, elev=None):
+    pack = _f32(pack).reshape(-1)
+    pts = _f32(pts)
+    vel = _f32(vel)
+    n = pts.shape[0]
+    uvdt = np.zeros((n, 4), np.float32)
+    mask = np.zeros(n, np.uint8)
+    lib().xsgo_projection(C.c_int(CAM[cam]), _p(pack), _p(_f32(elev)), _p(pts), _p(vel), C.c_int64(n),
+                          C.c_float(thr), C.c_float(max_res), C.c_float(margin), C.c_int(mode), C.c_int(int(nojac)),
+                          _p(uvdt), _p(mask))
+    return uvdt, mask.astype(bool)
+
+
+def projection_utgs(cam, pack, pts, vel, scales, quats, opac, W, H, ua=0.1, ub=2.0, uk=0.0, thr=1e-4,
+                    max_res=0.002, margin=1.0, phm=False, elev=None):
+    pack = _f32(pack).reshape(-1)
+    pts, vel, scales, quats, opac = (_f32(a) for a in (pts, vel, scales, quats, opac))
+    n = pts.shape[0]
+    flags = np.zeros(n, np.uint8)
+    radii = np.zeros((n, 2), np.float32)
+    means2d = np.zeros((n, 2), np.float32)
+    depths = np.zeros(n, np.float32)
+    lib().xsgo_projection_utgs(C.c_int(CAM[cam]), _p(pack), _p(_f32(elev)), _p(pts), _p(vel), _p(scales),
+                               _p(quats), _p(opac), C.c_int64(n), C.c_float(W), C.c_float(H), C.c_float(ua),
+                               C.c_float(ub), C.c_float(uk), C.c_float(thr), C.c_float(max_res),
+                               C.c_float(margin), C.c_int(int(phm)), _p(flags), _p(radii), _p(means2d),
+                               _p(depths))
+    return flags, radii, means2d, depths
+
+
+def mask_radii(radii, mask=None, packed=None):
+    radii = _f32(radii).copy()
+    n = radii.shape[0]
+    m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+    pk = None if packed is None else np.ascontiguousarray(packed, dtype=np.uint32)
+    lib().xsgo_mask_radii(_p(m), _p(pk), C.c_int64(n), _p(radii))
+    return radii
+
+
+def isect_regular(means2d, radii, depths, W, H, tsx=16, tsy=16, sort=True):
+    means2d, radii, depths = _f32(means2d), _f32(radii), _f32(depths)
+    n = means2d.shape[0]
+    tpg = np.zeros(n, np.int32)
+    total = lib().xsgo_isect_regular(_p(means2d), _p(radii), _p(depths), C.c_int64(n), C.c_int(W), C.c_int(H),
+                                     C.c_int(tsx), C.c_int(tsy), C.c_int(int(sort)), _p(tpg), None, None)
+    ids = np.zeros(total, np.int64)
+    flat = np.zeros(total, np.int32)
+    lib().xsgo_isect_regular(_p(means2d), _p(radii), _p(depths), C.c_int64(n), C.c_int(W), C.c_int(H), C.c_int(tsx),
+                             C.c_int(tsy), C.c_int(int(sort)), _p(tpg), _p(ids), _p(flat))
+    return tpg, ids, flat
+
+
+def isect_spherical(lidar, pack, elev_values, pts, vel, scales, quats, opac, flags, means2d, radii, depths,
+                    elev_bounds, tsx, tsy, W, H, ua=0.1, ub=2.0, uk=0.0, sort=True):
+    pack = _f32(pack).reshape(-1)
+    pts, vel, scales, quats, opac = (_f32(a) for a in (pts, vel, scales, quats, opac))
+    means2d, radii, depths = _f32(means2d), _f32(radii), _f32(depths)
+    flags = np.ascontiguousarray(flags, dtype=np.uint8)
+    eb = _f32(elev_bounds)
+    n_eb = 0 if eb is None else eb.shape[0]
+    n = means2d.shape[0]
+    tpg = np.zeros(n, np.int32)
+    args = [C.c_int(int(lidar)), _p(pack), _p(_f32(elev_values)), _p(pts), _p(vel), _p(scales), _p(quats),
+            _p(opac), _p(flags), _p(means2d), _p(radii), _p(depths), _p(eb), C.c_int(n_eb), C.c_int64(n),
+            C.c_int(tsx), C.c_int(tsy), C.c_float(W), C.c_float(H), C.c_float(ua), C.c_float(ub), C.c_float(uk),
+            C.c_int(int(sort)), _p(tpg)]
+    total = lib().xsgo_isect_spherical(*args, None, None)
+    ids = np.zeros(total, np.int64)
+    flat = np.zeros(total, np.int32)
+    lib().xsgo_isect_spherical(*args, _p(ids), _p(flat))
+    return tpg, ids, flat
+
+
+def isect_offset_encode(isect_ids, tw, th):
+    ids = np.ascontiguousarray(isect_ids, dtype=np.int64)
+    out = np.zeros((th, tw), np.int32)
+    lib().xsgo_isect_offset_encode(_p(ids), C.c_int64(ids.shape[0]), C.c_int(tw), C.c_int(th), _p(out))
+    return out
+
+
+def rasterize_fwd(means, quats, scales, colors, opac, W, H, tsx, tsy, ray_o, ray_d, offsets, flatten,
+                  velocity=None, ray_t=None):
+    means, quats, scales, opac = (_f32(a) for a in (means, quats, scales, opac))
+    colors = _f32(colors)
+    cdim = 0 if colors is None else colors.shape[-1]
+    ray_o, ray_d, vel, ray_t = _f32(ray_o), _f32(ray_d), _f32(velocity), _f32(ray_t)
+    offsets = np.ascontiguousarray(offsets, dtype=np.int32)
+    flatten = np.ascontiguousarray(flatten, dtype=np.int32)
+    th, tw = offsets.shape
+    rgb = np.zeros((H, W, cdim), np.float32)
+    depth = np.zeros((H, W), np.float32)
+    alpha = np.zeros((H, W), np.float32)
+    last = np.zeros((H, W), np.int32)
+    near = np.zeros((H, W), np.uint8)
+    lib().xsgo_rasterize_fwd(_p(means), _p(vel), _p(quats), _p(scales), _p(colors), C.c_int(cdim), _p(opac),
+                             C.c_int(W), C.c_int(H), C.c_int(tsx), C.c_int(tsy), _p(ray_o), _p(ray_d), _p(ray_t),
+                             _p(offsets), C.c_int(tw), C.c_int(th), _p(flatten), C.c_int64(flatten.shape[0]),
+                             _p(rgb), _p(depth), _p(alpha), _p(last), _p(near))
+    return rgb, depth, alpha, last, near.astype(bool)
+
+
+def rasterize_bwd(means, quats, scales, colors, opac, W, H, tsx, tsy, ray_o, ray_d, offsets, flatten,
+                  render_alpha, last_ids, v_rgb, v_depth, v_alpha, velocity=None, ray_t=None):
+    means, quats, scales, opac = (_f32(a) for a in (means, quats, scales, opac))
+    colors = _f32(colors)
+    cdim = 0 if colors is None else colors.shape[-1]
+    ray_o, ray_d, vel, ray_t = _f32(ray_o), _f32(ray_d), _f32(velocity), _f32(ray_t)
+    offsets = np.ascontiguousarray(offsets, dtype=np.int32)
+    flatten = np.ascontiguousarray(flatten, dtype=np.int32)
+    render_alpha, v_rgb, v_depth, v_alpha = (_f32(a) for a in (render_alpha, v_rgb, v_depth, v_alpha))
+    last_ids = np.ascontiguousarray(last_ids, dtype=np.int32)
+    th, tw = offsets.shape
+    n = means.shape[0]
+    out = dict(v_means=np.zeros((n, 3), np.float32), v_quats=np.zeros((n, 4), np.float32),
+               v_scales=np.zeros((n, 3), np.float32), v_opacities=np.zeros(n, np.float32),
+               v_colors=np.zeros((n, cdim), np.float32) if cdim else None,
+               v_ray_o=np.zeros((H, W, 3), np.float32), v_ray_d=np.zeros((H, W, 3), np.float32))
+    if vel is not None:
+        out["v_velocity"] = np.zeros((n, 3), np.float32)
+        out["v_ray_t"] = np.zeros((H, W), np.float32)
+    lib().xsgo_rasterize_bwd(_p(means), _p(vel), _p(quats), _p(scales), _p(colors), C.c_int(cdim), _p(opac),
+                             C.c_int(W), C.c_int(H), C.c_int(tsx), C.c_int(tsy), _p(ray_o), _p(ray_d), _p(ray_t),
+                             _p(offsets), C.c_int(tw), C.c_int(th), _p(flatten), C.c_int64(flatten.shape[0]),
+                             C.c_int64(n), _p(render_alpha), _p(last_ids), _p(v_rgb), _p(v_depth), _p(v_alpha),
+                             _p(out["v_means"]), _p(out.get("v_velocity")), _p(out["v_quats"]),
+                             _p(out["v_scales"]), _p(out["v_colors"]), _p(out["v_opacities"]), _p(out["v_ray_o"]),
+                             _p(out["v_ray_d"]), _p(out.get("v_ray_t")))
+    return out
+
+
+def _sh_dims(coeffs, layout_3kn):
+    n = coeffs.shape[2] if layout_3kn else coeffs.shape[0]
+    return n, coeffs.shape[1]
+
+
+def sh_fwd(degree, origin, pos, coeffs, dc=None, mask=None, layout_3kn=False):
+    origin, pos, coeffs, dc = _f32(origin), _f32(pos), _f32(coeffs), _f32(dc)
+    mask = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint32)
+    n, dim = _sh_dims(coeffs, layout_3kn)
+    out = np.zeros((n, 3), np.float32)
+    lib().xsgo_sh_fwd(C.c_int(degree), _p(origin), _p(pos), _p(coeffs), _p(dc), _p(mask), C.c_int(int(layout_3kn)),
+                      C.c_int64(n), C.c_int(dim), _p(out))
+    return out
+
+
+def sh_bwd(degree, origin, pos, coeffs, d_out, dc=None, mask=None, layout_3kn=False):
+    origin, pos, coeffs, dc, d_out = _f32(origin), _f32(pos), _f32(coeffs), _f32(dc), _f32(d_out)
+    mask = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint32)
+    n, dim = _sh_dims(coeffs, layout_3kn)
+    d_coeffs = np.zeros_like(coeffs)
+    d_dc = None if dc is None else np.zeros_like(dc)
+    d_pos = np.zeros((n, 3), np.float32)
+    d_origin = np.zeros(3, np.float32)
+    lib().xsgo_sh_bwd(C.c_int(degree), _p(origin), _p(pos), _p(coeffs), _p(dc), _p(mask), C.c_int(int(layout_3kn)),
+                      C.c_int64(n), C.c_int(dim), _p(d_out), _p(d_coeffs), _p(d_dc), _p(d_pos), _p(d_origin))
+    return d_coeffs, d_dc, d_pos, d_origin

@@ -1,0 +1,4 @@
+from .ext_camera import (  # noqa: F401
+    FusedRSCamera, PerspectiveCamera, FisheyeCamera, SphericalCamera, LidarCamera,
+    look_at_quat, rotmat_to_quat, data_addr_tensor, cornering_values_from_pixel_values,
+)

@@ -1,0 +1,573 @@
+// xsimgs_b200._C — the PyTorch extension with the reference's `xsimgs._C`
+// operator surface (csrc/ext.cpp:12-20 and the bind_* functions it calls):
+// the same function and class names, keyword arguments, defaults, tensor
+// layouts and error wording.  Each op checks its tensors, allocates outputs
+// and scratch with the caching allocator and calls the C ABI of
+// libxsimgs_b200.so (include/xsimgs_b200.h) on the current CUDA stream.
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/extension.h>
+
+#include <optional>
+#include <string>
+#include <vector>
+
+#include "xsimgs_b200.h"
+
+namespace py = pybind11;
+using at::Tensor;
+using OptT = std::optional<Tensor>;
+
+namespace {
+
+void check(int rc) {
+    if (rc != XSG_OK) throw std::runtime_error(xsg_last_error());
+}
+
+xsg_stream_t stream() { return reinterpret_cast<xsg_stream_t>(c10::cuda::getCurrentCUDAStream().stream()); }
+
+void require_cuda(const Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+void require_contig(const Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+void require_f32(const Tensor& t, const char* name) {
+    TORCH_CHECK(t.scalar_type() == at::kFloat, name, " must be float32");
+}
+
+void check_tensor(const Tensor& t, const char* name, const Tensor& ref) {
+    require_cuda(t, name);
+    require_contig(t, name);
+    TORCH_CHECK(t.device() == ref.device(), name, " must be on the same device as the other inputs");
+}
+
+const float* fptr(const Tensor& t) { return t.data_ptr<float>(); }
+const float* fptr(const OptT& t) { return t.has_value() && t->defined() ? t->data_ptr<float>() : nullptr; }
+float* fptr_mut(const Tensor& t) { return t.data_ptr<float>(); }
+
+Tensor workspace(size_t bytes, const Tensor& like) {
+    return at::empty({static_cast<int64_t>(bytes > 0 ? bytes : 1)}, like.options().dtype(at::kByte));
+}
+
+bool has(const OptT& t) { return t.has_value() && t->defined(); }
+
+// -------------------------------------------------------------- cameras --
+enum class ProjectionMode : int { Central = 0, NegativeDelta = 1, PositiveDelta = 2 };
+
+constexpr float kResidualEarlyStop = 1e-4f;  // include/cameras/bind.h:17-20
+constexpr float kResidualMax = 0.002f;
+constexpr float kMaxMargin = 1.0f;
+
+struct CameraSpec {
+    int type;
+    const char* name;
+    std::vector<int> impl_dims;  // last dims of the intrinsics tensors
+};
+
+const std::vector<int> kBaseDims = {4, 3, 3, 3, 2, 1, 1};  // camera.h:144
+
+// Camera tensors -> one [1, P] float pack (layout in xsimgs_b200.h); built
+// from differentiable ATen ops, so gradients reach the camera tensors.
+Tensor camera_pack(const CameraSpec& spec, const std::vector<Tensor>& tensors) {
+    const size_t total = kBaseDims.size() + spec.impl_dims.size();
+    if (tensors.size() != total)
+        throw std::runtime_error("Tensor list size mismatch. Expected " + std::to_string(total) +
+                                 ", but found: " + std::to_string(tensors.size()));
+    std::vector<Tensor> parts;
+    for (size_t i = 0; i < tensors.size(); ++i) {
+        const Tensor& t = tensors[i];
+        TORCH_CHECK(t.scalar_type() == at::kFloat, "Camera tensors must be float32");
+        const int want = i < kBaseDims.size() ? kBaseDims[i] : spec.impl_dims[i - kBaseDims.size()];
+        TORCH_CHECK(t.dim() >= 1 && t.size(-1) == want, "Camera tensor ", i, " must have last dimension ", want);
+        TORCH_CHECK(t.numel() == want, "Only single camera is currently supported");
+        TORCH_CHECK(t.device() == tensors[0].device(), "Camera tensors must be on the same device");
+        parts.push_back(t.reshape({want}));
+        if (i == 3) parts.push_back(at::zeros({1}, t.options()));  // padding word 13
+    }
+    return at::cat(parts).view({1, -1});
+}
+
+void validate_pack(const CameraSpec& spec, const Tensor& pack) {
+    TORCH_CHECK(pack.numel() == xsg_camera_pack_words(spec.type), "Only single camera is currently supported");
+    TORCH_CHECK(pack.scalar_type() == at::kFloat, "Camera type must be float32");
+    TORCH_CHECK(pack.is_contiguous(), "Camera pack must be contiguous tensor");
+    require_cuda(pack, "camera pack");
+}
+
+py::object camera_rays(const CameraSpec& spec, const Tensor& pack, int64_t width, int64_t height,
+                       bool world_space, bool normalized, bool return_origins, bool return_valid) {
+    validate_pack(spec, pack);
+    c10::cuda::CUDAGuard g(pack.device());
+    auto opt = pack.options();
+    Tensor ray_o = return_origins ? at::empty({height, width, 3}, opt) : Tensor();
+    Tensor ray_d = at::empty({height, width, 3}, opt);
+    Tensor valid = return_valid ? at::empty({height, width}, opt.dtype(at::kBool)) : Tensor();
+    check(xsg_camera_rays(spec.type, fptr(pack), int(width), int(height), world_space, normalized,
+                          return_origins ? fptr_mut(ray_o) : nullptr, fptr_mut(ray_d),
+                          return_valid ? reinterpret_cast<uint8_t*>(valid.data_ptr()) : nullptr, stream()));
+    py::list out;
+    out.append(return_origins ? py::cast(ray_o) : py::none());
+    out.append(py::cast(ray_d));
+    if (return_valid) out.append(py::cast(valid));
+    return std::move(out);
+}
+
+Tensor pixel_time(const CameraSpec& spec, const Tensor& pack, int64_t width, int64_t height, bool delta) {
+    validate_pack(spec, pack);
+    c10::cuda::CUDAGuard g(pack.device());
+    Tensor out = at::empty({height, width}, pack.options());
+    check(xsg_pixel_time(spec.type, fptr(pack), int(width), int(height), delta, fptr_mut(out), stream()));
+    return out;
+}
+
+Tensor pixel_time_from_uv(const CameraSpec& spec, const Tensor& pack, const Tensor& uv, bool delta) {
+    validate_pack(spec, pack);
+    TORCH_CHECK(uv.size(-1) == 2, "UV coordinates last dimension must be 2");
+    TORCH_CHECK(uv.device() == pack.device(), "Camera and UV-s must be on the same device");
+    TORCH_CHECK(uv.scalar_type() == at::kFloat, "UV coordinates must be float32 tensor");
+    c10::cuda::CUDAGuard g(pack.device());
+    Tensor u = uv.contiguous();
+    auto sizes = u.sizes().vec();
+    sizes.pop_back();
+    Tensor out = at::empty(sizes, u.options());
+    check(xsg_pixel_time_from_uv(spec.type, fptr(pack), fptr(u), u.numel() / 2, delta, fptr_mut(out), stream()));
+    return out;
+}
+
+std::tuple<Tensor, Tensor> projection(const CameraSpec& spec, bool nojac, const Tensor& pack, const Tensor& points,
+                                      const OptT& vel, float thr, float max_res, float margin, ProjectionMode mode) {
+    validate_pack(spec, pack);
+    check_tensor(points, "points", pack);
+    if (has(vel)) check_tensor(*vel, "points_velocity", pack);
+    c10::cuda::CUDAGuard g(pack.device());
+    const int64_t n = points.size(0);
+    Tensor uvdt = at::empty({n, 4}, pack.options());
+    Tensor mask = at::empty({n}, pack.options().dtype(at::kBool));
+    check(xsg_projection(spec.type, fptr(pack), fptr(points), fptr(vel), n, thr, max_res, margin, int(mode), nojac,
+                         fptr_mut(uvdt), reinterpret_cast<uint8_t*>(mask.data_ptr()), stream()));
+    return {uvdt, mask};
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> projection_utgs(const CameraSpec& spec, bool phm, const Tensor& pack,
+                                                           const Tensor& points, const OptT& vel,
+                                                           const Tensor& scales, const Tensor& quats,
+                                                           const OptT& opacity, float width, float height, float ua,
+                                                           float ub, float uk, float thr, float max_res,
+                                                           float margin) {
+    validate_pack(spec, pack);
+    check_tensor(points, "points", pack);
+    check_tensor(scales, "scales", pack);
+    check_tensor(quats, "quats", pack);
+    if (has(vel)) check_tensor(*vel, "points_velocity", pack);
+    if (has(opacity)) check_tensor(*opacity, "opacity", pack);
+    c10::cuda::CUDAGuard g(pack.device());
+    const int64_t n = points.size(0);
+    auto opt = points.options();
+    Tensor flags = at::empty({n}, opt.dtype(at::kByte));
+    Tensor radii = at::empty({n, 2}, opt);
+    Tensor means2d = at::empty({n, 2}, opt);
+    Tensor depths = at::empty({n}, opt);
+    check(xsg_projection_utgs(spec.type, fptr(pack), fptr(points), fptr(vel), fptr(scales), fptr(quats),
+                              fptr(opacity), n, width, height, ua, ub, uk, thr, max_res, margin, phm,
+                              flags.data_ptr<uint8_t>(), fptr_mut(radii), fptr_mut(means2d), fptr_mut(depths),
+                              stream()));
+    return {flags, radii, means2d, depths};
+}
+
+template <typename Cls>
+void bind_camera(py::module& m, const char* name, CameraSpec spec, bool with_phm) {
+    auto cls = py::class_<Cls>(m, name);
+    cls.def_static("pack", [spec](const std::vector<Tensor>& tensors) { return camera_pack(spec, tensors); },
+                   py::arg("tensors"));
+    cls.def_static("camera_rays",
+                   [spec](const Tensor& pack, int64_t width, int64_t height, bool world_space, bool normalized,
+                          bool return_origins, bool return_valid) {
+                       return camera_rays(spec, pack, width, height, world_space, normalized, return_origins,
+                                          return_valid);
+                   },
+                   py::arg("pack"), py::arg("width"), py::arg("height"), py::arg("world_space") = true,
+                   py::arg("normalized") = true, py::arg("return_origins") = true, py::arg("return_valid") = false);
+    cls.def_static("pixel_time",
+                   [spec](const Tensor& pack, int64_t w, int64_t h) { return pixel_time(spec, pack, w, h, false); },
+                   py::arg("pack"), py::arg("width"), py::arg("height"));
+    cls.def_static("pixel_time_delta",
+                   [spec](const Tensor& pack, int64_t w, int64_t h) { return pixel_time(spec, pack, w, h, true); },
+                   py::arg("pack"), py::arg("width"), py::arg("height"));
+    cls.def_static("pixel_time_from_uv",
+                   [spec](const Tensor& pack, const Tensor& uv) { return pixel_time_from_uv(spec, pack, uv, false); },
+                   py::arg("pack"), py::arg("uvs"));
+    cls.def_static("pixel_time_delta_from_uv",
+                   [spec](const Tensor& pack, const Tensor& uv) { return pixel_time_from_uv(spec, pack, uv, true); },
+                   py::arg("pack"), py::arg("uvs"));
+    for (int nojac = 0; nojac < 2; ++nojac) {
+        cls.def_static(nojac ? "projection_nojac" : "projection",
+                       [spec, nojac](const Tensor& pack, const Tensor& points, const OptT& vel, float thr,
+                                     float max_res, float margin, ProjectionMode mode) {
+                           return projection(spec, nojac != 0, pack, points, vel, thr, max_res, margin, mode);
+                       },
+                       py::arg("pack"), py::arg("points"), py::arg("points_velocity") = py::none(),
+                       py::arg("residual_thr_early_stop") = kResidualEarlyStop,
+                       py::arg("max_residual") = kResidualMax, py::arg("max_margin") = kMaxMargin,
+                       py::arg("projection_mode") = ProjectionMode::Central);
+    }
+    for (int phm = 0; phm < (with_phm ? 2 : 1); ++phm) {
+        cls.def_static(phm ? "projection_utgs_phm" : "projection_utgs",
+                       [spec, phm](const Tensor& pack, const Tensor& points, const OptT& vel, const Tensor& scales,
+                                   const Tensor& quats, const OptT& opacity, float width, float height, float ua,
+                                   float ub, float uk, float thr, float max_res, float margin) {
+                           return projection_utgs(spec, phm != 0, pack, points, vel, scales, quats, opacity, width,
+                                                  height, ua, ub, uk, thr, max_res, margin);
+                       },
+                       py::arg("pack"), py::arg("points"), py::arg("points_velocity"), py::arg("scales"),
+                       py::arg("quats"), py::arg("opacity"), py::arg("width"), py::arg("height"),
+                       py::arg("ut_alpha") = 0.1f, py::arg("ut_beta") = 2.0f, py::arg("ut_kappa") = 0.0f,
+                       py::arg("residual_thr_early_stop") = kResidualEarlyStop,
+                       py::arg("max_residual") = kResidualMax, py::arg("max_margin") = kMaxMargin);
+    }
+}
+
+struct PerspectiveCamera {};
+struct OpenCVFisheyeCamera {};
+struct SphericalCamera {};
+struct LidarCamera {};
+
+// --------------------------------------------------------------- tiling --
+std::tuple<Tensor, Tensor, Tensor> isect_regular_tiles(const Tensor& means2d, const Tensor& radii,
+                                                       const Tensor& depths, int64_t img_width, int64_t img_height,
+                                                       int64_t tile_size_x, int64_t tile_size_y, bool sort,
+                                                       bool /*double_buffer*/) {
+    check_tensor(means2d, "means2d", means2d);
+    check_tensor(radii, "radii", means2d);
+    check_tensor(depths, "depth", means2d);
+    c10::cuda::CUDAGuard g(means2d.device());
+    const int64_t n = means2d.numel() / 2;
+    auto opt = depths.options();
+    Tensor tiles_per_gauss = at::empty_like(depths, opt.dtype(at::kInt));
+    Tensor ws = workspace(xsg_isect_workspace_size(n, 0), means2d);
+    int64_t n_isects = 0;
+    check(xsg_isect_regular_count(fptr(means2d), fptr(radii), n, int(img_width), int(img_height), int(tile_size_x),
+                                  int(tile_size_y), tiles_per_gauss.data_ptr<int32_t>(), &n_isects,
+                                  ws.data_ptr(), size_t(ws.numel()), stream()));
+    Tensor isect_ids = at::empty({n_isects}, opt.dtype(at::kLong));
+    Tensor flatten_ids = at::empty({n_isects}, opt.dtype(at::kInt));
+    if (n_isects == 0) return {tiles_per_gauss, isect_ids, flatten_ids};
+    const size_t need = xsg_isect_workspace_size(n, sort ? n_isects : 0);
+    if (size_t(ws.numel()) < need) ws = workspace(need, means2d);
+    check(xsg_isect_regular_emit(fptr(means2d), fptr(radii), fptr(depths), n, int(img_width), int(img_height),
+                                 int(tile_size_x), int(tile_size_y), sort, tiles_per_gauss.data_ptr<int32_t>(),
+                                 n_isects, isect_ids.data_ptr<int64_t>(), flatten_ids.data_ptr<int32_t>(),
+                                 ws.data_ptr(), size_t(ws.numel()), stream()));
+    return {tiles_per_gauss, isect_ids, flatten_ids};
+}
+
+std::tuple<Tensor, Tensor, Tensor> isect_range_tiles(bool lidar, const Tensor& pack, const Tensor& points,
+                                                     const OptT& vel, const Tensor& scale, const Tensor& quat,
+                                                     const OptT& opacity, const Tensor& flag, const Tensor& means2d,
+                                                     const Tensor& radii, const Tensor& depths, const OptT& elev,
+                                                     int64_t tsx, int64_t tsy, float W, float H, float ua, float ub,
+                                                     float uk, bool sort) {
+    TORCH_CHECK(pack.is_cuda(), "camera_pack must be CUDA tensor");
+    for (auto* t : {&pack, &points, &scale, &quat, &flag, &means2d, &radii, &depths}) check_tensor(*t, "input", pack);
+    if (has(vel)) check_tensor(*vel, "points_velocity", pack);
+    if (has(opacity)) check_tensor(*opacity, "opacity", pack);
+    if (lidar) check_tensor(*elev, "elev_boundaries", pack);
+    TORCH_CHECK(pack.numel() == xsg_camera_pack_words(lidar ? XSG_CAM_LIDAR : XSG_CAM_SPHERICAL),
+                "Only single camera is currently supported");
+    c10::cuda::CUDAGuard g(pack.device());
+    const int64_t n = means2d.numel() / 2;
+    auto opt = depths.options();
+    Tensor tiles_per_gauss = at::zeros_like(depths, opt.dtype(at::kInt));
+    const float* eb = lidar ? fptr(*elev) : nullptr;
+    const int n_elev = lidar ? int(elev->size(0)) : 0;
+    Tensor ws = workspace(xsg_isect_workspace_size(n, 0), means2d);
+    int64_t n_isects = 0;
+    check(xsg_isect_spherical_count(lidar, fptr(pack), fptr(points), fptr(vel), fptr(scale), fptr(quat), fptr(opacity),
+                                    flag.data_ptr<uint8_t>(), fptr(means2d), fptr(radii), fptr(depths), eb, n_elev, n,
+                                    int(tsx), int(tsy), W, H, ua, ub, uk, tiles_per_gauss.data_ptr<int32_t>(),
+                                    &n_isects, ws.data_ptr(), size_t(ws.numel()), stream()));
+    Tensor isect_ids = at::empty({n_isects}, opt.dtype(at::kLong));
+    Tensor flatten_ids = at::empty({n_isects}, opt.dtype(at::kInt));
+    if (n_isects == 0) return {tiles_per_gauss, isect_ids, flatten_ids};
+    const size_t need = xsg_isect_workspace_size(n, sort ? n_isects : 0);
+    if (size_t(ws.numel()) < need) ws = workspace(need, means2d);
+    check(xsg_isect_spherical_emit(lidar, fptr(pack), fptr(points), fptr(vel), fptr(scale), fptr(quat), fptr(opacity),
+                                   flag.data_ptr<uint8_t>(), fptr(means2d), fptr(radii), fptr(depths), eb, n_elev, n,
+                                   int(tsx), int(tsy), W, H, ua, ub, uk, sort, tiles_per_gauss.data_ptr<int32_t>(),
+                                   n_isects, isect_ids.data_ptr<int64_t>(), flatten_ids.data_ptr<int32_t>(),
+                                   ws.data_ptr(), size_t(ws.numel()), stream()));
+    return {tiles_per_gauss, isect_ids, flatten_ids};
+}
+
+Tensor isect_offset_encode(const Tensor& isect_ids, int64_t tile_width, int64_t tile_height) {
+    TORCH_CHECK(isect_ids.is_cuda() && isect_ids.is_contiguous(), "isect_ids must be contiguous cuda tensor");
+    c10::cuda::CUDAGuard g(isect_ids.device());
+    const int64_t n = isect_ids.size(0);
+    Tensor offsets = at::empty({tile_height, tile_width}, isect_ids.options().dtype(at::kInt));
+    check(xsg_isect_offset_encode(n ? isect_ids.data_ptr<int64_t>() : nullptr, n, int(tile_width), int(tile_height),
+                                  offsets.data_ptr<int32_t>(), stream()));
+    return offsets;
+}
+
+void mask_radii(const Tensor& mask, const Tensor& radii) {
+    if (radii.size(-1) != 2) throw std::runtime_error("radii must be [..., 2] tensor");
+    TORCH_CHECK(mask.scalar_type() == at::kBool, "Mask must be torch.bool tensor");
+    const int64_t n = radii.numel() / 2;
+    TORCH_CHECK(mask.numel() == n, "Mask size mismatch with radii");
+    check_tensor(mask, "mask", radii);
+    check_tensor(radii, "radii", radii);
+    c10::cuda::CUDAGuard g(radii.device());
+    check(xsg_mask_radii(reinterpret_cast<const uint8_t*>(mask.data_ptr()), nullptr, n, fptr_mut(radii), stream()));
+}
+
+void mask_radii_packed(const Tensor& packed_mask, const Tensor& radii) {
+    if (radii.size(-1) != 2) throw std::runtime_error("radii must be [..., 2] tensor");
+    TORCH_CHECK(packed_mask.element_size() == 4 && !packed_mask.is_floating_point(),
+                "Packed mask must be UInt32 tensor");
+    const int64_t n = radii.numel() / 2;
+    TORCH_CHECK(packed_mask.numel() * 32 >= n, "Packed mask size mismatch with radii");
+    check_tensor(packed_mask, "packed_mask", radii);
+    check_tensor(radii, "radii", radii);
+    c10::cuda::CUDAGuard g(radii.device());
+    check(xsg_mask_radii(nullptr, reinterpret_cast<const uint32_t*>(packed_mask.data_ptr()), n, fptr_mut(radii),
+                         stream()));
+}
+
+// ---------------------------------------------------------- rasteriser ---
+std::vector<int64_t> eval3d_supported_ndims() {
+    int buf[64];
+    const int n = xsg_raster_supported_channels(buf, 64);
+    return std::vector<int64_t>(buf, buf + n);
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> raster_fwd(const Tensor& means, const OptT& velocity, const Tensor& quats,
+                                                      const Tensor& scales, const OptT& colors,
+                                                      const Tensor& opacities, int64_t W, int64_t H, int64_t tsx,
+                                                      int64_t tsy, const Tensor& ray_o, const Tensor& ray_d,
+                                                      const OptT& ray_t, const Tensor& tile_offsets,
+                                                      const Tensor& flatten_ids) {
+    for (auto* t : {&means, &quats, &scales, &opacities, &ray_o, &ray_d, &tile_offsets, &flatten_ids})
+        check_tensor(*t, "rasterize input", means);
+    if (has(colors)) check_tensor(*colors, "colors", means);
+    if (has(velocity)) check_tensor(*velocity, "velocity", means);
+    if (has(ray_t)) check_tensor(*ray_t, "ray_time_delta", means);
+    c10::cuda::CUDAGuard g(means.device());
+    const int64_t channels = has(colors) ? colors->size(-1) : 0;
+    const int64_t n = means.numel() / 3;
+    auto opt = means.options();
+    Tensor renders = at::empty({H, W, channels}, opt);
+    Tensor depths = at::empty({H, W}, opt);
+    Tensor alphas = at::empty({H, W}, opt);
+    Tensor last_ids = at::empty({H, W}, opt.dtype(at::kInt));
+    Tensor ws = workspace(xsg_rasterize_workspace_size(n, int(channels)), means);
+    check(xsg_rasterize_fwd(fptr(means), fptr(velocity), fptr(quats), fptr(scales), fptr(colors), int(channels),
+                            fptr(opacities), n, int(W), int(H), int(tsx), int(tsy), fptr(ray_o), fptr(ray_d),
+                            fptr(ray_t), tile_offsets.data_ptr<int32_t>(), int(tile_offsets.size(-1)),
+                            int(tile_offsets.size(-2)), flatten_ids.data_ptr<int32_t>(), flatten_ids.numel(),
+                            channels ? fptr_mut(renders) : nullptr, fptr_mut(depths), fptr_mut(alphas),
+                            last_ids.data_ptr<int32_t>(), ws.data_ptr(), size_t(ws.numel()), stream()));
+    return {renders, depths, alphas, last_ids};
+}
+
+struct BwdOut {
+    Tensor v_points, v_velocity, v_quat, v_scale, v_opacity;
+    OptT v_colors;
+    Tensor v_ray_o, v_ray_d, v_time;
+};
+
+BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scale, const Tensor& quat,
+                  const Tensor& opacity, const OptT& colors, const Tensor& ray_o, const Tensor& ray_d,
+                  const OptT& ray_t, int64_t tsx, int64_t tsy, const Tensor& tile_offsets, const Tensor& flatten_ids,
+                  const Tensor& render_alpha, const Tensor& last_ids, const OptT& v_colors_in, const Tensor& v_depth,
+                  const Tensor& v_alpha) {
+    if (has(v_colors_in) && !v_colors_in->is_contiguous())
+        throw std::runtime_error("v_render_colors must be contiguous");
+    for (auto* t : {&points, &scale, &quat, &opacity, &ray_o, &ray_d, &tile_offsets, &flatten_ids, &render_alpha,
+                    &last_ids, &v_depth, &v_alpha})
+        check_tensor(*t, "rasterize_bwd input", points);
+    if (has(colors)) check_tensor(*colors, "colors", points);
+    if (has(velocity)) check_tensor(*velocity, "velocity", points);
+    c10::cuda::CUDAGuard g(points.device());
+    const int64_t H = ray_o.size(0), W = ray_o.size(1);
+    const int64_t n = points.numel() / 3;
+    const int64_t cdim = has(colors) ? colors->size(1) : 0;
+    BwdOut o;
+    o.v_points = at::empty_like(points);
+    o.v_scale = at::empty_like(scale);
+    o.v_quat = at::empty_like(quat);
+    o.v_opacity = at::empty_like(opacity);
+    if (has(colors)) o.v_colors = at::empty_like(*colors);
+    o.v_ray_o = at::empty_like(ray_o);
+    o.v_ray_d = at::empty_like(ray_d);
+    const bool dyn = has(velocity);
+    if (dyn) {
+        o.v_velocity = at::empty_like(*velocity);
+        o.v_time = at::empty_like(*ray_t);
+    }
+    Tensor ws = workspace(xsg_rasterize_workspace_size(n, int(cdim)), points);
+    check(xsg_rasterize_bwd(fptr(points), fptr(velocity), fptr(quat), fptr(scale), fptr(colors), int(cdim),
+                            fptr(opacity), n, int(W), int(H), int(tsx), int(tsy), fptr(ray_o), fptr(ray_d),
+                            fptr(ray_t), tile_offsets.data_ptr<int32_t>(), int(tile_offsets.size(1)),
+                            int(tile_offsets.size(0)), flatten_ids.data_ptr<int32_t>(), flatten_ids.numel(),
+                            fptr(render_alpha), last_ids.data_ptr<int32_t>(), fptr(v_colors_in), fptr(v_depth),
+                            fptr(v_alpha), fptr_mut(o.v_points), dyn ? fptr_mut(o.v_velocity) : nullptr,
+                            fptr_mut(o.v_quat), fptr_mut(o.v_scale), has(colors) ? fptr_mut(*o.v_colors) : nullptr,
+                            fptr_mut(o.v_opacity), fptr_mut(o.v_ray_o), fptr_mut(o.v_ray_d),
+                            dyn ? fptr_mut(o.v_time) : nullptr, ws.data_ptr(), size_t(ws.numel()), stream()));
+    return o;
+}
+
+// ------------------------------------------------------------------ SH ---
+Tensor sh_fwd(int64_t degree, const Tensor& origin, const Tensor& positions, const Tensor& coeffs, const OptT& mask,
+              bool layout_3kn, const OptT& coeffs_dc, const OptT& output) {
+    for (auto* t : {&origin, &positions, &coeffs}) check_tensor(*t, "spherical harmonics input", positions);
+    if (has(mask)) check_tensor(*mask, "mask", positions);
+    if (has(coeffs_dc)) check_tensor(*coeffs_dc, "coeffs_dc", positions);
+    if (has(output)) check_tensor(*output, "output", positions);
+    TORCH_CHECK(coeffs.dim() == 3 && coeffs.size(layout_3kn ? 0 : 2) == 3,
+                "coeffs tensor must be [3, K, N] if layout_3kn else [N, K, 3]");
+    const int64_t n = layout_3kn ? coeffs.size(2) : coeffs.size(0);
+    const int64_t dim = coeffs.size(1);
+    if (has(coeffs_dc)) {
+        const auto dd = coeffs_dc->dim();
+        TORCH_CHECK(dd == 2 || dd == 3, "coeffs_dc must be 2D or 3D");
+        const int64_t ch_axis = layout_3kn ? 0 : dd - 1, n_axis = layout_3kn ? dd - 1 : 0;
+        TORCH_CHECK(coeffs_dc->size(ch_axis) == 3 && coeffs_dc->size(n_axis) == n && coeffs_dc->numel() == 3 * n,
+                    "coeffs_dc must hold a single SH band: [N, 3] or [N, 1, 3] if !layout_3kn else [3, N] or [3, 1, N]");
+    }
+    c10::cuda::CUDAGuard g(positions.device());
+    Tensor out = has(output) ? *output : at::zeros({n, 3}, positions.options());
+    check(xsg_sh_fwd(int(degree), fptr(origin), fptr(positions), fptr(coeffs), fptr(coeffs_dc),
+                     has(mask) ? reinterpret_cast<const uint32_t*>(mask->data_ptr()) : nullptr, layout_3kn, n, int(dim),
+                     fptr_mut(out), stream()));
+    return out;
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> sh_bwd(int64_t degree, const Tensor& origin, const Tensor& positions,
+                                                  const Tensor& coeffs, const OptT& mask, bool layout_3kn,
+                                                  const Tensor& d_output, const OptT& coeffs_dc) {
+    TORCH_CHECK(d_output.is_contiguous(), "d_output must be contiguous");
+    for (auto* t : {&origin, &positions, &coeffs, &d_output}) check_tensor(*t, "spherical harmonics input", positions);
+    if (has(mask)) check_tensor(*mask, "mask", positions);
+    if (has(coeffs_dc)) check_tensor(*coeffs_dc, "coeffs_dc", positions);
+    c10::cuda::CUDAGuard g(positions.device());
+    const int64_t n = layout_3kn ? coeffs.size(2) : coeffs.size(0);
+    const int64_t dim = coeffs.size(1);
+    Tensor d_coeffs = at::empty_like(coeffs);
+    Tensor d_dc = has(coeffs_dc) ? at::empty_like(*coeffs_dc) : at::empty({0}, coeffs.options());
+    Tensor d_pos = at::empty_like(positions);
+    Tensor d_origin = at::empty({3}, origin.options());
+    Tensor ws = workspace(xsg_sh_bwd_workspace_size(n), positions);
+    check(xsg_sh_bwd(int(degree), fptr(origin), fptr(positions), fptr(coeffs), fptr(coeffs_dc),
+                     has(mask) ? reinterpret_cast<const uint32_t*>(mask->data_ptr()) : nullptr, layout_3kn, n, int(dim),
+                     fptr(d_output), fptr_mut(d_coeffs), has(coeffs_dc) ? fptr_mut(d_dc) : nullptr, fptr_mut(d_pos),
+                     fptr_mut(d_origin), ws.data_ptr(), size_t(ws.numel()), stream()));
+    return {d_coeffs, d_dc, d_pos, d_origin};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.doc() = "xsimgs-b200: B200-native kernels behind the xsimgs._C operator surface";
+    m.def("version", []() { return std::string(xsg_version()); });
+
+    py::enum_<ProjectionMode>(m, "ProjectionMode")
+        .value("Central", ProjectionMode::Central)
+        .value("NegativeDelta", ProjectionMode::NegativeDelta)
+        .value("PositiveDelta", ProjectionMode::PositiveDelta);
+
+    bind_camera<PerspectiveCamera>(m, "PerspectiveCamera", {XSG_CAM_PINHOLE, "PerspectiveCamera", {4}}, false);
+    bind_camera<OpenCVFisheyeCamera>(m, "OpenCVFisheyeCamera", {XSG_CAM_FISHEYE, "OpenCVFisheyeCamera", {4, 4}}, false);
+    bind_camera<SphericalCamera>(m, "SphericalCamera", {XSG_CAM_SPHERICAL, "SphericalCamera", {4}}, true);
+    bind_camera<LidarCamera>(m, "LidarCamera", {XSG_CAM_LIDAR, "LidarCamera", {4, 2}}, true);
+
+    m.def("isect_regular_tiles", &isect_regular_tiles, py::arg("means2d"), py::arg("radii"), py::arg("depth"),
+          py::arg("img_width"), py::arg("img_height"), py::arg("tile_size_x"), py::arg("tile_size_y"),
+          py::arg("sort") = true, py::arg("double_buffer") = true);
+    m.def("isect_lidar_tiles",
+          [](const Tensor& pack, const Tensor& points, const OptT& vel, const Tensor& scale, const Tensor& quat,
+             const OptT& opacity, const Tensor& flag, const Tensor& means2d, const Tensor& radii, const Tensor& depths,
+             const Tensor& elev_boundaries, int64_t tile_size_x, float img_width, float img_height, float ua, float ub,
+             float uk, bool sort, bool /*double_buffer*/) {
+              return isect_range_tiles(true, pack, points, vel, scale, quat, opacity, flag, means2d, radii, depths,
+                                       elev_boundaries, tile_size_x, 1, img_width, img_height, ua, ub, uk, sort);
+          },
+          py::arg("camera_pack"), py::arg("points"), py::arg("points_velocity"), py::arg("scale"), py::arg("quat"),
+          py::arg("opacity"), py::arg("flag"), py::arg("means2d"), py::arg("radii"), py::arg("depths"),
+          py::arg("elev_boundaries"), py::arg("tile_size_x"), py::arg("img_width"), py::arg("img_height"),
+          py::arg("ut_alpha") = 0.1f, py::arg("ut_beta") = 2.0f, py::arg("ut_kappa") = 0.0f, py::arg("sort") = true,
+          py::arg("double_buffer") = true);
+    m.def("isect_spherical_tiles",
+          [](const Tensor& pack, const Tensor& points, const OptT& vel, const Tensor& scale, const Tensor& quat,
+             const OptT& opacity, const Tensor& flag, const Tensor& means2d, const Tensor& radii, const Tensor& depths,
+             int64_t tile_size_x, int64_t tile_size_y, float img_width, float img_height, float ua, float ub, float uk,
+             bool sort, bool /*double_buffer*/) {
+              return isect_range_tiles(false, pack, points, vel, scale, quat, opacity, flag, means2d, radii, depths,
+                                       std::nullopt, tile_size_x, tile_size_y, img_width, img_height, ua, ub, uk,
+                                       sort);
+          },
+          py::arg("camera_pack"), py::arg("points"), py::arg("points_velocity"), py::arg("scale"), py::arg("quat"),
+          py::arg("opacity"), py::arg("flag"), py::arg("means2d"), py::arg("radii"), py::arg("depths"),
+          py::arg("tile_size_x"), py::arg("tile_size_y"), py::arg("img_width"), py::arg("img_height"),
+          py::arg("ut_alpha") = 0.1f, py::arg("ut_beta") = 2.0f, py::arg("ut_kappa") = 0.0f, py::arg("sort") = true,
+          py::arg("double_buffer") = true);
+    m.def("isect_offset_encode", &isect_offset_encode, py::arg("isect_ids"), py::arg("tile_width"),
+          py::arg("tile_height"));
+    m.def("mask_radii_packed", &mask_radii_packed, py::arg("packed_mask"), py::arg("radii"));
+    m.def("mask_radii", &mask_radii, py::arg("mask"), py::arg("radii"));
+
+    m.def("eval3d_supported_ndims", &eval3d_supported_ndims);
+    m.def("rasterize_eval3d_fwd",
+          [](const Tensor& means, const Tensor& quats, const Tensor& scales, const OptT& colors, const Tensor& opac,
+             int64_t W, int64_t H, int64_t tsx, int64_t tsy, const Tensor& ray_o, const Tensor& ray_d,
+             const Tensor& offsets, const Tensor& flatten) {
+              return raster_fwd(means, std::nullopt, quats, scales, colors, opac, W, H, tsx, tsy, ray_o, ray_d,
+                                std::nullopt, offsets, flatten);
+          },
+          py::arg("means"), py::arg("quats"), py::arg("scales"), py::arg("colors"), py::arg("opacities"),
+          py::arg("image_width"), py::arg("image_height"), py::arg("tile_size_width"), py::arg("tile_size_height"),
+          py::arg("ray_origs"), py::arg("ray_dirs"), py::arg("tile_offsets"), py::arg("flatten_ids"));
+    m.def("rasterize_eval3d_dynamic_fwd",
+          [](const Tensor& means, const OptT& vel, const Tensor& quats, const Tensor& scales, const OptT& colors,
+             const Tensor& opac, int64_t W, int64_t H, int64_t tsx, int64_t tsy, const Tensor& ray_o,
+             const Tensor& ray_d, const OptT& ray_t, const Tensor& offsets, const Tensor& flatten) {
+              return raster_fwd(means, vel, quats, scales, colors, opac, W, H, tsx, tsy, ray_o, ray_d, ray_t,
+                                offsets, flatten);
+          },
+          py::arg("means"), py::arg("velocity"), py::arg("quats"), py::arg("scales"), py::arg("colors"),
+          py::arg("opacities"), py::arg("image_width"), py::arg("image_height"), py::arg("tile_size_width"),
+          py::arg("tile_size_height"), py::arg("ray_origs"), py::arg("ray_dirs"), py::arg("ray_time_delta"),
+          py::arg("tile_offsets"), py::arg("flatten_ids"));
+    m.def("rasterize_eval3d_bwd",
+          [](const Tensor& points, const Tensor& scale, const Tensor& quat, const Tensor& opacity, const OptT& colors,
+             const Tensor& ray_o, const Tensor& ray_d, int64_t tsx, int64_t tsy, const Tensor& offsets,
+             const Tensor& flatten, const Tensor& render_alpha, const Tensor& last_ids, const OptT& v_colors,
+             const Tensor& v_depth, const Tensor& v_alpha) {
+              BwdOut o = raster_bwd(points, std::nullopt, scale, quat, opacity, colors, ray_o, ray_d, std::nullopt,
+                                    tsx, tsy, offsets, flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha);
+              return py::make_tuple(o.v_points, o.v_quat, o.v_scale, o.v_opacity,
+                                    o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), o.v_ray_o, o.v_ray_d);
+          });
+    m.def("rasterize_eval3d_dynamic_bwd",
+          [](const Tensor& points, const Tensor& vel, const Tensor& scale, const Tensor& quat, const Tensor& opacity,
+             const OptT& colors, const Tensor& ray_o, const Tensor& ray_d, const Tensor& ray_t, int64_t tsx,
+             int64_t tsy, const Tensor& offsets, const Tensor& flatten, const Tensor& render_alpha,
+             const Tensor& last_ids, const OptT& v_colors, const Tensor& v_depth, const Tensor& v_alpha) {
+              check_tensor(vel, "velocity", points);
+              check_tensor(ray_t, "ray_time_delta", points);
+              BwdOut o = raster_bwd(points, vel, scale, quat, opacity, colors, ray_o, ray_d, ray_t, tsx, tsy, offsets,
+                                    flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha);
+              return py::make_tuple(o.v_points, o.v_velocity, o.v_quat, o.v_scale, o.v_opacity,
+                                    o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), o.v_ray_o, o.v_ray_d,
+                                    o.v_time);
+          });
+
+    m.def("spherical_harmonics_fused_fwd", &sh_fwd, py::arg("degree_to_use"), py::arg("origin"),
+          py::arg("positions"), py::arg("coeffs"), py::arg("mask"), py::arg("layout_3kn"),
+          py::arg("coeffs_dc") = py::none(), py::arg("output") = py::none());
+    m.def("spherical_harmonics_fused_bwd", &sh_bwd, py::arg("degree_to_use"), py::arg("origin"),
+          py::arg("positions"), py::arg("coeffs"), py::arg("mask"), py::arg("layout_3kn"), py::arg("d_output"),
+          py::arg("coeffs_dc") = py::none());
+}

@@ -1,0 +1,766 @@
+// Per-tile 3D-evaluation alpha compositing, forward and backward, for
+// sm_100a.  Semantics: rasterize_eval3d_fwd / _bwd and their dynamic
+// variants in the reference (csrc/rasterization/eval3d_fwd.cu:34-166,
+// eval3d_bwd.cu:38-294, eval3d_dynamic_fwd.cu:38-173,
+// eval3d_dynamic_bwd.cu:68-310).
+//
+// Design (B200):
+//  * A pack kernel turns each Gaussian into one 64-byte record
+//      {M row 0, mu.x} {M row 1, mu.y} {M row 2, mu.z} {opacity, velocity}
+//    with M = S^-1 R^T computed exactly as the reference does per load, so
+//    the tile loops fetch one aligned record (4 x 16 B) per intersection
+//    instead of gathering five arrays.
+//  * One CTA per image tile (one thread per pixel), batches of records staged
+//    in shared memory, block-wide early exit when every pixel is saturated.
+//  * Static scenes whose tile shares one ray origin (global shutter: every
+//    pixel of the tile has bitwise the same ray_o) compute M (o - mu) once per
+//    Gaussian while staging instead of once per pixel — the same arithmetic,
+//    so the same bits.
+//  * Backward: per (warp, Gaussian) the 16 gradient values are reduced with a
+//    transpose butterfly (16 shuffles instead of 80), pre-reduced across the
+//    CTA's warps in shared memory, and flushed once per (tile, Gaussian) with
+//    vector reductions (red.global.add.v4.f32) into a 16-float-per-Gaussian
+//    accumulator; a final pass scatters that into the output layout.
+#include "common.cuh"
+
+namespace xsg {
+
+constexpr int kRecF4 = 4;  // float4 words per Gaussian record
+
+struct RasterArgs {
+    const float4* rec;        // [N][4]
+    const float* means;       // [N,3] (bwd)
+    const float* quats;       // [N,4] (bwd)
+    const float* scales;      // [N,3] (bwd)
+    const float* colors;      // [N,C]
+    const float* ray_o;       // [H,W,3]
+    const float* ray_d;       // [H,W,3]
+    const float* ray_t;       // [H,W] (dynamic)
+    const int32_t* offsets;   // [tiles]
+    const int32_t* flatten;   // [n_isects]
+    int64_t n_isects;
+    int W, H, tsx, tsy, ntx, nty;
+    // forward outputs
+    float* out_rgb;
+    float* out_depth;
+    float* out_alpha;
+    int32_t* out_last;
+    // backward inputs/outputs
+    const float* render_alpha;
+    const int32_t* last_ids;
+    const float* v_rgb;
+    const float* v_depth;
+    const float* v_alpha;
+    float* G;                 // [N][NACC] gradient accumulator
+    float* v_colors_direct;   // [N,C] when C > 4
+    float* v_ray_o;
+    float* v_ray_d;
+    float* v_ray_t;
+    unsigned long long* pair_counters;  // evaluated, contributing (optional)
+};
+
+static unsigned long long* g_pair_counters = nullptr;
+
+// --------------------------------------------------------------- pack ----
+// quat_to_rotmat (rasterization/utils.h:61-83) and S^-1 R^T
+// (eval3d_fwd.cu:92-106): row i of M is (1 / s_i) * column i of R.
+__global__ void pack_records_kernel(const float* __restrict__ means, const float* __restrict__ vel,
+                                    const float* __restrict__ quats, const float* __restrict__ scales,
+                                    const float* __restrict__ opac, int64_t n, float4* __restrict__ rec) {
+    const int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    float w = quats[4 * g], x = quats[4 * g + 1], y = quats[4 * g + 2], z = quats[4 * g + 3];
+    const float inv_norm = rsqrtf(x * x + y * y + z * z + w * w);
+    x *= inv_norm; y *= inv_norm; z *= inv_norm; w *= inv_norm;
+    const float x2 = x * x, y2 = y * y, z2 = z * z;
+    const float xy = x * y, xz = x * z, yz = y * z;
+    const float wx = w * x, wy = w * y, wz = w * z;
+    // columns of R
+    const float c00 = 1.f - 2.f * (y2 + z2), c01 = 2.f * (xy + wz), c02 = 2.f * (xz - wy);
+    const float c10 = 2.f * (xy - wz), c11 = 1.f - 2.f * (x2 + z2), c12 = 2.f * (yz + wx);
+    const float c20 = 2.f * (xz + wy), c21 = 2.f * (yz - wx), c22 = 1.f - 2.f * (x2 + y2);
+    const float sx = 1.0f / scales[3 * g], sy = 1.0f / scales[3 * g + 1], sz = 1.0f / scales[3 * g + 2];
+    float4* r = rec + kRecF4 * g;
+    r[0] = make_float4(sx * c00, sx * c01, sx * c02, means[3 * g]);
+    r[1] = make_float4(sy * c10, sy * c11, sy * c12, means[3 * g + 1]);
+    r[2] = make_float4(sz * c20, sz * c21, sz * c22, means[3 * g + 2]);
+    if (vel) r[3] = make_float4(opac[g], vel[3 * g], vel[3 * g + 1], vel[3 * g + 2]);
+    else r[3] = make_float4(opac[g], 0.f, 0.f, 0.f);
+}
+
+struct TileCtx {
+    int tile, px, py;
+    bool inside;
+    int64_t pix;
+    int32_t start, end;
+};
+
+__device__ __forceinline__ TileCtx tile_ctx(const RasterArgs& a) {
+    TileCtx c;
+    c.tile = blockIdx.x;
+    const int ty = c.tile / a.ntx, tx = c.tile - ty * a.ntx;
+    const int t = threadIdx.x;
+    c.px = tx * a.tsx + t % a.tsx;
+    c.py = ty * a.tsy + t / a.tsx;
+    c.inside = c.px < a.W && c.py < a.H;
+    const int64_t lin = int64_t(c.py) * a.W + c.px;
+    const int64_t last = int64_t(a.W) * a.H - 1;
+    c.pix = lin < last ? lin : last;
+    c.start = a.offsets[c.tile];
+    c.end = (c.tile == a.ntx * a.nty - 1) ? int32_t(a.n_isects) : a.offsets[c.tile + 1];
+    return c;
+}
+
+// M v with M rows (r0,r1,r2).xyz, in glm's mat3 * vec3 order
+__device__ __forceinline__ v3 mrows(float4 r0, float4 r1, float4 r2, v3 v) {
+    return mk3(r0.x * v.x + r0.y * v.y + r0.z * v.z, r1.x * v.x + r1.y * v.y + r1.z * v.z,
+               r2.x * v.x + r2.y * v.y + r2.z * v.z);
+}
+
+// All pixels of the tile that lie inside the image see the same ray origin
+// (thread 0's pixel, the tile's top-left, is always inside); returns it in o_tile.
+__device__ __forceinline__ bool tile_origin_uniform(const TileCtx& c, v3 o, v3& o_tile) {
+    __shared__ float s_o[3];
+    if (threadIdx.x == 0) { s_o[0] = o.x; s_o[1] = o.y; s_o[2] = o.z; }
+    __syncthreads();
+    o_tile = mk3(s_o[0], s_o[1], s_o[2]);
+    const bool same = !c.inside || (__float_as_uint(o.x) == __float_as_uint(o_tile.x) &&
+                                    __float_as_uint(o.y) == __float_as_uint(o_tile.y) &&
+                                    __float_as_uint(o.z) == __float_as_uint(o_tile.z));
+    return __syncthreads_and(same) != 0;
+}
+
+// ------------------------------------------------------------ forward ----
+template <int CDIM, bool kDyn>
+__global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
+    constexpr bool kStageColor = CDIM > 0 && CDIM <= 4;
+    constexpr int CSZ = CDIM > 0 ? CDIM : 1;
+    extern __shared__ float4 smem4[];
+    const int bs = blockDim.x;
+    float4* s0 = smem4;
+    float4* s1 = s0 + bs;
+    float4* s2 = s1 + bs;
+    float4* s3 = s2 + bs;
+    float4* sc = s3 + bs;                                    // colours (C <= 4)
+    int32_t* sid = reinterpret_cast<int32_t*>(sc + bs);       // Gaussian ids (C > 4)
+
+    const TileCtx c = tile_ctx(a);
+    const int tr = threadIdx.x;
+    const v3 o = c.inside ? ld3(a.ray_o + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
+    const v3 d = c.inside ? ld3(a.ray_d + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
+    const float rt = (kDyn && c.inside && a.ray_t) ? a.ray_t[c.pix] : 0.0f;
+    v3 o_tile = o;
+    const bool uni = !kDyn && tile_origin_uniform(c, o, o_tile);
+
+    bool done = !c.inside;
+    float T = 1.0f, depth = 0.0f;
+    float acc[CSZ];
+#pragma unroll
+    for (int k = 0; k < CSZ; ++k) acc[k] = 0.f;
+    int32_t cur = 0;
+    unsigned n_eval = 0, n_contrib = 0;
+    const int nb = (c.end - c.start + bs - 1) / bs;
+    for (int b = 0; b < nb; ++b) {
+        if (__syncthreads_count(done) >= bs) break;
+        const int32_t bstart = c.start + b * bs;
+        const int32_t idx = bstart + tr;
+        if (idx < c.end) {
+            const int32_t g = a.flatten[idx];
+            const float4* r = a.rec + int64_t(kRecF4) * g;
+            float4 r0 = r[0], r1 = r[1], r2 = r[2];
+            const float4 r3 = r[3];
+            if (uni) {
+                // gro = M (o - mu), once per Gaussian for the whole tile
+                const v3 omm = o_tile - mk3(r0.w, r1.w, r2.w);
+                const v3 gro = mrows(r0, r1, r2, omm);
+                r0.w = gro.x; r1.w = gro.y; r2.w = gro.z;
+            }
+            s0[tr] = r0; s1[tr] = r1; s2[tr] = r2; s3[tr] = r3;
+            if constexpr (kStageColor) {
+                float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
+                const float* cp = a.colors + int64_t(g) * CDIM;
+                cc.x = cp[0];
+                if (CDIM > 1) cc.y = cp[1];
+                if (CDIM > 2) cc.z = cp[2];
+                if (CDIM > 3) cc.w = cp[3];
+                sc[tr] = cc;
+            } else {
+                sid[tr] = g;
+            }
+        }
+        __syncthreads();
+        const int bsize = min(bs, c.end - bstart);
+        for (int t = 0; (t < bsize) && !done; ++t) {
+            const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
+            ++n_eval;
+            v3 gro;
+            if (uni) {
+                gro = mk3(r0.w, r1.w, r2.w);
+            } else {
+                v3 mu = mk3(r0.w, r1.w, r2.w);
+                if (kDyn) mu = mu + rt * mk3(r3.y, r3.z, r3.w);
+                gro = mrows(r0, r1, r2, o - mu);
+            }
+            const v3 grd = mrows(r0, r1, r2, d);
+            const float l = dot3(grd, grd);
+            const v3 gn = l > 0.0f ? grd * rsqrtf(l) : grd;
+            const v3 gc = cross3(gn, gro);
+            const float power = -0.5f * dot3(gc, gc);
+            const float alpha = fminf(0.999f, r3.x * __expf(power));
+            if (alpha < 1.f / 255.f) continue;
+            const float hit_t = -dot3(gro, grd) / dot3(grd, grd);
+            const float nT = T * (1.0f - alpha);
+            if (nT <= 1e-4f) {
+                done = true;
+                break;
+            }
+            const float vis = alpha * T;
+            depth += vis * hit_t;
+            if constexpr (kStageColor) {
+                const float4 cc = sc[t];
+                acc[0] += cc.x * vis;
+                if (CDIM > 1) acc[1] += cc.y * vis;
+                if (CDIM > 2) acc[2] += cc.z * vis;
+                if (CDIM > 3) acc[3] += cc.w * vis;
+            } else if constexpr (CDIM > 0) {
+                const float* cp = a.colors + int64_t(sid[t]) * CDIM;
+#pragma unroll 4
+                for (int k = 0; k < CDIM; ++k) acc[k] += cp[k] * vis;
+            }
+            cur = bstart + t;
+            T = nT;
+            ++n_contrib;
+        }
+    }
+    if (a.pair_counters) {
+        unsigned long long e = n_eval, k = n_contrib;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            e += __shfl_xor_sync(0xffffffffu, e, o);
+            k += __shfl_xor_sync(0xffffffffu, k, o);
+        }
+        if ((threadIdx.x & 31) == 0) {
+            atomicAdd(a.pair_counters, e);
+            atomicAdd(a.pair_counters + 1, k);
+        }
+    }
+    if (c.inside) {
+        a.out_alpha[c.pix] = 1.0f - T;
+        a.out_depth[c.pix] = depth;
+#pragma unroll
+        for (int k = 0; k < CDIM; ++k) a.out_rgb[c.pix * CDIM + k] = acc[k];
+        a.out_last[c.pix] = cur;
+    }
+}
+
+// ----------------------------------------------------------- backward ----
+// Gradient accumulator slots per Gaussian.
+//   0-2 v_mean  3 v_opacity  4-7 v_quat  8-10 v_scale  11 -  12-15 v_colour
+//   (C <= 4)    16-18 v_velocity (dynamic)
+template <bool kDyn>
+struct Acc {
+    static constexpr int N = kDyn ? 20 : 16;
+};
+
+// Transpose butterfly: on entry every lane holds v[0..15]; on exit lane L
+// holds in v[0] the warp-wide sum of value index (L >> 1) & 15.
+__device__ __forceinline__ void butterfly16(float (&v)[16], int lane) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const bool up = lane & 16;
+        const float send = up ? v[i] : v[i + 8];
+        const float keep = up ? v[i + 8] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const bool up = lane & 8;
+        const float send = up ? v[i] : v[i + 4];
+        const float keep = up ? v[i + 4] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const bool up = lane & 4;
+        const float send = up ? v[i] : v[i + 2];
+        const float keep = up ? v[i + 2] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    {
+        const bool up = lane & 2;
+        const float send = up ? v[0] : v[1];
+        const float keep = up ? v[1] : v[0];
+        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <int CDIM, bool kDyn>
+__global__ void __launch_bounds__(256) raster_bwd_kernel(RasterArgs a) {
+    constexpr bool kStageColor = CDIM > 0 && CDIM <= 4;
+    constexpr int CSZ = CDIM > 0 ? CDIM : 1;
+    constexpr int NA = Acc<kDyn>::N;
+    extern __shared__ float4 smem4[];
+    const int bs = blockDim.x;
+    float4* s0 = smem4;
+    float4* s1 = s0 + bs;
+    float4* s2 = s1 + bs;
+    float4* s3 = s2 + bs;
+    float4* sq = s3 + bs;         // raw quaternion
+    float4* ss = sq + bs;         // raw scale
+    float4* sc = ss + bs;         // colours (C <= 4)
+    float* sacc = reinterpret_cast<float*>(sc + bs);   // [bs][NA]
+    int32_t* sid = reinterpret_cast<int32_t*>(sacc + bs * NA);
+    int32_t* sflag = sid + bs;
+    __shared__ int32_t s_maxbin;
+
+    const TileCtx c = tile_ctx(a);
+    const int tr = threadIdx.x;
+    const int lane = tr & 31;
+    const v3 o = c.inside ? ld3(a.ray_o + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
+    const v3 d = c.inside ? ld3(a.ray_d + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
+    const float rt = (kDyn && c.inside) ? a.ray_t[c.pix] : 0.0f;
+
+    const bool inside = c.inside;
+    const float T_final = 1.0f - a.render_alpha[c.pix];
+    float T = T_final;
+    float buf[CSZ];
+    float vc[CSZ];
+#pragma unroll
+    for (int k = 0; k < CSZ; ++k) {
+        buf[k] = 0.f;
+        vc[k] = 0.f;
+    }
+    const int32_t bin_final = inside ? a.last_ids[c.pix] : 0;
+    if (a.v_rgb) {
+#pragma unroll
+        for (int k = 0; k < CDIM; ++k) vc[k] = inside ? a.v_rgb[c.pix * CDIM + k] : 0.f;
+    }
+    const float vd = inside ? a.v_depth[c.pix] : 0.f;
+    const float va = inside ? a.v_alpha[c.pix] : 0.f;
+    v3 vro = mk3(0.f, 0.f, 0.f), vrd = mk3(0.f, 0.f, 0.f);
+    float vtime = 0.f, dbuf = 0.f;
+
+    if (tr == 0) s_maxbin = -1;
+    __syncthreads();
+    if (inside) atomicMax(&s_maxbin, bin_final);
+    for (int k = 0; k < NA; ++k) sacc[tr * NA + k] = 0.f;
+    sflag[tr] = 0;
+    __syncthreads();
+    const int32_t maxbin = s_maxbin;
+
+    const int nb = (c.end - c.start + bs - 1) / bs;
+    for (int b = 0; b < nb; ++b) {
+        const int32_t bend = c.end - 1 - b * bs;
+        const int32_t bsize = min(bs, bend + 1 - c.start);
+        // every intersection of this batch lies past the last contributor of
+        // every pixel of the tile: nothing to do (uniform across the block)
+        if (bend - (bsize - 1) > maxbin) continue;
+        const int32_t idx = bend - tr;
+        if (idx >= c.start) {
+            const int32_t g = a.flatten[idx];
+            const float4* r = a.rec + int64_t(kRecF4) * g;
+            s0[tr] = r[0]; s1[tr] = r[1]; s2[tr] = r[2]; s3[tr] = r[3];
+            sq[tr] = make_float4(a.quats[4 * int64_t(g)], a.quats[4 * int64_t(g) + 1],
+                                 a.quats[4 * int64_t(g) + 2], a.quats[4 * int64_t(g) + 3]);
+            ss[tr] = make_float4(a.scales[3 * int64_t(g)], a.scales[3 * int64_t(g) + 1],
+                                 a.scales[3 * int64_t(g) + 2], 0.f);
+            if constexpr (kStageColor) {
+                float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
+                const float* cp = a.colors + int64_t(g) * CDIM;
+                cc.x = cp[0];
+                if (CDIM > 1) cc.y = cp[1];
+                if (CDIM > 2) cc.z = cp[2];
+                if (CDIM > 3) cc.w = cp[3];
+                sc[tr] = cc;
+            }
+            sid[tr] = g;
+        }
+        __syncthreads();
+        // this warp's last contributor bounds where it starts in the batch
+        int32_t wmax = bin_final;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
+        const int t0 = max(0, bend - wmax);
+        for (int t = t0; t < bsize; ++t) {
+            bool valid = inside && (bend - t <= bin_final);
+            const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
+            v3 mu = mk3(r0.w, r1.w, r2.w);
+            const v3 vel = mk3(r3.y, r3.z, r3.w);
+            if (kDyn) mu = mu + rt * vel;
+            const v3 omm = o - mu;
+            const v3 gro = mrows(r0, r1, r2, omm);
+            const v3 grd = mrows(r0, r1, r2, d);
+            const float l = dot3(grd, grd);
+            const v3 gn = l > 0.0f ? grd * rsqrtf(l) : grd;
+            const v3 gc = cross3(gn, gro);
+            const float power = -0.5f * dot3(gc, gc);
+            const float vis = __expf(power);
+            const float op = r3.x;
+            const float alpha = fminf(0.99f, op * vis);
+            if (alpha < 1.f / 255.f) valid = false;
+            if (!__any_sync(0xffffffffu, valid)) continue;
+
+            float gv[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) gv[k] = 0.f;
+            float gvel[3] = {0.f, 0.f, 0.f};
+            float gcol[CSZ];
+#pragma unroll
+            for (int k = 0; k < CSZ; ++k) gcol[k] = 0.f;
+            if (valid) {
+                const float hit_t = -dot3(grd, gro) / dot3(grd, grd);
+                const float ra = 1.0f / fmaxf(1e-6f, 1.0f - alpha);
+                T *= ra;
+                const float fac = alpha * T;
+                float rgb[CSZ];
+                if constexpr (kStageColor) {
+                    const float4 cc = sc[t];
+                    rgb[0] = cc.x;
+                    if (CDIM > 1) rgb[1] = cc.y;
+                    if (CDIM > 2) rgb[2] = cc.z;
+                    if (CDIM > 3) rgb[3] = cc.w;
+                } else if constexpr (CDIM > 0) {
+                    const float* cp = a.colors + int64_t(sid[t]) * CDIM;
+#pragma unroll 4
+                    for (int k = 0; k < CDIM; ++k) rgb[k] = cp[k];
+                }
+                float v_alpha = 0.f;
+#pragma unroll
+                for (int k = 0; k < CDIM; ++k) {
+                    gcol[k] = vc[k] * fac;
+                    v_alpha += (rgb[k] * T - buf[k] * ra) * vc[k];
+                }
+                v_alpha += (hit_t * T - dbuf * ra) * vd;
+                v_alpha += T_final * ra * va;
+                const float dd = dot3(grd, grd);
+                const float od = dot3(gro, grd);
+                const float dLdt = vd * fac;
+                v3 v_gro = (-1.0f * grd) * dLdt * (1.0f / dd);
+                v3 v_grd = (2.0f * od * grd - dd * gro) * dLdt * (1.0f / (dd * dd));
+                if (op * vis <= 0.99f) {
+                    const float v_vis = op * v_alpha;
+                    const float v_dist = -0.5f * vis * v_vis;
+                    const v3 v_gc = 2.0f * v_dist * gc;
+                    const v3 v_gn = -1.0f * cross3(v_gc, gro);
+                    v_gro = v_gro + cross3(v_gc, gn);
+                    if (l > 0.0f) {
+                        const float il = rsqrtf(l);
+                        const float il3 = il * il * il;
+                        v_grd = v_grd + (il * v_gn - il3 * dot3(v_gn, grd) * grd);
+                    } else {
+                        v_grd = v_grd + v_gn;
+                    }
+                    // v_(o - mu) = M^T v_gro ; v_ray_d = M^T v_grd
+                    const v3 v_omm = mk3(r0.x * v_gro.x + r1.x * v_gro.y + r2.x * v_gro.z,
+                                         r0.y * v_gro.x + r1.y * v_gro.y + r2.y * v_gro.z,
+                                         r0.z * v_gro.x + r1.z * v_gro.y + r2.z * v_gro.z);
+                    const v3 v_d = mk3(r0.x * v_grd.x + r1.x * v_grd.y + r2.x * v_grd.z,
+                                       r0.y * v_grd.x + r1.y * v_grd.y + r2.y * v_grd.z,
+                                       r0.z * v_grd.x + r1.z * v_grd.y + r2.z * v_grd.z);
+                    gv[0] = -v_omm.x; gv[1] = -v_omm.y; gv[2] = -v_omm.z;
+                    vro = vro + v_omm;
+                    vrd = vrd + v_d;
+                    if (kDyn) {
+                        gvel[0] = -v_omm.x * rt; gvel[1] = -v_omm.y * rt; gvel[2] = -v_omm.z * rt;
+                        vtime += -dot3(v_omm, vel);
+                    }
+                    // gradient of M rows: vM[i] = v_grd[i] d + v_gro[i] (o - mu)
+                    const v3 vM0 = v_grd.x * d + v_gro.x * omm;
+                    const v3 vM1 = v_grd.y * d + v_gro.y * omm;
+                    const v3 vM2 = v_grd.z * d + v_gro.z * omm;
+                    // quat_scale_to_preci_half_vjp (utils.h:232-263)
+                    const float4 q = sq[t];
+                    const float4 s = ss[t];
+                    float w = q.x, x = q.y, y = q.z, z = q.w;
+                    const float inv = rsqrtf(x * x + y * y + z * z + w * w);
+                    x *= inv; y *= inv; z *= inv; w *= inv;
+                    const float x2 = x * x, y2 = y * y, z2 = z * z;
+                    const float xy = x * y, xz = x * z, yz = y * z;
+                    const float wx = w * x, wy = w * y, wz = w * z;
+                    // columns of R
+                    const v3 C0 = mk3(1.f - 2.f * (y2 + z2), 2.f * (xy + wz), 2.f * (xz - wy));
+                    const v3 C1 = mk3(2.f * (xy - wz), 1.f - 2.f * (x2 + z2), 2.f * (yz + wx));
+                    const v3 C2 = mk3(2.f * (xz + wy), 2.f * (yz - wx), 1.f - 2.f * (x2 + y2));
+                    const float isx = 1.0f / s.x, isy = 1.0f / s.y, isz = 1.0f / s.z;
+                    gv[8] = -isx * isx * dot3(C0, vM0);
+                    gv[9] = -isy * isy * dot3(C1, vM1);
+                    gv[10] = -isz * isz * dot3(C2, vM2);
+                    // V(c, r) = dL/dR[row r][col c] = vM[c][r] / s_c
+                    const v3 V0 = isx * vM0, V1 = isy * vM1, V2 = isz * vM2;
+                    const float gw = 2.f * (x * (V1.z - V2.y) + y * (V2.x - V0.z) + z * (V0.y - V1.x));
+                    const float gx = 2.f * (-2.f * x * (V1.y + V2.z) + y * (V0.y + V1.x) + z * (V0.z + V2.x) +
+                                            w * (V1.z - V2.y));
+                    const float gy = 2.f * (x * (V0.y + V1.x) - 2.f * y * (V0.x + V2.z) + z * (V1.z + V2.y) +
+                                            w * (V2.x - V0.z));
+                    const float gz = 2.f * (x * (V0.z + V2.x) + y * (V1.z + V2.y) - 2.f * z * (V0.x + V1.y) +
+                                            w * (V0.y - V1.x));
+                    const float dq = gw * w + gx * x + gy * y + gz * z;
+                    gv[4] = (gw - dq * w) * inv;
+                    gv[5] = (gx - dq * x) * inv;
+                    gv[6] = (gy - dq * y) * inv;
+                    gv[7] = (gz - dq * z) * inv;
+                    gv[3] = vis * v_alpha;
+                }
+#pragma unroll
+                for (int k = 0; k < CDIM; ++k) buf[k] += rgb[k] * fac;
+                dbuf += fac * hit_t;
+            }
+            if constexpr (kStageColor) {
+#pragma unroll
+                for (int k = 0; k < CDIM; ++k) gv[12 + k] = gcol[k];
+            }
+            butterfly16(gv, lane);
+            float* slot = sacc + t * NA;
+            if ((lane & 1) == 0) atomicAdd(slot + (lane >> 1), gv[0]);
+            if (kDyn) {
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    const float s = warp_sum(gvel[k]);
+                    if (lane == 0) atomicAdd(slot + 16 + k, s);
+                }
+            }
+            if constexpr (!kStageColor && CDIM > 0) {
+                // wide colours: warp-reduced straight into the output
+                for (int k = 0; k < CDIM; ++k) {
+                    const float s = warp_sum(gcol[k]);
+                    if (lane == 0 && s != 0.f) atomicAdd(a.v_colors_direct + int64_t(sid[t]) * CDIM + k, s);
+                }
+            }
+            if (lane == 0) sflag[t] = 1;
+        }
+        __syncthreads();
+        // flush this batch's per-Gaussian sums, one vector reduction per 4 slots
+        if (sflag[tr]) {
+            float* dst = a.G + int64_t(sid[tr]) * NA;
+            float* src = sacc + tr * NA;
+#pragma unroll
+            for (int k = 0; k < NA; k += 4) {
+                red_add_v4(dst + k, src[k], src[k + 1], src[k + 2], src[k + 3]);
+                src[k] = 0.f; src[k + 1] = 0.f; src[k + 2] = 0.f; src[k + 3] = 0.f;
+            }
+            sflag[tr] = 0;
+        }
+        __syncthreads();
+    }
+    if (inside) {
+        st3(a.v_ray_o + 3 * c.pix, vro);
+        st3(a.v_ray_d + 3 * c.pix, vrd);
+        if (kDyn) a.v_ray_t[c.pix] = vtime;
+    }
+}
+
+// Accumulator -> output layout.
+template <bool kDyn>
+__global__ void grads_finalize_kernel(const float* __restrict__ G, int64_t n, int cdim, float* __restrict__ v_means,
+                                      float* __restrict__ v_vel, float* __restrict__ v_quats,
+                                      float* __restrict__ v_scales, float* __restrict__ v_opac,
+                                      float* __restrict__ v_colors) {
+    constexpr int NA = Acc<kDyn>::N;
+    const int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    const float4* s = reinterpret_cast<const float4*>(G + g * NA);
+    const float4 a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+    v_means[3 * g] = a0.x; v_means[3 * g + 1] = a0.y; v_means[3 * g + 2] = a0.z;
+    v_opac[g] = a0.w;
+    v_quats[4 * g] = a1.x; v_quats[4 * g + 1] = a1.y; v_quats[4 * g + 2] = a1.z; v_quats[4 * g + 3] = a1.w;
+    v_scales[3 * g] = a2.x; v_scales[3 * g + 1] = a2.y; v_scales[3 * g + 2] = a2.z;
+    if (v_colors && cdim <= 4) {
+        const float cc[4] = {a3.x, a3.y, a3.z, a3.w};
+        for (int k = 0; k < cdim; ++k) v_colors[g * cdim + k] = cc[k];
+    }
+    if (kDyn) {
+        const float4 a4 = s[4];
+        v_vel[3 * g] = a4.x; v_vel[3 * g + 1] = a4.y; v_vel[3 * g + 2] = a4.z;
+    }
+}
+
+// ------------------------------------------------------------ dispatch ---
+#define XSG_CDIM_CASES(X) \
+    X(0) X(1) X(2) X(3) X(4) X(5) X(8) X(9) X(16) X(17) X(32) X(33) X(64) X(65) X(128) X(129) X(256) X(257) X(512) X(513)
+
+static const int kSupported[] = {0, 1, 2, 3, 4, 5, 8, 9, 16, 17, 32, 33, 64, 65, 128, 129, 256, 257, 512, 513};
+
+static size_t fwd_smem(int bs) { return size_t(bs) * (5 * sizeof(float4) + sizeof(int32_t)); }
+static size_t bwd_smem(int bs, bool dyn) {
+    const int na = dyn ? 20 : 16;
+    return size_t(bs) * (7 * sizeof(float4) + na * sizeof(float) + 2 * sizeof(int32_t));
+}
+
+template <int CDIM, bool kDyn>
+static int launch_fwd(const RasterArgs& a, int bs, cudaStream_t st) {
+    const size_t sm = fwd_smem(bs);
+    auto fn = raster_fwd_kernel<CDIM, kDyn>;
+    if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
+    {
+        ScopedTimer tm("rasterize_fwd", st);
+        launch(fn, unsigned(a.ntx * a.nty), bs, sm, st, a);
+    }
+    return check_launch("rasterize_fwd");
+}
+
+template <int CDIM, bool kDyn>
+static int launch_bwd(const RasterArgs& a, int bs, cudaStream_t st) {
+    const size_t sm = bwd_smem(bs, kDyn);
+    auto fn = raster_bwd_kernel<CDIM, kDyn>;
+    if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
+    {
+        ScopedTimer tm("rasterize_bwd", st);
+        launch(fn, unsigned(a.ntx * a.nty), bs, sm, st, a);
+    }
+    return check_launch("rasterize_bwd");
+}
+
+static bool cdim_supported(int c) {
+    for (int v : kSupported)
+        if (v == c) return true;
+    return false;
+}
+
+static int check_common(int64_t n_gauss, int W, int H, int tsx, int tsy, int tiles_w, int tiles_h,
+                        int64_t n_isects, int cdim) {
+    XSG_REQUIRE(n_gauss >= 0 && n_isects >= 0 && W > 0 && H > 0, "rasterize: bad sizes");
+    XSG_REQUIRE(tsx > 0 && tsy > 0 && tsx * tsy <= 1024 && (tsx * tsy) % 32 == 0,
+                "rasterize: tile_size_x * tile_size_y must be a multiple of 32 and at most 1024");
+    XSG_REQUIRE(tiles_w > 0 && tiles_h > 0, "rasterize: bad tile grid");
+    XSG_REQUIRE(n_isects < (int64_t(1) << 31), "rasterize: too many intersections");
+    if (!cdim_supported(cdim))
+        return set_error(XSG_ERR_UNSUPPORTED, "Unsupported number of channels: " + std::to_string(cdim));
+    return XSG_OK;
+}
+
+}  // namespace xsg
+
+using namespace xsg;
+
+extern "C" {
+
+void xsg_set_pair_counters(unsigned long long* counters) { g_pair_counters = counters; }
+
+int xsg_raster_supported_channels(int* out, int cap) {
+    const int n = int(sizeof(kSupported) / sizeof(int));
+    for (int i = 0; i < n && i < cap; ++i) out[i] = kSupported[i];
+    return n;
+}
+
+size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim) {
+    (void)cdim;
+    if (n_gauss < 0) n_gauss = 0;
+    // packed records + the (dynamic-sized) gradient accumulator
+    return Arena::round(size_t(n_gauss) * kRecF4 * sizeof(float4)) + Arena::round(size_t(n_gauss) * 20 * sizeof(float));
+}
+
+int xsg_rasterize_fwd(const float* means, const float* velocity, const float* quats, const float* scales,
+                      const float* colors, int cdim, const float* opacities, int64_t n_gauss, int W, int H,
+                      int tsx, int tsy, const float* ray_o, const float* ray_d, const float* ray_time_delta,
+                      const int32_t* tile_offsets, int tiles_w, int tiles_h, const int32_t* flatten_ids,
+                      int64_t n_isects, float* renders, float* depths, float* alphas, int32_t* last_ids,
+                      void* workspace, size_t ws_bytes, xsg_stream_t stream) {
+    int rc = check_common(n_gauss, W, H, tsx, tsy, tiles_w, tiles_h, n_isects, cdim);
+    if (rc != XSG_OK) return rc;
+    XSG_REQUIRE(means && quats && scales && opacities && ray_o && ray_d && tile_offsets && depths && alphas &&
+                    last_ids, "rasterize_fwd: null argument");
+    XSG_REQUIRE(cdim == 0 || (colors && renders), "rasterize_fwd: colors required");
+    XSG_REQUIRE(n_isects == 0 || flatten_ids, "rasterize_fwd: null flatten_ids");
+    cudaStream_t st = as_cuda(stream);
+    Arena ar(workspace, ws_bytes);
+    float4* rec = ar.take<float4>(size_t(n_gauss) * kRecF4);
+    if ((n_gauss > 0 && !rec) || (n_gauss > 0 && !workspace))
+        return set_error(XSG_ERR_WORKSPACE, "rasterize_fwd: workspace too small");
+    const bool dyn = velocity != nullptr;
+    if (n_gauss > 0)
+        launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales, opacities,
+                                                                      n_gauss, rec);
+    RasterArgs a{};
+    a.rec = rec; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
+    a.ray_o = ray_o; a.ray_d = ray_d; a.ray_t = ray_time_delta;
+    a.offsets = tile_offsets; a.flatten = flatten_ids; a.n_isects = n_isects;
+    a.W = W; a.H = H; a.tsx = tsx; a.tsy = tsy; a.ntx = tiles_w; a.nty = tiles_h;
+    a.out_rgb = renders; a.out_depth = depths; a.out_alpha = alphas; a.out_last = last_ids;
+    a.pair_counters = g_pair_counters;
+    const int bs = tsx * tsy;
+#define XSG_FWD_CASE(C)                                                             \
+    case C:                                                                         \
+        return dyn ? launch_fwd<C, true>(a, bs, st) : launch_fwd<C, false>(a, bs, st);
+    switch (cdim) {
+        XSG_CDIM_CASES(XSG_FWD_CASE)
+        default: break;
+    }
+#undef XSG_FWD_CASE
+    return set_error(XSG_ERR_UNSUPPORTED, "Unsupported number of channels: " + std::to_string(cdim));
+}
+
+int xsg_rasterize_bwd(const float* means, const float* velocity, const float* quats, const float* scales,
+                      const float* colors, int cdim, const float* opacities, int64_t n_gauss, int W, int H,
+                      int tsx, int tsy, const float* ray_o, const float* ray_d, const float* ray_time_delta,
+                      const int32_t* tile_offsets, int tiles_w, int tiles_h, const int32_t* flatten_ids,
+                      int64_t n_isects, const float* render_alphas, const int32_t* last_ids,
+                      const float* v_renders, const float* v_depths, const float* v_alphas, float* v_means,
+                      float* v_velocity, float* v_quats, float* v_scales, float* v_colors, float* v_opacities,
+                      float* v_ray_o, float* v_ray_d, float* v_ray_time_delta, void* workspace, size_t ws_bytes,
+                      xsg_stream_t stream) {
+    int rc = check_common(n_gauss, W, H, tsx, tsy, tiles_w, tiles_h, n_isects, cdim);
+    if (rc != XSG_OK) return rc;
+    const bool dyn = velocity != nullptr;
+    XSG_REQUIRE(means && quats && scales && opacities && ray_o && ray_d && tile_offsets && render_alphas &&
+                    last_ids && v_depths && v_alphas && v_means && v_quats && v_scales && v_opacities &&
+                    v_ray_o && v_ray_d, "rasterize_bwd: null argument");
+    XSG_REQUIRE(cdim == 0 || (colors && v_colors), "rasterize_bwd: colors required");
+    XSG_REQUIRE(!dyn || (ray_time_delta && v_velocity && v_ray_time_delta),
+                "rasterize_dynamic_bwd: ray_time_delta is required");
+    XSG_REQUIRE(n_isects == 0 || flatten_ids, "rasterize_bwd: null flatten_ids");
+    cudaStream_t st = as_cuda(stream);
+    Arena ar(workspace, ws_bytes);
+    float4* rec = ar.take<float4>(size_t(n_gauss) * kRecF4);
+    const int na = dyn ? 20 : 16;
+    float* G = ar.take<float>(size_t(n_gauss) * na);
+    if (n_gauss > 0 && (!rec || !G)) return set_error(XSG_ERR_WORKSPACE, "rasterize_bwd: workspace too small");
+    const int64_t npx = int64_t(W) * H;
+    XSG_CUDA(cudaMemsetAsync(v_ray_o, 0, size_t(npx) * 12, st));
+    XSG_CUDA(cudaMemsetAsync(v_ray_d, 0, size_t(npx) * 12, st));
+    if (dyn) XSG_CUDA(cudaMemsetAsync(v_ray_time_delta, 0, size_t(npx) * 4, st));
+    if (n_gauss > 0) {
+        XSG_CUDA(cudaMemsetAsync(G, 0, size_t(n_gauss) * na * sizeof(float), st));
+        if (cdim > 4) XSG_CUDA(cudaMemsetAsync(v_colors, 0, size_t(n_gauss) * cdim * sizeof(float), st));
+        launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales, opacities,
+                                                                      n_gauss, rec);
+    }
+    RasterArgs a{};
+    a.rec = rec; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
+    a.ray_o = ray_o; a.ray_d = ray_d; a.ray_t = ray_time_delta;
+    a.offsets = tile_offsets; a.flatten = flatten_ids; a.n_isects = n_isects;
+    a.W = W; a.H = H; a.tsx = tsx; a.tsy = tsy; a.ntx = tiles_w; a.nty = tiles_h;
+    a.render_alpha = render_alphas; a.last_ids = last_ids;
+    a.v_rgb = v_renders; a.v_depth = v_depths; a.v_alpha = v_alphas;
+    a.G = G; a.v_colors_direct = v_colors;
+    a.v_ray_o = v_ray_o; a.v_ray_d = v_ray_d; a.v_ray_t = v_ray_time_delta;
+    const int bs = tsx * tsy;
+    int lrc = XSG_OK;
+#define XSG_BWD_CASE(C)                                                                          \
+    case C:                                                                                      \
+        lrc = dyn ? launch_bwd<C, true>(a, bs, st) : launch_bwd<C, false>(a, bs, st);            \
+        break;
+    switch (cdim) {
+        XSG_CDIM_CASES(XSG_BWD_CASE)
+        default: return set_error(XSG_ERR_UNSUPPORTED, "unsupported feature dimension: " + std::to_string(cdim));
+    }
+#undef XSG_BWD_CASE
+    if (lrc != XSG_OK) return lrc;
+    if (n_gauss > 0) {
+        if (dyn)
+            launch(grads_finalize_kernel<true>, blocks_for(n_gauss, 256), 256, 0, st, 
+                G, n_gauss, cdim, v_means, v_velocity, v_quats, v_scales, v_opacities, v_colors);
+        else
+            launch(grads_finalize_kernel<false>, blocks_for(n_gauss, 256), 256, 0, st, 
+                G, n_gauss, cdim, v_means, nullptr, v_quats, v_scales, v_opacities, v_colors);
+    }
+    return check_launch("rasterize_bwd_finalize");
+}
+
+}  // extern "C"

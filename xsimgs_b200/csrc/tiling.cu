@@ -1,0 +1,621 @@
+// Tile intersection for pinhole/fisheye images (regular 2D tiles) and for
+// spherical/lidar range images (azimuth x elevation tiles), the sort of the
+// intersections and the per-tile offsets.
+//
+// Order contract (the reference's cub::DeviceRadixSort::SortPairs on keys
+// `tile << 32 | depth bits`, tiling_common.cu:102-162, is a stable sort of
+// the emission order, which is Gaussian index then tile row-major):
+//   sorted by (tile, depth bits as u32, Gaussian index, tile row-major).
+// It is produced here without sorting 64-bit keys:
+//   1. the visible Gaussians are compacted and radix-sorted by depth bits
+//      (stable, so ties keep Gaussian order);
+//   2. their intersections are emitted in that order, keyed by tile only;
+//   3. a stable LSD radix sort on the tile bits moves them into tile order,
+//      and its last pass writes the 64-bit ids and the flatten ids.
+// Negative depths (never produced by the projections) would make the
+// reference's sign-extended key fill the tile bits; they are keyed with the
+// all-ones tile value so the order still matches.
+#include "cameras.cuh"
+#include "scan_sort.cuh"
+
+namespace xsg {
+
+constexpr int kTileThreads = 256;
+
+__host__ __device__ inline int tile_bits_for(int64_t n_tiles) {
+    // floor(log2(float(n))) + 1, as tiling_common.cu:236 computes it
+    int b = 0;
+    while ((int64_t(1) << (b + 1)) <= n_tiles) ++b;
+    return b + 1;
+}
+
+// float -> int with the device's saturating conversion (as the reference's
+// static_cast<int>(floorf(...)) compiles on sm_100a)
+__device__ __forceinline__ int f2i(float v) { return __float2int_rz(v); }
+
+struct Rect {
+    int x0, y0, x1, y1;  // [x0, x1) x [y0, y1)
+    __device__ __forceinline__ int count() const { return (y1 - y0) * (x1 - x0); }
+};
+
+// Tile rectangle of one Gaussian on a regular grid, regular_tiling.cu:34-56
+__device__ __forceinline__ bool regular_rect(float2 m, float2 r, float2 ts, int ntx, int nty, Rect& rc) {
+    rc = {0, 0, 0, 0};
+    if (r.x <= 0 || r.y <= 0) return false;
+    const float mx = m.x / ts.x, my = m.y / ts.y;
+    const float rx = r.x / ts.x, ry = r.y / ts.y;
+    rc.x0 = min(ntx, max(0, f2i(floorf(mx - rx))));
+    rc.y0 = min(nty, max(0, f2i(floorf(my - ry))));
+    rc.x1 = min(ntx, max(0, f2i(ceilf(mx + rx))));
+    rc.y1 = min(nty, max(0, f2i(ceilf(my + ry))));
+    return true;
+}
+
+// --------------------------------------------------------- regular grid --
+__global__ void __launch_bounds__(kTileThreads)
+    regular_count_kernel(const float2* __restrict__ means2d, const float2* __restrict__ radii, int64_t n,
+                         float2 ts, int ntx, int nty, int32_t* __restrict__ counts,
+                         unsigned long long* __restrict__ total) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    int c = 0;
+    if (i < n) {
+        Rect rc;
+        if (regular_rect(means2d[i], radii[i], ts, ntx, nty, rc)) c = rc.count();
+        counts[i] = c;
+    }
+    // warp-aggregated total
+    unsigned s = unsigned(c);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0 && s) atomicAdd(total, (unsigned long long)s);
+}
+
+// Writes each Gaussian's intersections; with `order` (a permutation of the
+// visible Gaussians) in that order and keyed by tile bucket, else in
+// Gaussian order with the reference's 64-bit keys.
+template <bool kSorted>
+__global__ void __launch_bounds__(kTileThreads)
+    regular_emit_kernel(const float2* __restrict__ means2d, const float2* __restrict__ radii,
+                        const float* __restrict__ depths, int64_t n_items, float2 ts, int ntx, int nty,
+                        int bucket_neg, const uint32_t* __restrict__ order,
+                        const int64_t* __restrict__ offsets, uint32_t* __restrict__ bucket_keys,
+                        uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
+                        int32_t* __restrict__ flatten_ids) {
+    const int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (p >= n_items) return;
+    const uint32_t g = kSorted ? order[p] : uint32_t(p);
+    Rect rc;
+    if (!regular_rect(means2d[g], radii[g], ts, ntx, nty, rc)) return;
+    int64_t off = offsets[p];
+    const int32_t bits = __float_as_int(depths[g]);
+    for (int y = rc.y0; y < rc.y1; ++y)
+        for (int x = rc.x0; x < rc.x1; ++x) {
+            const uint32_t tile = uint32_t(y) * uint32_t(ntx) + uint32_t(x);
+            if constexpr (kSorted) {
+                bucket_keys[off] = bits < 0 ? uint32_t(bucket_neg) : tile;
+                bucket_vals[off] = g;
+            } else {
+                const uint64_t hi = bits < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(tile) << 32);
+                isect_ids[off] = int64_t(hi | uint64_t(uint32_t(bits)));
+                flatten_ids[off] = int32_t(g);
+            }
+            ++off;
+        }
+}
+
+// Visible (count > 0) Gaussians -> (depth bits, index) pairs, in index order.
+__global__ void compact_visible_kernel(const int32_t* __restrict__ counts, const int64_t* __restrict__ pos,
+                                       const float* __restrict__ depths, int64_t n,
+                                       uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n || counts[i] <= 0) return;
+    const int64_t p = pos[i];
+    keys[p] = __float_as_uint(depths[i]);
+    vals[p] = uint32_t(i);
+}
+
+__global__ void gather_counts_kernel(const int32_t* __restrict__ counts, const uint32_t* __restrict__ order,
+                                     int64_t n, int32_t* __restrict__ out) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = counts[order[i]];
+}
+
+// isect_offset_encode_kernel semantics (tiling_common.cu:25-71): offsets[t]
+// is the first intersection index whose tile is >= t.
+__global__ void offset_encode_kernel(const int64_t* __restrict__ ids, int64_t n, int64_t n_tiles, int tb,
+                                     int32_t* __restrict__ offsets) {
+    const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= n) return;
+    auto tile_of = [&](int64_t key) {
+        const int64_t hi = key >> 32;
+        return (hi >> tb) * n_tiles + (hi & ((int64_t(1) << tb) - 1));
+    };
+    const int64_t hc = ids[idx] >> 32;
+    const int64_t cur = tile_of(ids[idx]);
+    if (idx == 0)
+        for (int64_t t = 0; t < cur + 1 && t < n_tiles; ++t) offsets[t] = 0;
+    if (idx == n - 1)
+        for (int64_t t = max(cur + 1, int64_t(0)); t < n_tiles; ++t) offsets[t] = int32_t(n);
+    if (idx > 0) {
+        const int64_t hp = ids[idx - 1] >> 32;
+        if (hp == hc) return;
+        const int64_t prev = tile_of(ids[idx - 1]);
+        for (int64_t t = max(prev + 1, int64_t(0)); t < cur + 1 && t < n_tiles; ++t) offsets[t] = int32_t(idx);
+    }
+}
+
+// ------------------------------------------------ spherical / lidar grid --
+struct SphTiling {
+    int lidar;
+    int n_az, n_el;
+    float u_per_tile, v_per_tile;
+    float2 img;
+    const float* elev_bounds;
+};
+
+// tile_limits_irregular (phm_lidar_tiling.cu:52-91, increasing elevation
+// boundaries) and tile_limits_regular (phm_spherical_tiling.cu:15-44) in
+// exclusive [x0, x1) x [y0, y1) form.
+__device__ __forceinline__ int sph_limits(const SphTiling& T, float2 m, float2 r, float umin, float umax,
+                                          Rect& rc) {
+    rc = {0, 0, 0, 0};
+    const float lo = fmaxf(m.x - r.x, umin);
+    const float hi = fminf(m.x + r.x, umax);
+    if (hi <= lo) return 0;
+    if (T.lidar) {
+        const int tx0 = f2i(floorf(lo / T.u_per_tile));
+        const int tx1 = f2i(ceilf(hi / T.u_per_tile)) - 1;
+        const float vmin = m.y - r.y, vmax = m.y + r.y;
+        const int N = T.n_el;
+        int i = 0;
+        while (i < N && T.elev_bounds[i] < vmin) ++i;
+        const int ty0 = min(max(i - 1, 0), N - 1);
+        while (i < N && T.elev_bounds[i] < vmax) ++i;
+        const int ty1 = min(max(i - 1, 0), N - 1);
+        rc = {tx0, ty0, tx1 + 1, ty1 + 1};
+        return (ty1 - ty0 + 1) * (tx1 - tx0 + 1);
+    }
+    const int tx0 = f2i(floorf(lo / T.u_per_tile));
+    const int ty0 = min(T.n_el, max(0, f2i(floorf((m.y - r.y) / T.v_per_tile))));
+    const int tx1 = f2i(ceilf(hi / T.u_per_tile));
+    const int ty1 = min(T.n_el, max(0, f2i(ceilf((m.y + r.y) / T.v_per_tile))));
+    rc = {tx0, ty0, tx1, ty1};
+    return (ty1 - ty0) * (tx1 - tx0);
+}
+
+}  // namespace xsg
+
+// The UT projection pieces are shared with project.cu through this include.
+#include "ut_device.cuh"
+
+namespace xsg {
+
+// Both rectangles of one Gaussian (the second only for flag 2, after a
+// PositiveDelta re-projection): isect_lidar_tiles_kernel
+// (phm_lidar_tiling.cu:96-234) / isect_spherical_tiles_kernel
+// (phm_spherical_tiling.cu:47-174).
+template <typename Cam>
+__device__ __forceinline__ int sph_rects(const Cam& k, const SphTiling& T, const UTParams& up, int64_t i,
+                                         const float* pts, const float* vel, const float* scales,
+                                         const float4* quats, const float* opac, const uint8_t* flags,
+                                         const float2* means2d, const float2* radii, Rect& r1, Rect& r2,
+                                         bool& has2, float& depth2) {
+    r1 = {0, 0, 0, 0};
+    r2 = {0, 0, 0, 0};
+    has2 = false;
+    depth2 = 0.f;
+    float2 rr = radii[i];
+    const uint8_t fl = flags[i];
+    if (rr.x <= 0 || rr.y <= 0 || fl == 0) return 0;
+    float umin = 0.0f, umax = 1.0f;
+    const float u_pose = fabsf(k.rolling.x) > 0.0f ? (k.pose - k.trigger) / k.rolling.x : 0.5f;
+    if (fl == 2) {
+        if (k.rolling.x > 0) umax = u_pose;
+        else umin = u_pose;
+    }
+    const float2 m0 = means2d[i];
+    const float2 m = make_float2(m0.x / T.img.x, m0.y / T.img.y);
+    rr = make_float2(rr.x / T.img.x, rr.y / T.img.y);
+    int cnt = sph_limits(T, m, rr, umin, umax, r1);
+    if (fl == 2) {
+        const v3 P = ld3(pts + 3 * i);
+        const v3 V = vel ? ld3(vel + 3 * i) : mk3(0.f, 0.f, 0.f);
+        const float o = opac ? opac[i] : 1.0f;
+        v3 d[3];
+        ut_deltas(up.sq, quats[i], ld3(scales + 3 * i), d);
+        float2 m2, rad2;
+        float dp2, tmp;
+        if (ut_project(k, up, MODE_POS, P, V, o, d, m2, rad2, dp2, tmp)) {
+            if (k.rolling.x > 0) {
+                umin = ceilf(u_pose / T.u_per_tile) * T.u_per_tile + 1e-6f;
+                umax = 1.0f;
+            } else {
+                umin = 0.0f;
+                umax = floorf(u_pose / T.u_per_tile) * T.u_per_tile - 1e-6f;
+            }
+            cnt += sph_limits(T, make_float2(m2.x / T.img.x, m2.y / T.img.y),
+                              make_float2(rad2.x / T.img.x, rad2.y / T.img.y), umin, umax, r2);
+            has2 = true;
+            depth2 = dp2;
+        }
+    }
+    return cnt;
+}
+
+struct SphInputs {
+    const float* pack;
+    const float* pts;
+    const float* vel;
+    const float* scales;
+    const float4* quats;
+    const float* opac;
+    const uint8_t* flags;
+    const float2* means2d;
+    const float2* radii;
+    const float* depths;
+};
+
+template <typename Cam>
+__global__ void __launch_bounds__(kTileThreads / 2)
+    sph_count_kernel(SphInputs in, SphTiling T, UTParams up, int64_t n, int32_t* __restrict__ counts,
+                     unsigned long long* __restrict__ total) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    int c = 0;
+    if (i < n) {
+        Cam k;
+        k.load(in.pack);
+        Rect r1, r2;
+        bool has2;
+        float d2;
+        c = sph_rects(k, T, up, i, in.pts, in.vel, in.scales, in.quats, in.opac, in.flags, in.means2d,
+                      in.radii, r1, r2, has2, d2);
+        counts[i] = c;
+    }
+    unsigned s = unsigned(c);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0 && s) atomicAdd(total, (unsigned long long)s);
+}
+
+// Second-rectangle depths differ from depths[i]; the sorted path keys those
+// intersections by a per-intersection depth kept in `isect_depth`.
+template <typename Cam, bool kSorted>
+__global__ void __launch_bounds__(kTileThreads / 2)
+    sph_emit_kernel(SphInputs in, SphTiling T, UTParams up, int64_t n_items, const uint32_t* __restrict__ order,
+                    const int64_t* __restrict__ offsets, uint32_t* __restrict__ bucket_keys,
+                    uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
+                    int32_t* __restrict__ flatten_ids, int bucket_neg) {
+    const int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (p >= n_items) return;
+    const uint32_t g = kSorted ? order[p] : uint32_t(p);
+    Cam k;
+    k.load(in.pack);
+    Rect r1, r2;
+    bool has2;
+    float d2;
+    const int c = sph_rects(k, T, up, g, in.pts, in.vel, in.scales, in.quats, in.opac, in.flags, in.means2d,
+                            in.radii, r1, r2, has2, d2);
+    if (c <= 0) return;
+    int64_t off = offsets[p];
+    auto fill = [&](const Rect& rc, float depth) {
+        const int32_t bits = __float_as_int(depth);
+        for (int y = rc.y0; y < rc.y1; ++y)
+            for (int x = rc.x0; x < rc.x1; ++x) {
+                const uint32_t tile = uint32_t(int64_t(y) * T.n_az + x);
+                if constexpr (kSorted) {
+                    bucket_keys[off] = bits < 0 ? uint32_t(bucket_neg) : tile;
+                    bucket_vals[off] = g;
+                } else {
+                    const uint64_t hi = bits < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(tile) << 32);
+                    isect_ids[off] = int64_t(hi | uint64_t(uint32_t(bits)));
+                    flatten_ids[off] = int32_t(g);
+                }
+                ++off;
+            }
+    };
+    fill(r1, in.depths[g]);
+    if (has2) fill(r2, d2);
+}
+
+// -------------------------------------------------------- host drivers --
+// Workspace layout shared by the count and emit phases.
+struct IsectWs {
+    unsigned long long* total;
+    int64_t* scan_out;      // n + 1
+    void* scan_tmp;
+    uint32_t *gk, *gv, *gk2, *gv2;  // Gaussian presort, n each
+    int32_t* cnt_sorted;    // n
+    uint32_t *bk, *bv, *bk2, *bv2;  // tile sort, max_isects each
+    void* sort_tmp;
+    size_t sort_tmp_bytes;
+    int64_t* kcopy;         // max_isects (generic 64-bit key sort)
+    int32_t* fcopy;         // max_isects
+};
+
+static size_t isect_ws_layout(int64_t n, int64_t m, void* base, size_t cap, IsectWs* ws) {
+    Arena a(base, cap);
+    const int64_t big = n > m ? n : m;
+    IsectWs w{};
+    w.total = a.take<unsigned long long>(1);
+    w.scan_out = a.take<int64_t>(size_t(n + 1));
+    w.scan_tmp = a.take<char>(scan_workspace_bytes(big + 1));
+    w.gk = a.take<uint32_t>(size_t(n)); w.gv = a.take<uint32_t>(size_t(n));
+    w.gk2 = a.take<uint32_t>(size_t(n)); w.gv2 = a.take<uint32_t>(size_t(n));
+    w.cnt_sorted = a.take<int32_t>(size_t(n));
+    w.bk = a.take<uint32_t>(size_t(m)); w.bv = a.take<uint32_t>(size_t(m));
+    w.bk2 = a.take<uint32_t>(size_t(m)); w.bv2 = a.take<uint32_t>(size_t(m));
+    w.sort_tmp_bytes = radix_workspace_bytes(big);
+    w.sort_tmp = a.take<char>(w.sort_tmp_bytes);
+    w.kcopy = a.take<int64_t>(size_t(m));
+    w.fcopy = a.take<int32_t>(size_t(m));
+    if (ws) *ws = w;
+    // `used` is what the layout needs even when cap was too small
+    size_t need = 0;
+    need += Arena::round(8) + Arena::round(size_t(n + 1) * 8) + scan_workspace_bytes(big + 1);
+    need += 4 * Arena::round(size_t(n) * 4) + Arena::round(size_t(n) * 4);
+    need += 4 * Arena::round(size_t(m) * 4) + radix_workspace_bytes(big);
+    need += Arena::round(size_t(m) * 8) + Arena::round(size_t(m) * 4);
+    return need;
+}
+
+__global__ void split_key_kernel(const int64_t* __restrict__ ids, int64_t n, uint32_t* __restrict__ lo,
+                                 uint32_t* __restrict__ idx) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    lo[i] = uint32_t(uint64_t(ids[i]));
+    idx[i] = uint32_t(i);
+}
+
+__global__ void gather_hi_kernel(const int64_t* __restrict__ ids, const uint32_t* __restrict__ perm, int64_t n,
+                                 int tb, uint32_t* __restrict__ hi, uint32_t* __restrict__ idx) {
+    const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    const uint32_t p = perm[j];
+    hi[j] = uint32_t((uint64_t(ids[p]) >> 32) & ((uint64_t(1) << tb) - 1));
+    idx[j] = p;
+}
+
+__global__ void permute_isects_kernel(const int64_t* __restrict__ kin, const int32_t* __restrict__ fin,
+                                      const uint32_t* __restrict__ perm, int64_t n, int64_t* __restrict__ kout,
+                                      int32_t* __restrict__ fout) {
+    const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    const uint32_t p = perm[j];
+    kout[j] = kin[p];
+    fout[j] = fin[p];
+}
+
+// Stable sort of emitted (64-bit id, flatten id) pairs on id bits
+// [0, 32 + tb), in place: by the depth word, then stably by the tile bits.
+static int sort_isect_pairs_inplace(int64_t* ids, int32_t* flat, int64_t n, int tb, const struct IsectWs& w,
+                                    cudaStream_t st) {
+    launch(split_key_kernel, blocks_for(n, 256), 256, 0, st, ids, n, w.bk, w.bv);
+    uint32_t *ks, *vs;
+    int rc = radix_sort_pairs(w.bk, w.bv, w.bk2, w.bv2, n, 32, w.sort_tmp, w.sort_tmp_bytes, st, nullptr, &ks, &vs);
+    if (rc != XSG_OK) return rc;
+    uint32_t* k2 = (ks == w.bk) ? w.bk2 : w.bk;
+    uint32_t* v2 = (vs == w.bv) ? w.bv2 : w.bv;
+    launch(gather_hi_kernel, blocks_for(n, 256), 256, 0, st, ids, vs, n, tb, k2, v2);
+    rc = radix_sort_pairs(k2, v2, ks, vs, n, tb, w.sort_tmp, w.sort_tmp_bytes, st, nullptr, &ks, &vs);
+    if (rc != XSG_OK) return rc;
+    XSG_CUDA(cudaMemcpyAsync(w.kcopy, ids, size_t(n) * 8, cudaMemcpyDeviceToDevice, st));
+    XSG_CUDA(cudaMemcpyAsync(w.fcopy, flat, size_t(n) * 4, cudaMemcpyDeviceToDevice, st));
+    launch(permute_isects_kernel, blocks_for(n, 256), 256, 0, st, w.kcopy, w.fcopy, vs, n, ids, flat);
+    return check_launch("sort_isect_pairs");
+}
+
+// Sorted emission shared by regular and spherical tilings: presort the
+// visible Gaussians by depth, scan their counts in that order and let
+// `emit(order, offsets, n_vis)` write tile-keyed pairs, then bucket-sort.
+template <typename Emit>
+static int sorted_isects(const int32_t* counts, const float* depths, int64_t n, int64_t n_isects,
+                         int64_t n_tiles, const IsectWs& w, int64_t* isect_ids, int32_t* flatten_ids,
+                         cudaStream_t st, Emit&& emit) {
+    // 1. compact visible Gaussians (count > 0)
+    int rc = exclusive_scan<int32_t, true>(counts, n, w.scan_out, w.scan_out + n, w.scan_tmp, st);
+    if (rc != XSG_OK) return rc;
+    int64_t n_vis = 0;
+    XSG_CUDA(cudaMemcpyAsync(&n_vis, w.scan_out + n, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+    XSG_CUDA(cudaStreamSynchronize(st));
+    launch(compact_visible_kernel, blocks_for(n, 256), 256, 0, st, counts, w.scan_out, depths, n, w.gk, w.gv);
+    // 2. stable sort by depth bits
+    uint32_t *ks, *vs;
+    rc = radix_sort_pairs(w.gk, w.gv, w.gk2, w.gv2, n_vis, 32, w.sort_tmp, w.sort_tmp_bytes, st, nullptr,
+                          &ks, &vs);
+    if (rc != XSG_OK) return rc;
+    // 3. counts in depth order -> emission offsets
+    launch(gather_counts_kernel, blocks_for(n_vis, 256), 256, 0, st, counts, vs, n_vis, w.cnt_sorted);
+    rc = exclusive_scan<int32_t>(w.cnt_sorted, n_vis, w.scan_out, nullptr, w.scan_tmp, st);
+    if (rc != XSG_OK) return rc;
+    emit(vs, w.scan_out, n_vis);
+    // 4. stable bucket sort by tile; the last pass writes the outputs
+    const int tb = tile_bits_for(n_tiles);
+    IsectEpilogue ep{depths, isect_ids, flatten_ids};
+    return radix_sort_pairs(w.bk, w.bv, w.bk2, w.bv2, n_isects, tb, w.sort_tmp, w.sort_tmp_bytes, st, &ep,
+                            nullptr, nullptr);
+}
+
+}  // namespace xsg
+
+using namespace xsg;
+
+extern "C" {
+
+size_t xsg_isect_workspace_size(int64_t n_gauss, int64_t max_isects) {
+    return isect_ws_layout(n_gauss < 0 ? 0 : n_gauss, max_isects < 0 ? 0 : max_isects, nullptr, 0, nullptr);
+}
+
+int xsg_isect_regular_count(const float* means2d, const float* radii, int64_t n, int W, int H, int tsx,
+                            int tsy, int32_t* counts, int64_t* n_isects_host, void* workspace,
+                            size_t ws_bytes, xsg_stream_t stream) {
+    XSG_REQUIRE(n >= 0 && W > 0 && H > 0 && tsx > 0 && tsy > 0 && n_isects_host, "isect_regular_tiles: bad arguments");
+    XSG_REQUIRE(n == 0 || (means2d && radii && counts), "isect_regular_tiles: null input");
+    cudaStream_t st = as_cuda(stream);
+    IsectWs w;
+    const size_t need = isect_ws_layout(n, 0, workspace, ws_bytes, &w);
+    if (ws_bytes < need || !workspace) return set_error(XSG_ERR_WORKSPACE, "isect_regular_tiles: workspace too small");
+    XSG_CUDA(cudaMemsetAsync(w.total, 0, sizeof(unsigned long long), st));
+    const int ntx = (W + tsx - 1) / tsx, nty = (H + tsy - 1) / tsy;
+    if (n > 0)
+        launch(regular_count_kernel, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
+            reinterpret_cast<const float2*>(means2d), reinterpret_cast<const float2*>(radii), n,
+            make_float2(float(tsx), float(tsy)), ntx, nty, counts, w.total);
+    unsigned long long tot = 0;
+    XSG_CUDA(cudaMemcpyAsync(&tot, w.total, sizeof(tot), cudaMemcpyDeviceToHost, st));
+    XSG_CUDA(cudaStreamSynchronize(st));
+    *n_isects_host = int64_t(tot);
+    if (tot >= (1ull << 31)) return set_error(XSG_ERR_UNSUPPORTED, "isect_regular_tiles: more than 2^31 intersections");
+    return check_launch("isect_regular_count");
+}
+
+int xsg_isect_regular_emit(const float* means2d, const float* radii, const float* depths, int64_t n, int W,
+                           int H, int tsx, int tsy, int sort, const int32_t* counts, int64_t n_isects,
+                           int64_t* isect_ids, int32_t* flatten_ids, void* workspace, size_t ws_bytes,
+                           xsg_stream_t stream) {
+    XSG_REQUIRE(n >= 0 && n_isects >= 0 && W > 0 && H > 0 && tsx > 0 && tsy > 0, "isect_regular_tiles: bad arguments");
+    if (n_isects == 0) return XSG_OK;
+    XSG_REQUIRE(means2d && radii && depths && counts && isect_ids && flatten_ids, "isect_regular_tiles: null input");
+    cudaStream_t st = as_cuda(stream);
+    IsectWs w;
+    const size_t need = isect_ws_layout(n, sort ? n_isects : 0, workspace, ws_bytes, &w);
+    if (ws_bytes < need || !workspace) return set_error(XSG_ERR_WORKSPACE, "isect_regular_tiles: workspace too small");
+    const int ntx = (W + tsx - 1) / tsx, nty = (H + tsy - 1) / tsy;
+    const float2 ts = make_float2(float(tsx), float(tsy));
+    auto* m2 = reinterpret_cast<const float2*>(means2d);
+    auto* r2 = reinterpret_cast<const float2*>(radii);
+    if (!sort) {
+        int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
+        if (rc != XSG_OK) return rc;
+        launch(regular_emit_kernel<false>, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
+            m2, r2, depths, n, ts, ntx, nty, 0, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids);
+        return check_launch("isect_regular_emit");
+    }
+    const int64_t n_tiles = int64_t(ntx) * nty;
+    const int bucket_neg = int((int64_t(1) << tile_bits_for(n_tiles)) - 1);
+    return sorted_isects(counts, depths, n, n_isects, n_tiles, w, isect_ids, flatten_ids, st,
+                         [&](const uint32_t* order, const int64_t* offs, int64_t n_vis) {
+                             launch(regular_emit_kernel<true>, blocks_for(n_vis, kTileThreads), kTileThreads, 0, st, 
+                                 m2, r2, depths, n_vis, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv,
+                                 nullptr, nullptr);
+                         });
+}
+
+static SphTiling make_sph_tiling(int lidar, const float* elev_bounds, int n_elev, int tsx, int tsy, float W,
+                                 float H) {
+    SphTiling T;
+    T.lidar = lidar;
+    T.img = make_float2(W, H);
+    T.elev_bounds = elev_bounds;
+    T.u_per_tile = float(tsx) / W;
+    if (lidar) {
+        T.n_az = (int(W) + tsx - 1) / tsx;
+        T.n_el = n_elev;
+        T.v_per_tile = ceilf(H / float(n_elev)) / H;
+    } else {
+        T.n_az = int(ceilf(W / float(tsx)));
+        T.n_el = int(ceilf(H / float(tsy)));
+        T.v_per_tile = float(tsy) / H;
+    }
+    return T;
+}
+
+#define XSG_SPH_DISPATCH(lidar, BODY)                   \
+    do {                                                \
+        if (lidar) {                                    \
+            using Cam = Spherical<true>;                \
+            BODY;                                       \
+        } else {                                        \
+            using Cam = Spherical<false>;               \
+            BODY;                                       \
+        }                                               \
+    } while (0)
+
+int xsg_isect_spherical_count(int lidar, const float* pack, const float* pts, const float* vel,
+                              const float* scales, const float* quats, const float* opac, const uint8_t* flags,
+                              const float* means2d, const float* radii, const float* depths,
+                              const float* elev_bounds, int n_elev, int64_t n, int tsx, int tsy, float W,
+                              float H, float ua, float ub, float uk, int32_t* counts, int64_t* n_isects_host,
+                              void* workspace, size_t ws_bytes, xsg_stream_t stream) {
+    XSG_REQUIRE(n >= 0 && tsx > 0 && tsy > 0 && W > 0 && H > 0 && n_isects_host, "isect_spherical_tiles: bad arguments");
+    XSG_REQUIRE(!lidar || (elev_bounds && n_elev > 0), "isect_lidar_tiles: elevation boundaries required");
+    XSG_REQUIRE(n == 0 || (pack && pts && scales && quats && flags && means2d && radii && depths && counts),
+                "isect_spherical_tiles: null input");
+    XSG_REQUIRE(reinterpret_cast<uintptr_t>(quats) % 16 == 0, "isect_spherical_tiles: quats must be 16-byte aligned");
+    cudaStream_t st = as_cuda(stream);
+    IsectWs w;
+    const size_t need = isect_ws_layout(n, 0, workspace, ws_bytes, &w);
+    if (ws_bytes < need || !workspace) return set_error(XSG_ERR_WORKSPACE, "isect_spherical_tiles: workspace too small");
+    XSG_CUDA(cudaMemsetAsync(w.total, 0, sizeof(unsigned long long), st));
+    const SphTiling T = make_sph_tiling(lidar, elev_bounds, n_elev, tsx, tsy, W, H);
+    const UTParams up = ut_params(ua, ub, uk, 1e-4f, 0.002f, 1.0f, W, H);
+    SphInputs in{pack, pts, vel, scales, reinterpret_cast<const float4*>(quats), opac, flags,
+                 reinterpret_cast<const float2*>(means2d), reinterpret_cast<const float2*>(radii), depths};
+    if (n > 0)
+        XSG_SPH_DISPATCH(lidar, (launch(sph_count_kernel<Cam>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
+                                    in, T, up, n, counts, w.total)));
+    unsigned long long tot = 0;
+    XSG_CUDA(cudaMemcpyAsync(&tot, w.total, sizeof(tot), cudaMemcpyDeviceToHost, st));
+    XSG_CUDA(cudaStreamSynchronize(st));
+    *n_isects_host = int64_t(tot);
+    if (tot >= (1ull << 31)) return set_error(XSG_ERR_UNSUPPORTED, "isect_spherical_tiles: more than 2^31 intersections");
+    return check_launch("isect_spherical_count");
+}
+
+int xsg_isect_spherical_emit(int lidar, const float* pack, const float* pts, const float* vel,
+                             const float* scales, const float* quats, const float* opac, const uint8_t* flags,
+                             const float* means2d, const float* radii, const float* depths,
+                             const float* elev_bounds, int n_elev, int64_t n, int tsx, int tsy, float W,
+                             float H, float ua, float ub, float uk, int sort, const int32_t* counts,
+                             int64_t n_isects, int64_t* isect_ids, int32_t* flatten_ids, void* workspace,
+                             size_t ws_bytes, xsg_stream_t stream) {
+    XSG_REQUIRE(n >= 0 && n_isects >= 0 && tsx > 0 && tsy > 0 && W > 0 && H > 0, "isect_spherical_tiles: bad arguments");
+    if (n_isects == 0) return XSG_OK;
+    XSG_REQUIRE(pack && pts && scales && quats && flags && means2d && radii && depths && counts && isect_ids &&
+                    flatten_ids, "isect_spherical_tiles: null input");
+    XSG_REQUIRE(reinterpret_cast<uintptr_t>(quats) % 16 == 0, "isect_spherical_tiles: quats must be 16-byte aligned");
+    cudaStream_t st = as_cuda(stream);
+    IsectWs w;
+    const size_t need = isect_ws_layout(n, sort ? n_isects : 0, workspace, ws_bytes, &w);
+    if (ws_bytes < need || !workspace) return set_error(XSG_ERR_WORKSPACE, "isect_spherical_tiles: workspace too small");
+    const SphTiling T = make_sph_tiling(lidar, elev_bounds, n_elev, tsx, tsy, W, H);
+    const UTParams up = ut_params(ua, ub, uk, 1e-4f, 0.002f, 1.0f, W, H);
+    SphInputs in{pack, pts, vel, scales, reinterpret_cast<const float4*>(quats), opac, flags,
+                 reinterpret_cast<const float2*>(means2d), reinterpret_cast<const float2*>(radii), depths};
+    const int64_t n_tiles = int64_t(T.n_az) * T.n_el;
+    const int bucket_neg = int((int64_t(1) << tile_bits_for(n_tiles)) - 1);
+    if (!sort) {
+        int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
+        if (rc != XSG_OK) return rc;
+        XSG_SPH_DISPATCH(lidar, (launch(sph_emit_kernel<Cam, false>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
+                                    in, T, up, n, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
+                                    bucket_neg)));
+        return check_launch("isect_spherical_emit");
+    }
+    // The second (wrap) rectangle of a flag-2 Gaussian carries its own depth,
+    // so the presort by Gaussian depth does not order those intersections.
+    // They are rare; the general path below sorts intersections by
+    // (tile, depth bits) with two chained stable sorts instead.
+    int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
+    if (rc != XSG_OK) return rc;
+    XSG_SPH_DISPATCH(lidar, (launch(sph_emit_kernel<Cam, false>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
+                                in, T, up, n, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
+                                bucket_neg)));
+    return sort_isect_pairs_inplace(isect_ids, flatten_ids, n_isects, tile_bits_for(n_tiles), w, st);
+}
+
+int xsg_isect_offset_encode(const int64_t* isect_ids, int64_t n_isects, int tw, int th, int32_t* offsets,
+                            xsg_stream_t stream) {
+    XSG_REQUIRE(tw > 0 && th > 0 && offsets && n_isects >= 0, "isect_offset_encode: bad arguments");
+    cudaStream_t st = as_cuda(stream);
+    const int64_t n_tiles = int64_t(tw) * th;
+    if (n_isects == 0) {
+        XSG_CUDA(cudaMemsetAsync(offsets, 0, size_t(n_tiles) * sizeof(int32_t), st));
+        return XSG_OK;
+    }
+    XSG_REQUIRE(isect_ids, "isect_offset_encode: null isect_ids");
+    launch(offset_encode_kernel, blocks_for(n_isects, 256), 256, 0, st, isect_ids, n_isects, n_tiles,
+                                                                   tile_bits_for(n_tiles), offsets);
+    return check_launch("isect_offset_encode");
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+"""Autograd wrapper of the dynamic (per-Gaussian velocity) compositing ops.
+
+Mirrors the reference's UTGSDynamicRasterize
+(src/xsimgs/rendering/rasterize_dynamic.py:10-114).
+"""
+import torch
+
+from .._native import _C
+from ..utils import apply_grad_mask
+
+
+class UTGSDynamicRasterize(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, positions, velocity, rotation, scale, density, colors, ray_o, ray_d,
+                ray_time_delta, isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int):
+        height, width = ray_o.shape[:2]
+        out_rgb, out_depth, out_alpha, last_ids = _C.rasterize_eval3d_dynamic_fwd(
+            means=positions,
+            velocity=velocity,
+            quats=rotation,
+            scales=scale,
+            opacities=density.view(1, -1),
+            colors=colors.unsqueeze(0) if colors is not None else None,
+            ray_origs=ray_o,
+            ray_dirs=ray_d,
+            ray_time_delta=ray_time_delta,
+            image_width=width,
+            image_height=height,
+            tile_size_width=tile_size_x,
+            tile_size_height=tile_size_y,
+            tile_offsets=isect_offsets,
+            flatten_ids=flatten_ids,
+        )
+        ctx.tile_size_x = tile_size_x
+        ctx.tile_size_y = tile_size_y
+        ctx.save_for_backward(positions, velocity, rotation, scale, density, colors,
+                              ray_o, ray_d, ray_time_delta, isect_offsets, flatten_ids,
+                              out_rgb, out_depth, out_alpha, last_ids)
+        return out_rgb, out_depth, out_alpha
+
+    @staticmethod
+    def backward(ctx, grad_rgb, grad_depth, grad_alpha):
+        (positions, velocity, rotation, scale, density, colors, ray_o, ray_d, ray_time_delta,
+         isect_offsets, flatten_ids, out_rgb, out_depth, out_alpha, last_ids) = ctx.saved_tensors
+        # v_points, v_velocity, v_quat, v_scale, v_opacity, v_colors, v_ray_o, v_ray_d, v_time_delta
+        grads = _C.rasterize_eval3d_dynamic_bwd(
+            positions, velocity, scale, rotation, density, colors,
+            ray_o, ray_d, ray_time_delta,
+            ctx.tile_size_x, ctx.tile_size_y, isect_offsets, flatten_ids,
+            out_alpha, last_ids,
+            grad_rgb.contiguous() if grad_rgb is not None else None,
+            grad_depth.contiguous(),
+            grad_alpha.contiguous(),
+        )
+        return apply_grad_mask(ctx, list(grads) + [None, None, None, None])
+
+
+def ut_gs_dynamic_rasterize(positions, velocity, rotation, scale, density, colors, ray_o, ray_d,
+                            ray_time_delta, isect_offsets, flatten_ids, tile_size_x: int,
+                            tile_size_y: int):
+    return UTGSDynamicRasterize.apply(positions, velocity, rotation, scale, density, colors,
+                                      ray_o, ray_d, ray_time_delta, isect_offsets, flatten_ids,
+                                      tile_size_x, tile_size_y)

@@ -1,0 +1,42 @@
+"""Frozen algorithmic work model of the compositing kernels (FLOP counts per
+pair), used by bench.py for `roofline.achieved`.
+
+Counts are of the reference's expressions (csrc/rasterization/eval3d_fwd.cu
+and eval3d_bwd.cu), one FLOP per add/mul/compare/min, two per FMA, and one
+per MUFU operation (rsqrt, ex2, rcp), independent of how a kernel schedules
+them:
+
+forward, every evaluated (pixel, Gaussian) pair (eval3d_fwd.cu:116-131)
+    o - mu 3, M (o - mu) 15, M d 15, |Md|^2 5, normalise 3 + rsqrt 1,
+    cross 9, |cross|^2 5, power 1, exp 1 + ex2 1, opacity * 1, min 1,
+    alpha test 1                                                      = 62
+forward, every contributing pair (eval3d_fwd.cu:133-153)
+    hit distance 5 + 5 + 1 + div 1, T (1 - alpha) 2, test 1, vis 1,
+    depth 2, colour 2 C                                            = 18 + 2C
+backward, every pair up to the pixel's last contributor (eval3d_bwd.cu:172-206)
+    the forward's 62
+backward, every contributing pair (eval3d_bwd.cu:219-271): 1/(1-alpha),
+    T, fac 4; colour grad C; v_alpha 4 C + 7; hit-distance terms 30;
+    power-term branch 135 (cross products, normalise backward, outer
+    products, M^T products); quat/scale VJP 136; opacity 1; buffers 2 C + 2
+                                                                  = 315 + 7 C
+"""
+
+FWD_EVAL = 62
+BWD_EVAL = 62
+
+
+def fwd_contrib(cdim: int) -> int:
+    return 18 + 2 * cdim
+
+
+def bwd_contrib(cdim: int) -> int:
+    return 315 + 7 * cdim
+
+
+def fwd_flops(n_eval: int, n_contrib: int, cdim: int) -> float:
+    return float(FWD_EVAL * n_eval + fwd_contrib(cdim) * n_contrib)
+
+
+def bwd_flops(n_eval_bwd: int, n_contrib: int, cdim: int) -> float:
+    return float(BWD_EVAL * n_eval_bwd + bwd_contrib(cdim) * n_contrib)
