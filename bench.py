@@ -207,25 +207,32 @@ def gpu_arm(args, world, rank, local):
     cam = spec.make(dev)
     W, H = spec.width, spec.height
     leaves = {k: v.clone().requires_grad_(True) for k, v in sc.params().items()}
-    # all gradients live in one flat buffer so one all-reduce covers them
-    sizes = [v.numel() for v in leaves.values()]
-    flat_grad = torch.zeros(sum(sizes), device=dev)
-    off = 0
-    for v, n in zip(leaves.values(), sizes):
-        v.grad = flat_grad[off:off + n].view_as(v)
-        off += n
     origin = cam.t0
     g_rgb, g_d, g_a = (t.to(dev) for t in scenes.upstream_grads(H, W, 3, seed=1 + rank))
 
+    def allreduce_grads():
+        """Sum the Gaussian gradients over ranks: one NCCL all-reduce per
+        parameter tensor, issued as one coalesced group."""
+        grads = [v.grad for v in leaves.values()]
+        cm = getattr(dist, "_coalescing_manager", None)
+        if cm is not None:
+            with cm(async_ops=False):
+                for g in grads:
+                    dist.all_reduce(g)
+        else:
+            for g in grads:
+                dist.all_reduce(g)
+
     def step(gr, gd, ga):
-        flat_grad.zero_()
+        for v in leaves.values():
+            v.grad = None
         colors = X.spherical_harmonics_fused(leaves["sh"], leaves["means"], origin, DEG_C2)
         color, depth, alpha, _ = X.ut_gs_render(cam, leaves["means"], leaves["scales"], leaves["quats"],
                                                 leaves["opacities"], W, H, colors=colors)
         loss = (color * gr).sum() + (depth * gd).sum() + (alpha * ga).sum()
         loss.backward()
         if world > 1:
-            dist.all_reduce(flat_grad)
+            allreduce_grads()
         return loss
 
     def barrier():

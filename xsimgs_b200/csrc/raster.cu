@@ -57,9 +57,12 @@ struct RasterArgs {
     float* v_ray_d;
     float* v_ray_t;
     unsigned long long* pair_counters;  // evaluated, contributing (optional)
+    const int32_t* tile_order;          // launch order of the tiles (optional)
 };
 
 static unsigned long long* g_pair_counters = nullptr;
+// tile-order scratch is sized for images up to this many tiles (16k x 16k at 16x16)
+constexpr int64_t kMaxTiles = int64_t(1) << 20;
 
 // --------------------------------------------------------------- pack ----
 // quat_to_rotmat (rasterization/utils.h:61-83) and S^-1 R^T
@@ -88,6 +91,56 @@ __global__ void pack_records_kernel(const float* __restrict__ means, const float
     else r[3] = make_float4(opac[g], 0.f, 0.f, 0.f);
 }
 
+// Heavy tiles first: tiles bucketed by floor(log2(intersection count)),
+// buckets in descending order, tile order kept inside a bucket.  One CTA.
+__global__ void __launch_bounds__(1024) tile_order_kernel(const int32_t* __restrict__ offsets, int n_tiles,
+                                                          int32_t n_isects, int32_t* __restrict__ order) {
+    __shared__ int hist[33];
+    __shared__ int base[33];
+    if (threadIdx.x < 33) hist[threadIdx.x] = 0;
+    __syncthreads();
+    auto bucket = [&](int t) {
+        const int32_t e = (t == n_tiles - 1) ? n_isects : offsets[t + 1];
+        const int32_t c = e - offsets[t];
+        return c > 0 ? 32 - __clz(c) : 0;  // 0 for empty, 1 + floor(log2 c)
+    };
+    for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) atomicAdd(&hist[bucket(t)], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int b = 32; b >= 0; --b) {
+            base[b] = run;
+            run += hist[b];
+        }
+    }
+    __syncthreads();
+    // stable scatter: one pass per chunk of blockDim tiles, ranks by warp match
+    for (int t0 = 0; t0 < n_tiles; t0 += blockDim.x) {
+        const int t = t0 + threadIdx.x;
+        const int b = t < n_tiles ? bucket(t) : -1;
+        __shared__ int cnt[32][33];
+        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int k = lane; k < 33; k += 32) cnt[w][k] = 0;
+        __syncthreads();
+        const unsigned peers = __match_any_sync(0xffffffffu, b);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        if (b >= 0 && rank == 0) cnt[w][b] = __popc(peers);
+        __syncthreads();
+        if (b >= 0) {
+            int before = 0;
+            for (int ww = 0; ww < w; ++ww) before += cnt[ww][b];
+            order[base[b] + before + rank] = t;
+        }
+        __syncthreads();
+        if (threadIdx.x < 33) {
+            int tot = 0;
+            for (int ww = 0; ww < int(blockDim.x >> 5); ++ww) tot += cnt[ww][threadIdx.x];
+            base[threadIdx.x] += tot;
+        }
+        __syncthreads();
+    }
+}
+
 struct TileCtx {
     int tile, px, py;
     bool inside;
@@ -97,7 +150,7 @@ struct TileCtx {
 
 __device__ __forceinline__ TileCtx tile_ctx(const RasterArgs& a) {
     TileCtx c;
-    c.tile = blockIdx.x;
+    c.tile = a.tile_order ? a.tile_order[blockIdx.x] : int(blockIdx.x);
     const int ty = c.tile / a.ntx, tx = c.tile - ty * a.ntx;
     const int t = threadIdx.x;
     c.px = tx * a.tsx + t % a.tsx;
@@ -208,7 +261,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
             const float power = -0.5f * dot3(gc, gc);
             const float alpha = fminf(0.999f, r3.x * __expf(power));
             if (alpha < 1.f / 255.f) continue;
-            const float hit_t = -dot3(gro, grd) / dot3(grd, grd);
+            const float hit_t = __fdividef(-dot3(gro, grd), l);
             const float nT = T * (1.0f - alpha);
             if (nT <= 1e-4f) {
                 done = true;
@@ -254,12 +307,18 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
 }
 
 // ----------------------------------------------------------- backward ----
-// Gradient accumulator slots per Gaussian.
-//   0-2 v_mean  3 v_opacity  4-7 v_quat  8-10 v_scale  11 -  12-15 v_colour
-//   (C <= 4)    16-18 v_velocity (dynamic)
-template <bool kDyn>
+// Per-Gaussian gradient accumulator (floats):
+//   0-2 v_mean   3 v_opacity   4-12 dL/dM (3x3, row-major)   13-15 v_colour
+//   16 v_colour[3] (C == 4)   then v_velocity (dynamic).
+// The quaternion/scale gradients are linear in dL/dM for a fixed Gaussian, so
+// dL/dM is summed over all pixels and the reference's per-pair
+// quat_scale_to_preci_half_vjp (rasterization/utils.h:232-263) is applied
+// once per Gaussian in the finalize pass.
+template <int CDIM, bool kDyn>
 struct Acc {
-    static constexpr int N = kDyn ? 20 : 16;
+    static constexpr int kExtraColor = (CDIM == 4) ? 1 : 0;
+    static constexpr int kVel = 16 + kExtraColor;
+    static constexpr int N = (kDyn || CDIM == 4) ? 20 : 16;
 };
 
 // Transpose butterfly: on entry every lane holds v[0..15]; on exit lane L
@@ -302,19 +361,18 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 template <int CDIM, bool kDyn>
-__global__ void __launch_bounds__(256) raster_bwd_kernel(RasterArgs a) {
+__global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     constexpr bool kStageColor = CDIM > 0 && CDIM <= 4;
     constexpr int CSZ = CDIM > 0 ? CDIM : 1;
-    constexpr int NA = Acc<kDyn>::N;
+    using AC = Acc<CDIM, kDyn>;
+    constexpr int NA = AC::N;
     extern __shared__ float4 smem4[];
     const int bs = blockDim.x;
     float4* s0 = smem4;
     float4* s1 = s0 + bs;
     float4* s2 = s1 + bs;
     float4* s3 = s2 + bs;
-    float4* sq = s3 + bs;         // raw quaternion
-    float4* ss = sq + bs;         // raw scale
-    float4* sc = ss + bs;         // colours (C <= 4)
+    float4* sc = s3 + bs;                               // colours (C <= 4)
     float* sacc = reinterpret_cast<float*>(sc + bs);   // [bs][NA]
     int32_t* sid = reinterpret_cast<int32_t*>(sacc + bs * NA);
     int32_t* sflag = sid + bs;
@@ -367,10 +425,6 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterArgs a) {
             const int32_t g = a.flatten[idx];
             const float4* r = a.rec + int64_t(kRecF4) * g;
             s0[tr] = r[0]; s1[tr] = r[1]; s2[tr] = r[2]; s3[tr] = r[3];
-            sq[tr] = make_float4(a.quats[4 * int64_t(g)], a.quats[4 * int64_t(g) + 1],
-                                 a.quats[4 * int64_t(g) + 2], a.quats[4 * int64_t(g) + 3]);
-            ss[tr] = make_float4(a.scales[3 * int64_t(g)], a.scales[3 * int64_t(g) + 1],
-                                 a.scales[3 * int64_t(g) + 2], 0.f);
             if constexpr (kStageColor) {
                 float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
                 const float* cp = a.colors + int64_t(g) * CDIM;
@@ -415,8 +469,9 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterArgs a) {
 #pragma unroll
             for (int k = 0; k < CSZ; ++k) gcol[k] = 0.f;
             if (valid) {
-                const float hit_t = -dot3(grd, gro) / dot3(grd, grd);
-                const float ra = 1.0f / fmaxf(1e-6f, 1.0f - alpha);
+                const float od = dot3(gro, grd);
+                const float hit_t = __fdividef(-od, l);
+                const float ra = __fdividef(1.0f, fmaxf(1e-6f, 1.0f - alpha));
                 T *= ra;
                 const float fac = alpha * T;
                 float rgb[CSZ];
@@ -439,11 +494,11 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterArgs a) {
                 }
                 v_alpha += (hit_t * T - dbuf * ra) * vd;
                 v_alpha += T_final * ra * va;
-                const float dd = dot3(grd, grd);
-                const float od = dot3(gro, grd);
+                // hit distance t* = -(gro . grd) / (grd . grd)
                 const float dLdt = vd * fac;
-                v3 v_gro = (-1.0f * grd) * dLdt * (1.0f / dd);
-                v3 v_grd = (2.0f * od * grd - dd * gro) * dLdt * (1.0f / (dd * dd));
+                const float il2 = __fdividef(1.0f, l);
+                v3 v_gro = (-dLdt * il2) * grd;
+                v3 v_grd = (dLdt * il2 * il2) * (2.0f * od * grd - l * gro);
                 if (op * vis <= 0.99f) {
                     const float v_vis = op * v_alpha;
                     const float v_dist = -0.5f * vis * v_vis;
@@ -471,42 +526,14 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterArgs a) {
                         gvel[0] = -v_omm.x * rt; gvel[1] = -v_omm.y * rt; gvel[2] = -v_omm.z * rt;
                         vtime += -dot3(v_omm, vel);
                     }
-                    // gradient of M rows: vM[i] = v_grd[i] d + v_gro[i] (o - mu)
+                    gv[3] = vis * v_alpha;
+                    // dL/dM row i = v_grd[i] d + v_gro[i] (o - mu)
                     const v3 vM0 = v_grd.x * d + v_gro.x * omm;
                     const v3 vM1 = v_grd.y * d + v_gro.y * omm;
                     const v3 vM2 = v_grd.z * d + v_gro.z * omm;
-                    // quat_scale_to_preci_half_vjp (utils.h:232-263)
-                    const float4 q = sq[t];
-                    const float4 s = ss[t];
-                    float w = q.x, x = q.y, y = q.z, z = q.w;
-                    const float inv = rsqrtf(x * x + y * y + z * z + w * w);
-                    x *= inv; y *= inv; z *= inv; w *= inv;
-                    const float x2 = x * x, y2 = y * y, z2 = z * z;
-                    const float xy = x * y, xz = x * z, yz = y * z;
-                    const float wx = w * x, wy = w * y, wz = w * z;
-                    // columns of R
-                    const v3 C0 = mk3(1.f - 2.f * (y2 + z2), 2.f * (xy + wz), 2.f * (xz - wy));
-                    const v3 C1 = mk3(2.f * (xy - wz), 1.f - 2.f * (x2 + z2), 2.f * (yz + wx));
-                    const v3 C2 = mk3(2.f * (xz + wy), 2.f * (yz - wx), 1.f - 2.f * (x2 + y2));
-                    const float isx = 1.0f / s.x, isy = 1.0f / s.y, isz = 1.0f / s.z;
-                    gv[8] = -isx * isx * dot3(C0, vM0);
-                    gv[9] = -isy * isy * dot3(C1, vM1);
-                    gv[10] = -isz * isz * dot3(C2, vM2);
-                    // V(c, r) = dL/dR[row r][col c] = vM[c][r] / s_c
-                    const v3 V0 = isx * vM0, V1 = isy * vM1, V2 = isz * vM2;
-                    const float gw = 2.f * (x * (V1.z - V2.y) + y * (V2.x - V0.z) + z * (V0.y - V1.x));
-                    const float gx = 2.f * (-2.f * x * (V1.y + V2.z) + y * (V0.y + V1.x) + z * (V0.z + V2.x) +
-                                            w * (V1.z - V2.y));
-                    const float gy = 2.f * (x * (V0.y + V1.x) - 2.f * y * (V0.x + V2.z) + z * (V1.z + V2.y) +
-                                            w * (V2.x - V0.z));
-                    const float gz = 2.f * (x * (V0.z + V2.x) + y * (V1.z + V2.y) - 2.f * z * (V0.x + V1.y) +
-                                            w * (V0.y - V1.x));
-                    const float dq = gw * w + gx * x + gy * y + gz * z;
-                    gv[4] = (gw - dq * w) * inv;
-                    gv[5] = (gx - dq * x) * inv;
-                    gv[6] = (gy - dq * y) * inv;
-                    gv[7] = (gz - dq * z) * inv;
-                    gv[3] = vis * v_alpha;
+                    gv[4] = vM0.x; gv[5] = vM0.y; gv[6] = vM0.z;
+                    gv[7] = vM1.x; gv[8] = vM1.y; gv[9] = vM1.z;
+                    gv[10] = vM2.x; gv[11] = vM2.y; gv[12] = vM2.z;
                 }
 #pragma unroll
                 for (int k = 0; k < CDIM; ++k) buf[k] += rgb[k] * fac;
@@ -514,23 +541,27 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterArgs a) {
             }
             if constexpr (kStageColor) {
 #pragma unroll
-                for (int k = 0; k < CDIM; ++k) gv[12 + k] = gcol[k];
+                for (int k = 0; k < (CDIM < 3 ? CDIM : 3); ++k) gv[13 + k] = gcol[k];
             }
             butterfly16(gv, lane);
             float* slot = sacc + t * NA;
             if ((lane & 1) == 0) atomicAdd(slot + (lane >> 1), gv[0]);
-            if (kDyn) {
+            if constexpr (CDIM == 4) {
+                const float s4 = warp_sum(gcol[3]);
+                if (lane == 0) atomicAdd(slot + 16, s4);
+            }
+            if constexpr (kDyn) {
 #pragma unroll
                 for (int k = 0; k < 3; ++k) {
-                    const float s = warp_sum(gvel[k]);
-                    if (lane == 0) atomicAdd(slot + 16 + k, s);
+                    const float sv = warp_sum(gvel[k]);
+                    if (lane == 0) atomicAdd(slot + AC::kVel + k, sv);
                 }
             }
             if constexpr (!kStageColor && CDIM > 0) {
                 // wide colours: warp-reduced straight into the output
                 for (int k = 0; k < CDIM; ++k) {
-                    const float s = warp_sum(gcol[k]);
-                    if (lane == 0 && s != 0.f) atomicAdd(a.v_colors_direct + int64_t(sid[t]) * CDIM + k, s);
+                    const float sv = warp_sum(gcol[k]);
+                    if (lane == 0 && sv != 0.f) atomicAdd(a.v_colors_direct + int64_t(sid[t]) * CDIM + k, sv);
                 }
             }
             if (lane == 0) sflag[t] = 1;
@@ -556,28 +587,59 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterArgs a) {
     }
 }
 
-// Accumulator -> output layout.
-template <bool kDyn>
-__global__ void grads_finalize_kernel(const float* __restrict__ G, int64_t n, int cdim, float* __restrict__ v_means,
+// Accumulator -> output layout, with the quaternion / scale VJP of the summed
+// dL/dM (quat_scale_to_preci_half_vjp, rasterization/utils.h:208-263).
+template <int CDIM, bool kDyn>
+__global__ void grads_finalize_kernel(const float* __restrict__ G, const float* __restrict__ quats,
+                                      const float* __restrict__ scales, int64_t n, float* __restrict__ v_means,
                                       float* __restrict__ v_vel, float* __restrict__ v_quats,
                                       float* __restrict__ v_scales, float* __restrict__ v_opac,
                                       float* __restrict__ v_colors) {
-    constexpr int NA = Acc<kDyn>::N;
+    using AC = Acc<CDIM, kDyn>;
+    constexpr int NA = AC::N;
     const int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (g >= n) return;
+    float A[NA];
     const float4* s = reinterpret_cast<const float4*>(G + g * NA);
-    const float4 a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
-    v_means[3 * g] = a0.x; v_means[3 * g + 1] = a0.y; v_means[3 * g + 2] = a0.z;
-    v_opac[g] = a0.w;
-    v_quats[4 * g] = a1.x; v_quats[4 * g + 1] = a1.y; v_quats[4 * g + 2] = a1.z; v_quats[4 * g + 3] = a1.w;
-    v_scales[3 * g] = a2.x; v_scales[3 * g + 1] = a2.y; v_scales[3 * g + 2] = a2.z;
-    if (v_colors && cdim <= 4) {
-        const float cc[4] = {a3.x, a3.y, a3.z, a3.w};
-        for (int k = 0; k < cdim; ++k) v_colors[g * cdim + k] = cc[k];
+#pragma unroll
+    for (int k = 0; k < NA / 4; ++k) {
+        const float4 v = s[k];
+        A[4 * k] = v.x; A[4 * k + 1] = v.y; A[4 * k + 2] = v.z; A[4 * k + 3] = v.w;
     }
-    if (kDyn) {
-        const float4 a4 = s[4];
-        v_vel[3 * g] = a4.x; v_vel[3 * g + 1] = a4.y; v_vel[3 * g + 2] = a4.z;
+    v_means[3 * g] = A[0]; v_means[3 * g + 1] = A[1]; v_means[3 * g + 2] = A[2];
+    v_opac[g] = A[3];
+    const v3 vM0 = mk3(A[4], A[5], A[6]), vM1 = mk3(A[7], A[8], A[9]), vM2 = mk3(A[10], A[11], A[12]);
+    float w = quats[4 * g], x = quats[4 * g + 1], y = quats[4 * g + 2], z = quats[4 * g + 3];
+    const float inv = rsqrtf(x * x + y * y + z * z + w * w);
+    x *= inv; y *= inv; z *= inv; w *= inv;
+    const float x2 = x * x, y2 = y * y, z2 = z * z;
+    const float xy = x * y, xz = x * z, yz = y * z;
+    const float wx = w * x, wy = w * y, wz = w * z;
+    // columns of R
+    const v3 C0 = mk3(1.f - 2.f * (y2 + z2), 2.f * (xy + wz), 2.f * (xz - wy));
+    const v3 C1 = mk3(2.f * (xy - wz), 1.f - 2.f * (x2 + z2), 2.f * (yz + wx));
+    const v3 C2 = mk3(2.f * (xz + wy), 2.f * (yz - wx), 1.f - 2.f * (x2 + y2));
+    const float isx = 1.0f / scales[3 * g], isy = 1.0f / scales[3 * g + 1], isz = 1.0f / scales[3 * g + 2];
+    v_scales[3 * g] = -isx * isx * dot3(C0, vM0);
+    v_scales[3 * g + 1] = -isy * isy * dot3(C1, vM1);
+    v_scales[3 * g + 2] = -isz * isz * dot3(C2, vM2);
+    // V(c, r) = dL/dR[row r][col c] = dL/dM[c][r] / s_c
+    const v3 V0 = isx * vM0, V1 = isy * vM1, V2 = isz * vM2;
+    const float gw = 2.f * (x * (V1.z - V2.y) + y * (V2.x - V0.z) + z * (V0.y - V1.x));
+    const float gx = 2.f * (-2.f * x * (V1.y + V2.z) + y * (V0.y + V1.x) + z * (V0.z + V2.x) + w * (V1.z - V2.y));
+    const float gy = 2.f * (x * (V0.y + V1.x) - 2.f * y * (V0.x + V2.z) + z * (V1.z + V2.y) + w * (V2.x - V0.z));
+    const float gz = 2.f * (x * (V0.z + V2.x) + y * (V1.z + V2.y) - 2.f * z * (V0.x + V1.y) + w * (V0.y - V1.x));
+    const float dq = gw * w + gx * x + gy * y + gz * z;
+    v_quats[4 * g] = (gw - dq * w) * inv;
+    v_quats[4 * g + 1] = (gx - dq * x) * inv;
+    v_quats[4 * g + 2] = (gy - dq * y) * inv;
+    v_quats[4 * g + 3] = (gz - dq * z) * inv;
+    if constexpr (CDIM > 0 && CDIM <= 4) {
+#pragma unroll
+        for (int k = 0; k < CDIM; ++k) v_colors[g * CDIM + k] = (k < 3) ? A[13 + k] : A[16];
+    }
+    if constexpr (kDyn) {
+        v_vel[3 * g] = A[AC::kVel]; v_vel[3 * g + 1] = A[AC::kVel + 1]; v_vel[3 * g + 2] = A[AC::kVel + 2];
     }
 }
 
@@ -588,9 +650,8 @@ __global__ void grads_finalize_kernel(const float* __restrict__ G, int64_t n, in
 static const int kSupported[] = {0, 1, 2, 3, 4, 5, 8, 9, 16, 17, 32, 33, 64, 65, 128, 129, 256, 257, 512, 513};
 
 static size_t fwd_smem(int bs) { return size_t(bs) * (5 * sizeof(float4) + sizeof(int32_t)); }
-static size_t bwd_smem(int bs, bool dyn) {
-    const int na = dyn ? 20 : 16;
-    return size_t(bs) * (7 * sizeof(float4) + na * sizeof(float) + 2 * sizeof(int32_t));
+static size_t bwd_smem(int bs, int na) {
+    return size_t(bs) * (5 * sizeof(float4) + na * sizeof(float) + 2 * sizeof(int32_t));
 }
 
 template <int CDIM, bool kDyn>
@@ -605,15 +666,22 @@ static int launch_fwd(const RasterArgs& a, int bs, cudaStream_t st) {
     return check_launch("rasterize_fwd");
 }
 
+struct FinalizeOut {
+    float *v_means, *v_vel, *v_quats, *v_scales, *v_opac, *v_colors;
+};
+
 template <int CDIM, bool kDyn>
-static int launch_bwd(const RasterArgs& a, int bs, cudaStream_t st) {
-    const size_t sm = bwd_smem(bs, kDyn);
+static int launch_bwd(const RasterArgs& a, int bs, cudaStream_t st, int64_t n_gauss, FinalizeOut fin) {
+    const size_t sm = bwd_smem(bs, Acc<CDIM, kDyn>::N);
     auto fn = raster_bwd_kernel<CDIM, kDyn>;
     if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
     {
         ScopedTimer tm("rasterize_bwd", st);
         launch(fn, unsigned(a.ntx * a.nty), bs, sm, st, a);
     }
+    if (a.G && n_gauss > 0)
+        launch(grads_finalize_kernel<CDIM, kDyn>, blocks_for(n_gauss, 256), 256, 0, st, a.G, a.quats, a.scales,
+               n_gauss, fin.v_means, fin.v_vel, fin.v_quats, fin.v_scales, fin.v_opac, fin.v_colors);
     return check_launch("rasterize_bwd");
 }
 
@@ -653,7 +721,8 @@ size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim) {
     (void)cdim;
     if (n_gauss < 0) n_gauss = 0;
     // packed records + the (dynamic-sized) gradient accumulator
-    return Arena::round(size_t(n_gauss) * kRecF4 * sizeof(float4)) + Arena::round(size_t(n_gauss) * 20 * sizeof(float));
+    return Arena::round(size_t(n_gauss) * kRecF4 * sizeof(float4)) + Arena::round(size_t(n_gauss) * 20 * sizeof(float)) +
+           Arena::round(size_t(kMaxTiles) * sizeof(int32_t));
 }
 
 int xsg_rasterize_fwd(const float* means, const float* velocity, const float* quats, const float* scales,
@@ -671,9 +740,12 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
     cudaStream_t st = as_cuda(stream);
     Arena ar(workspace, ws_bytes);
     float4* rec = ar.take<float4>(size_t(n_gauss) * kRecF4);
+    const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
+    int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
     if ((n_gauss > 0 && !rec) || (n_gauss > 0 && !workspace))
         return set_error(XSG_ERR_WORKSPACE, "rasterize_fwd: workspace too small");
     const bool dyn = velocity != nullptr;
+    if (order) launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
     if (n_gauss > 0)
         launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales, opacities,
                                                                       n_gauss, rec);
@@ -684,6 +756,7 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
     a.W = W; a.H = H; a.tsx = tsx; a.tsy = tsy; a.ntx = tiles_w; a.nty = tiles_h;
     a.out_rgb = renders; a.out_depth = depths; a.out_alpha = alphas; a.out_last = last_ids;
     a.pair_counters = g_pair_counters;
+    a.tile_order = order;
     const int bs = tsx * tsy;
 #define XSG_FWD_CASE(C)                                                             \
     case C:                                                                         \
@@ -718,13 +791,14 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     cudaStream_t st = as_cuda(stream);
     Arena ar(workspace, ws_bytes);
     float4* rec = ar.take<float4>(size_t(n_gauss) * kRecF4);
-    const int na = dyn ? 20 : 16;
+    const int na = (dyn || cdim == 4) ? 20 : 16;  // Acc<CDIM, kDyn>::N
     float* G = ar.take<float>(size_t(n_gauss) * na);
+    const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
+    int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
     if (n_gauss > 0 && (!rec || !G)) return set_error(XSG_ERR_WORKSPACE, "rasterize_bwd: workspace too small");
-    const int64_t npx = int64_t(W) * H;
-    XSG_CUDA(cudaMemsetAsync(v_ray_o, 0, size_t(npx) * 12, st));
-    XSG_CUDA(cudaMemsetAsync(v_ray_d, 0, size_t(npx) * 12, st));
-    if (dyn) XSG_CUDA(cudaMemsetAsync(v_ray_time_delta, 0, size_t(npx) * 4, st));
+    // every pixel of the image belongs to exactly one tile thread, which
+    // writes its v_ray_o / v_ray_d (/ v_ray_time_delta): no pre-zeroing
+    if (order) launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
     if (n_gauss > 0) {
         XSG_CUDA(cudaMemsetAsync(G, 0, size_t(n_gauss) * na * sizeof(float), st));
         if (cdim > 4) XSG_CUDA(cudaMemsetAsync(v_colors, 0, size_t(n_gauss) * cdim * sizeof(float), st));
@@ -739,12 +813,14 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     a.render_alpha = render_alphas; a.last_ids = last_ids;
     a.v_rgb = v_renders; a.v_depth = v_depths; a.v_alpha = v_alphas;
     a.G = G; a.v_colors_direct = v_colors;
+    a.tile_order = order;
     a.v_ray_o = v_ray_o; a.v_ray_d = v_ray_d; a.v_ray_t = v_ray_time_delta;
     const int bs = tsx * tsy;
+    FinalizeOut fin{v_means, v_velocity, v_quats, v_scales, v_opacities, v_colors};
     int lrc = XSG_OK;
 #define XSG_BWD_CASE(C)                                                                          \
     case C:                                                                                      \
-        lrc = dyn ? launch_bwd<C, true>(a, bs, st) : launch_bwd<C, false>(a, bs, st);            \
+        lrc = dyn ? launch_bwd<C, true>(a, bs, st, n_gauss, fin) : launch_bwd<C, false>(a, bs, st, n_gauss, fin); \
         break;
     switch (cdim) {
         XSG_CDIM_CASES(XSG_BWD_CASE)
@@ -752,15 +828,7 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     }
 #undef XSG_BWD_CASE
     if (lrc != XSG_OK) return lrc;
-    if (n_gauss > 0) {
-        if (dyn)
-            launch(grads_finalize_kernel<true>, blocks_for(n_gauss, 256), 256, 0, st, 
-                G, n_gauss, cdim, v_means, v_velocity, v_quats, v_scales, v_opacities, v_colors);
-        else
-            launch(grads_finalize_kernel<false>, blocks_for(n_gauss, 256), 256, 0, st, 
-                G, n_gauss, cdim, v_means, nullptr, v_quats, v_scales, v_opacities, v_colors);
-    }
-    return check_launch("rasterize_bwd_finalize");
+    return XSG_OK;
 }
 
 }  // extern "C"

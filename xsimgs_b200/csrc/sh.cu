@@ -109,44 +109,85 @@ struct ShLayout {
     __device__ __forceinline__ int64_t di(int64_t i, int ch) const { return l3kn ? int64_t(ch) * n + i : i * 3 + ch; }
 };
 
-template <int DEG>
-__global__ void __launch_bounds__(256)
+// Coefficients of 32 consecutive Gaussians are staged per warp in shared
+// memory: [N, K, 3] rows are read (and, in the backward, written) with
+// coalesced accesses, and each lane then walks its own row with an odd stride
+// (3K + 1 floats) so the per-lane reads do not conflict on banks.  The
+// [3, K, N] layout is already coalesced along N and is read directly.
+constexpr int kShWarps = 4;
+constexpr int kShThreads = kShWarps * 32;
+
+template <int DEG, bool kL3KN>
+__global__ void __launch_bounds__(kShThreads)
     sh_fwd_kernel(const float* __restrict__ origin, const float* __restrict__ pos, const float* __restrict__ coeffs,
                   const float* __restrict__ dc, const uint32_t* __restrict__ mask, ShLayout L,
                   float* __restrict__ out) {
     constexpr int NB = (DEG + 1) * (DEG + 1);
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= L.n) return;
+    extern __shared__ float stage[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t g0 = (int64_t(blockIdx.x) * kShWarps + w) * 32;
+    if (g0 >= L.n) return;
+    const int cnt = int(min(int64_t(32), L.n - g0));
+    const int S = L.dim * 3, SP = S + 1;
+    float* wb = stage + w * 32 * SP;
+    if constexpr (!kL3KN) {
+        const float* src = coeffs + g0 * S;
+        for (int gi = 0; gi < cnt; ++gi)
+            for (int r = lane; r < S; r += 32) wb[gi * SP + r] = src[gi * S + r];
+        __syncwarp();
+    }
+    const int64_t i = g0 + lane;
+    if (lane >= cnt) return;
     if (mask && !((mask[i >> 5] >> (i & 31)) & 1u)) return;
     v3 dir = ld3(pos + 3 * i) - mk3(origin[0], origin[1], origin[2]);
     dir = dir * rsqrtf(dot3(dir, dir));
     float b[25];
     sh_basis<DEG>(dir.x, dir.y, dir.z, b);
+    const int kb = L.has_dc ? 1 : 0;  // first band held in coeffs
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch) {
-        float r = b[0] * (L.has_dc ? dc[L.di(i, ch)] : coeffs[L.ci(i, 0, ch)]);
+        auto cf = [&](int k) {
+            return kL3KN ? coeffs[(int64_t(ch) * L.dim + (k - kb)) * L.n + i] : wb[lane * SP + (k - kb) * 3 + ch];
+        };
+        float r = b[0] * (L.has_dc ? dc[L.di(i, ch)] : cf(0));
 #pragma unroll
-        for (int k = 1; k < NB; ++k) r += b[k] * coeffs[L.ci(i, k, ch)];
+        for (int k = 1; k < NB; ++k) r += b[k] * cf(k);
         out[3 * i + ch] = r + 0.5f;
     }
 }
 
-template <int DEG>
-__global__ void __launch_bounds__(256)
+template <int DEG, bool kL3KN>
+__global__ void __launch_bounds__(kShThreads)
     sh_bwd_kernel(const float* __restrict__ origin, const float* __restrict__ pos, const float* __restrict__ coeffs,
                   const float* __restrict__ dc, const uint32_t* __restrict__ mask, ShLayout L,
                   const float* __restrict__ d_out, float* __restrict__ d_coeffs, float* __restrict__ d_dc,
                   float* __restrict__ d_pos, float* __restrict__ block_origin) {
     constexpr int NB = (DEG + 1) * (DEG + 1);
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    extern __shared__ float stage[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t g0 = (int64_t(blockIdx.x) * kShWarps + w) * 32;
+    const int S = L.dim * 3, SP = S + 1;
+    float* wb = stage + w * 32 * SP;
+    const int cnt = g0 < L.n ? int(min(int64_t(32), L.n - g0)) : 0;
+    if constexpr (!kL3KN) {
+        const float* src = coeffs + g0 * S;
+        for (int gi = 0; gi < cnt; ++gi)
+            for (int r = lane; r < S; r += 32) wb[gi * SP + r] = src[gi * S + r];
+        __syncwarp();
+    }
+    const int64_t i = g0 + lane;
+    const int kb = L.has_dc ? 1 : 0;
     v3 dorig = mk3(0.f, 0.f, 0.f);
-    if (i < L.n) {
+    if (lane < cnt) {
         const bool on = !mask || ((mask[i >> 5] >> (i & 31)) & 1u);
         if (!on) {
             // masked Gaussians get zero gradients (outputs are overwritten)
-            for (int k = 0; k < L.dim; ++k)
-                for (int ch = 0; ch < 3; ++ch)
-                    d_coeffs[L.l3kn ? (int64_t(ch) * L.dim + k) * L.n + i : (i * L.dim + k) * 3 + ch] = 0.f;
+            if constexpr (kL3KN) {
+                for (int k = 0; k < L.dim; ++k)
+                    for (int ch = 0; ch < 3; ++ch) d_coeffs[(int64_t(ch) * L.dim + k) * L.n + i] = 0.f;
+            } else {
+                for (int r = 0; r < S; ++r) wb[lane * SP + r] = 0.f;
+            }
             if (L.has_dc)
                 for (int ch = 0; ch < 3; ++ch) d_dc[L.di(i, ch)] = 0.f;
             st3(d_pos + 3 * i, mk3(0.f, 0.f, 0.f));
@@ -162,22 +203,34 @@ __global__ void __launch_bounds__(256)
             for (int ch = 0; ch < 3; ++ch) {
                 const float g = d_out[3 * i + ch];
                 if (L.has_dc) d_dc[L.di(i, ch)] = b[0] * g;
-                else d_coeffs[L.ci(i, 0, ch)] = b[0] * g;
 #pragma unroll
-                for (int k = 1; k < NB; ++k) {
-                    const int64_t o = L.ci(i, k, ch);
-                    d_coeffs[o] = b[k] * g;
-                    const float cg = coeffs[o] * g;
-                    gd.x += bx[k] * cg;
-                    gd.y += by[k] * cg;
-                    gd.z += bz[k] * cg;
+                for (int k = 0; k < NB; ++k) {
+                    if (k == 0 && L.has_dc) continue;
+                    const int kk = k - kb;
+                    float cf;
+                    if constexpr (kL3KN) {
+                        const int64_t o = (int64_t(ch) * L.dim + kk) * L.n + i;
+                        cf = coeffs[o];
+                        d_coeffs[o] = b[k] * g;
+                    } else {
+                        float* e = wb + lane * SP + kk * 3 + ch;
+                        cf = *e;
+                        *e = b[k] * g;  // the staged row becomes the gradient row
+                    }
+                    if (k > 0) {
+                        const float cg = cf * g;
+                        gd.x += bx[k] * cg;
+                        gd.y += by[k] * cg;
+                        gd.z += bz[k] * cg;
+                    }
                 }
             }
             // bands stored beyond the degree in use get zero gradient
-            const int first_unused = L.has_dc ? NB - 1 : NB;
-            for (int k = first_unused; k < L.dim; ++k)
-                for (int ch = 0; ch < 3; ++ch)
-                    d_coeffs[L.l3kn ? (int64_t(ch) * L.dim + k) * L.n + i : (i * L.dim + k) * 3 + ch] = 0.f;
+            for (int kk = NB - kb; kk < L.dim; ++kk)
+                for (int ch = 0; ch < 3; ++ch) {
+                    if constexpr (kL3KN) d_coeffs[(int64_t(ch) * L.dim + kk) * L.n + i] = 0.f;
+                    else wb[lane * SP + kk * 3 + ch] = 0.f;
+                }
             // normalize backward: il * g - il^3 (g . v) v
             const float il3 = il * il * il;
             const float gv = dot3(gd, diff);
@@ -186,20 +239,25 @@ __global__ void __launch_bounds__(256)
             dorig = -1.0f * dp;
         }
     }
+    if constexpr (!kL3KN) {
+        __syncwarp();
+        float* dst = d_coeffs + g0 * S;
+        for (int gi = 0; gi < cnt; ++gi)
+            for (int r = lane; r < S; r += 32) dst[gi * S + r] = wb[gi * SP + r];
+    }
     // per-block partial of d_origin
-    __shared__ float s[3][8];
+    __shared__ float s[3][kShWarps];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         dorig.x += __shfl_xor_sync(0xffffffffu, dorig.x, o);
         dorig.y += __shfl_xor_sync(0xffffffffu, dorig.y, o);
         dorig.z += __shfl_xor_sync(0xffffffffu, dorig.z, o);
     }
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) { s[0][w] = dorig.x; s[1][w] = dorig.y; s[2][w] = dorig.z; }
+    if (lane == 0) { s[0][w] = dorig.x; s[1][w] = dorig.y; s[2][w] = dorig.z; }
     __syncthreads();
     if (threadIdx.x < 3) {
         float t = 0.f;
-        for (int k = 0; k < int(blockDim.x >> 5); ++k) t += s[threadIdx.x][k];
+        for (int k = 0; k < kShWarps; ++k) t += s[threadIdx.x][k];
         block_origin[int64_t(blockIdx.x) * 3 + threadIdx.x] = t;
     }
 }
@@ -224,6 +282,8 @@ __global__ void sum_partials_kernel(const float* __restrict__ p, int64_t nb, flo
     }
 }
 
+static size_t sh_stage_bytes(int dim) { return size_t(kShWarps) * 32 * (3 * dim + 1) * sizeof(float); }
+
 static int sh_check(int degree, int64_t n, int dim, bool has_dc) {
     XSG_REQUIRE(degree >= 0 && degree <= 4, "Unsupported spherical harmonics degree: " + std::to_string(degree));
     XSG_REQUIRE(n >= 0 && dim >= 0, "spherical_harmonics: bad sizes");
@@ -247,19 +307,30 @@ int xsg_sh_fwd(int degree, const float* origin, const float* pos, const float* c
     XSG_REQUIRE(origin && pos && out && (coeffs || dim == 0), "spherical_harmonics_fwd: null argument");
     ShLayout L{n, dim, layout_3kn != 0, dc != nullptr};
     cudaStream_t st = as_cuda(stream);
-    const unsigned nb = blocks_for(n, 256);
+    const unsigned nb = blocks_for(n, kShThreads);
+    const size_t sm = layout_3kn ? 0 : sh_stage_bytes(dim);
+    int rc2 = XSG_OK;
+    auto go = [&](auto kernel) {
+        if (sm > 48 * 1024 && cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)) != cudaSuccess)
+            rc2 = set_error(XSG_ERR_UNSUPPORTED, "spherical_harmonics_fwd: too many coefficient bands");
+        else
+            launch(kernel, nb, kShThreads, sm, st, origin, pos, coeffs, dc, mask, L, out);
+    };
+#define XSG_SHF(D) (layout_3kn ? go(sh_fwd_kernel<D, true>) : go(sh_fwd_kernel<D, false>))
     switch (degree) {
-        case 0: launch(sh_fwd_kernel<0>, nb, 256, 0, st, origin, pos, coeffs, dc, mask, L, out); break;
-        case 1: launch(sh_fwd_kernel<1>, nb, 256, 0, st, origin, pos, coeffs, dc, mask, L, out); break;
-        case 2: launch(sh_fwd_kernel<2>, nb, 256, 0, st, origin, pos, coeffs, dc, mask, L, out); break;
-        case 3: launch(sh_fwd_kernel<3>, nb, 256, 0, st, origin, pos, coeffs, dc, mask, L, out); break;
-        default: launch(sh_fwd_kernel<4>, nb, 256, 0, st, origin, pos, coeffs, dc, mask, L, out); break;
+        case 0: XSG_SHF(0); break;
+        case 1: XSG_SHF(1); break;
+        case 2: XSG_SHF(2); break;
+        case 3: XSG_SHF(3); break;
+        default: XSG_SHF(4); break;
     }
+#undef XSG_SHF
+    if (rc2 != XSG_OK) return rc2;
     return check_launch("spherical_harmonics_fwd");
 }
 
 size_t xsg_sh_bwd_workspace_size(int64_t n) {
-    return Arena::round(size_t(n < 0 ? 0 : (n + 255) / 256 + 1) * 3 * sizeof(float));
+    return Arena::round(size_t(n < 0 ? 0 : (n + kShThreads - 1) / kShThreads + 1) * 3 * sizeof(float));
 }
 
 int xsg_sh_bwd(int degree, const float* origin, const float* pos, const float* coeffs, const float* dc,
@@ -278,10 +349,18 @@ int xsg_sh_bwd(int degree, const float* origin, const float* pos, const float* c
     if (!workspace || ws_bytes < xsg_sh_bwd_workspace_size(n))
         return set_error(XSG_ERR_WORKSPACE, "spherical_harmonics_bwd: workspace too small");
     ShLayout L{n, dim, layout_3kn != 0, dc != nullptr};
-    const unsigned nb = blocks_for(n, 256);
+    const unsigned nb = blocks_for(n, kShThreads);
     float* part = static_cast<float*>(workspace);
-#define XSG_SH_BWD(D) \
-    launch(sh_bwd_kernel<D>, nb, 256, 0, st, origin, pos, coeffs, dc, mask, L, d_out, d_coeffs, d_dc, d_pos, part)
+    const size_t sm = layout_3kn ? 0 : sh_stage_bytes(dim);
+    int rc2 = XSG_OK;
+    auto go = [&](auto kernel) {
+        if (sm > 48 * 1024 && cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)) != cudaSuccess)
+            rc2 = set_error(XSG_ERR_UNSUPPORTED, "spherical_harmonics_bwd: too many coefficient bands");
+        else
+            launch(kernel, nb, kShThreads, sm, st, origin, pos, coeffs, dc, mask, L, d_out, d_coeffs, d_dc, d_pos,
+                   part);
+    };
+#define XSG_SH_BWD(D) (layout_3kn ? go(sh_bwd_kernel<D, true>) : go(sh_bwd_kernel<D, false>))
     switch (degree) {
         case 0: XSG_SH_BWD(0); break;
         case 1: XSG_SH_BWD(1); break;
@@ -290,6 +369,7 @@ int xsg_sh_bwd(int degree, const float* origin, const float* pos, const float* c
         default: XSG_SH_BWD(4); break;
     }
 #undef XSG_SH_BWD
+    if (rc2 != XSG_OK) return rc2;
     launch(sum_partials_kernel, 1, 1024, 0, st, part, nb, d_origin);
     return check_launch("spherical_harmonics_bwd");
 }
