@@ -170,40 +170,44 @@ __device__ __forceinline__ v3 mrows(float4 r0, float4 r1, float4 r2, v3 v) {
                r2.x * v.x + r2.y * v.y + r2.z * v.z);
 }
 
-// All pixels of the tile that lie inside the image see the same ray origin
-// (thread 0's pixel, the tile's top-left, is always inside); returns it in o_tile.
-__device__ __forceinline__ bool tile_origin_uniform(const TileCtx& c, v3 o, v3& o_tile) {
-    __shared__ float s_o[3];
-    if (threadIdx.x == 0) { s_o[0] = o.x; s_o[1] = o.y; s_o[2] = o.z; }
-    __syncthreads();
-    o_tile = mk3(s_o[0], s_o[1], s_o[2]);
-    const bool same = !c.inside || (__float_as_uint(o.x) == __float_as_uint(o_tile.x) &&
-                                    __float_as_uint(o.y) == __float_as_uint(o_tile.y) &&
-                                    __float_as_uint(o.z) == __float_as_uint(o_tile.z));
-    return __syncthreads_and(same) != 0;
+// ------------------------------------------------------------ forward ----
+// Warp-independent: each warp owns 32 pixels (two rows of a 16-wide tile),
+// stages the tile's records 32 at a time in its own slice of shared memory
+// and stops as soon as all its pixels are saturated.  There is no block-wide
+// barrier; the CTA only groups a tile's warps on one SM so they share L1.
+constexpr int kWarpSlot = 32;
+
+// shared memory per warp: 4 record float4 + 1 colour float4 per slot, ids
+__host__ __device__ constexpr size_t warp_stage_bytes() {
+    return size_t(kWarpSlot) * (5 * sizeof(float4) + sizeof(int32_t));
 }
 
-// ------------------------------------------------------------ forward ----
 template <int CDIM, bool kDyn>
 __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
     constexpr bool kStageColor = CDIM > 0 && CDIM <= 4;
     constexpr int CSZ = CDIM > 0 ? CDIM : 1;
     extern __shared__ float4 smem4[];
-    const int bs = blockDim.x;
-    float4* s0 = smem4;
-    float4* s1 = s0 + bs;
-    float4* s2 = s1 + bs;
-    float4* s3 = s2 + bs;
-    float4* sc = s3 + bs;                                    // colours (C <= 4)
-    int32_t* sid = reinterpret_cast<int32_t*>(sc + bs);       // Gaussian ids (C > 4)
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    float4* s0 = smem4 + wid * (5 * kWarpSlot);
+    float4* s1 = s0 + kWarpSlot;
+    float4* s2 = s1 + kWarpSlot;
+    float4* s3 = s2 + kWarpSlot;
+    float4* sc = s3 + kWarpSlot;
+    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 5 * kWarpSlot) + wid * kWarpSlot;
 
     const TileCtx c = tile_ctx(a);
-    const int tr = threadIdx.x;
     const v3 o = c.inside ? ld3(a.ray_o + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
     const v3 d = c.inside ? ld3(a.ray_d + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
     const float rt = (kDyn && c.inside && a.ray_t) ? a.ray_t[c.pix] : 0.0f;
-    v3 o_tile = o;
-    const bool uni = !kDyn && tile_origin_uniform(c, o, o_tile);
+    // lane 0 has the warp's left-most, top-most pixel: if it is outside the
+    // image every lane is
+    const v3 o0 = mk3(__shfl_sync(0xffffffffu, o.x, 0), __shfl_sync(0xffffffffu, o.y, 0),
+                      __shfl_sync(0xffffffffu, o.z, 0));
+    const bool same = !c.inside || (__float_as_uint(o.x) == __float_as_uint(o0.x) &&
+                                    __float_as_uint(o.y) == __float_as_uint(o0.y) &&
+                                    __float_as_uint(o.z) == __float_as_uint(o0.z));
+    // static scene and one ray origin for the warp: M (o - mu) once per Gaussian
+    const bool uni = !kDyn && __all_sync(0xffffffffu, same);
 
     bool done = !c.inside;
     float T = 1.0f, depth = 0.0f;
@@ -212,23 +216,19 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
     for (int k = 0; k < CSZ; ++k) acc[k] = 0.f;
     int32_t cur = 0;
     unsigned n_eval = 0, n_contrib = 0;
-    const int nb = (c.end - c.start + bs - 1) / bs;
-    for (int b = 0; b < nb; ++b) {
-        if (__syncthreads_count(done) >= bs) break;
-        const int32_t bstart = c.start + b * bs;
-        const int32_t idx = bstart + tr;
+    for (int32_t base = c.start; base < c.end; base += kWarpSlot) {
+        if (__all_sync(0xffffffffu, done)) break;
+        const int32_t idx = base + lane;
         if (idx < c.end) {
             const int32_t g = a.flatten[idx];
             const float4* r = a.rec + int64_t(kRecF4) * g;
             float4 r0 = r[0], r1 = r[1], r2 = r[2];
             const float4 r3 = r[3];
             if (uni) {
-                // gro = M (o - mu), once per Gaussian for the whole tile
-                const v3 omm = o_tile - mk3(r0.w, r1.w, r2.w);
-                const v3 gro = mrows(r0, r1, r2, omm);
+                const v3 gro = mrows(r0, r1, r2, o0 - mk3(r0.w, r1.w, r2.w));
                 r0.w = gro.x; r1.w = gro.y; r2.w = gro.z;
             }
-            s0[tr] = r0; s1[tr] = r1; s2[tr] = r2; s3[tr] = r3;
+            s0[lane] = r0; s1[lane] = r1; s2[lane] = r2; s3[lane] = r3;
             if constexpr (kStageColor) {
                 float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
                 const float* cp = a.colors + int64_t(g) * CDIM;
@@ -236,14 +236,14 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
                 if (CDIM > 1) cc.y = cp[1];
                 if (CDIM > 2) cc.z = cp[2];
                 if (CDIM > 3) cc.w = cp[3];
-                sc[tr] = cc;
+                sc[lane] = cc;
             } else {
-                sid[tr] = g;
+                sid[lane] = g;
             }
         }
-        __syncthreads();
-        const int bsize = min(bs, c.end - bstart);
-        for (int t = 0; (t < bsize) && !done; ++t) {
+        __syncwarp();
+        const int n = min(kWarpSlot, c.end - base);
+        for (int t = 0; (t < n) && !done; ++t) {
             const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
             ++n_eval;
             v3 gro;
@@ -280,19 +280,20 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
 #pragma unroll 4
                 for (int k = 0; k < CDIM; ++k) acc[k] += cp[k] * vis;
             }
-            cur = bstart + t;
+            cur = base + t;
             T = nT;
             ++n_contrib;
         }
+        __syncwarp();
     }
     if (a.pair_counters) {
         unsigned long long e = n_eval, k = n_contrib;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            e += __shfl_xor_sync(0xffffffffu, e, o);
-            k += __shfl_xor_sync(0xffffffffu, k, o);
+        for (int o_ = 16; o_ > 0; o_ >>= 1) {
+            e += __shfl_xor_sync(0xffffffffu, e, o_);
+            k += __shfl_xor_sync(0xffffffffu, k, o_);
         }
-        if ((threadIdx.x & 31) == 0) {
+        if (lane == 0) {
             atomicAdd(a.pair_counters, e);
             atomicAdd(a.pair_counters + 1, k);
         }
@@ -360,6 +361,10 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Warp-independent like the forward: each warp walks the tile's list back to
+// front from its own last contributor, and every (warp, Gaussian) event with a
+// contributing lane is reduced in registers (butterfly) and added to the
+// Gaussian's accumulator with four vector reductions.
 template <int CDIM, bool kDyn>
 __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     constexpr bool kStageColor = CDIM > 0 && CDIM <= 4;
@@ -367,25 +372,19 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     using AC = Acc<CDIM, kDyn>;
     constexpr int NA = AC::N;
     extern __shared__ float4 smem4[];
-    const int bs = blockDim.x;
-    float4* s0 = smem4;
-    float4* s1 = s0 + bs;
-    float4* s2 = s1 + bs;
-    float4* s3 = s2 + bs;
-    float4* sc = s3 + bs;                               // colours (C <= 4)
-    float* sacc = reinterpret_cast<float*>(sc + bs);   // [bs][NA]
-    int32_t* sid = reinterpret_cast<int32_t*>(sacc + bs * NA);
-    int32_t* sflag = sid + bs;
-    __shared__ int32_t s_maxbin;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    float4* s0 = smem4 + wid * (5 * kWarpSlot);
+    float4* s1 = s0 + kWarpSlot;
+    float4* s2 = s1 + kWarpSlot;
+    float4* s3 = s2 + kWarpSlot;
+    float4* sc = s3 + kWarpSlot;
+    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 5 * kWarpSlot) + wid * kWarpSlot;
 
     const TileCtx c = tile_ctx(a);
-    const int tr = threadIdx.x;
-    const int lane = tr & 31;
-    const v3 o = c.inside ? ld3(a.ray_o + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
-    const v3 d = c.inside ? ld3(a.ray_d + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
-    const float rt = (kDyn && c.inside) ? a.ray_t[c.pix] : 0.0f;
-
     const bool inside = c.inside;
+    const v3 o = inside ? ld3(a.ray_o + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
+    const v3 d = inside ? ld3(a.ray_d + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
+    const float rt = (kDyn && inside) ? a.ray_t[c.pix] : 0.0f;
     const float T_final = 1.0f - a.render_alpha[c.pix];
     float T = T_final;
     float buf[CSZ];
@@ -395,7 +394,7 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
         buf[k] = 0.f;
         vc[k] = 0.f;
     }
-    const int32_t bin_final = inside ? a.last_ids[c.pix] : 0;
+    const int32_t bin_final = inside ? a.last_ids[c.pix] : -1;
     if (a.v_rgb) {
 #pragma unroll
         for (int k = 0; k < CDIM; ++k) vc[k] = inside ? a.v_rgb[c.pix * CDIM + k] : 0.f;
@@ -405,26 +404,16 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     v3 vro = mk3(0.f, 0.f, 0.f), vrd = mk3(0.f, 0.f, 0.f);
     float vtime = 0.f, dbuf = 0.f;
 
-    if (tr == 0) s_maxbin = -1;
-    __syncthreads();
-    if (inside) atomicMax(&s_maxbin, bin_final);
-    for (int k = 0; k < NA; ++k) sacc[tr * NA + k] = 0.f;
-    sflag[tr] = 0;
-    __syncthreads();
-    const int32_t maxbin = s_maxbin;
-
-    const int nb = (c.end - c.start + bs - 1) / bs;
-    for (int b = 0; b < nb; ++b) {
-        const int32_t bend = c.end - 1 - b * bs;
-        const int32_t bsize = min(bs, bend + 1 - c.start);
-        // every intersection of this batch lies past the last contributor of
-        // every pixel of the tile: nothing to do (uniform across the block)
-        if (bend - (bsize - 1) > maxbin) continue;
-        const int32_t idx = bend - tr;
+    // this warp's last contributor bounds where it starts
+    int32_t wmax = bin_final;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
+    for (int32_t top = min(c.end - 1, wmax); top >= c.start; top -= kWarpSlot) {
+        const int32_t idx = top - lane;
         if (idx >= c.start) {
             const int32_t g = a.flatten[idx];
             const float4* r = a.rec + int64_t(kRecF4) * g;
-            s0[tr] = r[0]; s1[tr] = r[1]; s2[tr] = r[2]; s3[tr] = r[3];
+            s0[lane] = r[0]; s1[lane] = r[1]; s2[lane] = r[2]; s3[lane] = r[3];
             if constexpr (kStageColor) {
                 float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
                 const float* cp = a.colors + int64_t(g) * CDIM;
@@ -432,18 +421,14 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
                 if (CDIM > 1) cc.y = cp[1];
                 if (CDIM > 2) cc.z = cp[2];
                 if (CDIM > 3) cc.w = cp[3];
-                sc[tr] = cc;
+                sc[lane] = cc;
             }
-            sid[tr] = g;
+            sid[lane] = g;
         }
-        __syncthreads();
-        // this warp's last contributor bounds where it starts in the batch
-        int32_t wmax = bin_final;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
-        const int t0 = max(0, bend - wmax);
-        for (int t = t0; t < bsize; ++t) {
-            bool valid = inside && (bend - t <= bin_final);
+        __syncwarp();
+        const int n = min(kWarpSlot, top - c.start + 1);
+        for (int t = 0; t < n; ++t) {
+            bool valid = inside && (top - t <= bin_final);
             const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
             v3 mu = mk3(r0.w, r1.w, r2.w);
             const v3 vel = mk3(r3.y, r3.z, r3.w);
@@ -544,18 +529,21 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
                 for (int k = 0; k < (CDIM < 3 ? CDIM : 3); ++k) gv[13 + k] = gcol[k];
             }
             butterfly16(gv, lane);
-            float* slot = sacc + t * NA;
-            if ((lane & 1) == 0) atomicAdd(slot + (lane >> 1), gv[0]);
-            if constexpr (CDIM == 4) {
-                const float s4 = warp_sum(gcol[3]);
-                if (lane == 0) atomicAdd(slot + 16, s4);
-            }
-            if constexpr (kDyn) {
-#pragma unroll
-                for (int k = 0; k < 3; ++k) {
-                    const float sv = warp_sum(gvel[k]);
-                    if (lane == 0) atomicAdd(slot + AC::kVel + k, sv);
+            // lanes 8k+0/2/4/6 hold values 4k..4k+3: gather them into lane 8k
+            const float g1 = __shfl_down_sync(0xffffffffu, gv[0], 2);
+            const float g2 = __shfl_down_sync(0xffffffffu, gv[0], 4);
+            const float g3 = __shfl_down_sync(0xffffffffu, gv[0], 6);
+            float* dst = a.G + int64_t(sid[t]) * NA;
+            if ((lane & 7) == 0) red_add_v4(dst + (lane >> 1), gv[0], g1, g2, g3);
+            if constexpr (NA > 16) {
+                float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
+                if constexpr (CDIM == 4) e0 = warp_sum(gcol[3]);
+                if constexpr (kDyn) {
+                    const float x0 = warp_sum(gvel[0]), x1 = warp_sum(gvel[1]), x2 = warp_sum(gvel[2]);
+                    if (AC::kVel == 16) { e0 = x0; e1 = x1; e2 = x2; }
+                    else { e1 = x0; e2 = x1; e3 = x2; }
                 }
+                if (lane == 0) red_add_v4(dst + 16, e0, e1, e2, e3);
             }
             if constexpr (!kStageColor && CDIM > 0) {
                 // wide colours: warp-reduced straight into the output
@@ -564,21 +552,8 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
                     if (lane == 0 && sv != 0.f) atomicAdd(a.v_colors_direct + int64_t(sid[t]) * CDIM + k, sv);
                 }
             }
-            if (lane == 0) sflag[t] = 1;
         }
-        __syncthreads();
-        // flush this batch's per-Gaussian sums, one vector reduction per 4 slots
-        if (sflag[tr]) {
-            float* dst = a.G + int64_t(sid[tr]) * NA;
-            float* src = sacc + tr * NA;
-#pragma unroll
-            for (int k = 0; k < NA; k += 4) {
-                red_add_v4(dst + k, src[k], src[k + 1], src[k + 2], src[k + 3]);
-                src[k] = 0.f; src[k + 1] = 0.f; src[k + 2] = 0.f; src[k + 3] = 0.f;
-            }
-            sflag[tr] = 0;
-        }
-        __syncthreads();
+        __syncwarp();
     }
     if (inside) {
         st3(a.v_ray_o + 3 * c.pix, vro);
@@ -649,10 +624,8 @@ __global__ void grads_finalize_kernel(const float* __restrict__ G, const float* 
 
 static const int kSupported[] = {0, 1, 2, 3, 4, 5, 8, 9, 16, 17, 32, 33, 64, 65, 128, 129, 256, 257, 512, 513};
 
-static size_t fwd_smem(int bs) { return size_t(bs) * (5 * sizeof(float4) + sizeof(int32_t)); }
-static size_t bwd_smem(int bs, int na) {
-    return size_t(bs) * (5 * sizeof(float4) + na * sizeof(float) + 2 * sizeof(int32_t));
-}
+static size_t fwd_smem(int bs) { return size_t(bs / 32) * warp_stage_bytes(); }
+static size_t bwd_smem(int bs, int) { return size_t(bs / 32) * warp_stage_bytes(); }
 
 template <int CDIM, bool kDyn>
 static int launch_fwd(const RasterArgs& a, int bs, cudaStream_t st) {

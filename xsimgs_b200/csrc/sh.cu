@@ -117,6 +117,46 @@ struct ShLayout {
 constexpr int kShWarps = 4;
 constexpr int kShThreads = kShWarps * 32;
 
+// Copies `total` consecutive floats of global memory into a warp's staging
+// rows (row length S, padded row stride S + 1), eight loads in flight per
+// lane.  Row/column of element j come from a float reciprocal: (j + 0.5) / S
+// is at least 0.5 / S away from an integer, far more than its rounding error.
+__device__ __forceinline__ void stage_rows_in(const float* __restrict__ src, int total, int S, float* wb,
+                                              int lane) {
+    const float invS = 1.0f / float(S);
+    for (int base = 0; base < total; base += 32 * 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = base + u * 32 + lane;
+            v[u] = j < total ? src[j] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = base + u * 32 + lane;
+            if (j < total) {
+                const int row = int((float(j) + 0.5f) * invS);
+                wb[row * (S + 1) + (j - row * S)] = v[u];
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void stage_rows_out(float* __restrict__ dst, int total, int S, const float* wb,
+                                               int lane) {
+    const float invS = 1.0f / float(S);
+    for (int base = 0; base < total; base += 32 * 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = base + u * 32 + lane;
+            if (j < total) {
+                const int row = int((float(j) + 0.5f) * invS);
+                dst[j] = wb[row * (S + 1) + (j - row * S)];
+            }
+        }
+    }
+}
+
 template <int DEG, bool kL3KN>
 __global__ void __launch_bounds__(kShThreads)
     sh_fwd_kernel(const float* __restrict__ origin, const float* __restrict__ pos, const float* __restrict__ coeffs,
@@ -131,9 +171,7 @@ __global__ void __launch_bounds__(kShThreads)
     const int S = L.dim * 3, SP = S + 1;
     float* wb = stage + w * 32 * SP;
     if constexpr (!kL3KN) {
-        const float* src = coeffs + g0 * S;
-        for (int gi = 0; gi < cnt; ++gi)
-            for (int r = lane; r < S; r += 32) wb[gi * SP + r] = src[gi * S + r];
+        stage_rows_in(coeffs + g0 * S, cnt * S, S, wb, lane);
         __syncwarp();
     }
     const int64_t i = g0 + lane;
@@ -170,9 +208,7 @@ __global__ void __launch_bounds__(kShThreads)
     float* wb = stage + w * 32 * SP;
     const int cnt = g0 < L.n ? int(min(int64_t(32), L.n - g0)) : 0;
     if constexpr (!kL3KN) {
-        const float* src = coeffs + g0 * S;
-        for (int gi = 0; gi < cnt; ++gi)
-            for (int r = lane; r < S; r += 32) wb[gi * SP + r] = src[gi * S + r];
+        if (cnt > 0) stage_rows_in(coeffs + g0 * S, cnt * S, S, wb, lane);
         __syncwarp();
     }
     const int64_t i = g0 + lane;
@@ -241,9 +277,7 @@ __global__ void __launch_bounds__(kShThreads)
     }
     if constexpr (!kL3KN) {
         __syncwarp();
-        float* dst = d_coeffs + g0 * S;
-        for (int gi = 0; gi < cnt; ++gi)
-            for (int r = lane; r < S; r += 32) dst[gi * S + r] = wb[gi * SP + r];
+        if (cnt > 0) stage_rows_out(d_coeffs + g0 * S, cnt * S, S, wb, lane);
     }
     // per-block partial of d_origin
     __shared__ float s[3][kShWarps];
