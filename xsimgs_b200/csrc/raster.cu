@@ -170,6 +170,83 @@ __device__ __forceinline__ v3 mrows(float4 r0, float4 r1, float4 r2, v3 v) {
                r2.x * v.x + r2.y * v.y + r2.z * v.z);
 }
 
+// ------------------------------------------------------- warp culling ----
+// A warp's 32 pixel rays are bounded by one origin o_c (all origins within
+// r_o of it) and a double cone of lines around the unit axis `ax` with
+// half-angle theta (cos_t, sin_t).  A Gaussian can reach alpha >= 1/255 on a
+// line only if the line meets the ellipsoid |M (x - mu)|^2 <= 2 ln(255 o),
+// which lies inside the sphere of radius sqrt(2 ln(255 o)) * s_max around mu
+// (s_max = 1 / min_i |row_i(M)|).  If every line of the cone misses that
+// sphere, inflated by relative and absolute margins far larger than the
+// rounding of either computation, no lane of the warp can accept the Gaussian:
+// the forward and backward skip it without changing any result.
+struct WarpCone {
+    v3 oc, ax;
+    float cos_t, sin_t, r_o, rt_max;
+    bool on;
+};
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_min_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ WarpCone warp_cone(bool inside, v3 o, v3 d, float rt) {
+    WarpCone w;
+    const float dl = dot3(d, d);
+    const v3 dh = (inside && dl > 0.f) ? d * rsqrtf(dl) : mk3(0.f, 0.f, 0.f);
+    v3 sum = dh;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        sum.x += __shfl_xor_sync(0xffffffffu, sum.x, off);
+        sum.y += __shfl_xor_sync(0xffffffffu, sum.y, off);
+        sum.z += __shfl_xor_sync(0xffffffffu, sum.z, off);
+    }
+    const float sl = dot3(sum, sum);
+    w.ax = sl > 0.f ? sum * rsqrtf(sl) : mk3(0.f, 0.f, 1.f);
+    w.cos_t = warp_min_f(inside ? dot3(dh, w.ax) : 1.0f) - 1e-5f;
+    w.sin_t = sqrtf(fmaxf(0.f, 1.0f - w.cos_t * w.cos_t));
+    w.oc = mk3(__shfl_sync(0xffffffffu, o.x, 0), __shfl_sync(0xffffffffu, o.y, 0),
+               __shfl_sync(0xffffffffu, o.z, 0));
+    const v3 dv = o - w.oc;
+    w.r_o = warp_max_f(inside ? sqrtf(dot3(dv, dv)) : 0.f);
+    w.rt_max = warp_max_f(inside ? fabsf(rt) : 0.f);
+    // cull only narrow cones of directions (the pixels of one warp are a few
+    // degrees apart); anything unusual keeps every Gaussian
+    w.on = (w.cos_t > 0.5f) && __all_sync(0xffffffffu, !inside || (dl > 0.f && isfinite(dl)));
+    return w;
+}
+
+// true: some line of the warp's cone may see alpha >= 1/255 of this Gaussian
+__device__ __forceinline__ bool cone_may_hit(const WarpCone& w, float4 r0, float4 r1, float4 r2, float4 r3,
+                                             bool dyn) {
+    if (!w.on) return true;
+    const float op = r3.x;
+    if (!(op * 255.0f > 1.0f)) return false;  // alpha <= opacity < 1/255 everywhere
+    const float m0 = r0.x * r0.x + r0.y * r0.y + r0.z * r0.z;
+    const float m1 = r1.x * r1.x + r1.y * r1.y + r1.z * r1.z;
+    const float m2 = r2.x * r2.x + r2.y * r2.y + r2.z * r2.z;
+    const float mmin = fminf(m0, fminf(m1, m2));  // 1 / s_max^2
+    if (!(mmin > 0.f) || !isfinite(op)) return true;
+    float R = sqrtf(2.0f * logf(op * 255.0f) / mmin);
+    if (dyn) R += w.rt_max * sqrtf(r3.y * r3.y + r3.z * r3.z + r3.w * r3.w);
+    const v3 v = mk3(r0.w, r1.w, r2.w) - w.oc;
+    const float vn = sqrtf(dot3(v, v));
+    R = (R + w.r_o) * 1.01f + 1e-4f * vn + 1e-6f;
+    if (!isfinite(R) || !isfinite(vn) || vn <= R) return true;
+    const float cp = fabsf(dot3(v, w.ax)) / vn;  // cos of the angle to the cone axis
+    if (cp >= w.cos_t) return true;              // inside the cone
+    const float sp = sqrtf(fmaxf(0.f, 1.0f - cp * cp));
+    const float s_pt = sp * w.cos_t - cp * w.sin_t;  // sin(phi - theta) > 0
+    return vn * s_pt <= R;
+}
+
 // ------------------------------------------------------------ forward ----
 // Warp-independent: each warp owns 32 pixels (two rows of a 16-wide tile),
 // stages the tile's records 32 at a time in its own slice of shared memory
@@ -208,6 +285,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
                                     __float_as_uint(o.z) == __float_as_uint(o0.z));
     // static scene and one ray origin for the warp: M (o - mu) once per Gaussian
     const bool uni = !kDyn && __all_sync(0xffffffffu, same);
+    const WarpCone cone = warp_cone(c.inside, o, d, rt);
 
     bool done = !c.inside;
     float T = 1.0f, depth = 0.0f;
@@ -215,15 +293,18 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
 #pragma unroll
     for (int k = 0; k < CSZ; ++k) acc[k] = 0.f;
     int32_t cur = 0;
-    unsigned n_eval = 0, n_contrib = 0;
+    int32_t stop = c.end;  // index of the terminating pair, for the pair counters
+    unsigned n_contrib = 0;
     for (int32_t base = c.start; base < c.end; base += kWarpSlot) {
         if (__all_sync(0xffffffffu, done)) break;
         const int32_t idx = base + lane;
+        bool keep = false;
         if (idx < c.end) {
             const int32_t g = a.flatten[idx];
             const float4* r = a.rec + int64_t(kRecF4) * g;
             float4 r0 = r[0], r1 = r[1], r2 = r[2];
             const float4 r3 = r[3];
+            keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
             if (uni) {
                 const v3 gro = mrows(r0, r1, r2, o0 - mk3(r0.w, r1.w, r2.w));
                 r0.w = gro.x; r1.w = gro.y; r2.w = gro.z;
@@ -241,11 +322,12 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
                 sid[lane] = g;
             }
         }
+        unsigned live = __ballot_sync(0xffffffffu, keep);
         __syncwarp();
-        const int n = min(kWarpSlot, c.end - base);
-        for (int t = 0; (t < n) && !done; ++t) {
+        while (live && !done) {
+            const int t = __ffs(live) - 1;
+            live &= live - 1;
             const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
-            ++n_eval;
             v3 gro;
             if (uni) {
                 gro = mk3(r0.w, r1.w, r2.w);
@@ -265,6 +347,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
             const float nT = T * (1.0f - alpha);
             if (nT <= 1e-4f) {
                 done = true;
+                stop = base + t;
                 break;
             }
             const float vis = alpha * T;
@@ -287,7 +370,10 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
         __syncwarp();
     }
     if (a.pair_counters) {
-        unsigned long long e = n_eval, k = n_contrib;
+        // evaluated pairs as the reference counts them: every pair of the
+        // tile's list up to and including the terminating one
+        unsigned long long e = c.inside ? (unsigned long long)(min(stop + 1, c.end) - c.start) : 0ull;
+        unsigned long long k = n_contrib;
 #pragma unroll
         for (int o_ = 16; o_ > 0; o_ >>= 1) {
             e += __shfl_xor_sync(0xffffffffu, e, o_);
@@ -404,16 +490,20 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     v3 vro = mk3(0.f, 0.f, 0.f), vrd = mk3(0.f, 0.f, 0.f);
     float vtime = 0.f, dbuf = 0.f;
 
+    const WarpCone cone = warp_cone(inside, o, d, rt);
     // this warp's last contributor bounds where it starts
     int32_t wmax = bin_final;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
     for (int32_t top = min(c.end - 1, wmax); top >= c.start; top -= kWarpSlot) {
         const int32_t idx = top - lane;
+        bool keep = false;
         if (idx >= c.start) {
             const int32_t g = a.flatten[idx];
             const float4* r = a.rec + int64_t(kRecF4) * g;
-            s0[lane] = r[0]; s1[lane] = r[1]; s2[lane] = r[2]; s3[lane] = r[3];
+            const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
+            keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
+            s0[lane] = r0; s1[lane] = r1; s2[lane] = r2; s3[lane] = r3;
             if constexpr (kStageColor) {
                 float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
                 const float* cp = a.colors + int64_t(g) * CDIM;
@@ -425,9 +515,11 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
             }
             sid[lane] = g;
         }
+        unsigned live = __ballot_sync(0xffffffffu, keep);
         __syncwarp();
-        const int n = min(kWarpSlot, top - c.start + 1);
-        for (int t = 0; t < n; ++t) {
+        while (live) {
+            const int t = __ffs(live) - 1;
+            live &= live - 1;
             bool valid = inside && (top - t <= bin_final);
             const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
             v3 mu = mk3(r0.w, r1.w, r2.w);
