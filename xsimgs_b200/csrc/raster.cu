@@ -153,8 +153,15 @@ __device__ __forceinline__ TileCtx tile_ctx(const RasterArgs& a) {
     c.tile = a.tile_order ? a.tile_order[blockIdx.x] : int(blockIdx.x);
     const int ty = c.tile / a.ntx, tx = c.tile - ty * a.ntx;
     const int t = threadIdx.x;
-    c.px = tx * a.tsx + t % a.tsx;
-    c.py = ty * a.tsy + t / a.tsx;
+    if ((a.tsx % 8 == 0) && (a.tsy % 4 == 0)) {
+        // each warp covers an 8 x 4 block of the tile (lane 0 at its top-left)
+        const int w = t >> 5, l = t & 31, wc = a.tsx >> 3;
+        c.px = tx * a.tsx + (w % wc) * 8 + (l & 7);
+        c.py = ty * a.tsy + (w / wc) * 4 + (l >> 3);
+    } else {
+        c.px = tx * a.tsx + t % a.tsx;
+        c.py = ty * a.tsy + t / a.tsx;
+    }
     c.inside = c.px < a.W && c.py < a.H;
     const int64_t lin = int64_t(c.py) * a.W + c.px;
     const int64_t last = int64_t(a.W) * a.H - 1;
@@ -247,6 +254,73 @@ __device__ __forceinline__ bool cone_may_hit(const WarpCone& w, float4 r0, float
     return vn * s_pt <= R;
 }
 
+// Exact per-pixel pre-test for warps whose pixels share one ray origin o
+// (and, for moving Gaussians, one time offset).  With g = M (o - mu) and
+// rho^2 = 2 ln(255 opacity), the line o + s d reaches alpha >= 1/255 iff its
+// whitened distance to the centre is at most rho, i.e. iff
+//   q(d) = d^T A d >= 0,  A = b b^T - k M^T M,  b = M^T g,  k = |g|^2 - rho^2
+// (q(d) = |M d|^2 (rho^2 - dist^2)).  A is built once per Gaussian by the
+// staging lane; every lane then evaluates q for its own direction with six
+// FMAs and a Gaussian stays in the warp's list if any lane may see it.  The
+// margin (in dist^2 units, scaled by max |M d|^2 / |d|^2) covers the float
+// rounding of q and of the alpha computation with a wide safety factor.
+struct Quad {
+    float4 a;  // a00, a11, a22, 2 a01
+    float4 b;  // 2 a02, 2 a12, margin * lambda_max, unused
+};
+
+__device__ __forceinline__ Quad quad_keep_all() {
+    Quad q;
+    q.a = make_float4(0.f, 0.f, 0.f, 0.f);
+    q.b = make_float4(0.f, 0.f, 1.0f, 0.f);
+    return q;
+}
+
+__device__ __forceinline__ Quad make_quad(float4 r0, float4 r1, float4 r2, float op, v3 mu, v3 o) {
+    Quad q;
+    if (!(op * 255.0f > 1.0f)) {  // alpha <= opacity < 1/255 on every line
+        q.a = make_float4(0.f, 0.f, 0.f, 0.f);
+        q.b = make_float4(0.f, 0.f, -1.0f, 0.f);
+        return q;
+    }
+    const v3 m0 = mk3(r0.x, r0.y, r0.z), m1 = mk3(r1.x, r1.y, r1.z), m2 = mk3(r2.x, r2.y, r2.z);
+    const v3 om = o - mu;
+    const v3 g = mk3(dot3(m0, om), dot3(m1, om), dot3(m2, om));
+    const float g2 = dot3(g, g);
+    const float rho2 = 2.0f * logf(op * 255.0f);
+    const float k = g2 - rho2;
+    if (!(k > 0.0f) || !isfinite(g2)) return quad_keep_all();  // origin inside the ellipsoid
+    const v3 b = g.x * m0 + g.y * m1 + g.z * m2;
+    // M^T M = sum_i row_i row_i^T
+    const float s00 = m0.x * m0.x + m1.x * m1.x + m2.x * m2.x;
+    const float s11 = m0.y * m0.y + m1.y * m1.y + m2.y * m2.y;
+    const float s22 = m0.z * m0.z + m1.z * m1.z + m2.z * m2.z;
+    const float s01 = m0.x * m0.y + m1.x * m1.y + m2.x * m2.y;
+    const float s02 = m0.x * m0.z + m1.x * m1.z + m2.x * m2.z;
+    const float s12 = m0.y * m0.z + m1.y * m1.z + m2.y * m2.z;
+    const float lmax = fmaxf(dot3(m0, m0), fmaxf(dot3(m1, m1), dot3(m2, m2)));
+    const float marg = 1e-3f * rho2 + 1e-5f * sqrtf(g2) * (sqrtf(rho2) + 1.0f) + 1e-6f + 4e-6f * (g2 + fabsf(k));
+    q.a = make_float4(b.x * b.x - k * s00, b.y * b.y - k * s11, b.z * b.z - k * s22, 2.0f * (b.x * b.y - k * s01));
+    q.b = make_float4(2.0f * (b.x * b.z - k * s02), 2.0f * (b.y * b.z - k * s12), marg * lmax, 0.f);
+    if (!isfinite(q.a.x) || !isfinite(q.a.y) || !isfinite(q.a.z) || !isfinite(q.a.w) || !isfinite(q.b.x) ||
+        !isfinite(q.b.y) || !isfinite(q.b.z))
+        return quad_keep_all();
+    return q;
+}
+
+// per-lane direction products for the quadric pre-test
+struct DirQ {
+    float xx, yy, zz, xy, xz, yz, dd;
+};
+__device__ __forceinline__ DirQ dir_q(v3 d) {
+    DirQ r{d.x * d.x, d.y * d.y, d.z * d.z, d.x * d.y, d.x * d.z, d.y * d.z, 0.f};
+    r.dd = r.xx + r.yy + r.zz;
+    return r;
+}
+__device__ __forceinline__ float eval_quad(const float4& A, const float4& B, const DirQ& q) {
+    return A.x * q.xx + A.y * q.yy + A.z * q.zz + A.w * q.xy + B.x * q.xz + B.y * q.yz + B.z * q.dd;
+}
+
 // ------------------------------------------------------------ forward ----
 // Warp-independent: each warp owns 32 pixels (two rows of a 16-wide tile),
 // stages the tile's records 32 at a time in its own slice of shared memory
@@ -255,8 +329,9 @@ __device__ __forceinline__ bool cone_may_hit(const WarpCone& w, float4 r0, float
 constexpr int kWarpSlot = 32;
 
 // shared memory per warp: 4 record float4 + 1 colour float4 per slot, ids
+// per slot: 4 record float4, 1 colour float4, 2 quadric float4, the id
 __host__ __device__ constexpr size_t warp_stage_bytes() {
-    return size_t(kWarpSlot) * (5 * sizeof(float4) + sizeof(int32_t));
+    return size_t(kWarpSlot) * (7 * sizeof(float4) + sizeof(int32_t));
 }
 
 template <int CDIM, bool kDyn>
@@ -265,12 +340,14 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
     constexpr int CSZ = CDIM > 0 ? CDIM : 1;
     extern __shared__ float4 smem4[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    float4* s0 = smem4 + wid * (5 * kWarpSlot);
+    float4* s0 = smem4 + wid * (7 * kWarpSlot);
     float4* s1 = s0 + kWarpSlot;
     float4* s2 = s1 + kWarpSlot;
     float4* s3 = s2 + kWarpSlot;
     float4* sc = s3 + kWarpSlot;
-    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 5 * kWarpSlot) + wid * kWarpSlot;
+    float4* sqa = sc + kWarpSlot;
+    float4* sqb = sqa + kWarpSlot;
+    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 7 * kWarpSlot) + wid * kWarpSlot;
 
     const TileCtx c = tile_ctx(a);
     const v3 o = c.inside ? ld3(a.ray_o + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
@@ -286,6 +363,10 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
     // static scene and one ray origin for the warp: M (o - mu) once per Gaussian
     const bool uni = !kDyn && __all_sync(0xffffffffu, same);
     const WarpCone cone = warp_cone(c.inside, o, d, rt);
+    // the quadric pre-test needs one origin (and one time offset) per warp
+    const float rt0 = __shfl_sync(0xffffffffu, rt, 0);
+    const bool qcull = __all_sync(0xffffffffu, same && (!kDyn || !c.inside || rt == rt0));
+    const DirQ dq = dir_q(d);
 
     bool done = !c.inside;
     float T = 1.0f, depth = 0.0f;
@@ -305,6 +386,14 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
             float4 r0 = r[0], r1 = r[1], r2 = r[2];
             const float4 r3 = r[3];
             keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
+            Quad qd = quad_keep_all();
+            if (qcull && keep) {
+                v3 mu = mk3(r0.w, r1.w, r2.w);
+                if (kDyn) mu = mu + rt0 * mk3(r3.y, r3.z, r3.w);
+                qd = make_quad(r0, r1, r2, r3.x, mu, o0);
+            }
+            sqa[lane] = qd.a;
+            sqb[lane] = qd.b;
             if (uni) {
                 const v3 gro = mrows(r0, r1, r2, o0 - mk3(r0.w, r1.w, r2.w));
                 r0.w = gro.x; r1.w = gro.y; r2.w = gro.z;
@@ -324,6 +413,16 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
         }
         unsigned live = __ballot_sync(0xffffffffu, keep);
         __syncwarp();
+        if (qcull) {
+            unsigned m = live;
+            live = 0u;
+            while (m) {
+                const int t = __ffs(m) - 1;
+                m &= m - 1;
+                const float q = eval_quad(sqa[t], sqb[t], dq);
+                if (__any_sync(0xffffffffu, !done && q >= 0.0f)) live |= 1u << t;
+            }
+        }
         while (live && !done) {
             const int t = __ffs(live) - 1;
             live &= live - 1;
@@ -459,12 +558,14 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     constexpr int NA = AC::N;
     extern __shared__ float4 smem4[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    float4* s0 = smem4 + wid * (5 * kWarpSlot);
+    float4* s0 = smem4 + wid * (7 * kWarpSlot);
     float4* s1 = s0 + kWarpSlot;
     float4* s2 = s1 + kWarpSlot;
     float4* s3 = s2 + kWarpSlot;
     float4* sc = s3 + kWarpSlot;
-    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 5 * kWarpSlot) + wid * kWarpSlot;
+    float4* sqa = sc + kWarpSlot;
+    float4* sqb = sqa + kWarpSlot;
+    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 7 * kWarpSlot) + wid * kWarpSlot;
 
     const TileCtx c = tile_ctx(a);
     const bool inside = c.inside;
@@ -491,6 +592,14 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     float vtime = 0.f, dbuf = 0.f;
 
     const WarpCone cone = warp_cone(inside, o, d, rt);
+    const v3 o0 = mk3(__shfl_sync(0xffffffffu, o.x, 0), __shfl_sync(0xffffffffu, o.y, 0),
+                      __shfl_sync(0xffffffffu, o.z, 0));
+    const float rt0 = __shfl_sync(0xffffffffu, rt, 0);
+    const bool qcull = __all_sync(0xffffffffu, !inside || (__float_as_uint(o.x) == __float_as_uint(o0.x) &&
+                                                          __float_as_uint(o.y) == __float_as_uint(o0.y) &&
+                                                          __float_as_uint(o.z) == __float_as_uint(o0.z) &&
+                                                          (!kDyn || rt == rt0)));
+    const DirQ dq = dir_q(d);
     // this warp's last contributor bounds where it starts
     int32_t wmax = bin_final;
 #pragma unroll
@@ -503,6 +612,14 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
             const float4* r = a.rec + int64_t(kRecF4) * g;
             const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
             keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
+            Quad qd = quad_keep_all();
+            if (qcull && keep) {
+                v3 mu = mk3(r0.w, r1.w, r2.w);
+                if (kDyn) mu = mu + rt0 * mk3(r3.y, r3.z, r3.w);
+                qd = make_quad(r0, r1, r2, r3.x, mu, o0);
+            }
+            sqa[lane] = qd.a;
+            sqb[lane] = qd.b;
             s0[lane] = r0; s1[lane] = r1; s2[lane] = r2; s3[lane] = r3;
             if constexpr (kStageColor) {
                 float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -517,6 +634,16 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
         }
         unsigned live = __ballot_sync(0xffffffffu, keep);
         __syncwarp();
+        if (qcull) {
+            unsigned m = live;
+            live = 0u;
+            while (m) {
+                const int t = __ffs(m) - 1;
+                m &= m - 1;
+                const float q = eval_quad(sqa[t], sqb[t], dq);
+                if (__any_sync(0xffffffffu, inside && (top - t <= bin_final) && q >= 0.0f)) live |= 1u << t;
+            }
+        }
         while (live) {
             const int t = __ffs(live) - 1;
             live &= live - 1;
