@@ -1,7 +1,7 @@
 """Loads the in-tree native extension (``_C*.so`` + ``libxsimgs_b200.so``).
 
-There is no fallback: if the extension was not built (``python -m
-xsimgs_b200.build``) importing the package raises ImportError naming the
+There is no fallback: if the extension was not built (``python
+xsimgs_b200/build.py``) importing the package raises ImportError naming the
 missing file, so no CPU or eager-PyTorch path can silently stand in for the
 CUDA kernels.
 """
@@ -27,7 +27,7 @@ def _load_ext():
     if not hits or not os.path.exists(lib_path()):
         raise ImportError(
             "xsimgs_b200 native extension not built: expected _C*.so and "
-            f"libxsimgs_b200.so in {_PKG}; run `python -m xsimgs_b200.build`")
+            f"libxsimgs_b200.so in {_PKG}; run `python xsimgs_b200/build.py`")
     name = "xsimgs_b200._C"
     if name in sys.modules:
         return sys.modules[name]

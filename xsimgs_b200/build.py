@@ -8,7 +8,8 @@
    $ORIGIN rpath so both load from this directory.
 
 Objects are cached under xsimgs_b200/_build/ and rebuilt when a source or
-header is newer.  `python -m xsimgs_b200.build` builds everything.
+header is newer.  `python xsimgs_b200/build.py` builds everything (run it as
+a script: importing the package needs the extension already built).
 """
 from __future__ import annotations
 
