@@ -38,8 +38,13 @@ def assert_images_close(gpu, ref, near, atol=IMG_ATOL, what="image"):
     assert worst <= atol, f"{what}: max-abs {worst} > {atol} at {np.unravel_index(diff.argmax(), diff.shape)}"
 
 
-def assert_grads_close(gpu, ref, what="grad", rtol=GRAD_RTOL):
+def assert_grads_close(gpu, ref, what="grad", rtol=GRAD_RTOL, pixel_mask=None):
+    """Per-element and relative-L2 check; `pixel_mask` [H, W] (True = compare)
+    drops the threshold-ambiguous pixels from per-pixel gradient images."""
     gpu, ref = to_np(gpu).astype(np.float64), to_np(ref).astype(np.float64)
+    if pixel_mask is not None:
+        keep = to_np(pixel_mask).astype(bool)
+        gpu, ref = gpu[keep], ref[keep]
     assert gpu.shape == ref.shape, f"{what}: shape {gpu.shape} vs {ref.shape}"
     scale = np.abs(ref).max() if ref.size else 0.0
     err = np.abs(gpu - ref)

@@ -144,8 +144,10 @@ def test_rasterize_fwd_bwd_match_oracle(c1, cuda):
     assert_grads_close(v_scales, rg["v_scales"], "v_scales")
     assert_grads_close(v_opac, rg["v_opacities"], "v_opacities")
     assert_grads_close(v_colors, rg["v_colors"], "v_colors")
-    assert_grads_close(v_ro, rg["v_ray_o"], "v_ray_o")
-    assert_grads_close(v_rd, rg["v_ray_d"], "v_ray_d")
+    # per-pixel ray gradients: the forward's threshold-ambiguous pixels are
+    # also ill-conditioned here (transmittance near the 1e-4 cut-off)
+    assert_grads_close(v_ro, rg["v_ray_o"], "v_ray_o", pixel_mask=~near)
+    assert_grads_close(v_rd, rg["v_ray_d"], "v_ray_d", pixel_mask=~near)
 
 
 @pytest.mark.parametrize("degree", [0, 1, 2, 3, 4])
@@ -225,4 +227,4 @@ def test_raster_anisotropic_and_near_camera(cuda, spread):
                          sc.opacities.numpy(), W, H, 16, 16, to_np(ro), to_np(rd), to_np(off), to_np(flat),
                          to_np(alpha), to_np(last), vr.numpy(), vd.numpy(), va.numpy())
     for got, key in zip(grads, ["v_means", "v_quats", "v_scales", "v_opacities", "v_colors", "v_ray_o", "v_ray_d"]):
-        assert_grads_close(got, rg[key], key)
+        assert_grads_close(got, rg[key], key, pixel_mask=~nearpx if key.startswith("v_ray") else None)

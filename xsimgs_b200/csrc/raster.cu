@@ -335,7 +335,7 @@ __host__ __device__ constexpr size_t warp_stage_bytes() {
 }
 
 template <int CDIM, bool kDyn>
-__global__ void __launch_bounds__(256) raster_fwd_kernel(RasterArgs a) {
+__global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
     constexpr bool kStageColor = CDIM > 0 && CDIM <= 4;
     constexpr int CSZ = CDIM > 0 ? CDIM : 1;
     extern __shared__ float4 smem4[];
