@@ -233,6 +233,26 @@ int xsg_sh_bwd(int degree, const float* origin, const float* positions, const fl
                float* d_positions, float* d_origin, void* workspace, size_t workspace_bytes,
                xsg_stream_t stream);
 
+/* Allocation-free spherical-harmonics backward.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory (a host
+ * runtime that only lends the library the buffers it owns, or code that must
+ * not call cudaMalloc).  Same arguments and results as xsg_sh_bwd without the
+ * workspace; its scratch (per-block partial sums of d_origin) is a fixed
+ * 768 KiB device array that each GPU loading the library keeps until exit.
+ *   - n may be at most xsg_sh_bwd_noalloc_max_gaussians() (2^23); larger n
+ *     returns XSG_ERR_INVALID_ARGUMENT.
+ *   - The first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls share the one array: calls that overlap on the GPU (other
+ *     streams, other threads) race and must be serialised by the caller.
+ *     Each call writes every partial it reads, so no clearing is needed.
+ *   - Nothing is allocated or freed. */
+int64_t xsg_sh_bwd_noalloc_max_gaussians(void);
+int xsg_sh_bwd_noalloc(int degree, const float* origin, const float* positions, const float* coeffs,
+                       const float* coeffs_dc, const uint32_t* mask, int layout_3kn, int64_t n, int dim,
+                       const float* d_out, float* d_coeffs, float* d_coeffs_dc, float* d_positions,
+                       float* d_origin, xsg_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

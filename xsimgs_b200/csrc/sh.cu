@@ -7,6 +7,9 @@
 // (the reference spends one thread per channel); the backward owns each
 // Gaussian's gradients outright, so it needs no atomics except the
 // per-block partial of d_origin, which a second pass sums deterministically.
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 
 namespace xsg {
@@ -406,6 +409,96 @@ int xsg_sh_bwd(int degree, const float* origin, const float* pos, const float* c
     if (rc2 != XSG_OK) return rc2;
     launch(sum_partials_kernel, 1, 1024, 0, st, part, nb, d_origin);
     return check_launch("spherical_harmonics_bwd");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------- allocation-free variant --
+// xsg_sh_bwd_noalloc: the same spherical-harmonics backward for callers that
+// cannot allocate device memory themselves (for example a host runtime that
+// hands the library only the tensors it owns, or a process that must not
+// call cudaMalloc on a hot path).  Its only scratch, the per-block partial
+// sums of d_origin, lives in the fixed device array below, which every GPU
+// that loads this library holds until the process exits.
+namespace xsg {
+
+constexpr int64_t kShNoAllocMaxGaussians = int64_t(1) << 23;  // 8,388,608
+constexpr int64_t kShNoAllocMaxBlocks = (kShNoAllocMaxGaussians + kShThreads - 1) / kShThreads;
+
+// 65,536 blocks x 3 floats = 768 KiB per device.
+static __device__ __align__(256) float g_sh_noalloc_partials[kShNoAllocMaxBlocks * 3];
+
+// Device address of the array, looked up once per device (host code may not
+// use the symbol itself as a pointer).
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[64] = {nullptr};
+
+static int sh_noalloc_scratch(float** out) {
+    int dev = -1;
+    XSG_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(XSG_ERR_UNSUPPORTED, "spherical_harmonics_bwd_noalloc: device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_sh_noalloc_partials);
+        if (e != cudaSuccess)
+            return set_error(XSG_ERR_CUDA, std::string("spherical_harmonics_bwd_noalloc: cudaGetSymbolAddress: ") +
+                                               cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return XSG_OK;
+}
+
+}  // namespace xsg
+
+extern "C" {
+
+int64_t xsg_sh_bwd_noalloc_max_gaussians(void) { return xsg::kShNoAllocMaxGaussians; }
+
+int xsg_sh_bwd_noalloc(int degree, const float* origin, const float* pos, const float* coeffs, const float* dc,
+                       const uint32_t* mask, int layout_3kn, int64_t n, int dim, const float* d_out,
+                       float* d_coeffs, float* d_dc, float* d_pos, float* d_origin, xsg_stream_t stream) {
+    int rc = sh_check(degree, n, dim, dc != nullptr);
+    if (rc != XSG_OK) return rc;
+    XSG_REQUIRE(d_origin, "spherical_harmonics_bwd_noalloc: null d_origin");
+    if (n > kShNoAllocMaxGaussians)
+        return set_error(XSG_ERR_INVALID_ARGUMENT,
+                         "spherical_harmonics_bwd_noalloc: " + std::to_string(n) + " Gaussians exceed the maximum of " +
+                             std::to_string(kShNoAllocMaxGaussians) + "; use xsg_sh_bwd with a workspace");
+    cudaStream_t st = as_cuda(stream);
+    if (n == 0) {
+        XSG_CUDA(cudaMemsetAsync(d_origin, 0, 3 * sizeof(float), st));
+        return XSG_OK;
+    }
+    XSG_REQUIRE(origin && pos && d_out && d_coeffs && d_pos && (!dc || d_dc),
+                "spherical_harmonics_bwd_noalloc: null argument");
+    float* part = nullptr;
+    rc = sh_noalloc_scratch(&part);
+    if (rc != XSG_OK) return rc;
+    // every block writes its own partial before the final sum reads it, so
+    // nothing left from an earlier call is read and nothing needs clearing
+    ShLayout L{n, dim, layout_3kn != 0, dc != nullptr};
+    const unsigned nb = blocks_for(n, kShThreads);
+    const size_t sm = layout_3kn ? 0 : sh_stage_bytes(dim);
+    int rc2 = XSG_OK;
+    auto go = [&](auto kernel) {
+        if (sm > 48 * 1024 && cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)) != cudaSuccess)
+            rc2 = set_error(XSG_ERR_UNSUPPORTED, "spherical_harmonics_bwd_noalloc: too many coefficient bands");
+        else
+            launch(kernel, nb, kShThreads, sm, st, origin, pos, coeffs, dc, mask, L, d_out, d_coeffs, d_dc, d_pos,
+                   part);
+    };
+    switch (degree) {
+        case 0: layout_3kn ? go(sh_bwd_kernel<0, true>) : go(sh_bwd_kernel<0, false>); break;
+        case 1: layout_3kn ? go(sh_bwd_kernel<1, true>) : go(sh_bwd_kernel<1, false>); break;
+        case 2: layout_3kn ? go(sh_bwd_kernel<2, true>) : go(sh_bwd_kernel<2, false>); break;
+        case 3: layout_3kn ? go(sh_bwd_kernel<3, true>) : go(sh_bwd_kernel<3, false>); break;
+        default: layout_3kn ? go(sh_bwd_kernel<4, true>) : go(sh_bwd_kernel<4, false>); break;
+    }
+    if (rc2 != XSG_OK) return rc2;
+    launch(sum_partials_kernel, 1, 1024, 0, st, part, nb, d_origin);
+    return check_launch("spherical_harmonics_bwd_noalloc");
 }
 
 }  // extern "C"
