@@ -322,7 +322,10 @@ def gpu_arm(args, world, rank, local):
         ach_f = fl_f / (fwd_avg * 1e-3) / 1e12
         roof = {"kernel": "rasterize_bwd (raster_bwd_kernel<3,false>)", "bound": "fp32",
                 "achieved": round(ach_b, 2), "peak": round(peak_flops / 1e12, 2), "unit": "TFLOP/s",
-                "frac": round(ach_b / (peak_flops / 1e12), 3), "traffic": None,
+                "frac": round(ach_b / (peak_flops / 1e12), 3),
+                "traffic": roofline.BWD_DRAM_BYTES_C2 if args.gaussians == N_C2 else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture of this kernel "
+                                  "on this workload (bytes per launch)",
                 "peak_source": "measured: FP32 FMA probe in this run (MEASURED_PEAKS.json has only HBM and bf16)",
                 "avg_launch_ms": round(bwd_avg, 4), "flops_per_launch": fl_b,
                 "pairs": {"evaluated_fwd": n_eval_f, "evaluated_bwd": n_eval_b, "contributing": n_contrib},

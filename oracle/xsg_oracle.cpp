@@ -852,11 +852,34 @@ static inline f3 safe_normalize(f3 v) {
     return l > 0.0f ? v * (1.0f / std::sqrt(l)) : v;
 }
 
+// How far apart two float32 evaluations of one pair's alpha may land,
+// relative (different summation order or fused multiply-adds, 2-ulp exp /
+// rsqrt).  gro = M (o - mu) sums terms of size |M_ij| |(o - mu)_j| and
+// cancels down to |gro|; gc = normalize(grd) x gro cancels again down to
+// |gc|; so gc moves by a few ulps of (terms + |gro|) and power = -|gc|^2 / 2
+// by |gc| |d gc|.  The factor 3 is about five times the largest difference
+// seen between this oracle and the CUDA kernels on the parity scenes.
+static inline float alpha_rel_error(const f3 M[3], f3 mu, f3 om, f3 gro, f3 gc, float power, bool moving) {
+    const float eps = 5.97e-8f;  // 2^-24
+    float terms = 0.f, mmax = 0.f;
+    for (int i = 0; i < 3; ++i) {
+        terms = std::fmax(terms, std::fabs(M[i].x * om.x) + std::fabs(M[i].y * om.y) + std::fabs(M[i].z * om.z));
+        mmax = std::fmax(mmax, std::fabs(M[i].x) + std::fabs(M[i].y) + std::fabs(M[i].z));
+    }
+    // a moving centre mu + t v may round differently (fused or not)
+    const float d_mu = moving ? mmax * std::fmax(std::fmax(std::fabs(mu.x), std::fabs(mu.y)), std::fabs(mu.z)) : 0.f;
+    const float d_gc = 3.f * eps * (terms + d_mu + std::sqrt(dot(gro, gro)));
+    return std::sqrt(dot(gc, gc)) * d_gc + 8.f * eps * (1.f + std::fabs(power)) + 1e-6f;
+}
+
 // Front-to-back 3D-evaluation compositing, eval3d_fwd.cu:34-166 (static) and
 // eval3d_dynamic_fwd.cu:38-173 (velocity, per-pixel time).  `near` (may be
-// null) returns, per pixel, 1 when an alpha test or the termination test was
-// within a relative 2e-5 of its threshold (the outcome may differ between
-// CPU and GPU rounding there).
+// null) returns, per pixel, 1 when a test whose outcome two float32
+// evaluations may decide differently was within the pair's alpha error
+// band of its threshold: the alpha >= 1/255 test, the termination test
+// T (1 - alpha) <= 1e-4 (with the accumulated error of T), or the backward's
+// opacity * vis <= 0.99 gate (eval3d_bwd.cu:190-205), which switches the
+// power-term gradient on or off.
 void xsgo_rasterize_fwd(const float* means, const float* vel, const float* quats,
                         const float* scales, const float* colors, int cdim, const float* opac,
                         int W, int H, int tsx, int tsy, const float* ray_o, const float* ray_d,
@@ -877,22 +900,30 @@ void xsgo_rasterize_fwd(const float* means, const float* vel, const float* quats
         float acc[600] = {0};
         int64_t cur = 0;
         bool amb = false;
+        float t_err = 1e-5f;  // relative error bound of T
         for (int64_t k = start; k < end; ++k) {
             const int32_t g = flatten[k];
             f3 M[3], R[3];
             gauss_M(quats + 4 * g, scales + 3 * g, M, R);
             f3 mu{means[3 * g], means[3 * g + 1], means[3 * g + 2]};
             if (vel) mu = mu + t_ray * f3{vel[3 * g], vel[3 * g + 1], vel[3 * g + 2]};
-            const f3 gro = mat_vec(M, o - mu);
+            const f3 om = o - mu;
+            const f3 gro = mat_vec(M, om);
             const f3 grd = mat_vec(M, d);
             const f3 gc = cross(safe_normalize(grd), gro);
             const float power = -0.5f * dot(gc, gc);
-            const float alpha = std::fmin(0.999f, opac[g] * std::exp(power));
-            if (std::fabs(alpha * 255.0f - 1.0f) < 2e-5f) amb = true;
+            const float a_raw = opac[g] * std::exp(power);
+            const float alpha = std::fmin(0.999f, a_raw);
+            if (near) {
+                const float band = alpha_rel_error(M, mu, om, gro, gc, power, vel != nullptr);
+                if (std::fabs(a_raw * 255.0f - 1.0f) < band) amb = true;
+                if (a_raw >= 1.f / 255.f && std::fabs(a_raw / 0.99f - 1.0f) < band) amb = true;
+                if (alpha >= 1.f / 255.f) t_err += band * alpha / std::fmax(1.0f - alpha, 1e-3f);
+            }
             if (alpha < 1.f / 255.f) continue;
             const float hit_t = -dot(gro, grd) / dot(grd, grd);
             const float nT = T * (1.0f - alpha);
-            if (std::fabs(nT * 1e4f - 1.0f) < 2e-5f) amb = true;
+            if (std::fabs(nT * 1e4f - 1.0f) < t_err) amb = true;
             if (nT <= 1e-4f) break;
             const float vis = alpha * T;
             depth += vis * hit_t;

@@ -40,3 +40,11 @@ def fwd_flops(n_eval: int, n_contrib: int, cdim: int) -> float:
 
 def bwd_flops(n_eval_bwd: int, n_contrib: int, cdim: int) -> float:
     return float(BWD_EVAL * n_eval_bwd + bwd_contrib(cdim) * n_contrib)
+
+
+# DRAM bytes per launch of the compositing backward on the C2 view (1M
+# Gaussians, 1920x1080, 16x16 tiles), dram__bytes_read.sum +
+# dram__bytes_write.sum from one capture:
+#   ncu --set full --clock-control none -k regex:raster_bwd_kernel -s 1 -c 1 \
+#       python bench.py --steps 2 --warmup 1 --no-cpu-baseline
+BWD_DRAM_BYTES_C2 = 234.43e6 + 63.23e6
