@@ -253,6 +253,72 @@ int xsg_sh_bwd_noalloc(int degree, const float* origin, const float* positions, 
                        const float* d_out, float* d_coeffs, float* d_coeffs_dc, float* d_positions,
                        float* d_origin, xsg_stream_t stream);
 
+/* ------------------------------------------------------------- SMPL ---- *
+ * 24-joint SMPL kinematic chain (parents as csrc/nodes/smpl_local_to_global
+ * .cu:42-46).  Quaternions (w, x, y, z), 16-byte aligned arrays.  Bodies are
+ * addressed by uint32 ids into the N "object" arrays; ids >= n_objects are
+ * skipped (their outputs are left untouched). */
+
+/* Replaces smpl_local_to_global_fwd (csrc/nodes/smpl_local_to_global.cu:91-122).
+ * For b < batch and obj = local_q_ids[b]: global transform of each joint
+ * (local transforms std(local_q[obj, j]) with translations joints[obj, j] -
+ * joints[obj, parent], composed root to leaf, translated by -R J_j, then
+ * composed with (a0_inv_q, a0_inv_t)[obj, j]) -> out_q [batch, 24, 4],
+ * out_t [batch, 24, 3].  local_q, joints, a0_inv_*: [n_objects, 24, .]. */
+int xsg_smpl_local_to_global_fwd(const uint32_t* local_q_ids, int64_t batch, const float* local_q,
+                                 const float* joints, const float* a0_inv_q, const float* a0_inv_t,
+                                 int64_t n_objects, float* out_q, float* out_t, xsg_stream_t stream);
+
+/* Replaces smpl_local_to_global_bwd (csrc/nodes/smpl_local_to_global.cu:282-325).
+ * Gradients w.r.t. local_q (through std()) and a0_inv_q / a0_inv_t, written
+ * at the rows of the objects named in local_q_ids (callers zero the rest);
+ * the local translations (joints) get none, as in the reference.  The
+ * forward outputs the reference also passes are not needed: the chain is
+ * recomputed. */
+int xsg_smpl_local_to_global_bwd(const uint32_t* local_q_ids, int64_t batch, const float* local_q,
+                                 const float* joints, const float* a0_inv_q, const float* a0_inv_t,
+                                 int64_t n_objects, const float* grad_out_q, const float* grad_out_t,
+                                 float* d_local_q, float* d_a0_inv_q, float* d_a0_inv_t, xsg_stream_t stream);
+
+/* Replaces smpl_lbs_skinning (csrc/nodes/smpl_lbs_skinning.cu:94-134).  For
+ * b < n_valid, obj = valid_ids[b], v < n_vertices: W = sum_j weights[obj, j,
+ * v] [R(global_q[b, j]) | global_t[b, j]]; written at row r = global_offset +
+ * obj * n_vertices + v of the container: out_positions[r] = W [x; 1] +
+ * instance_t[instance_ids[obj]], out_rotations[r] = std(from_matrix(W)) (x)
+ * quats[obj, v], out_velocities[r] = instance_v[instance_ids[obj]] (if given),
+ * out_mask[r] = 1 (if given).  vertices [N, V, 3], quats [N, V, 4], weights
+ * [N, 24, V]; global_offset + N * V <= container_size. */
+int xsg_smpl_lbs_skinning_fwd(const uint32_t* valid_ids, int64_t n_valid, const float* global_q,
+                              const float* global_t, const float* vertices, const float* quats,
+                              const float* weights, int64_t n_objects, int64_t n_vertices,
+                              const uint32_t* instance_ids, const float* instance_t, const float* instance_v,
+                              int64_t n_instances, int64_t global_offset, int64_t container_size,
+                              float* out_positions, float* out_rotations, float* out_velocities,
+                              uint8_t* out_mask, xsg_stream_t stream);
+
+/* Replaces smpl_lbs_skinning_bwd (csrc/nodes/smpl_lbs_skinning.cu:271-341).
+ * d_global_q / d_global_t [n_valid, 24, .] and d_instance_t / d_instance_v
+ * [n_instances, 3] are ACCUMULATED (zero them first); d_vertices, d_quats,
+ * d_weights are written at the valid objects' rows.  grad_velocities and
+ * d_instance_v may be null (no velocity gradient). */
+int xsg_smpl_lbs_skinning_bwd(const uint32_t* valid_ids, int64_t n_valid, const uint32_t* instance_ids,
+                              const float* global_q, const float* global_t, const float* vertices,
+                              const float* quats, const float* weights, int64_t n_objects, int64_t n_vertices,
+                              int64_t n_instances, int64_t global_offset, int64_t container_size,
+                              const float* grad_positions, const float* grad_rotations,
+                              const float* grad_velocities, float* d_global_q, float* d_global_t,
+                              float* d_vertices, float* d_quats, float* d_weights, float* d_instance_v,
+                              float* d_instance_t, xsg_stream_t stream);
+
+/* Replaces smpl_ids_compaction (csrc/nodes/smpl.cu:52-86): the indices i <
+ * n, ascending, with instance_mask[instance_ids[i]] != 0 (ids >=
+ * n_instances count as masked out) -> out_ids [n], their number in *count
+ * (device) and *n_out_host.  Synchronises `stream` once for the count; any
+ * n (the reference's kernel stops at 1024). */
+int xsg_smpl_ids_compaction(const uint32_t* instance_ids, int64_t n, const uint8_t* instance_mask,
+                            int64_t n_instances, uint32_t* out_ids, int64_t* count, int64_t* n_out_host,
+                            xsg_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,6 +1,7 @@
 """Build recipe for the CPU oracle (test infrastructure, not a product path).
 
-Compiles oracle/xsg_oracle.cpp with g++ into oracle/_build/libxsg_oracle.so.
+Compiles oracle/xsg_oracle.cpp (render path) and oracle/xsg_oracle_smpl.cpp
+(SMPL skinning) with g++ into oracle/_build/libxsg_oracle.so.
 -ffp-contract=off and no -march flag keep every float operation rounded as
 written, so the oracle is the plain scalar restatement of the reference's
 arithmetic.  OpenMP parallelises over pixels/Gaussians for the timed CPU
@@ -11,7 +12,7 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-SRC = os.path.join(HERE, "xsg_oracle.cpp")
+SRCS = [os.path.join(HERE, "xsg_oracle.cpp"), os.path.join(HERE, "xsg_oracle_smpl.cpp")]
 OUT_DIR = os.path.join(HERE, "_build")
 OUT = os.path.join(OUT_DIR, "libxsg_oracle.so")
 
@@ -19,10 +20,10 @@ OUT = os.path.join(OUT_DIR, "libxsg_oracle.so")
 def build(force: bool = False) -> str:
     os.makedirs(OUT_DIR, exist_ok=True)
     if (not force and os.path.exists(OUT)
-            and os.path.getmtime(OUT) >= os.path.getmtime(SRC)):
+            and os.path.getmtime(OUT) >= max(os.path.getmtime(s) for s in SRCS)):
         return OUT
     cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-fopenmp",
-           "-ffp-contract=off", "-fno-fast-math", SRC, "-o", OUT + ".tmp"]
+           "-ffp-contract=off", "-fno-fast-math", *SRCS, "-o", OUT + ".tmp"]
     subprocess.run(cmd, check=True)
     os.replace(OUT + ".tmp", OUT)
     return OUT

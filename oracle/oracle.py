@@ -27,6 +27,7 @@ def lib():
         _lib.xsgo_isect_regular.restype = C.c_int64
         _lib.xsgo_isect_spherical.restype = C.c_int64
         _lib.xsgo_num_threads.restype = C.c_int
+        _lib.xsgo_smpl_ids_compaction.restype = C.c_int64
     return _lib
 
 
@@ -226,3 +227,68 @@ def sh_bwd(degree, origin, pos, coeffs, d_out, dc=None, mask=None, layout_3kn=Fa
     lib().xsgo_sh_bwd(C.c_int(degree), _p(origin), _p(pos), _p(coeffs), _p(dc), _p(mask), C.c_int(int(layout_3kn)),
                       C.c_int64(n), C.c_int(dim), _p(d_out), _p(d_coeffs), _p(d_dc), _p(d_pos), _p(d_origin))
     return d_coeffs, d_dc, d_pos, d_origin
+
+
+# ------------------------------------------------------------------ SMPL --
+def _u32(a):
+    return np.ascontiguousarray(a, dtype=np.uint32)
+
+
+def smpl_local_to_global_fwd(ids, local_q, joints, a0q, a0t):
+    ids, local_q, joints, a0q, a0t = _u32(ids), _f32(local_q), _f32(joints), _f32(a0q), _f32(a0t)
+    b = ids.shape[0]
+    out_q = np.zeros((b, 24, 4), np.float32)
+    out_t = np.zeros((b, 24, 3), np.float32)
+    lib().xsgo_smpl_local_to_global_fwd(C.c_int64(b), _p(ids), _p(local_q), _p(joints), _p(a0q), _p(a0t),
+                                        _p(out_q), _p(out_t))
+    return out_q, out_t
+
+
+def smpl_local_to_global_bwd(ids, local_q, joints, a0q, a0t, out_q, out_t, gq, gt):
+    ids, local_q, joints, a0q, a0t = _u32(ids), _f32(local_q), _f32(joints), _f32(a0q), _f32(a0t)
+    out_q, out_t, gq, gt = _f32(out_q), _f32(out_t), _f32(gq), _f32(gt)
+    d_local_q, d_a0q, d_a0t = np.zeros_like(local_q), np.zeros_like(a0q), np.zeros_like(a0t)
+    lib().xsgo_smpl_local_to_global_bwd(C.c_int64(ids.shape[0]), _p(ids), _p(local_q), _p(joints), _p(a0q),
+                                        _p(a0t), _p(out_q), _p(out_t), _p(gq), _p(gt), _p(d_local_q), _p(d_a0q),
+                                        _p(d_a0t))
+    return d_local_q, d_a0q, d_a0t
+
+
+def smpl_lbs_fwd(valid_ids, gq, gt, vertices, quats, weights, inst_ids, inst_t, inst_v, global_offset,
+                 container_size, with_vel=True, with_mask=True):
+    valid_ids, inst_ids = _u32(valid_ids), _u32(inst_ids)
+    gq, gt, vertices, quats, weights, inst_t, inst_v = (_f32(a) for a in (gq, gt, vertices, quats, weights, inst_t,
+                                                                         inst_v))
+    V = vertices.shape[1]
+    pos = np.zeros((container_size, 3), np.float32)
+    rot = np.zeros((container_size, 4), np.float32)
+    vel = np.zeros((container_size, 3), np.float32) if with_vel else None
+    mask = np.zeros(container_size, np.uint8) if with_mask else None
+    lib().xsgo_smpl_lbs_fwd(C.c_int64(valid_ids.shape[0]), C.c_int64(V), _p(valid_ids), _p(gq), _p(gt),
+                            _p(vertices), _p(quats), _p(weights), _p(inst_ids), _p(inst_t), _p(inst_v),
+                            C.c_int64(global_offset), _p(pos), _p(rot), _p(vel), _p(mask))
+    return pos, rot, vel, mask
+
+
+def smpl_lbs_bwd(valid_ids, inst_ids, gq, gt, vertices, quats, weights, global_offset, n_instances, g_pos, g_rot,
+                 g_vel=None):
+    valid_ids, inst_ids = _u32(valid_ids), _u32(inst_ids)
+    gq, gt, vertices, quats, weights = (_f32(a) for a in (gq, gt, vertices, quats, weights))
+    g_pos, g_rot, g_vel = _f32(g_pos), _f32(g_rot), _f32(g_vel)
+    V = vertices.shape[1]
+    d = dict(global_q=np.zeros_like(gq), global_t=np.zeros_like(gt), vertices=np.zeros_like(vertices),
+             quats=np.zeros_like(quats), weights=np.zeros_like(weights),
+             instance_v=np.zeros((n_instances, 3), np.float32), instance_t=np.zeros((n_instances, 3), np.float32))
+    lib().xsgo_smpl_lbs_bwd(C.c_int64(valid_ids.shape[0]), C.c_int64(V), _p(valid_ids), _p(inst_ids), _p(gq),
+                            _p(gt), _p(vertices), _p(quats), _p(weights), C.c_int64(global_offset), _p(g_pos),
+                            _p(g_rot), _p(g_vel), _p(d["global_q"]), _p(d["global_t"]), _p(d["vertices"]),
+                            _p(d["quats"]), _p(d["weights"]), _p(d["instance_v"]), _p(d["instance_t"]))
+    return d
+
+
+def smpl_ids_compaction(instance_ids, instance_mask):
+    ids = _u32(instance_ids)
+    mask = np.ascontiguousarray(instance_mask, dtype=np.uint8)
+    out = np.zeros(ids.shape[0], np.uint32)
+    c = lib().xsgo_smpl_ids_compaction(_p(ids), C.c_int64(ids.shape[0]), _p(mask), _p(out))
+    return out[:c]

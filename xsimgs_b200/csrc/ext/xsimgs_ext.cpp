@@ -467,6 +467,112 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> sh_bwd(int64_t degree, const Tensor& 
     return {d_coeffs, d_dc, d_pos, d_origin};
 }
 
+// ----------------------------------------------------------------- SMPL --
+// csrc/nodes/smpl_local_to_global.cu:91-337, smpl_lbs_skinning.cu:94-352,
+// smpl.cu:52-95.  Id tensors are 32-bit (int32 or uint32), read as uint32.
+const uint32_t* u32ptr(const Tensor& t, const char* name) {
+    TORCH_CHECK(t.element_size() == 4 && !t.is_floating_point(), name, " must be a 32-bit integer tensor");
+    return reinterpret_cast<const uint32_t*>(t.data_ptr());
+}
+
+std::tuple<Tensor, Tensor> smpl_local_to_global_fwd(const Tensor& ids, const Tensor& local_q, const Tensor& joints,
+                                                    const Tensor& a0q, const Tensor& a0t) {
+    for (auto* t : {&ids, &local_q, &joints, &a0q, &a0t}) check_tensor(*t, "smpl_local_to_global_fwd input", local_q);
+    for (auto* t : {&local_q, &joints, &a0q, &a0t}) require_f32(*t, "smpl_local_to_global_fwd input");
+    TORCH_CHECK(local_q.dim() == 3 && local_q.size(1) == 24 && local_q.size(2) == 4, "local_q must be [N, 24, 4]");
+    c10::cuda::CUDAGuard g(local_q.device());
+    const int64_t b = ids.numel();
+    Tensor out_q = at::empty({b, 24, 4}, local_q.options());
+    Tensor out_t = at::empty({b, 24, 3}, local_q.options());
+    check(xsg_smpl_local_to_global_fwd(u32ptr(ids, "local_q_ids"), b, fptr(local_q), fptr(joints), fptr(a0q),
+                                       fptr(a0t), local_q.size(0), fptr_mut(out_q), fptr_mut(out_t), stream()));
+    return {out_q, out_t};
+}
+
+std::tuple<Tensor, Tensor, Tensor> smpl_local_to_global_bwd(const Tensor& ids, const Tensor& local_q,
+                                                            const Tensor& joints, const Tensor& a0q,
+                                                            const Tensor& a0t, const Tensor& out_q,
+                                                            const Tensor& out_t, const Tensor& gq, const Tensor& gt) {
+    for (auto* t : {&ids, &local_q, &joints, &a0q, &a0t, &gq, &gt})
+        check_tensor(*t, "smpl_local_to_global_bwd input", local_q);
+    TORCH_CHECK(gq.numel() == ids.numel() * 96 && gt.numel() == ids.numel() * 72,
+                "grad_output_q / grad_output_t must be [B, 24, 4] / [B, 24, 3]");
+    c10::cuda::CUDAGuard g(local_q.device());
+    Tensor d_local_q = at::zeros_like(local_q);
+    Tensor d_a0q = at::zeros_like(a0q);
+    Tensor d_a0t = at::zeros_like(a0t);
+    check(xsg_smpl_local_to_global_bwd(u32ptr(ids, "local_q_ids"), ids.numel(), fptr(local_q), fptr(joints),
+                                       fptr(a0q), fptr(a0t), local_q.size(0), fptr(gq), fptr(gt),
+                                       fptr_mut(d_local_q), fptr_mut(d_a0q), fptr_mut(d_a0t), stream()));
+    return {d_local_q, d_a0q, d_a0t};
+}
+
+void smpl_lbs_skinning_fwd(const Tensor& valid_ids, const Tensor& global_q, const Tensor& global_t,
+                           const Tensor& vertices, const Tensor& quats, const Tensor& weights,
+                           const Tensor& instance_ids, const Tensor& instance_t, const Tensor& instance_v,
+                           int64_t global_offset, const Tensor& out_positions, const Tensor& out_rotations,
+                           const OptT& out_velocities, const OptT& out_mask) {
+    for (auto* t : {&valid_ids, &global_q, &global_t, &vertices, &quats, &weights, &instance_ids, &instance_t,
+                    &instance_v, &out_positions, &out_rotations})
+        check_tensor(*t, "smpl_lbs_skinning input", vertices);
+    TORCH_CHECK(vertices.dim() == 3 && vertices.size(2) == 3, "vertices must be [N, V, 3]");
+    TORCH_CHECK(weights.dim() == 3 && weights.size(1) == 24 && weights.size(2) == vertices.size(1),
+                "weights must be [N, 24, V]");
+    if (has(out_velocities)) check_tensor(*out_velocities, "out_velocities", vertices);
+    if (has(out_mask)) {
+        check_tensor(*out_mask, "out_mask", vertices);
+        TORCH_CHECK(out_mask->element_size() == 1, "out_mask must be a bool or uint8 tensor");
+    }
+    c10::cuda::CUDAGuard g(vertices.device());
+    check(xsg_smpl_lbs_skinning_fwd(
+        u32ptr(valid_ids, "valid_ids"), valid_ids.numel(), fptr(global_q), fptr(global_t), fptr(vertices),
+        fptr(quats), fptr(weights), vertices.size(0), vertices.size(1), u32ptr(instance_ids, "instance_ids"),
+        fptr(instance_t), fptr(instance_v), instance_t.size(0), global_offset, out_positions.size(0),
+        fptr_mut(out_positions), fptr_mut(out_rotations), has(out_velocities) ? fptr_mut(*out_velocities) : nullptr,
+        has(out_mask) ? reinterpret_cast<uint8_t*>(out_mask->data_ptr()) : nullptr, stream()));
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> smpl_lbs_skinning_bwd(
+    const Tensor& valid_ids, const Tensor& instance_ids, const Tensor& global_q, const Tensor& global_t,
+    const Tensor& vertices, const Tensor& quats, const Tensor& weights, int64_t global_offset, int64_t num_instances,
+    const Tensor& grad_pos, const Tensor& grad_rot, const OptT& grad_vel) {
+    for (auto* t : {&valid_ids, &instance_ids, &global_q, &global_t, &vertices, &quats, &weights, &grad_pos,
+                    &grad_rot})
+        check_tensor(*t, "smpl_lbs_skinning_bwd input", vertices);
+    if (has(grad_vel)) check_tensor(*grad_vel, "grad_out_velocities", vertices);
+    c10::cuda::CUDAGuard g(vertices.device());
+    Tensor d_global_q = at::zeros_like(global_q);
+    Tensor d_global_t = at::zeros_like(global_t);
+    Tensor d_vertices = at::zeros_like(vertices);
+    Tensor d_quats = at::zeros_like(quats);
+    Tensor d_weights = at::zeros_like(weights);
+    Tensor d_instance_v = at::zeros({num_instances, 3}, global_q.options());
+    Tensor d_instance_t = at::zeros({num_instances, 3}, global_q.options());
+    check(xsg_smpl_lbs_skinning_bwd(
+        u32ptr(valid_ids, "valid_ids"), valid_ids.numel(), u32ptr(instance_ids, "instance_ids"), fptr(global_q),
+        fptr(global_t), fptr(vertices), fptr(quats), fptr(weights), vertices.size(0), vertices.size(1),
+        num_instances, global_offset, grad_pos.size(0), fptr(grad_pos), fptr(grad_rot),
+        has(grad_vel) ? fptr(*grad_vel) : nullptr, fptr_mut(d_global_q), fptr_mut(d_global_t), fptr_mut(d_vertices),
+        fptr_mut(d_quats), fptr_mut(d_weights), has(grad_vel) ? fptr_mut(d_instance_v) : nullptr,
+        fptr_mut(d_instance_t), stream()));
+    return {d_global_q, d_global_t, d_vertices, d_quats, d_weights, d_instance_v, d_instance_t};
+}
+
+Tensor smpl_ids_compaction(const Tensor& instance_ids, const Tensor& instance_mask) {
+    check_tensor(instance_ids, "instance_ids", instance_ids);
+    check_tensor(instance_mask, "instance_mask", instance_ids);
+    TORCH_CHECK(instance_mask.element_size() == 1, "instance_mask must be a bool or uint8 tensor");
+    c10::cuda::CUDAGuard g(instance_ids.device());
+    Tensor out = at::empty({instance_ids.numel()}, instance_ids.options());
+    Tensor count = at::empty({1}, instance_ids.options().dtype(at::kLong));
+    int64_t n_out = 0;
+    check(xsg_smpl_ids_compaction(u32ptr(instance_ids, "instance_ids"), instance_ids.numel(),
+                                  reinterpret_cast<const uint8_t*>(instance_mask.data_ptr()), instance_mask.numel(),
+                                  reinterpret_cast<uint32_t*>(out.data_ptr()), count.data_ptr<int64_t>(), &n_out,
+                                  stream()));
+    return out.slice(0, 0, n_out);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -570,4 +676,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("spherical_harmonics_fused_bwd", &sh_bwd, py::arg("degree_to_use"), py::arg("origin"),
           py::arg("positions"), py::arg("coeffs"), py::arg("mask"), py::arg("layout_3kn"), py::arg("d_output"),
           py::arg("coeffs_dc") = py::none());
+    m.def("smpl_local_to_global_fwd", &smpl_local_to_global_fwd, py::arg("local_q_ids"), py::arg("local_q"),
+          py::arg("joints"), py::arg("a0_inv_q"), py::arg("a0_inv_t"));
+    m.def("smpl_local_to_global_bwd", &smpl_local_to_global_bwd, py::arg("local_q_ids"), py::arg("local_q"),
+          py::arg("joints"), py::arg("a0_inv_q"), py::arg("a0_inv_t"), py::arg("output_q"), py::arg("output_t"),
+          py::arg("grad_output_q"), py::arg("grad_output_t"));
+    m.def("smpl_lbs_skinning", &smpl_lbs_skinning_fwd, py::arg("valid_ids"), py::arg("global_q"),
+          py::arg("global_t"), py::arg("vertices"), py::arg("quats"), py::arg("weights"), py::arg("instance_ids"),
+          py::arg("instance_t"), py::arg("instance_v"), py::arg("global_offset"), py::arg("out_positions"),
+          py::arg("out_rotations"), py::arg("out_velocities"), py::arg("out_mask"));
+    m.def("smpl_lbs_skinning_bwd", &smpl_lbs_skinning_bwd, py::arg("valid_ids"), py::arg("instance_ids"),
+          py::arg("global_q"), py::arg("global_t"), py::arg("vertices"), py::arg("quats"), py::arg("weights"),
+          py::arg("global_offset"), py::arg("num_instances"), py::arg("grad_out_vertices"),
+          py::arg("grad_out_quats"), py::arg("grad_out_velocities") = py::none());
+    m.def("smpl_ids_compaction", &smpl_ids_compaction, py::arg("instance_ids"), py::arg("instance_mask"));
 }

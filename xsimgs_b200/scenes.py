@@ -178,3 +178,82 @@ def upstream_grads(height: int, width: int, channels: int, seed: int = 1):
     g = torch.Generator().manual_seed(seed)
     return (torch.randn(height, width, channels, generator=g), torch.randn(height, width, generator=g),
             torch.randn(height, width, generator=g))
+
+
+# ------------------------------------------------------------------ C5 --
+SMPL_PARENTS = (-1, 0, 0, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 9, 9, 12, 13, 14, 16, 17, 18, 19, 20, 21)
+
+
+def axis_angle_to_quat(aa: torch.Tensor) -> torch.Tensor:
+    """Rotation vectors [..., 3] -> unit quaternions [..., 4] (w, x, y, z)."""
+    theta = aa.norm(dim=-1, keepdim=True)
+    half = 0.5 * theta
+    k = torch.where(theta > 1e-8, torch.sin(half) / theta.clamp_min(1e-8), 0.5 - theta ** 2 / 48.0)
+    return torch.cat([torch.cos(half), aa * k], dim=-1)
+
+
+def c5_smpl(n_bodies: int = 8, gauss_per_body: int = 20_000, template_verts: int = 6890, seed: int = 0,
+            pose_sigma: float = 0.3):
+    """Synthetic SMPL-style bodies (no model assets are needed): a template
+    of `template_verts` vertices ~ N(0, 0.3), 24 joints at the means of the
+    vertices nearest to 24 seed vertices, per-vertex LBS weights
+    Dirichlet(0.5) over the 4 nearest joints, axis-angle pose ~ N(0,
+    pose_sigma) per joint, a0_inv = identity.  Each body carries
+    `gauss_per_body` Gaussians bound to random template vertices (rest
+    position = vertex + N(0, 0.01), inheriting its weights), so V =
+    gauss_per_body.  Bodies stand on the ground 6..14 m in front of the
+    origin (+X), one instance per body.
+
+    Returns a dict of CPU tensors with the reference's layouts (quaternions
+    w, x, y, z; ids uint32 stored as int32)."""
+    g = torch.Generator().manual_seed(seed)
+    tv = torch.randn(template_verts, 3, generator=g) * 0.3
+    seeds = tv[torch.randperm(template_verts, generator=g)[:24]]
+    d = torch.cdist(seeds, tv)                                   # [24, T]
+    near = d.topk(64, dim=1, largest=False).indices               # [24, 64]
+    joints0 = tv[near].mean(dim=1)                                # [24, 3]
+    dj = torch.cdist(tv, joints0)                                 # [T, 24]
+    nn4 = dj.topk(4, dim=1, largest=False).indices                # [T, 4]
+    conc = torch.full((template_verts, 4), 0.5)
+    w4 = _dirichlet(g, conc)
+    tw = torch.zeros(template_verts, 24)
+    tw.scatter_(1, nn4, w4)
+    V = gauss_per_body
+    bind = torch.randint(0, template_verts, (n_bodies, V), generator=g)
+    vertices = tv[bind] + torch.randn(n_bodies, V, 3, generator=g) * 0.01
+    weights = tw[bind].permute(0, 2, 1).contiguous()               # [N, 24, V]
+    quats = torch.randn(n_bodies, V, 4, generator=g)
+    quats = quats / quats.norm(dim=-1, keepdim=True)
+    local_q = axis_angle_to_quat(torch.randn(n_bodies, 24, 3, generator=g) * pose_sigma)
+    joints = joints0.expand(n_bodies, 24, 3).contiguous()
+    a0_inv_q = torch.zeros(n_bodies, 24, 4)
+    a0_inv_q[..., 0] = 1.0
+    a0_inv_t = torch.zeros(n_bodies, 24, 3)
+    instance_t = torch.stack([6.0 + 8.0 * torch.rand(n_bodies, generator=g),
+                              -4.0 + 8.0 * torch.rand(n_bodies, generator=g), torch.full((n_bodies,), 0.9)], dim=1)
+    instance_v = torch.randn(n_bodies, 3, generator=g) * 0.5
+    instance_ids = torch.arange(n_bodies, dtype=torch.int32)
+    return dict(local_q=local_q, joints=joints, a0_inv_q=a0_inv_q, a0_inv_t=a0_inv_t, vertices=vertices,
+                quats=quats, weights=weights, instance_ids=instance_ids, instance_t=instance_t,
+                instance_v=instance_v, valid_ids=torch.arange(n_bodies, dtype=torch.int32))
+
+
+def _dirichlet(g, conc):
+    """Dirichlet samples from gamma draws (Marsaglia-Tsang for shape >= 1,
+    boosted for shape < 1) with the given generator."""
+    a = conc + 1.0
+    d = a - 1.0 / 3.0
+    c = 1.0 / torch.sqrt(9.0 * d)
+    out = torch.empty_like(conc)
+    todo = torch.ones_like(conc, dtype=torch.bool)
+    while todo.any():
+        x = torch.randn(conc.shape, generator=g)
+        v = (1.0 + c * x) ** 3
+        u = torch.rand(conc.shape, generator=g)
+        ok = (v > 0) & (torch.log(u.clamp_min(1e-30)) < 0.5 * x * x + d - d * v + d * torch.log(v.clamp_min(1e-30)))
+        take = todo & ok
+        out[take] = (d * v)[take]
+        todo &= ~ok
+    u = torch.rand(conc.shape, generator=g)
+    gam = out * u ** (1.0 / conc)
+    return gam / gam.sum(dim=-1, keepdim=True)
