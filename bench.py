@@ -45,7 +45,11 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--gaussians", type=int, default=N_C2)
+    p.add_argument("--no-lidar", action="store_true", help="skip the C4 lidar rays/s measurement")
+    p.add_argument("--gaussians", type=int, default=0, help="override the workload's Gaussian count")
+    p.add_argument("--workload", default="c2", choices=["c2", "c3", "c3-8"],
+                   help="c2: one C2 view per rank (weak scaling, the default); c3 / c3-8: the rig's views "
+                        "sharded over the ranks (strong scaling)")
     return p.parse_args()
 
 
@@ -65,7 +69,7 @@ def cpu_count():
 
 # ------------------------------------------------------------ CPU oracle --
 def oracle_view(sc, spec, rows=None):
-    """One fwd+bwd view of the C2 workload on the CPU oracle; `rows` limits
+    """One fwd+bwd view (pinhole or fisheye) on the CPU oracle; `rows` limits
     compositing to a band of tile rows (projection and tiling always cover
     the whole view).  Returns (seconds, pixels composited)."""
     import numpy as np
@@ -77,11 +81,11 @@ def oracle_view(sc, spec, rows=None):
     m, q, s, o, sh = (t.numpy() for t in (sc.means, sc.quats, sc.scales, sc.opacities, sc.sh))
     vr, vd, va = (t.numpy() for t in scenes.upstream_grads(H, W, 3))
     t0 = time.perf_counter()
-    flags, radii, m2, dep = O.projection_utgs("pinhole", pack, m, None, s, q, o, W, H)
+    flags, radii, m2, dep = O.projection_utgs(spec.kind, pack, m, None, s, q, o, W, H)
     tpg, ids, flat = O.isect_regular(m2, radii, dep, W, H, 16, 16)
     tw, th = (W + 15) // 16, (H + 15) // 16
     off = O.isect_offset_encode(ids, tw, th)
-    ro, rd, _ = O.camera_rays("pinhole", pack, W, H)
+    ro, rd, _ = O.camera_rays(spec.kind, pack, W, H)
     cols = O.sh_fwd(DEG_C2, pack[4:7], m, sh)
     y0, y1 = (0, th) if rows is None else rows
     band = slice(y0 * 16, min(H, y1 * 16))
@@ -98,43 +102,56 @@ def oracle_view(sc, spec, rows=None):
 
 
 def reference_arm(args, world, rank):
-    """--impl reference: the CPU oracle on the box's host cores."""
+    """--impl reference: the CPU oracle on the box's host cores, on the same
+    workload (every view of one step), rank 0 only."""
     if rank != 0:
         return
     from oracle import oracle as O
     from xsimgs_b200 import scenes
-    sc = scenes.street_scene(args.gaussians)
-    spec = scenes.c2_camera()
-    th = (spec.height + 15) // 16
+    specs, n_default, scaling = workload_views(args.workload)
+    n_gauss = args.gaussians or n_default
+    # torchrun sets OMP_NUM_THREADS=1 per process: use every host core
+    O.set_threads(cpu_count())
+    sc = scenes.street_scene(n_gauss)
+    if scaling == "weak":
+        specs = specs * world   # every rank's view
     cores = O.num_threads()
-    # calibrate: a full view; bound the whole run to about three minutes
-    t_full, px_full = oracle_view(sc, spec)
+    # calibrate on full views; bound the whole run to about three minutes by
+    # compositing a centred band of tile rows of each view
+    t_full = sum(oracle_view(sc, sp)[0] for sp in specs[:1]) * len(specs)
     steps = args.steps + args.warmup
-    rows = None
-    per_step_budget = 170.0 / max(1, steps)
-    if t_full > per_step_budget:
-        frac = max(1.0 / th, per_step_budget / t_full)
-        nrows = max(1, int(th * frac))
-        y0 = max(0, th // 2 - nrows // 2)
-        rows = (y0, y0 + nrows)
+    budget = 170.0 / max(1, steps)
+    frac = min(1.0, budget / t_full)
+    bands = []
+    for sp in specs:
+        th = (sp.height + 15) // 16
+        if frac >= 1.0:
+            bands.append(None)
+        else:
+            nrows = max(1, int(th * frac))
+            y0 = max(0, th // 2 - nrows // 2)
+            bands.append((y0, y0 + nrows))
     for _ in range(args.warmup):
-        oracle_view(sc, spec, rows)
+        for sp, rows in zip(specs, bands):
+            oracle_view(sc, sp, rows)
     tot_t, tot_px = 0.0, 0
     for _ in range(args.steps):
-        t, px = oracle_view(sc, spec, rows)
-        tot_t += t
-        tot_px += px
+        for sp, rows in zip(specs, bands):
+            t, px = oracle_view(sc, sp, rows)
+            tot_t += t
+            tot_px += px
     value = tot_px / tot_t / 1e6
-    sample = ("full C2 view per step" if rows is None else
-              f"C2 projection+tiling of all {args.gaussians} Gaussians and fwd+bwd compositing of "
-              f"tile rows {rows[0]}-{rows[1] - 1} ({spec.width}x{min(spec.height, rows[1] * 16) - rows[0] * 16} px) "
-              f"per step")
+    if all(b is None for b in bands):
+        sample = f"every view of the step in full ({len(specs)} view(s))"
+    else:
+        sample = (f"projection + tiling of all {n_gauss} Gaussians and fwd+bwd compositing of a centred band of "
+                  f"{bands[0][1] - bands[0][0]} tile rows per view, {len(specs)} view(s) per step")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "Mpix/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1000 * tot_t / args.steps, 2), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded C2 scene)",
-        "config": {"workload": "C2: 1M Gaussians, SH deg 3, pinhole 1920x1080, fwd+bwd",
+        "ms_per_step": round(1000 * tot_t / args.steps, 2), "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": "f32", "data": f"synthetic (seeded {args.workload.upper()} scene)",
+        "config": {"workload": WORKLOAD_DESC[args.workload],
                    "implementation": "CPU oracle restatement (reference not buildable here)"},
         "cpu_baseline": {"value": round(value, 4), "unit": "Mpix/s", "cores": cores, "kind": "port",
                          "sample": sample},
@@ -190,6 +207,24 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+def workload_views(name: str):
+    """(camera specs, Gaussians, scaling) of a bench workload."""
+    from xsimgs_b200 import scenes
+    if name == "c2":
+        return [scenes.c2_camera()], N_C2, "weak"
+    if name in ("c3", "c3-8"):
+        return scenes.c3_rig(eight=name == "c3-8"), 2 * N_C2, "strong"
+    raise ValueError(name)
+
+
+WORKLOAD_DESC = {
+    "c2": "C2: 1M Gaussians, SH deg 3, pinhole 1920x1080, fwd+bwd per view (every rank renders the C2 view)",
+    "c3": "C3: 2M Gaussians, SH deg 3, 6-camera rig (3 pinholes 1920x1080, 3 KB fisheyes 1280x960), "
+          "fwd+bwd of all views per step, views sharded over ranks",
+    "c3-8": "C3-8: C3 plus 2 pinholes at yaw 30/210 deg (8 views), views sharded over ranks",
+}
+
+
 def gpu_arm(args, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -201,38 +236,36 @@ def gpu_arm(args, world, rank, local):
 
     import xsimgs_b200 as X
     from xsimgs_b200 import capi, scenes, roofline
+    from xsimgs_b200.multiview import GradientAllReduce, assign_views
 
-    sc = scenes.street_scene(args.gaussians).to(dev)
-    spec = scenes.c2_camera()
-    cam = spec.make(dev)
-    W, H = spec.width, spec.height
+    specs, n_default, scaling = workload_views(args.workload)
+    n_gauss = args.gaussians if args.gaussians else n_default
+    sc = scenes.street_scene(n_gauss).to(dev)
+    if scaling == "weak":
+        mine = [0]          # every rank renders the workload's one view
+        px_per_step = world * specs[0].width * specs[0].height
+    else:
+        mine = assign_views([s.width * s.height for s in specs], world)[rank]
+        px_per_step = sum(s.width * s.height for s in specs)
+    views = [(specs[i], specs[i].make(dev)) for i in mine]
     leaves = {k: v.clone().requires_grad_(True) for k, v in sc.params().items()}
-    origin = cam.t0
-    g_rgb, g_d, g_a = (t.to(dev) for t in scenes.upstream_grads(H, W, 3, seed=1 + rank))
+    # backward finishes the compositing's leaves first, then the SH backward's
+    red = GradientAllReduce([leaves[k] for k in ("quats", "scales", "opacities", "means", "sh")])
+    upstream = [tuple(t.to(dev) for t in scenes.upstream_grads(sp.height, sp.width, 3, seed=1 + rank * 16 + k))
+                for k, (sp, _) in enumerate(views)]
 
-    def allreduce_grads():
-        """Sum the Gaussian gradients over ranks: one NCCL all-reduce per
-        parameter tensor, issued as one coalesced group."""
-        grads = [v.grad for v in leaves.values()]
-        cm = getattr(dist, "_coalescing_manager", None)
-        if cm is not None:
-            with cm(async_ops=False):
-                for g in grads:
-                    dist.all_reduce(g)
-        else:
-            for g in grads:
-                dist.all_reduce(g)
-
-    def step(gr, gd, ga):
+    def step(grads):
         for v in leaves.values():
             v.grad = None
-        colors = X.spherical_harmonics_fused(leaves["sh"], leaves["means"], origin, DEG_C2)
-        color, depth, alpha, _ = X.ut_gs_render(cam, leaves["means"], leaves["scales"], leaves["quats"],
-                                                leaves["opacities"], W, H, colors=colors)
-        loss = (color * gr).sum() + (depth * gd).sum() + (alpha * ga).sum()
-        loss.backward()
-        if world > 1:
-            allreduce_grads()
+        loss = torch.zeros((), device=dev)
+        for (sp, cam), (gr, gd, ga) in zip(views, grads):
+            colors = X.spherical_harmonics_fused(leaves["sh"], leaves["means"], cam.t0, DEG_C2)
+            color, depth, alpha, _ = X.ut_gs_render(cam, leaves["means"], leaves["scales"], leaves["quats"],
+                                                    leaves["opacities"], sp.width, sp.height, colors=colors)
+            loss = loss + (color * gr).sum() + (depth * gd).sum() + (alpha * ga).sum()
+        if views:
+            loss.backward()
+        red.wait()
         return loss
 
     def barrier():
@@ -241,7 +274,7 @@ def gpu_arm(args, world, rank, local):
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        step(g_rgb, g_d, g_a)
+        step(upstream)
     barrier()
 
     # -------------------------------------------------- timed: value ----
@@ -254,7 +287,7 @@ def gpu_arm(args, world, rank, local):
     barrier()
     ev0.record()
     for _ in range(args.steps):
-        step(g_rgb, g_d, g_a)
+        step(upstream)
     ev1.record()
     barrier()
     launches = capi.launch_count() - launches0
@@ -265,74 +298,126 @@ def gpu_arm(args, world, rank, local):
     capi.timing_reset()
 
     # ---------------------------------------------------- timed: e2e ----
-    host = [t.cpu().pin_memory() for t in (g_rgb, g_d, g_a)]
-    dbuf = [torch.empty_like(t) for t in (g_rgb, g_d, g_a)]
-    h2d = sum(t.numel() * t.element_size() for t in host)
+    host = [[t.cpu().pin_memory() for t in g] for g in upstream]
+    dbuf = [[torch.empty_like(t) for t in g] for g in upstream]
+    h2d = sum(t.numel() * t.element_size() for g in host for t in g)
+
+    def copy_in():
+        for dg, hg in zip(dbuf, host):
+            for d, h in zip(dg, hg):
+                d.copy_(h, non_blocking=True)
+
     for _ in range(max(1, args.warmup // 2)):
-        for d, h in zip(dbuf, host):
-            d.copy_(h, non_blocking=True)
-        step(*dbuf).item()
+        copy_in()
+        step(dbuf).item()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        for d, h in zip(dbuf, host):
-            d.copy_(h, non_blocking=True)
-        step(*dbuf).item()
+        copy_in()
+        step(dbuf).item()
     e1.record()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
+
+    # ------------------------------ timed: C4 lidar rays/s (c2 scene) ----
+    lidar_ms = {}
+    if args.workload == "c2" and not args.no_lidar:
+        lspec = scenes.c4_lidar()
+        lcam = lspec.make(dev)
+        LW, LH = lspec.width, lspec.height
+        gen = torch.Generator().manual_seed(3)
+        inten = torch.rand(n_gauss, 1, generator=gen).to(dev).requires_grad_(True)
+        lg = [t.to(dev) for t in scenes.upstream_grads(LH, LW, 1, seed=40 + rank)]
+
+        def lstep(phm):
+            for v in list(leaves.values()) + [inten]:
+                v.grad = None
+            color, depth, alpha, _ = X.ut_gs_render(lcam, leaves["means"], leaves["scales"], leaves["quats"],
+                                                    leaves["opacities"], LW, LH, colors=inten, use_phm=phm)
+            ((color * lg[0]).sum() + (depth * lg[1]).sum() + (alpha * lg[2]).sum()).backward()
+            red.wait()
+
+        for phm in (False, True):
+            for _ in range(args.warmup):
+                lstep(phm)
+            barrier()
+            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0.record()
+            for _ in range(args.steps):
+                lstep(phm)
+            l1.record()
+            barrier()
+            lidar_ms["phm" if phm else "central"] = l0.elapsed_time(l1)
+
     clk = clocks.stop()
 
     # max over ranks
-    tt = torch.tensor([t_ms, e2e_ms], device=dev)
+    tt = torch.tensor([t_ms, e2e_ms, lidar_ms.get("central", 0.0), lidar_ms.get("phm", 0.0)], device=dev)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms = tt.tolist()
+    t_ms, e2e_ms, l_c, l_p = tt.tolist()
+    lidar = None
+    if lidar_ms:
+        rays = world * 128 * 2048 * args.steps
+        lidar = {"metric": "lidar rays/s (C4: 128 beams x 2048 azimuth bins, the C2 scene, depth + intensity + "
+                           "ray-drop alpha, fwd+bwd)", "unit": "rays/s", "scaling": "weak",
+                 "value": round(rays / (l_c * 1e-3)), "ms_per_step": round(l_c / args.steps, 3),
+                 "phm": {"value": round(rays / (l_p * 1e-3)), "ms_per_step": round(l_p / args.steps, 3)}}
 
     # ------------------------------------------------ roofline inputs ----
     roof = None
-    if rank == 0:
-        cnt = torch.zeros(2, dtype=torch.int64, device=dev)
-        capi.set_pair_counters(cnt.data_ptr())
-        with torch.no_grad():
-            colors = X.spherical_harmonics_fused(sc.sh, sc.means, origin, DEG_C2)
-            td = X.ut_gs_tiling(cam, sc.means, sc.scales, sc.quats, W, H, opacity=sc.opacities)
-            ro, rd = cam.camera_rays(W, H)
-            _, _, alpha, last = X._C.rasterize_eval3d_fwd(
-                means=sc.means, quats=sc.quats, scales=sc.scales, colors=colors.unsqueeze(0),
-                opacities=sc.opacities.view(1, -1), image_width=W, image_height=H, tile_size_width=16,
-                tile_size_height=16, ray_origs=ro, ray_dirs=rd, tile_offsets=td["isect_offsets"],
-                flatten_ids=td["flatten_ids"])
-        torch.cuda.synchronize()
-        capi.set_pair_counters(None)
-        n_eval_f, n_contrib = (int(x) for x in cnt.tolist())
-        # backward replays every pair up to each pixel's last contributor
-        tw = (W + 15) // 16
-        ty = torch.arange(H, device=dev) // 16
-        tx = torch.arange(W, device=dev) // 16
-        start = td["isect_offsets"].view(-1)[(ty[:, None] * tw + tx[None, :])]
-        n_eval_b = int(torch.where(alpha > 0, last - start + 1, torch.zeros_like(last)).sum())
+    if rank == 0 and views:
+        fl_b = fl_f = 0.0
+        pairs = {"evaluated_fwd": 0, "evaluated_bwd": 0, "contributing": 0}
+        for sp, cam in views:
+            W, H = sp.width, sp.height
+            cnt = torch.zeros(2, dtype=torch.int64, device=dev)
+            capi.set_pair_counters(cnt.data_ptr())
+            with torch.no_grad():
+                colors = X.spherical_harmonics_fused(sc.sh, sc.means, cam.t0, DEG_C2)
+                td = X.ut_gs_tiling(cam, sc.means, sc.scales, sc.quats, W, H, opacity=sc.opacities)
+                ro, rd = cam.camera_rays(W, H)
+                _, _, alpha, last = X._C.rasterize_eval3d_fwd(
+                    means=sc.means, quats=sc.quats, scales=sc.scales, colors=colors.unsqueeze(0),
+                    opacities=sc.opacities.view(1, -1), image_width=W, image_height=H, tile_size_width=16,
+                    tile_size_height=16, ray_origs=ro, ray_dirs=rd, tile_offsets=td["isect_offsets"],
+                    flatten_ids=td["flatten_ids"])
+            torch.cuda.synchronize()
+            capi.set_pair_counters(None)
+            n_eval_f, n_contrib = (int(x) for x in cnt.tolist())
+            # backward replays every pair up to each pixel's last contributor
+            tw = (W + 15) // 16
+            ty = torch.arange(H, device=dev) // 16
+            tx = torch.arange(W, device=dev) // 16
+            start = td["isect_offsets"].view(-1)[(ty[:, None] * tw + tx[None, :])]
+            n_eval_b = int(torch.where(alpha > 0, last - start + 1, torch.zeros_like(last)).sum())
+            fl_b += roofline.bwd_flops(n_eval_b, n_contrib, 3)
+            fl_f += roofline.fwd_flops(n_eval_f, n_contrib, 3)
+            pairs["evaluated_fwd"] += n_eval_f
+            pairs["evaluated_bwd"] += n_eval_b
+            pairs["contributing"] += n_contrib
         peak_flops = fp32_peak(dev)
-        bwd_avg = bwd_ms / max(1, bwd_n)
-        fwd_avg = fwd_ms / max(1, fwd_n)
-        fl_b = roofline.bwd_flops(n_eval_b, n_contrib, 3)
-        fl_f = roofline.fwd_flops(n_eval_f, n_contrib, 3)
-        ach_b = fl_b / (bwd_avg * 1e-3) / 1e12
-        ach_f = fl_f / (fwd_avg * 1e-3) / 1e12
+        # kernel time per step over the timed region (all of this rank's views)
+        bwd_step = bwd_ms / args.steps
+        fwd_step = fwd_ms / args.steps
+        ach_b = fl_b / (bwd_step * 1e-3) / 1e12
+        ach_f = fl_f / (fwd_step * 1e-3) / 1e12
+        c2_full = args.workload == "c2" and n_gauss == N_C2
         roof = {"kernel": "rasterize_bwd (raster_bwd_kernel<3,false>)", "bound": "fp32",
                 "achieved": round(ach_b, 2), "peak": round(peak_flops / 1e12, 2), "unit": "TFLOP/s",
                 "frac": round(ach_b / (peak_flops / 1e12), 3),
-                "traffic": roofline.BWD_DRAM_BYTES_C2 if args.gaussians == N_C2 else None,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture of this kernel "
-                                  "on this workload (bytes per launch)",
+                "traffic": roofline.BWD_DRAM_BYTES_C2 if c2_full else None,
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture of this kernel "
+                                   "on this workload (bytes per launch)") if c2_full else None,
                 "peak_source": "measured: FP32 FMA probe in this run (MEASURED_PEAKS.json has only HBM and bf16)",
-                "avg_launch_ms": round(bwd_avg, 4), "flops_per_launch": fl_b,
-                "pairs": {"evaluated_fwd": n_eval_f, "evaluated_bwd": n_eval_b, "contributing": n_contrib},
-                "fwd": {"achieved": round(ach_f, 2), "avg_launch_ms": round(fwd_avg, 4),
+                "avg_launch_ms": round(bwd_ms / max(1, bwd_n), 4),
+                "flops_per_launch": fl_b / len(views), "pairs": pairs,
+                "fwd": {"achieved": round(ach_f, 2), "avg_launch_ms": round(fwd_ms / max(1, fwd_n), 4),
                         "frac": round(ach_f / (peak_flops / 1e12), 3)},
-                "step_share": round((bwd_avg + fwd_avg) / (t_ms / args.steps), 3)}
+                "step_share": round((bwd_step + fwd_step) / (t_ms / args.steps), 3)}
 
+    red.remove()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -340,27 +425,31 @@ def gpu_arm(args, world, rank, local):
         return
 
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        t, px = oracle_view(scenes.street_scene(args.gaussians), spec)
+    if world == 1 and not args.no_cpu_baseline and args.workload == "c2":
         from oracle import oracle as O
+        O.set_threads(cpu_count())
+        t, px = oracle_view(scenes.street_scene(n_gauss), specs[0])
         cpu = {"value": round(px / t / 1e6, 4), "unit": "Mpix/s", "cores": O.num_threads(), "kind": "port",
                "sample": "one full C2 view (projection, tiling, SH, fwd+bwd compositing) on the CPU oracle"}
 
-    px_total = world * W * H * args.steps
+    px_total = px_per_step * args.steps
     value = px_total / (t_ms * 1e-3) / 1e6
     e2e = px_total / (e2e_ms * 1e-3) / 1e6
     gbytes = sum(v.numel() * 4 for v in leaves.values())
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "Mpix/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded C2 scene)",
-        "config": {"workload": "C2: 1M Gaussians, SH deg 3, pinhole 1920x1080, fwd+bwd per view",
-                   "views_per_gpu": 1, "parallelism": f"view-sharded dp{world} + NCCL all-reduce of grads",
-                   "gaussians": args.gaussians, "width": W, "height": H, "tile": 16,
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+        "data": f"synthetic (seeded {args.workload.upper()} scene)",
+        "config": {"workload": WORKLOAD_DESC[args.workload],
+                   "views_per_gpu": len(views) if scaling == "weak" else
+                   [len(v) for v in assign_views([s.width * s.height for s in specs], world)],
+                   "parallelism": f"view-sharded dp{world} + NCCL all-reduce of grads",
+                   "gaussians": n_gauss, "pixels_per_step": px_per_step, "tile": 16,
                    "l2": f"inputs larger than L2: Gaussian params {gbytes / 1e6:.0f} MB > 126 MB L2"},
         "e2e": {"value": round(e2e, 2), "unit": "Mpix/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches), "gpu_launches_per_step": round(launches / args.steps, 1),
-        "clocks": clk, "roofline": roof, "cpu_baseline": cpu,
+        "clocks": clk, "roofline": roof, "cpu_baseline": cpu, "lidar": lidar,
     }
     print(json.dumps(line), flush=True)
 

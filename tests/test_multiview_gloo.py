@@ -1,0 +1,138 @@
+"""Host logic of the multi-GPU path on CPU: view assignment, and the
+gradient all-reduce over two gloo ranks (the same code runs over NCCL on
+GPUs).  Each rank builds a small autograd graph shaped like the render step
+(a leaf feeding two consumers, like the Gaussian means feeding both the SH
+colour and the compositing) and checks that after backward + wait() every
+rank holds the sum of all ranks' gradients."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from xsimgs_b200.multiview import GradientAllReduce, assign_views
+
+
+def test_assign_views_balanced_and_deterministic():
+    costs = [2.07, 1.23, 2.07, 1.23, 2.07, 1.23]  # C3: 3 x 1080p pinholes, 3 x 1280x960 fisheyes (Mpix)
+    for world in (1, 2, 3, 4, 6, 8):
+        a = assign_views(costs, world)
+        assert a == assign_views(costs, world)
+        assert sorted(i for v in a for i in v) == list(range(len(costs)))
+        loads = [sum(costs[i] for i in v) for v in a]
+        assert max(loads) - min(loads) <= max(costs) + 1e-9
+    assert assign_views([1.0], 4) == [[0], [], [], []]
+    with pytest.raises(ValueError):
+        assign_views(costs, 0)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    """Two backward passes with the hooks registered once: each pass issues
+    one collective per leaf, and afterwards every rank holds the same
+    gradient."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        from datetime import timedelta
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        g = torch.Generator().manual_seed(100 + rank)
+        means = torch.randn(50, 3, generator=g).requires_grad_(True)
+        quats = torch.randn(50, 4, generator=g).requires_grad_(True)
+        sh = torch.randn(50, 16, 3, generator=g).requires_grad_(True)
+        red = GradientAllReduce([means, quats, sh])
+        for _ in range(2):
+            for t in (means, quats, sh):
+                t.grad = None
+            w = torch.randn(50, 3, generator=g)
+            ((sh[:, 0, :] * means.sin()).sum() + (means * w).sum() + (quats ** 2).sum() * (rank + 1)).backward()
+            n = red.wait()
+            assert n == 3, f"{n} collectives in one pass"
+            for t in (means, quats, sh):
+                lst = [torch.empty_like(t.grad) for _ in range(world)]
+                dist.all_gather(lst, t.grad)
+                assert all(torch.equal(o, t.grad) for o in lst)
+        red.remove()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, repr(e)))
+
+
+def _reference_sum(world, idle=()):
+    """The summed gradients recomputed without any collective."""
+    tot = None
+    for rank in range(world):
+        if rank in idle:
+            continue
+        g = torch.Generator().manual_seed(100 + rank)
+        means = torch.randn(50, 3, generator=g).requires_grad_(True)
+        quats = torch.randn(50, 4, generator=g).requires_grad_(True)
+        sh = torch.randn(50, 16, 3, generator=g).requires_grad_(True)
+        w = torch.randn(50, 3, generator=g)
+        ((sh[:, 0, :] * means.sin()).sum() + (means * w).sum() + (quats ** 2).sum() * (rank + 1)).backward()
+        grads = [means.grad, quats.grad, sh.grad]
+        tot = grads if tot is None else [a + b for a, b in zip(tot, grads)]
+    return tot
+
+
+def _worker_values(rank, world, port, q, idle=()):
+    """`idle` ranks run no backward (a rank without views): they contribute
+    zeros and still take part in every collective."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        from datetime import timedelta
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        g = torch.Generator().manual_seed(100 + rank)
+        means = torch.randn(50, 3, generator=g).requires_grad_(True)
+        quats = torch.randn(50, 4, generator=g).requires_grad_(True)
+        sh = torch.randn(50, 16, 3, generator=g).requires_grad_(True)
+        red = GradientAllReduce([means, quats, sh])
+        w = torch.randn(50, 3, generator=g)
+        if rank not in idle:
+            ((sh[:, 0, :] * means.sin()).sum() + (means * w).sum() + (quats ** 2).sum() * (rank + 1)).backward()
+        assert red.wait() == 3
+        q.put((rank, [t.grad.clone() for t in (means, quats, sh)]))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("target", ["consistency", "values", "idle_rank"])
+def test_gradient_allreduce_two_gloo_ranks(target):
+    world = 2
+    idle = (1,) if target == "idle_rank" else ()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    if target == "consistency":
+        procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    else:
+        procs = [ctx.Process(target=_worker_values, args=(r, world, port, q, idle)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r, v = q.get(timeout=120)
+        results[r] = v
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    if target == "consistency":
+        assert all(v == "ok" for v in results.values()), results
+    else:
+        assert all(not isinstance(v, str) for v in results.values()), results
+        ref = _reference_sum(world, idle)
+        for r in range(world):
+            for got, want in zip(results[r], ref):
+                torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-6)
