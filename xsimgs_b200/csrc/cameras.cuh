@@ -268,6 +268,29 @@ __device__ __forceinline__ void project_point(const Cam& k, v3 P, v3 Pv, float t
     if (mode == MODE_NEG) pt = -fabsf(k.rolling.x) * 0.5f;
     else if (mode == MODE_POS) pt = fabsf(k.rolling.x) * 0.5f;
     float residual = 0.0f;
+    if (k.w.x == 0.0f && k.w.y == 0.0f && k.w.z == 0.0f && Pv.x == k.v.x && Pv.y == k.v.y && Pv.z == k.v.z) {
+        // No angular velocity and no relative motion: the camera-frame point
+        // does not depend on the capture time, so every Newton step below
+        // projects the same point and has d residual / d t = 1.  Project
+        // once and iterate only the time update (same checks, same result).
+        uvd = k.to_uvd(mode, quat_rotate(k.qw, mk3(-k.qx, -k.qy, -k.qz), P - k.t0));
+        if ((uvd.z <= 0.0f) || (uvd.x < -margin) || (uvd.x > 1.0f + margin) || (uvd.y < -margin) ||
+            (uvd.y > 1.0f + margin)) {
+            valid = false;
+            uvdt = make_float4(0.f, 0.f, 0.f, 0.f);
+            return;
+        }
+        const float real = k.pixel_time(uvd.x, uvd.y);
+#pragma unroll 1
+        for (int it = 0; it < 5; ++it) {
+            residual = (k.pose + pt) - real;
+            pt -= residual;
+            if (fabsf(residual) < thr) break;
+        }
+        uvdt = make_float4(uvd.x, uvd.y, uvd.z, pt);
+        valid = valid && (fabsf(residual) < max_res) && (uvd.z > 0.0f);
+        return;
+    }
 #pragma unroll 1
     for (int it = 0; it < 5; ++it) {
         if constexpr (kUseJac && Cam::kJacobian) {

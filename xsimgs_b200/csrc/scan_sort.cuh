@@ -129,28 +129,110 @@ int exclusive_scan(const T* in, int64_t n, int64_t* out, int64_t* total, void* t
 }
 
 // ---------------------------------------------------------------- radix --
+// Stable LSD radix sort, 8-bit digits, warp-granular: the input is cut into
+// warp chunks of 32 x R consecutive keys (R = 16 or 64).  Per pass:
+//   1. hist:     every warp counts the digits of its chunk in its own
+//                shared-memory counters -> counts[digit][chunk];
+//   2. row scan: one CTA per digit scans its row over the chunks ->
+//                offsets[digit][chunk] (within the digit) and totals[digit];
+//   3. scatter:  every warp walks its chunk in order, 32 keys at a time,
+//                ranks equal digits among its lanes and keeps its own
+//                per-digit cursor in shared memory; the digit bases come
+//                from a scan of the 256 totals.  No block-wide barrier
+//                inside the loop; keys are prefetched 16 rounds at a time.
+// Warp chunks are processed in input order inside each digit, so the sort
+// is stable.
 constexpr int kSortThreads = 256;
-constexpr int kSortRounds = 16;
-constexpr int kSortChunk = kSortThreads * kSortRounds;  // items per block
+constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kRadixBits = 8;
 constexpr int kRadixBins = 1 << kRadixBits;
+constexpr int kRxBatch = 16;  // rounds prefetched together
 
-inline int64_t sort_blocks(int64_t n) { return (n + kSortChunk - 1) / kSortChunk; }
+inline int sort_rounds(int64_t n) { return n > (int64_t(4) << 20) ? 64 : 16; }
+inline int64_t sort_chunks(int64_t n) {
+    const int64_t per = int64_t(32) * sort_rounds(n);
+    return (n + per - 1) / per;
+}
+
+// Lanes of the warp holding the same digit (0..255, or 256 for a lane past
+// the end): nine ballots, constant time whatever the digits are.
+__device__ __forceinline__ unsigned match_digit(int digit) {
+    unsigned m = 0xffffffffu;
+#pragma unroll
+    for (int b = 0; b < kRadixBits + 1; ++b) {
+        const bool bit = (digit >> b) & 1;
+        const unsigned bal = __ballot_sync(0xffffffffu, bit);
+        m &= bit ? bal : ~bal;
+    }
+    return m;
+}
 
 __global__ void __launch_bounds__(kSortThreads)
-    radix_hist_kernel(const uint32_t* __restrict__ keys, int64_t n, int shift, int32_t* __restrict__ counts,
-                      int64_t nblocks) {
-    __shared__ int32_t h[kRadixBins];
-    h[threadIdx.x] = 0;
-    __syncthreads();
-    const int64_t base = int64_t(blockIdx.x) * kSortChunk;
-#pragma unroll 4
-    for (int r = 0; r < kSortRounds; ++r) {
-        const int64_t i = base + int64_t(r) * kSortThreads + threadIdx.x;
-        if (i < n) atomicAdd(&h[(keys[i] >> shift) & (kRadixBins - 1)], 1);
+    radix_hist_kernel(const uint32_t* __restrict__ keys, int64_t n, int shift, int rounds,
+                      int32_t* __restrict__ counts, int64_t nchunks) {
+    __shared__ int32_t h[kSortWarps][kRadixBins];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t c = int64_t(blockIdx.x) * kSortWarps + w;
+    if (c >= nchunks) return;  // warp-uniform; no block barrier below
+#pragma unroll
+    for (int k = 0; k < kRadixBins / 32; ++k) h[w][lane + 32 * k] = 0;
+    __syncwarp();
+    const int64_t base = c * 32 * rounds;
+    for (int b = 0; b < rounds; b += kRxBatch) {
+        int dg[kRxBatch];
+#pragma unroll
+        for (int r = 0; r < kRxBatch; ++r) {
+            const int64_t i = base + int64_t(b + r) * 32 + lane;
+            dg[r] = i < n ? int((keys[i] >> shift) & (kRadixBins - 1)) : kRadixBins;
+        }
+#pragma unroll
+        for (int r = 0; r < kRxBatch; ++r) {
+            const unsigned peers = match_digit(dg[r]);
+            if (dg[r] < kRadixBins && lane == __ffs(peers) - 1) h[w][dg[r]] += __popc(peers);
+            __syncwarp();
+        }
     }
+#pragma unroll
+    for (int k = 0; k < kRadixBins / 32; ++k) {
+        const int d = lane + 32 * k;
+        counts[int64_t(d) * nchunks + c] = h[w][d];
+    }
+}
+
+// One CTA per digit: exclusive scan of counts[d][*] -> offsets[d][*], eight
+// consecutive chunks per thread.
+constexpr int kRowItems = 8;
+__global__ void __launch_bounds__(1024)
+    radix_rowscan_kernel(const int32_t* __restrict__ counts, int64_t nchunks, int32_t* __restrict__ offsets,
+                         int64_t* __restrict__ totals) {
+    __shared__ int64_t carry;
+    const int64_t d = blockIdx.x;
+    if (threadIdx.x == 0) carry = 0;
     __syncthreads();
-    counts[int64_t(threadIdx.x) * nblocks + blockIdx.x] = h[threadIdx.x];
+    const int32_t* row = counts + d * nchunks;
+    int32_t* orow = offsets + d * nchunks;
+    const int64_t span = int64_t(blockDim.x) * kRowItems;
+    for (int64_t b = 0; b < nchunks; b += span) {
+        const int64_t i0 = b + int64_t(threadIdx.x) * kRowItems;
+        int32_t v[kRowItems];
+        int64_t s = 0;
+#pragma unroll
+        for (int k = 0; k < kRowItems; ++k) {
+            v[k] = (i0 + k < nchunks) ? row[i0 + k] : 0;
+            s += v[k];
+        }
+        int64_t tot;
+        int64_t run = block_excl_scan(s, &tot) + carry;
+#pragma unroll
+        for (int k = 0; k < kRowItems; ++k) {
+            if (i0 + k < nchunks) orow[i0 + k] = int32_t(run);
+            run += v[k];
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) carry += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) totals[d] = carry;
 }
 
 // Output mode of the final scatter of the tile sort: keys become the
@@ -163,69 +245,77 @@ struct IsectEpilogue {
 
 template <bool kIsect>
 __global__ void __launch_bounds__(kSortThreads)
-    radix_scatter_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
-                         int64_t n, int shift, const int64_t* __restrict__ offsets, int64_t nblocks,
-                         uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
-                         IsectEpilogue ep) {
-    __shared__ int64_t running[kRadixBins];
-    __shared__ int32_t wc[kSortThreads / 32][kRadixBins];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    running[threadIdx.x] = offsets[int64_t(threadIdx.x) * nblocks + blockIdx.x];
-    const int64_t base = int64_t(blockIdx.x) * kSortChunk;
-    const unsigned lt_mask = (1u << lane) - 1u;
-    for (int r = 0; r < kSortRounds; ++r) {
-        const int64_t i = base + int64_t(r) * kSortThreads + threadIdx.x;
-        if (base + int64_t(r) * kSortThreads >= n) break;  // uniform across the block
+    radix_scatter_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, int64_t n,
+                         int shift, int rounds, const int32_t* __restrict__ offsets,
+                         const int64_t* __restrict__ totals, int64_t nchunks, uint32_t* __restrict__ keys_out,
+                         uint32_t* __restrict__ vals_out, IsectEpilogue ep) {
+    __shared__ int64_t dbase[kRadixBins];
+    __shared__ int64_t cur[kSortWarps][kRadixBins];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    // digit bases: exclusive scan of the 256 digit totals (one per thread)
+    {
+        int64_t tot;
+        dbase[threadIdx.x] = block_excl_scan(totals[threadIdx.x], &tot);
+    }
+    __syncthreads();
+    const int64_t c = int64_t(blockIdx.x) * kSortWarps + w;
+    if (c >= nchunks) return;  // warp-uniform; no block barrier below
 #pragma unroll
-        for (int w = 0; w < kSortThreads / 32; ++w) wc[w][threadIdx.x] = 0;
-        __syncthreads();
-        const bool ok = i < n;
-        uint32_t key = 0, val = 0;
-        int digit = kRadixBins;  // sentinel for out-of-range lanes
-        if (ok) {
-            key = keys_in[i];
-            val = vals_in[i];
-            digit = (key >> shift) & (kRadixBins - 1);
+    for (int k = 0; k < kRadixBins / 32; ++k) {
+        const int d = lane + 32 * k;
+        cur[w][d] = dbase[d] + offsets[int64_t(d) * nchunks + c];
+    }
+    __syncwarp();
+    const unsigned lt = (1u << lane) - 1u;
+    const int64_t base = c * 32 * rounds;
+    for (int b = 0; b < rounds; b += kRxBatch) {
+        uint32_t kk[kRxBatch], vv[kRxBatch];
+#pragma unroll
+        for (int r = 0; r < kRxBatch; ++r) {
+            const int64_t i = base + int64_t(b + r) * 32 + lane;
+            kk[r] = i < n ? keys_in[i] : 0u;
+            vv[r] = i < n ? vals_in[i] : 0u;
         }
-        const unsigned peers = __match_any_sync(0xffffffffu, digit);
-        const int rank = __popc(peers & lt_mask);
-        if (ok && rank == 0) wc[wid][digit] = __popc(peers);
-        __syncthreads();
-        {
-            int64_t s = running[threadIdx.x];
 #pragma unroll
-            for (int w = 0; w < kSortThreads / 32; ++w) {
-                const int32_t c = wc[w][threadIdx.x];
-                wc[w][threadIdx.x] = int32_t(s - running[threadIdx.x]);
-                s += c;
-            }
-            // wc now holds offsets relative to running[]; store the new total
-            __syncthreads();
+        for (int r = 0; r < kRxBatch; ++r) {
+            const int64_t i = base + int64_t(b + r) * 32 + lane;
+            const bool ok = i < n;
+            const int digit = ok ? int((kk[r] >> shift) & (kRadixBins - 1)) : kRadixBins;
+            const unsigned peers = match_digit(digit);
+            const int leader = __ffs(peers) - 1;
+            int64_t p0 = 0;
+            if (ok && lane == leader) p0 = cur[w][digit];
+            p0 = __shfl_sync(0xffffffffu, p0, leader);
+            if (ok && lane == leader) cur[w][digit] = p0 + __popc(peers);
+            __syncwarp();
             if (ok) {
-                const int64_t pos = running[digit] + wc[wid][digit] + rank;
+                const int64_t pos = p0 + __popc(peers & lt);
                 if constexpr (kIsect) {
-                    const int32_t bits = __float_as_int(ep.depths[val]);
+                    const int32_t bits = __float_as_int(ep.depths[vv[r]]);
                     // negative depths: the sign extension fills the tile bits
-                    const uint64_t hi = bits < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(key) << 32);
+                    const uint64_t hi = bits < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(kk[r]) << 32);
                     ep.isect_ids[pos] = int64_t(hi | uint64_t(uint32_t(bits)));
-                    ep.flatten_ids[pos] = int32_t(val);
+                    ep.flatten_ids[pos] = int32_t(vv[r]);
                 } else {
-                    keys_out[pos] = key;
-                    vals_out[pos] = val;
+                    keys_out[pos] = kk[r];
+                    vals_out[pos] = vv[r];
                 }
             }
-            __syncthreads();
-            running[threadIdx.x] = s;
         }
-        __syncthreads();
     }
 }
 
+// largest chunk count of any sort of at most n keys
+inline int64_t sort_chunks_max(int64_t n) {
+    const int64_t small = n < (int64_t(4) << 20) ? n : (int64_t(4) << 20);
+    const int64_t a = sort_chunks(n), b = sort_chunks(small);
+    return a > b ? a : b;
+}
+
 inline size_t radix_workspace_bytes(int64_t n) {
-    const int64_t nb = sort_blocks(n);
-    return Arena::round(size_t(nb) * kRadixBins * sizeof(int32_t)) +
-           Arena::round(size_t(nb) * kRadixBins * sizeof(int64_t)) +
-           scan_workspace_bytes(nb * kRadixBins);
+    const int64_t nc = sort_chunks_max(n);
+    return 2 * Arena::round(size_t(nc) * kRadixBins * sizeof(int32_t)) +
+           Arena::round(size_t(kRadixBins) * sizeof(int64_t));
 }
 
 // Stable ascending sort of (key, value) pairs on key bits [0, bits).
@@ -238,26 +328,28 @@ inline int radix_sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, 
     if (keys_res) *keys_res = keys;
     if (vals_res) *vals_res = vals;
     if (n == 0) return XSG_OK;
-    const int64_t nb = sort_blocks(n);
+    if (n >= (int64_t(1) << 31)) return set_error(XSG_ERR_UNSUPPORTED, "radix sort: 2^31 or more keys");
+    const int64_t nc = sort_chunks(n);
+    const int rounds = sort_rounds(n);
     Arena a(tmp, tmp_bytes);
-    int32_t* counts = a.take<int32_t>(size_t(nb) * kRadixBins);
-    int64_t* offs = a.take<int64_t>(size_t(nb) * kRadixBins);
-    void* stmp = a.take<char>(scan_workspace_bytes(nb * kRadixBins));
-    if (!counts || !offs || !stmp) return set_error(XSG_ERR_WORKSPACE, "radix sort: workspace too small");
+    int32_t* counts = a.take<int32_t>(size_t(nc) * kRadixBins);
+    int32_t* offs = a.take<int32_t>(size_t(nc) * kRadixBins);
+    int64_t* totals = a.take<int64_t>(kRadixBins);
+    if (!counts || !offs || !totals) return set_error(XSG_ERR_WORKSPACE, "radix sort: workspace too small");
+    const unsigned grid = unsigned((nc + kSortWarps - 1) / kSortWarps);
     const int passes = (bits + kRadixBits - 1) / kRadixBits;
     IsectEpilogue none{};
     for (int p = 0; p < passes; ++p) {
         const int shift = p * kRadixBits;
-        launch(radix_hist_kernel, unsigned(nb), kSortThreads, 0, st, keys, n, shift, counts, nb);
-        int rc = exclusive_scan<int32_t>(counts, nb * kRadixBins, offs, nullptr, stmp, st);
-        if (rc != XSG_OK) return rc;
+        launch(radix_hist_kernel, grid, kSortThreads, 0, st, keys, n, shift, rounds, counts, nc);
+        launch(radix_rowscan_kernel, kRadixBins, 1024, 0, st, counts, nc, offs, totals);
         const bool last = (p == passes - 1);
         if (last && ep) {
-            launch(radix_scatter_kernel<true>, unsigned(nb), kSortThreads, 0, st, 
-                keys, vals, n, shift, offs, nb, nullptr, nullptr, *ep);
+            launch(radix_scatter_kernel<true>, grid, kSortThreads, 0, st, keys, vals, n, shift, rounds, offs,
+                   totals, nc, nullptr, nullptr, *ep);
         } else {
-            launch(radix_scatter_kernel<false>, unsigned(nb), kSortThreads, 0, st, 
-                keys, vals, n, shift, offs, nb, keys_alt, vals_alt, none);
+            launch(radix_scatter_kernel<false>, grid, kSortThreads, 0, st, keys, vals, n, shift, rounds, offs,
+                   totals, nc, keys_alt, vals_alt, none);
             uint32_t* t = keys; keys = keys_alt; keys_alt = t;
             t = vals; vals = vals_alt; vals_alt = t;
         }

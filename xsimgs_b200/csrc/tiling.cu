@@ -52,6 +52,24 @@ __device__ __forceinline__ bool regular_rect(float2 m, float2 r, float2 ts, int 
 }
 
 // --------------------------------------------------------- regular grid --
+// Adds the block's sum of `c` to *total with one atomic per block (a
+// per-warp atomic on one address serialises ~n/32 atomics).
+__device__ __forceinline__ void block_add_total(int c, unsigned long long* total) {
+    __shared__ unsigned long long part[32];
+    unsigned long long s = unsigned(c);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) part[w] = s;
+    __syncthreads();
+    if (w == 0) {
+        unsigned long long t = lane < int(blockDim.x >> 5) ? part[lane] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (lane == 0 && t) atomicAdd(total, t);
+    }
+}
+
 __global__ void __launch_bounds__(kTileThreads)
     regular_count_kernel(const float2* __restrict__ means2d, const float2* __restrict__ radii, int64_t n,
                          float2 ts, int ntx, int nty, int32_t* __restrict__ counts,
@@ -64,10 +82,7 @@ __global__ void __launch_bounds__(kTileThreads)
         counts[i] = c;
     }
     // warp-aggregated total
-    unsigned s = unsigned(c);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((threadIdx.x & 31) == 0 && s) atomicAdd(total, (unsigned long long)s);
+    block_add_total(c, total);
 }
 
 // Writes each Gaussian's intersections; with `order` (a permutation of the
@@ -271,10 +286,7 @@ __global__ void __launch_bounds__(kTileThreads / 2)
                       in.radii, r1, r2, has2, d2);
         counts[i] = c;
     }
-    unsigned s = unsigned(c);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((threadIdx.x & 31) == 0 && s) atomicAdd(total, (unsigned long long)s);
+    block_add_total(c, total);
 }
 
 // Second-rectangle depths differ from depths[i]; the sorted path keys those
