@@ -392,7 +392,8 @@ def gpu_arm(args, world, rank, local):
             tx = torch.arange(W, device=dev) // 16
             start = td["isect_offsets"].view(-1)[(ty[:, None] * tw + tx[None, :])]
             n_eval_b = int(torch.where(alpha > 0, last - start + 1, torch.zeros_like(last)).sum())
-            fl_b += roofline.bwd_flops(n_eval_b, n_contrib, 3)
+            # the render step's rays come from the camera: no ray gradients
+            fl_b += roofline.bwd_flops(n_eval_b, n_contrib, 3, ray_grads=False)
             fl_f += roofline.fwd_flops(n_eval_f, n_contrib, 3)
             pairs["evaluated_fwd"] += n_eval_f
             pairs["evaluated_bwd"] += n_eval_b
@@ -404,7 +405,7 @@ def gpu_arm(args, world, rank, local):
         ach_b = fl_b / (bwd_step * 1e-3) / 1e12
         ach_f = fl_f / (fwd_step * 1e-3) / 1e12
         c2_full = args.workload == "c2" and n_gauss == N_C2
-        roof = {"kernel": "rasterize_bwd (raster_bwd_kernel<3,false>)", "bound": "fp32",
+        roof = {"kernel": "rasterize_bwd (raster_bwd_kernel<3,false,false>, no ray gradients)", "bound": "fp32",
                 "achieved": round(ach_b, 2), "peak": round(peak_flops / 1e12, 2), "unit": "TFLOP/s",
                 "frac": round(ach_b / (peak_flops / 1e12), 3),
                 "traffic": roofline.BWD_DRAM_BYTES_C2 if c2_full else None,

@@ -199,7 +199,9 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
 /* Backward compositing.  Gradient outputs are overwritten (zeroed first):
  * v_means/v_velocity [N,3], v_quats [N,4], v_scales [N,3], v_opacities [N],
  * v_colors [N, cdim] (NULL when cdim = 0), v_ray_o/v_ray_d [H, W, 3],
- * v_ray_time_delta [H, W] (dynamic only).  v_renders may be NULL.
+ * v_ray_time_delta [H, W] (dynamic only).  v_renders may be NULL.  Passing
+ * NULL for all of v_ray_o, v_ray_d (and v_ray_time_delta) skips the per-pixel
+ * ray gradients, which is cheaper when the rays need none.
  * Replaces rasterize_eval3d_bwd, csrc/rasterization/eval3d_bwd.cu:297-403,
  * and rasterize_eval3d_dynamic_bwd, eval3d_dynamic_bwd.cu:312-429. */
 int xsg_rasterize_bwd(const float* means, const float* velocity, const float* quats,

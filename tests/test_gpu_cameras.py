@@ -286,6 +286,17 @@ def test_composite_fwd_bwd_per_camera(specs, shell, cuda, kind, dynamic):
         if key == "v_ray_t":
             got = to_np(got).reshape(H, W)
         assert_grads_close(got, ref[key], f"{kind} {key}")
+    # the variant without ray gradients gives the same Gaussian gradients
+    if dynamic:
+        fast = _C.rasterize_eval3d_dynamic_bwd(bwd_args[0], g(shell["vel"]), *bwd_args[1:], rt, 16, 16, *tail,
+                                               ray_grads=False)
+        assert fast[6] is None and fast[7] is None and fast[8] is None
+    else:
+        fast = _C.rasterize_eval3d_bwd(*bwd_args, 16, 16, *tail, ray_grads=False)
+        assert fast[5] is None and fast[6] is None
+    for got, key in zip(fast, names):
+        if not key.startswith("v_ray"):
+            assert_grads_close(got, ref[key], f"{kind} {key} (no ray grads)")
     assert n == to_np(out[0]).shape[0]
 
 

@@ -147,6 +147,13 @@ def test_rasterize_fwd_bwd_match_oracle(c1, cuda):
     assert_grads_close(v_colors, rg["v_colors"], "v_colors")
     assert_grads_close(v_ro, rg["v_ray_o"], "v_ray_o")
     assert_grads_close(v_rd, rg["v_ray_d"], "v_ray_d")
+    # without ray gradients (the variant that factors the shared ray origin
+    # out of the per-pixel sums): same Gaussian gradients, no ray outputs
+    fast = _C.rasterize_eval3d_bwd(g(sc.means), g(sc.scales), g(sc.quats), g(sc.opacities), g(colors), ro, rd,
+                                   16, 16, off, flat, alpha, last, g(vr), g(vd), g(va), ray_grads=False)
+    assert fast[5] is None and fast[6] is None
+    for got, key in zip(fast[:5], ["v_means", "v_quats", "v_scales", "v_opacities", "v_colors"]):
+        assert_grads_close(got, rg[key], key + " (no ray grads)")
 
 
 @pytest.mark.parametrize("degree", [0, 1, 2, 3, 4])

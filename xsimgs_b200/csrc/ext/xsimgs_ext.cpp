@@ -54,6 +54,8 @@ Tensor workspace(size_t bytes, const Tensor& like) {
 
 bool has(const OptT& t) { return t.has_value() && t->defined(); }
 
+py::object opt(const Tensor& t) { return t.defined() ? py::cast(t) : py::none(); }
+
 // -------------------------------------------------------------- cameras --
 enum class ProjectionMode : int { Central = 0, NegativeDelta = 1, PositiveDelta = 2 };
 
@@ -381,7 +383,7 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
                   const Tensor& opacity, const OptT& colors, const Tensor& ray_o, const Tensor& ray_d,
                   const OptT& ray_t, int64_t tsx, int64_t tsy, const Tensor& tile_offsets, const Tensor& flatten_ids,
                   const Tensor& render_alpha, const Tensor& last_ids, const OptT& v_colors_in, const Tensor& v_depth,
-                  const Tensor& v_alpha) {
+                  const Tensor& v_alpha, bool ray_grads) {
     if (has(v_colors_in) && !v_colors_in->is_contiguous())
         throw std::runtime_error("v_render_colors must be contiguous");
     for (auto* t : {&points, &scale, &quat, &opacity, &ray_o, &ray_d, &tile_offsets, &flatten_ids, &render_alpha,
@@ -399,12 +401,14 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
     o.v_quat = at::empty_like(quat);
     o.v_opacity = at::empty_like(opacity);
     if (has(colors)) o.v_colors = at::empty_like(*colors);
-    o.v_ray_o = at::empty_like(ray_o);
-    o.v_ray_d = at::empty_like(ray_d);
+    if (ray_grads) {
+        o.v_ray_o = at::empty_like(ray_o);
+        o.v_ray_d = at::empty_like(ray_d);
+    }
     const bool dyn = has(velocity);
     if (dyn) {
         o.v_velocity = at::empty_like(*velocity);
-        o.v_time = at::empty_like(*ray_t);
+        if (ray_grads) o.v_time = at::empty_like(*ray_t);
     }
     Tensor ws = workspace(xsg_rasterize_workspace_size(n, int(cdim)), points);
     check(xsg_rasterize_bwd(fptr(points), fptr(velocity), fptr(quat), fptr(scale), fptr(colors), int(cdim),
@@ -414,8 +418,9 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
                             fptr(render_alpha), last_ids.data_ptr<int32_t>(), fptr(v_colors_in), fptr(v_depth),
                             fptr(v_alpha), fptr_mut(o.v_points), dyn ? fptr_mut(o.v_velocity) : nullptr,
                             fptr_mut(o.v_quat), fptr_mut(o.v_scale), has(colors) ? fptr_mut(*o.v_colors) : nullptr,
-                            fptr_mut(o.v_opacity), fptr_mut(o.v_ray_o), fptr_mut(o.v_ray_d),
-                            dyn ? fptr_mut(o.v_time) : nullptr, ws.data_ptr(), size_t(ws.numel()), stream()));
+                            fptr_mut(o.v_opacity), ray_grads ? fptr_mut(o.v_ray_o) : nullptr,
+                            ray_grads ? fptr_mut(o.v_ray_d) : nullptr, dyn && ray_grads ? fptr_mut(o.v_time) : nullptr,
+                            ws.data_ptr(), size_t(ws.numel()), stream()));
     return o;
 }
 
@@ -650,25 +655,38 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           [](const Tensor& points, const Tensor& scale, const Tensor& quat, const Tensor& opacity, const OptT& colors,
              const Tensor& ray_o, const Tensor& ray_d, int64_t tsx, int64_t tsy, const Tensor& offsets,
              const Tensor& flatten, const Tensor& render_alpha, const Tensor& last_ids, const OptT& v_colors,
-             const Tensor& v_depth, const Tensor& v_alpha) {
+             const Tensor& v_depth, const Tensor& v_alpha, bool ray_grads) {
               BwdOut o = raster_bwd(points, std::nullopt, scale, quat, opacity, colors, ray_o, ray_d, std::nullopt,
-                                    tsx, tsy, offsets, flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha);
+                                    tsx, tsy, offsets, flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha,
+                                    ray_grads);
               return py::make_tuple(o.v_points, o.v_quat, o.v_scale, o.v_opacity,
-                                    o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), o.v_ray_o, o.v_ray_d);
-          });
+                                    o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), opt(o.v_ray_o),
+                                    opt(o.v_ray_d));
+          },
+          py::arg("points"), py::arg("scale"), py::arg("quat"), py::arg("opacity"), py::arg("colors"),
+          py::arg("ray_origins"), py::arg("ray_directions"), py::arg("tile_size_x"), py::arg("tile_size_y"),
+          py::arg("tile_offsets"), py::arg("flatten_ids"), py::arg("render_alpha"), py::arg("last_ids"),
+          py::arg("v_render_colors"), py::arg("v_render_depth"), py::arg("v_render_alpha"),
+          py::arg("ray_grads") = true);
     m.def("rasterize_eval3d_dynamic_bwd",
           [](const Tensor& points, const Tensor& vel, const Tensor& scale, const Tensor& quat, const Tensor& opacity,
              const OptT& colors, const Tensor& ray_o, const Tensor& ray_d, const Tensor& ray_t, int64_t tsx,
              int64_t tsy, const Tensor& offsets, const Tensor& flatten, const Tensor& render_alpha,
-             const Tensor& last_ids, const OptT& v_colors, const Tensor& v_depth, const Tensor& v_alpha) {
+             const Tensor& last_ids, const OptT& v_colors, const Tensor& v_depth, const Tensor& v_alpha,
+             bool ray_grads) {
               check_tensor(vel, "velocity", points);
               check_tensor(ray_t, "ray_time_delta", points);
               BwdOut o = raster_bwd(points, vel, scale, quat, opacity, colors, ray_o, ray_d, ray_t, tsx, tsy, offsets,
-                                    flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha);
+                                    flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha, ray_grads);
               return py::make_tuple(o.v_points, o.v_velocity, o.v_quat, o.v_scale, o.v_opacity,
-                                    o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), o.v_ray_o, o.v_ray_d,
-                                    o.v_time);
-          });
+                                    o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), opt(o.v_ray_o),
+                                    opt(o.v_ray_d), opt(o.v_time));
+          },
+          py::arg("points"), py::arg("velocity"), py::arg("scale"), py::arg("quat"), py::arg("opacity"),
+          py::arg("colors"), py::arg("ray_origins"), py::arg("ray_directions"), py::arg("ray_time_delta"),
+          py::arg("tile_size_x"), py::arg("tile_size_y"), py::arg("tile_offsets"), py::arg("flatten_ids"),
+          py::arg("render_alpha"), py::arg("last_ids"), py::arg("v_render_colors"), py::arg("v_render_depth"),
+          py::arg("v_render_alpha"), py::arg("ray_grads") = true);
 
     m.def("spherical_harmonics_fused_fwd", &sh_fwd, py::arg("degree_to_use"), py::arg("origin"),
           py::arg("positions"), py::arg("coeffs"), py::arg("mask"), py::arg("layout_3kn"),

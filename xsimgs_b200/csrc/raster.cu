@@ -500,12 +500,18 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
 // dL/dM is summed over all pixels and the reference's per-pair
 // quat_scale_to_preci_half_vjp (rasterization/utils.h:232-263) is applied
 // once per Gaussian in the finalize pass.
-template <int CDIM, bool kDyn>
+//   factored warps (static scene, no ray gradients, see raster_bwd_kernel):
+//   kFactSlot + 0-2 sum of v_gro, + 3 v_opacity.
+template <int CDIM, bool kDyn, bool kRayGrad>
 struct Acc {
     static constexpr int kExtraColor = (CDIM == 4) ? 1 : 0;
     static constexpr int kVel = 16 + kExtraColor;
-    static constexpr int N = (kDyn || CDIM == 4) ? 20 : 16;
+    static constexpr bool kFact = !kDyn && !kRayGrad;
+    static constexpr int kFactSlot = (CDIM == 4) ? 20 : 16;
+    static constexpr int N = kFact ? kFactSlot + 4 : ((kDyn || CDIM == 4) ? 20 : 16);
 };
+// largest accumulator width of any variant (floats per Gaussian)
+constexpr int kMaxAcc = 24;
 
 // Transpose butterfly: on entry every lane holds v[0..15]; on exit lane L
 // holds in v[0] the warp-wide sum of value index (L >> 1) & 15.
@@ -550,11 +556,21 @@ __device__ __forceinline__ float warp_sum(float v) {
 // front from its own last contributor, and every (warp, Gaussian) event with a
 // contributing lane is reduced in registers (butterfly) and added to the
 // Gaussian's accumulator with four vector reductions.
-template <int CDIM, bool kDyn>
+//
+// kRayGrad = false skips the per-pixel ray gradients (v_ray_o, v_ray_d,
+// v_ray_time_delta), which callers whose rays need no gradient do not use.
+// Then, in a warp whose pixels all share the ray origin of pixel 0 (static
+// scenes, global shutter), the terms linear in (o - mu) are factored out of
+// the per-pixel sums: each lane contributes v_gro instead of
+// v_mean = -M^T v_gro and only the v_grd (x) d part of dL/dM, the warp sums go
+// to the accumulator's factored slots, and the finalize pass adds
+// sum(v_gro) (x) (o - mu) to dL/dM and -M^T sum(v_gro) to v_mean once per
+// Gaussian.
+template <int CDIM, bool kDyn, bool kRayGrad>
 __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     constexpr bool kStageColor = CDIM > 0 && CDIM <= 4;
     constexpr int CSZ = CDIM > 0 ? CDIM : 1;
-    using AC = Acc<CDIM, kDyn>;
+    using AC = Acc<CDIM, kDyn, kRayGrad>;
     constexpr int NA = AC::N;
     extern __shared__ float4 smem4[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -600,6 +616,10 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
                                                           __float_as_uint(o.z) == __float_as_uint(o0.z) &&
                                                           (!kDyn || rt == rt0)));
     const DirQ dq = dir_q(d);
+    // warp-uniform: every pixel of the warp has pixel 0's ray origin
+    const bool fact = AC::kFact && qcull && __float_as_uint(o0.x) == __float_as_uint(a.ray_o[0]) &&
+                      __float_as_uint(o0.y) == __float_as_uint(a.ray_o[1]) &&
+                      __float_as_uint(o0.z) == __float_as_uint(a.ray_o[2]);
     // this warp's last contributor bounds where it starts
     int32_t wmax = bin_final;
 #pragma unroll
@@ -716,25 +736,36 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
                     } else {
                         v_grd = v_grd + v_gn;
                     }
-                    // v_(o - mu) = M^T v_gro ; v_ray_d = M^T v_grd
-                    const v3 v_omm = mk3(r0.x * v_gro.x + r1.x * v_gro.y + r2.x * v_gro.z,
-                                         r0.y * v_gro.x + r1.y * v_gro.y + r2.y * v_gro.z,
-                                         r0.z * v_gro.x + r1.z * v_gro.y + r2.z * v_gro.z);
-                    const v3 v_d = mk3(r0.x * v_grd.x + r1.x * v_grd.y + r2.x * v_grd.z,
-                                       r0.y * v_grd.x + r1.y * v_grd.y + r2.y * v_grd.z,
-                                       r0.z * v_grd.x + r1.z * v_grd.y + r2.z * v_grd.z);
-                    gv[0] = -v_omm.x; gv[1] = -v_omm.y; gv[2] = -v_omm.z;
-                    vro = vro + v_omm;
-                    vrd = vrd + v_d;
-                    if (kDyn) {
-                        gvel[0] = -v_omm.x * rt; gvel[1] = -v_omm.y * rt; gvel[2] = -v_omm.z * rt;
-                        vtime += -dot3(v_omm, vel);
+                    if (kRayGrad || kDyn || !fact) {
+                        // v_(o - mu) = M^T v_gro
+                        const v3 v_omm = mk3(r0.x * v_gro.x + r1.x * v_gro.y + r2.x * v_gro.z,
+                                             r0.y * v_gro.x + r1.y * v_gro.y + r2.y * v_gro.z,
+                                             r0.z * v_gro.x + r1.z * v_gro.y + r2.z * v_gro.z);
+                        gv[0] = -v_omm.x; gv[1] = -v_omm.y; gv[2] = -v_omm.z;
+                        if constexpr (kRayGrad) {
+                            // v_ray_d = M^T v_grd
+                            const v3 v_d = mk3(r0.x * v_grd.x + r1.x * v_grd.y + r2.x * v_grd.z,
+                                               r0.y * v_grd.x + r1.y * v_grd.y + r2.y * v_grd.z,
+                                               r0.z * v_grd.x + r1.z * v_grd.y + r2.z * v_grd.z);
+                            vro = vro + v_omm;
+                            vrd = vrd + v_d;
+                            if (kDyn) vtime += -dot3(v_omm, vel);
+                        }
+                        if (kDyn) {
+                            gvel[0] = -v_omm.x * rt; gvel[1] = -v_omm.y * rt; gvel[2] = -v_omm.z * rt;
+                        }
+                    } else {
+                        gv[0] = v_gro.x; gv[1] = v_gro.y; gv[2] = v_gro.z;
                     }
                     gv[3] = vis * v_alpha;
-                    // dL/dM row i = v_grd[i] d + v_gro[i] (o - mu)
-                    const v3 vM0 = v_grd.x * d + v_gro.x * omm;
-                    const v3 vM1 = v_grd.y * d + v_gro.y * omm;
-                    const v3 vM2 = v_grd.z * d + v_gro.z * omm;
+                    // dL/dM row i = v_grd[i] d + v_gro[i] (o - mu); in factored
+                    // warps the finalize pass adds the second term
+                    v3 vM0 = v_grd.x * d, vM1 = v_grd.y * d, vM2 = v_grd.z * d;
+                    if (!fact) {
+                        vM0 = vM0 + v_gro.x * omm;
+                        vM1 = vM1 + v_gro.y * omm;
+                        vM2 = vM2 + v_gro.z * omm;
+                    }
                     gv[4] = vM0.x; gv[5] = vM0.y; gv[6] = vM0.z;
                     gv[7] = vM1.x; gv[8] = vM1.y; gv[9] = vM1.z;
                     gv[10] = vM2.x; gv[11] = vM2.y; gv[12] = vM2.z;
@@ -753,8 +784,10 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
             const float g2 = __shfl_down_sync(0xffffffffu, gv[0], 4);
             const float g3 = __shfl_down_sync(0xffffffffu, gv[0], 6);
             float* dst = a.G + int64_t(sid[t]) * NA;
-            if ((lane & 7) == 0) red_add_v4(dst + (lane >> 1), gv[0], g1, g2, g3);
-            if constexpr (NA > 16) {
+            // a factored warp's first group (sum of v_gro, v_opacity) goes to its own slots
+            const int slot = (fact && lane == 0) ? AC::kFactSlot : (lane >> 1);
+            if ((lane & 7) == 0) red_add_v4(dst + slot, gv[0], g1, g2, g3);
+            if constexpr (CDIM == 4 || kDyn) {
                 float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
                 if constexpr (CDIM == 4) e0 = warp_sum(gcol[3]);
                 if constexpr (kDyn) {
@@ -774,7 +807,7 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
         }
         __syncwarp();
     }
-    if (inside) {
+    if (kRayGrad && inside) {
         st3(a.v_ray_o + 3 * c.pix, vro);
         st3(a.v_ray_d + 3 * c.pix, vrd);
         if (kDyn) a.v_ray_t[c.pix] = vtime;
@@ -783,13 +816,14 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
 
 // Accumulator -> output layout, with the quaternion / scale VJP of the summed
 // dL/dM (quat_scale_to_preci_half_vjp, rasterization/utils.h:208-263).
-template <int CDIM, bool kDyn>
+template <int CDIM, bool kDyn, bool kRayGrad>
 __global__ void grads_finalize_kernel(const float* __restrict__ G, const float* __restrict__ quats,
-                                      const float* __restrict__ scales, int64_t n, float* __restrict__ v_means,
+                                      const float* __restrict__ scales, const float* __restrict__ means,
+                                      const float* __restrict__ ray_o, int64_t n, float* __restrict__ v_means,
                                       float* __restrict__ v_vel, float* __restrict__ v_quats,
                                       float* __restrict__ v_scales, float* __restrict__ v_opac,
                                       float* __restrict__ v_colors) {
-    using AC = Acc<CDIM, kDyn>;
+    using AC = Acc<CDIM, kDyn, kRayGrad>;
     constexpr int NA = AC::N;
     const int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (g >= n) return;
@@ -800,9 +834,7 @@ __global__ void grads_finalize_kernel(const float* __restrict__ G, const float* 
         const float4 v = s[k];
         A[4 * k] = v.x; A[4 * k + 1] = v.y; A[4 * k + 2] = v.z; A[4 * k + 3] = v.w;
     }
-    v_means[3 * g] = A[0]; v_means[3 * g + 1] = A[1]; v_means[3 * g + 2] = A[2];
-    v_opac[g] = A[3];
-    const v3 vM0 = mk3(A[4], A[5], A[6]), vM1 = mk3(A[7], A[8], A[9]), vM2 = mk3(A[10], A[11], A[12]);
+    v3 vM0 = mk3(A[4], A[5], A[6]), vM1 = mk3(A[7], A[8], A[9]), vM2 = mk3(A[10], A[11], A[12]);
     float w = quats[4 * g], x = quats[4 * g + 1], y = quats[4 * g + 2], z = quats[4 * g + 3];
     const float inv = rsqrtf(x * x + y * y + z * z + w * w);
     x *= inv; y *= inv; z *= inv; w *= inv;
@@ -814,6 +846,22 @@ __global__ void grads_finalize_kernel(const float* __restrict__ G, const float* 
     const v3 C1 = mk3(2.f * (xy - wz), 1.f - 2.f * (x2 + z2), 2.f * (yz + wx));
     const v3 C2 = mk3(2.f * (xz + wy), 2.f * (yz - wx), 1.f - 2.f * (x2 + y2));
     const float isx = 1.0f / scales[3 * g], isy = 1.0f / scales[3 * g + 1], isz = 1.0f / scales[3 * g + 2];
+    v3 vmean = mk3(A[0], A[1], A[2]);
+    float vop = A[3];
+    if constexpr (AC::kFact) {
+        // factored warps: s = sum(v_gro) over pixels with the origin o of pixel 0
+        constexpr int F = AC::kFactSlot;
+        const v3 sg = mk3(A[F], A[F + 1], A[F + 2]);
+        vop += A[F + 3];
+        const v3 om = mk3(ray_o[0], ray_o[1], ray_o[2]) - ld3(means + 3 * g);
+        vM0 = vM0 + sg.x * om;
+        vM1 = vM1 + sg.y * om;
+        vM2 = vM2 + sg.z * om;
+        // row i of M = C_i / s_i:  v_mean -= M^T s
+        vmean = vmean - ((sg.x * isx) * C0 + (sg.y * isy) * C1 + (sg.z * isz) * C2);
+    }
+    v_means[3 * g] = vmean.x; v_means[3 * g + 1] = vmean.y; v_means[3 * g + 2] = vmean.z;
+    v_opac[g] = vop;
     v_scales[3 * g] = -isx * isx * dot3(C0, vM0);
     v_scales[3 * g + 1] = -isy * isy * dot3(C1, vM1);
     v_scales[3 * g + 2] = -isz * isz * dot3(C2, vM2);
@@ -862,18 +910,19 @@ struct FinalizeOut {
     float *v_means, *v_vel, *v_quats, *v_scales, *v_opac, *v_colors;
 };
 
-template <int CDIM, bool kDyn>
+template <int CDIM, bool kDyn, bool kRayGrad>
 static int launch_bwd(const RasterArgs& a, int bs, cudaStream_t st, int64_t n_gauss, FinalizeOut fin) {
-    const size_t sm = bwd_smem(bs, Acc<CDIM, kDyn>::N);
-    auto fn = raster_bwd_kernel<CDIM, kDyn>;
+    const size_t sm = bwd_smem(bs, Acc<CDIM, kDyn, kRayGrad>::N);
+    auto fn = raster_bwd_kernel<CDIM, kDyn, kRayGrad>;
     if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
     {
         ScopedTimer tm("rasterize_bwd", st);
         launch(fn, unsigned(a.ntx * a.nty), bs, sm, st, a);
     }
     if (a.G && n_gauss > 0)
-        launch(grads_finalize_kernel<CDIM, kDyn>, blocks_for(n_gauss, 256), 256, 0, st, a.G, a.quats, a.scales,
-               n_gauss, fin.v_means, fin.v_vel, fin.v_quats, fin.v_scales, fin.v_opac, fin.v_colors);
+        launch(grads_finalize_kernel<CDIM, kDyn, kRayGrad>, blocks_for(n_gauss, 256), 256, 0, st, a.G, a.quats,
+               a.scales, a.means, a.ray_o, n_gauss, fin.v_means, fin.v_vel, fin.v_quats, fin.v_scales, fin.v_opac,
+               fin.v_colors);
     return check_launch("rasterize_bwd");
 }
 
@@ -913,7 +962,8 @@ size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim) {
     (void)cdim;
     if (n_gauss < 0) n_gauss = 0;
     // packed records + the (dynamic-sized) gradient accumulator
-    return Arena::round(size_t(n_gauss) * kRecF4 * sizeof(float4)) + Arena::round(size_t(n_gauss) * 20 * sizeof(float)) +
+    return Arena::round(size_t(n_gauss) * kRecF4 * sizeof(float4)) +
+           Arena::round(size_t(n_gauss) * kMaxAcc * sizeof(float)) +
            Arena::round(size_t(kMaxTiles) * sizeof(int32_t));
 }
 
@@ -974,16 +1024,20 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     if (rc != XSG_OK) return rc;
     const bool dyn = velocity != nullptr;
     XSG_REQUIRE(means && quats && scales && opacities && ray_o && ray_d && tile_offsets && render_alphas &&
-                    last_ids && v_depths && v_alphas && v_means && v_quats && v_scales && v_opacities &&
-                    v_ray_o && v_ray_d, "rasterize_bwd: null argument");
+                    last_ids && v_depths && v_alphas && v_means && v_quats && v_scales && v_opacities,
+                "rasterize_bwd: null argument");
+    // the ray gradients are all requested or all skipped
+    const bool ray_grads = v_ray_o != nullptr;
+    XSG_REQUIRE((v_ray_d != nullptr) == ray_grads && (!dyn || (v_ray_time_delta != nullptr) == ray_grads),
+                "rasterize_bwd: pass all of v_ray_o / v_ray_d (/ v_ray_time_delta) or none");
     XSG_REQUIRE(cdim == 0 || (colors && v_colors), "rasterize_bwd: colors required");
-    XSG_REQUIRE(!dyn || (ray_time_delta && v_velocity && v_ray_time_delta),
-                "rasterize_dynamic_bwd: ray_time_delta is required");
+    XSG_REQUIRE(!dyn || (ray_time_delta && v_velocity), "rasterize_dynamic_bwd: ray_time_delta is required");
     XSG_REQUIRE(n_isects == 0 || flatten_ids, "rasterize_bwd: null flatten_ids");
     cudaStream_t st = as_cuda(stream);
     Arena ar(workspace, ws_bytes);
     float4* rec = ar.take<float4>(size_t(n_gauss) * kRecF4);
-    const int na = (dyn || cdim == 4) ? 20 : 16;  // Acc<CDIM, kDyn>::N
+    // Acc<CDIM, kDyn, kRayGrad>::N
+    const int na = (!dyn && !ray_grads) ? (cdim == 4 ? 24 : 20) : ((dyn || cdim == 4) ? 20 : 16);
     float* G = ar.take<float>(size_t(n_gauss) * na);
     const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
     int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
@@ -1012,7 +1066,10 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     int lrc = XSG_OK;
 #define XSG_BWD_CASE(C)                                                                          \
     case C:                                                                                      \
-        lrc = dyn ? launch_bwd<C, true>(a, bs, st, n_gauss, fin) : launch_bwd<C, false>(a, bs, st, n_gauss, fin); \
+        lrc = dyn ? (ray_grads ? launch_bwd<C, true, true>(a, bs, st, n_gauss, fin)                \
+                               : launch_bwd<C, true, false>(a, bs, st, n_gauss, fin))              \
+                  : (ray_grads ? launch_bwd<C, false, true>(a, bs, st, n_gauss, fin)               \
+                               : launch_bwd<C, false, false>(a, bs, st, n_gauss, fin));            \
         break;
     switch (cdim) {
         XSG_CDIM_CASES(XSG_BWD_CASE)

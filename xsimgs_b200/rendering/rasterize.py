@@ -39,7 +39,8 @@ class UTGSRasterize(torch.autograd.Function):
     def backward(ctx, grad_rgb, grad_depth, grad_alpha):
         (positions, rotation, scale, density, colors, ray_o, ray_d,
          isect_offsets, flatten_ids, out_alpha, last_ids) = ctx.saved_tensors
-        # v_points, v_quat, v_scale, v_opacity, v_colors, v_ray_o, v_ray_d
+        # v_points, v_quat, v_scale, v_opacity, v_colors, v_ray_o, v_ray_d; the
+        # per-pixel ray gradients are computed only when a ray needs them
         grads = _C.rasterize_eval3d_bwd(
             positions, scale, rotation, density, colors, ray_o, ray_d,
             ctx.tile_size_x, ctx.tile_size_y, isect_offsets, flatten_ids,
@@ -47,6 +48,7 @@ class UTGSRasterize(torch.autograd.Function):
             grad_rgb.contiguous() if grad_rgb is not None else None,
             grad_depth.contiguous(),
             grad_alpha.contiguous(),
+            ray_grads=bool(ctx.needs_input_grad[5] or ctx.needs_input_grad[6]),
         )
         return apply_grad_mask(ctx, list(grads) + [None, None, None, None])
 

@@ -51,6 +51,7 @@ class UTGSDynamicRasterize(torch.autograd.Function):
             grad_rgb.contiguous() if grad_rgb is not None else None,
             grad_depth.contiguous(),
             grad_alpha.contiguous(),
+            ray_grads=bool(ctx.needs_input_grad[6] or ctx.needs_input_grad[7] or ctx.needs_input_grad[8]),
         )
         return apply_grad_mask(ctx, list(grads) + [None, None, None, None])
 

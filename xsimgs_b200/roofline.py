@@ -30,16 +30,22 @@ def fwd_contrib(cdim: int) -> int:
     return 18 + 2 * cdim
 
 
-def bwd_contrib(cdim: int) -> int:
-    return 315 + 7 * cdim
+# per contributing pair, only for the per-pixel ray gradients (v_ray_d =
+# M^T v_grd: 9 mul + 6 add; accumulating v_ray_o / v_ray_d: 6 add); a
+# backward that is not asked for ray gradients does not owe them
+RAY_GRAD_FLOPS = 21
+
+
+def bwd_contrib(cdim: int, ray_grads: bool = True) -> int:
+    return 315 + 7 * cdim - (0 if ray_grads else RAY_GRAD_FLOPS)
 
 
 def fwd_flops(n_eval: int, n_contrib: int, cdim: int) -> float:
     return float(FWD_EVAL * n_eval + fwd_contrib(cdim) * n_contrib)
 
 
-def bwd_flops(n_eval_bwd: int, n_contrib: int, cdim: int) -> float:
-    return float(BWD_EVAL * n_eval_bwd + bwd_contrib(cdim) * n_contrib)
+def bwd_flops(n_eval_bwd: int, n_contrib: int, cdim: int, ray_grads: bool = True) -> float:
+    return float(BWD_EVAL * n_eval_bwd + bwd_contrib(cdim, ray_grads) * n_contrib)
 
 
 # DRAM bytes per launch of the compositing backward on the C2 view (1M
