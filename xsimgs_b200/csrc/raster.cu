@@ -29,6 +29,7 @@ constexpr int kRecF4 = 4;  // float4 words per Gaussian record
 
 struct RasterArgs {
     const float4* rec;        // [N][4]
+    const float4* ext;        // [N][3] view constants for rays from ray_o[0] (static scenes; may be null)
     const float* means;       // [N,3] (bwd)
     const float* quats;       // [N,4] (bwd)
     const float* scales;      // [N,3] (bwd)
@@ -65,11 +66,16 @@ static unsigned long long* g_pair_counters = nullptr;
 constexpr int64_t kMaxTiles = int64_t(1) << 20;
 
 // --------------------------------------------------------------- pack ----
+__device__ __forceinline__ void view_consts(float4 r0, float4 r1, float4 r2, float4 r3, v3 o, float4* e);
+
 // quat_to_rotmat (rasterization/utils.h:61-83) and S^-1 R^T
-// (eval3d_fwd.cu:92-106): row i of M is (1 / s_i) * column i of R.
+// (eval3d_fwd.cu:92-106): row i of M is (1 / s_i) * column i of R.  With
+// `ext` (static scenes) also the view constants of the rays that start at
+// o_ref[0..2], the origin of pixel 0.
 __global__ void pack_records_kernel(const float* __restrict__ means, const float* __restrict__ vel,
                                     const float* __restrict__ quats, const float* __restrict__ scales,
-                                    const float* __restrict__ opac, int64_t n, float4* __restrict__ rec) {
+                                    const float* __restrict__ opac, int64_t n, float4* __restrict__ rec,
+                                    const float* __restrict__ o_ref, float4* __restrict__ ext) {
     const int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (g >= n) return;
     float w = quats[4 * g], x = quats[4 * g + 1], y = quats[4 * g + 2], z = quats[4 * g + 3];
@@ -84,11 +90,13 @@ __global__ void pack_records_kernel(const float* __restrict__ means, const float
     const float c20 = 2.f * (xz + wy), c21 = 2.f * (yz - wx), c22 = 1.f - 2.f * (x2 + y2);
     const float sx = 1.0f / scales[3 * g], sy = 1.0f / scales[3 * g + 1], sz = 1.0f / scales[3 * g + 2];
     float4* r = rec + kRecF4 * g;
-    r[0] = make_float4(sx * c00, sx * c01, sx * c02, means[3 * g]);
-    r[1] = make_float4(sy * c10, sy * c11, sy * c12, means[3 * g + 1]);
-    r[2] = make_float4(sz * c20, sz * c21, sz * c22, means[3 * g + 2]);
-    if (vel) r[3] = make_float4(opac[g], vel[3 * g], vel[3 * g + 1], vel[3 * g + 2]);
-    else r[3] = make_float4(opac[g], 0.f, 0.f, 0.f);
+    const float4 q0 = make_float4(sx * c00, sx * c01, sx * c02, means[3 * g]);
+    const float4 q1 = make_float4(sy * c10, sy * c11, sy * c12, means[3 * g + 1]);
+    const float4 q2 = make_float4(sz * c20, sz * c21, sz * c22, means[3 * g + 2]);
+    const float4 q3 = vel ? make_float4(opac[g], vel[3 * g], vel[3 * g + 1], vel[3 * g + 2])
+                          : make_float4(opac[g], 0.f, 0.f, 0.f);
+    r[0] = q0; r[1] = q1; r[2] = q2; r[3] = q3;
+    if (ext) view_consts(q0, q1, q2, q3, mk3(o_ref[0], o_ref[1], o_ref[2]), ext + 3 * g);
 }
 
 // Heavy tiles first: tiles bucketed by floor(log2(intersection count)),
@@ -230,20 +238,28 @@ __device__ __forceinline__ WarpCone warp_cone(bool inside, v3 o, v3 d, float rt)
     return w;
 }
 
-// true: some line of the warp's cone may see alpha >= 1/255 of this Gaussian
-__device__ __forceinline__ bool cone_may_hit(const WarpCone& w, float4 r0, float4 r1, float4 r2, float4 r3,
-                                             bool dyn) {
-    if (!w.on) return true;
+// Radius of the sphere around mu that holds the Gaussian's alpha >= 1/255
+// region: negative when the Gaussian is nowhere visible (opacity <= 1/255),
+// infinite when no bound is known (keep it).
+__device__ __forceinline__ float cone_radius(float4 r0, float4 r1, float4 r2, float4 r3) {
     const float op = r3.x;
-    if (!(op * 255.0f > 1.0f)) return false;  // alpha <= opacity < 1/255 everywhere
+    if (!(op * 255.0f > 1.0f)) return -1.0f;  // alpha <= opacity < 1/255 everywhere
     const float m0 = r0.x * r0.x + r0.y * r0.y + r0.z * r0.z;
     const float m1 = r1.x * r1.x + r1.y * r1.y + r1.z * r1.z;
     const float m2 = r2.x * r2.x + r2.y * r2.y + r2.z * r2.z;
     const float mmin = fminf(m0, fminf(m1, m2));  // 1 / s_max^2
-    if (!(mmin > 0.f) || !isfinite(op)) return true;
-    float R = sqrtf(2.0f * logf(op * 255.0f) / mmin);
-    if (dyn) R += w.rt_max * sqrtf(r3.y * r3.y + r3.z * r3.z + r3.w * r3.w);
-    const v3 v = mk3(r0.w, r1.w, r2.w) - w.oc;
+    if (!(mmin > 0.f) || !isfinite(op)) return INFINITY;
+    return sqrtf(2.0f * logf(op * 255.0f) / mmin);
+}
+
+// true: some line of the warp's cone may see alpha >= 1/255 of the Gaussian
+// at mu (moving with vel when dyn) whose cone_radius is R0
+__device__ __forceinline__ bool cone_may_hit_r(const WarpCone& w, float R0, v3 mu, v3 vel, bool dyn) {
+    if (!w.on) return true;
+    if (R0 < 0.0f) return false;
+    float R = R0;
+    if (dyn) R += w.rt_max * sqrtf(dot3(vel, vel));
+    const v3 v = mu - w.oc;
     const float vn = sqrtf(dot3(v, v));
     R = (R + w.r_o) * 1.01f + 1e-4f * vn + 1e-6f;
     if (!isfinite(R) || !isfinite(vn) || vn <= R) return true;
@@ -252,6 +268,12 @@ __device__ __forceinline__ bool cone_may_hit(const WarpCone& w, float4 r0, float
     const float sp = sqrtf(fmaxf(0.f, 1.0f - cp * cp));
     const float s_pt = sp * w.cos_t - cp * w.sin_t;  // sin(phi - theta) > 0
     return vn * s_pt <= R;
+}
+
+__device__ __forceinline__ bool cone_may_hit(const WarpCone& w, float4 r0, float4 r1, float4 r2, float4 r3,
+                                             bool dyn) {
+    if (!w.on) return true;
+    return cone_may_hit_r(w, cone_radius(r0, r1, r2, r3), mk3(r0.w, r1.w, r2.w), mk3(r3.y, r3.z, r3.w), dyn);
 }
 
 // Exact per-pixel pre-test for warps whose pixels share one ray origin o
@@ -306,6 +328,18 @@ __device__ __forceinline__ Quad make_quad(float4 r0, float4 r1, float4 r2, float
         !isfinite(q.b.y) || !isfinite(q.b.z))
         return quad_keep_all();
     return q;
+}
+
+// The warp-independent work of staging a Gaussian for rays from origin o,
+// done once per Gaussian by the pack pass: e[0] = quadric a, e[1] =
+// (quadric b.xyz, cone_radius), e[2] = (M (o - mu), 0).
+__device__ __forceinline__ void view_consts(float4 r0, float4 r1, float4 r2, float4 r3, v3 o, float4* e) {
+    const v3 mu = mk3(r0.w, r1.w, r2.w);
+    const Quad q = make_quad(r0, r1, r2, r3.x, mu, o);
+    const v3 gro = mrows(r0, r1, r2, o - mu);
+    e[0] = q.a;
+    e[1] = make_float4(q.b.x, q.b.y, q.b.z, cone_radius(r0, r1, r2, r3));
+    e[2] = make_float4(gro.x, gro.y, gro.z, 0.f);
 }
 
 // per-lane direction products for the quadric pre-test
@@ -366,6 +400,10 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
     // the quadric pre-test needs one origin (and one time offset) per warp
     const float rt0 = __shfl_sync(0xffffffffu, rt, 0);
     const bool qcull = __all_sync(0xffffffffu, same && (!kDyn || !c.inside || rt == rt0));
+    // rays from pixel 0's origin: the pack pass has the view constants
+    const bool gref = !kDyn && a.ext && uni && __float_as_uint(o0.x) == __float_as_uint(a.ray_o[0]) &&
+                      __float_as_uint(o0.y) == __float_as_uint(a.ray_o[1]) &&
+                      __float_as_uint(o0.z) == __float_as_uint(a.ray_o[2]);
     const DirQ dq = dir_q(d);
 
     bool done = !c.inside;
@@ -385,19 +423,30 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
             const float4* r = a.rec + int64_t(kRecF4) * g;
             float4 r0 = r[0], r1 = r[1], r2 = r[2];
             const float4 r3 = r[3];
-            keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
             Quad qd = quad_keep_all();
-            if (qcull && keep) {
-                v3 mu = mk3(r0.w, r1.w, r2.w);
-                if (kDyn) mu = mu + rt0 * mk3(r3.y, r3.z, r3.w);
-                qd = make_quad(r0, r1, r2, r3.x, mu, o0);
+            if (gref) {
+                const float4* e = a.ext + 3 * int64_t(g);
+                const float4 e0 = e[0], e1 = e[1], e2 = e[2];
+                keep = cone_may_hit_r(cone, e1.w, mk3(r0.w, r1.w, r2.w), mk3(0.f, 0.f, 0.f), false);
+                if (keep) {
+                    qd.a = e0;
+                    qd.b = make_float4(e1.x, e1.y, e1.z, 0.f);
+                }
+                r0.w = e2.x; r1.w = e2.y; r2.w = e2.z;  // M (o - mu)
+            } else {
+                keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
+                if (qcull && keep) {
+                    v3 mu = mk3(r0.w, r1.w, r2.w);
+                    if (kDyn) mu = mu + rt0 * mk3(r3.y, r3.z, r3.w);
+                    qd = make_quad(r0, r1, r2, r3.x, mu, o0);
+                }
+                if (uni) {
+                    const v3 gro = mrows(r0, r1, r2, o0 - mk3(r0.w, r1.w, r2.w));
+                    r0.w = gro.x; r1.w = gro.y; r2.w = gro.z;
+                }
             }
             sqa[lane] = qd.a;
             sqb[lane] = qd.b;
-            if (uni) {
-                const v3 gro = mrows(r0, r1, r2, o0 - mk3(r0.w, r1.w, r2.w));
-                r0.w = gro.x; r1.w = gro.y; r2.w = gro.z;
-            }
             s0[lane] = r0; s1[lane] = r1; s2[lane] = r2; s3[lane] = r3;
             if constexpr (kStageColor) {
                 float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -574,14 +623,15 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     constexpr int NA = AC::N;
     extern __shared__ float4 smem4[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    float4* s0 = smem4 + wid * (7 * kWarpSlot);
+    float4* s0 = smem4 + wid * (8 * kWarpSlot);
     float4* s1 = s0 + kWarpSlot;
     float4* s2 = s1 + kWarpSlot;
     float4* s3 = s2 + kWarpSlot;
     float4* sc = s3 + kWarpSlot;
     float4* sqa = sc + kWarpSlot;
     float4* sqb = sqa + kWarpSlot;
-    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 7 * kWarpSlot) + wid * kWarpSlot;
+    float4* sgro = sqb + kWarpSlot;
+    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 8 * kWarpSlot) + wid * kWarpSlot;
 
     const TileCtx c = tile_ctx(a);
     const bool inside = c.inside;
@@ -617,9 +667,12 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
                                                           (!kDyn || rt == rt0)));
     const DirQ dq = dir_q(d);
     // warp-uniform: every pixel of the warp has pixel 0's ray origin
-    const bool fact = AC::kFact && qcull && __float_as_uint(o0.x) == __float_as_uint(a.ray_o[0]) &&
+    const bool oref = qcull && __float_as_uint(o0.x) == __float_as_uint(a.ray_o[0]) &&
                       __float_as_uint(o0.y) == __float_as_uint(a.ray_o[1]) &&
                       __float_as_uint(o0.z) == __float_as_uint(a.ray_o[2]);
+    const bool fact = AC::kFact && oref;
+    // rays from pixel 0's origin: the pack pass has the view constants
+    const bool gref = !kDyn && a.ext && oref;
     // this warp's last contributor bounds where it starts
     int32_t wmax = bin_final;
 #pragma unroll
@@ -631,12 +684,23 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
             const int32_t g = a.flatten[idx];
             const float4* r = a.rec + int64_t(kRecF4) * g;
             const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
-            keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
             Quad qd = quad_keep_all();
-            if (qcull && keep) {
-                v3 mu = mk3(r0.w, r1.w, r2.w);
-                if (kDyn) mu = mu + rt0 * mk3(r3.y, r3.z, r3.w);
-                qd = make_quad(r0, r1, r2, r3.x, mu, o0);
+            if (gref) {
+                const float4* e = a.ext + 3 * int64_t(g);
+                const float4 e0 = e[0], e1 = e[1];
+                sgro[lane] = e[2];  // M (o - mu)
+                keep = cone_may_hit_r(cone, e1.w, mk3(r0.w, r1.w, r2.w), mk3(0.f, 0.f, 0.f), false);
+                if (keep) {
+                    qd.a = e0;
+                    qd.b = make_float4(e1.x, e1.y, e1.z, 0.f);
+                }
+            } else {
+                keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
+                if (qcull && keep) {
+                    v3 mu = mk3(r0.w, r1.w, r2.w);
+                    if (kDyn) mu = mu + rt0 * mk3(r3.y, r3.z, r3.w);
+                    qd = make_quad(r0, r1, r2, r3.x, mu, o0);
+                }
             }
             sqa[lane] = qd.a;
             sqb[lane] = qd.b;
@@ -673,7 +737,13 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
             const v3 vel = mk3(r3.y, r3.z, r3.w);
             if (kDyn) mu = mu + rt * vel;
             const v3 omm = o - mu;
-            const v3 gro = mrows(r0, r1, r2, omm);
+            v3 gro;
+            if (gref) {
+                const float4 ge = sgro[t];
+                gro = mk3(ge.x, ge.y, ge.z);
+            } else {
+                gro = mrows(r0, r1, r2, omm);
+            }
             const v3 grd = mrows(r0, r1, r2, d);
             const float l = dot3(grd, grd);
             const v3 gn = l > 0.0f ? grd * rsqrtf(l) : grd;
@@ -892,7 +962,8 @@ __global__ void grads_finalize_kernel(const float* __restrict__ G, const float* 
 static const int kSupported[] = {0, 1, 2, 3, 4, 5, 8, 9, 16, 17, 32, 33, 64, 65, 128, 129, 256, 257, 512, 513};
 
 static size_t fwd_smem(int bs) { return size_t(bs / 32) * warp_stage_bytes(); }
-static size_t bwd_smem(int bs, int) { return size_t(bs / 32) * warp_stage_bytes(); }
+// the backward stages one more float4 per Gaussian (M (o - mu) of view-constant warps)
+static size_t bwd_smem(int bs, int) { return size_t(bs / 32) * (warp_stage_bytes() + kWarpSlot * sizeof(float4)); }
 
 template <int CDIM, bool kDyn>
 static int launch_fwd(const RasterArgs& a, int bs, cudaStream_t st) {
@@ -963,6 +1034,7 @@ size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim) {
     if (n_gauss < 0) n_gauss = 0;
     // packed records + the (dynamic-sized) gradient accumulator
     return Arena::round(size_t(n_gauss) * kRecF4 * sizeof(float4)) +
+           Arena::round(size_t(n_gauss) * 3 * sizeof(float4)) +
            Arena::round(size_t(n_gauss) * kMaxAcc * sizeof(float)) +
            Arena::round(size_t(kMaxTiles) * sizeof(int32_t));
 }
@@ -982,17 +1054,19 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
     cudaStream_t st = as_cuda(stream);
     Arena ar(workspace, ws_bytes);
     float4* rec = ar.take<float4>(size_t(n_gauss) * kRecF4);
+    float4* ext = ar.take<float4>(size_t(n_gauss) * 3);
     const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
     int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
-    if ((n_gauss > 0 && !rec) || (n_gauss > 0 && !workspace))
+    if ((n_gauss > 0 && (!rec || !ext)) || (n_gauss > 0 && !workspace))
         return set_error(XSG_ERR_WORKSPACE, "rasterize_fwd: workspace too small");
     const bool dyn = velocity != nullptr;
+    if (dyn) ext = nullptr;  // moving Gaussians: no per-view constants
     if (order) launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
     if (n_gauss > 0)
         launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales, opacities,
-                                                                      n_gauss, rec);
+               n_gauss, rec, ray_o, ext);
     RasterArgs a{};
-    a.rec = rec; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
+    a.rec = rec; a.ext = n_gauss > 0 ? ext : nullptr; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
     a.ray_o = ray_o; a.ray_d = ray_d; a.ray_t = ray_time_delta;
     a.offsets = tile_offsets; a.flatten = flatten_ids; a.n_isects = n_isects;
     a.W = W; a.H = H; a.tsx = tsx; a.tsy = tsy; a.ntx = tiles_w; a.nty = tiles_h;
@@ -1036,12 +1110,14 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     cudaStream_t st = as_cuda(stream);
     Arena ar(workspace, ws_bytes);
     float4* rec = ar.take<float4>(size_t(n_gauss) * kRecF4);
+    float4* ext = ar.take<float4>(size_t(n_gauss) * 3);
     // Acc<CDIM, kDyn, kRayGrad>::N
     const int na = (!dyn && !ray_grads) ? (cdim == 4 ? 24 : 20) : ((dyn || cdim == 4) ? 20 : 16);
     float* G = ar.take<float>(size_t(n_gauss) * na);
     const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
     int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
-    if (n_gauss > 0 && (!rec || !G)) return set_error(XSG_ERR_WORKSPACE, "rasterize_bwd: workspace too small");
+    if (n_gauss > 0 && (!rec || !ext || !G)) return set_error(XSG_ERR_WORKSPACE, "rasterize_bwd: workspace too small");
+    if (dyn) ext = nullptr;  // moving Gaussians: no per-view constants
     // every pixel of the image belongs to exactly one tile thread, which
     // writes its v_ray_o / v_ray_d (/ v_ray_time_delta): no pre-zeroing
     if (order) launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
@@ -1049,10 +1125,10 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
         XSG_CUDA(cudaMemsetAsync(G, 0, size_t(n_gauss) * na * sizeof(float), st));
         if (cdim > 4) XSG_CUDA(cudaMemsetAsync(v_colors, 0, size_t(n_gauss) * cdim * sizeof(float), st));
         launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales, opacities,
-                                                                      n_gauss, rec);
+               n_gauss, rec, ray_o, ext);
     }
     RasterArgs a{};
-    a.rec = rec; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
+    a.rec = rec; a.ext = n_gauss > 0 ? ext : nullptr; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
     a.ray_o = ray_o; a.ray_d = ray_d; a.ray_t = ray_time_delta;
     a.offsets = tile_offsets; a.flatten = flatten_ids; a.n_isects = n_isects;
     a.W = W; a.H = H; a.tsx = tsx; a.tsy = tsy; a.ntx = tiles_w; a.nty = tiles_h;
