@@ -262,7 +262,8 @@ def gpu_arm(args, world, rank, local):
             colors = X.spherical_harmonics_fused(leaves["sh"], leaves["means"], cam.t0, DEG_C2)
             color, depth, alpha, _ = X.ut_gs_render(cam, leaves["means"], leaves["scales"], leaves["quats"],
                                                     leaves["opacities"], sp.width, sp.height, colors=colors)
-            loss = loss + (color * gr).sum() + (depth * gd).sum() + (alpha * ga).sum()
+            loss = loss + (torch.dot(color.reshape(-1), gr.reshape(-1)) + torch.dot(depth.reshape(-1), gd.reshape(-1))
+                           + torch.dot(alpha.reshape(-1), ga.reshape(-1)))
         if views:
             loss.backward()
         red.wait()
@@ -335,7 +336,8 @@ def gpu_arm(args, world, rank, local):
                 v.grad = None
             color, depth, alpha, _ = X.ut_gs_render(lcam, leaves["means"], leaves["scales"], leaves["quats"],
                                                     leaves["opacities"], LW, LH, colors=inten, use_phm=phm)
-            ((color * lg[0]).sum() + (depth * lg[1]).sum() + (alpha * lg[2]).sum()).backward()
+            (torch.dot(color.reshape(-1), lg[0].reshape(-1)) + torch.dot(depth.reshape(-1), lg[1].reshape(-1))
+             + torch.dot(alpha.reshape(-1), lg[2].reshape(-1))).backward()
             red.wait()
 
         for phm in (False, True):

@@ -201,7 +201,10 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
  * v_colors [N, cdim] (NULL when cdim = 0), v_ray_o/v_ray_d [H, W, 3],
  * v_ray_time_delta [H, W] (dynamic only).  v_renders may be NULL.  Passing
  * NULL for all of v_ray_o, v_ray_d (and v_ray_time_delta) skips the per-pixel
- * ray gradients, which is cheaper when the rays need none.
+ * ray gradients, which is cheaper when the rays need none.  With
+ * workspace_from_forward != 0, `workspace` must be the one the matching
+ * xsg_rasterize_fwd call (same inputs) used, unchanged since: its packed
+ * Gaussian records and tile order are reused instead of rebuilt.
  * Replaces rasterize_eval3d_bwd, csrc/rasterization/eval3d_bwd.cu:297-403,
  * and rasterize_eval3d_dynamic_bwd, eval3d_dynamic_bwd.cu:312-429. */
 int xsg_rasterize_bwd(const float* means, const float* velocity, const float* quats,
@@ -216,7 +219,7 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
                       float* v_means, float* v_velocity, float* v_quats, float* v_scales,
                       float* v_colors, float* v_opacities, float* v_ray_o, float* v_ray_d,
                       float* v_ray_time_delta, void* workspace, size_t workspace_bytes,
-                      xsg_stream_t stream);
+                      int workspace_from_forward, xsg_stream_t stream);
 
 /* Spherical-harmonics colour, degree 0..4; layout_3kn selects [3, K, N]
  * coefficients (else [N, K, 3]); coeffs_dc optionally holds band 0 apart;

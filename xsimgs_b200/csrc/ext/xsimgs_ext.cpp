@@ -349,7 +349,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> raster_fwd(const Tensor& means, const
                                                       const Tensor& opacities, int64_t W, int64_t H, int64_t tsx,
                                                       int64_t tsy, const Tensor& ray_o, const Tensor& ray_d,
                                                       const OptT& ray_t, const Tensor& tile_offsets,
-                                                      const Tensor& flatten_ids) {
+                                                      const Tensor& flatten_ids, const OptT& workspace_in) {
     for (auto* t : {&means, &quats, &scales, &opacities, &ray_o, &ray_d, &tile_offsets, &flatten_ids})
         check_tensor(*t, "rasterize input", means);
     if (has(colors)) check_tensor(*colors, "colors", means);
@@ -363,13 +363,21 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> raster_fwd(const Tensor& means, const
     Tensor depths = at::empty({H, W}, opt);
     Tensor alphas = at::empty({H, W}, opt);
     Tensor last_ids = at::empty({H, W}, opt.dtype(at::kInt));
-    Tensor ws = workspace(xsg_rasterize_workspace_size(n, int(channels)), means);
+    const size_t ws_need = xsg_rasterize_workspace_size(n, int(channels));
+    Tensor ws;
+    if (has(workspace_in)) {
+        check_tensor(*workspace_in, "workspace", means);
+        TORCH_CHECK(size_t(workspace_in->nbytes()) >= ws_need, "workspace too small: need ", ws_need, " bytes");
+        ws = *workspace_in;
+    } else {
+        ws = workspace(ws_need, means);
+    }
     check(xsg_rasterize_fwd(fptr(means), fptr(velocity), fptr(quats), fptr(scales), fptr(colors), int(channels),
                             fptr(opacities), n, int(W), int(H), int(tsx), int(tsy), fptr(ray_o), fptr(ray_d),
                             fptr(ray_t), tile_offsets.data_ptr<int32_t>(), int(tile_offsets.size(-1)),
                             int(tile_offsets.size(-2)), flatten_ids.data_ptr<int32_t>(), flatten_ids.numel(),
                             channels ? fptr_mut(renders) : nullptr, fptr_mut(depths), fptr_mut(alphas),
-                            last_ids.data_ptr<int32_t>(), ws.data_ptr(), size_t(ws.numel()), stream()));
+                            last_ids.data_ptr<int32_t>(), ws.data_ptr(), size_t(ws.nbytes()), stream()));
     return {renders, depths, alphas, last_ids};
 }
 
@@ -383,7 +391,7 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
                   const Tensor& opacity, const OptT& colors, const Tensor& ray_o, const Tensor& ray_d,
                   const OptT& ray_t, int64_t tsx, int64_t tsy, const Tensor& tile_offsets, const Tensor& flatten_ids,
                   const Tensor& render_alpha, const Tensor& last_ids, const OptT& v_colors_in, const Tensor& v_depth,
-                  const Tensor& v_alpha, bool ray_grads) {
+                  const Tensor& v_alpha, bool ray_grads, const OptT& fwd_ws) {
     if (has(v_colors_in) && !v_colors_in->is_contiguous())
         throw std::runtime_error("v_render_colors must be contiguous");
     for (auto* t : {&points, &scale, &quat, &opacity, &ray_o, &ray_d, &tile_offsets, &flatten_ids, &render_alpha,
@@ -410,7 +418,15 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
         o.v_velocity = at::empty_like(*velocity);
         if (ray_grads) o.v_time = at::empty_like(*ray_t);
     }
-    Tensor ws = workspace(xsg_rasterize_workspace_size(n, int(cdim)), points);
+    const size_t ws_need = xsg_rasterize_workspace_size(n, int(cdim));
+    Tensor ws;
+    if (has(fwd_ws)) {
+        check_tensor(*fwd_ws, "forward_workspace", points);
+        TORCH_CHECK(size_t(fwd_ws->nbytes()) >= ws_need, "forward_workspace too small: need ", ws_need, " bytes");
+        ws = *fwd_ws;
+    } else {
+        ws = workspace(ws_need, points);
+    }
     check(xsg_rasterize_bwd(fptr(points), fptr(velocity), fptr(quat), fptr(scale), fptr(colors), int(cdim),
                             fptr(opacity), n, int(W), int(H), int(tsx), int(tsy), fptr(ray_o), fptr(ray_d),
                             fptr(ray_t), tile_offsets.data_ptr<int32_t>(), int(tile_offsets.size(1)),
@@ -420,7 +436,7 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
                             fptr_mut(o.v_quat), fptr_mut(o.v_scale), has(colors) ? fptr_mut(*o.v_colors) : nullptr,
                             fptr_mut(o.v_opacity), ray_grads ? fptr_mut(o.v_ray_o) : nullptr,
                             ray_grads ? fptr_mut(o.v_ray_d) : nullptr, dyn && ray_grads ? fptr_mut(o.v_time) : nullptr,
-                            ws.data_ptr(), size_t(ws.numel()), stream()));
+                            ws.data_ptr(), size_t(ws.nbytes()), has(fwd_ws) ? 1 : 0, stream()));
     return o;
 }
 
@@ -630,35 +646,42 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("mask_radii", &mask_radii, py::arg("mask"), py::arg("radii"));
 
     m.def("eval3d_supported_ndims", &eval3d_supported_ndims);
+    // bytes of the scratch a rasterize call uses: a caller that passes the
+    // forward's `workspace` on to the backward as `forward_workspace` lets
+    // the backward reuse the forward's packed records (not in the reference)
+    m.def("rasterize_workspace_size",
+          [](int64_t n_gauss, int64_t channels) { return int64_t(xsg_rasterize_workspace_size(n_gauss, int(channels))); },
+          py::arg("n_gauss"), py::arg("channels"));
     m.def("rasterize_eval3d_fwd",
           [](const Tensor& means, const Tensor& quats, const Tensor& scales, const OptT& colors, const Tensor& opac,
              int64_t W, int64_t H, int64_t tsx, int64_t tsy, const Tensor& ray_o, const Tensor& ray_d,
-             const Tensor& offsets, const Tensor& flatten) {
+             const Tensor& offsets, const Tensor& flatten, const OptT& ws) {
               return raster_fwd(means, std::nullopt, quats, scales, colors, opac, W, H, tsx, tsy, ray_o, ray_d,
-                                std::nullopt, offsets, flatten);
+                                std::nullopt, offsets, flatten, ws);
           },
           py::arg("means"), py::arg("quats"), py::arg("scales"), py::arg("colors"), py::arg("opacities"),
           py::arg("image_width"), py::arg("image_height"), py::arg("tile_size_width"), py::arg("tile_size_height"),
-          py::arg("ray_origs"), py::arg("ray_dirs"), py::arg("tile_offsets"), py::arg("flatten_ids"));
+          py::arg("ray_origs"), py::arg("ray_dirs"), py::arg("tile_offsets"), py::arg("flatten_ids"),
+          py::arg("workspace") = py::none());
     m.def("rasterize_eval3d_dynamic_fwd",
           [](const Tensor& means, const OptT& vel, const Tensor& quats, const Tensor& scales, const OptT& colors,
              const Tensor& opac, int64_t W, int64_t H, int64_t tsx, int64_t tsy, const Tensor& ray_o,
-             const Tensor& ray_d, const OptT& ray_t, const Tensor& offsets, const Tensor& flatten) {
+             const Tensor& ray_d, const OptT& ray_t, const Tensor& offsets, const Tensor& flatten, const OptT& ws) {
               return raster_fwd(means, vel, quats, scales, colors, opac, W, H, tsx, tsy, ray_o, ray_d, ray_t,
-                                offsets, flatten);
+                                offsets, flatten, ws);
           },
           py::arg("means"), py::arg("velocity"), py::arg("quats"), py::arg("scales"), py::arg("colors"),
           py::arg("opacities"), py::arg("image_width"), py::arg("image_height"), py::arg("tile_size_width"),
           py::arg("tile_size_height"), py::arg("ray_origs"), py::arg("ray_dirs"), py::arg("ray_time_delta"),
-          py::arg("tile_offsets"), py::arg("flatten_ids"));
+          py::arg("tile_offsets"), py::arg("flatten_ids"), py::arg("workspace") = py::none());
     m.def("rasterize_eval3d_bwd",
           [](const Tensor& points, const Tensor& scale, const Tensor& quat, const Tensor& opacity, const OptT& colors,
              const Tensor& ray_o, const Tensor& ray_d, int64_t tsx, int64_t tsy, const Tensor& offsets,
              const Tensor& flatten, const Tensor& render_alpha, const Tensor& last_ids, const OptT& v_colors,
-             const Tensor& v_depth, const Tensor& v_alpha, bool ray_grads) {
+             const Tensor& v_depth, const Tensor& v_alpha, bool ray_grads, const OptT& fwd_ws) {
               BwdOut o = raster_bwd(points, std::nullopt, scale, quat, opacity, colors, ray_o, ray_d, std::nullopt,
                                     tsx, tsy, offsets, flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha,
-                                    ray_grads);
+                                    ray_grads, fwd_ws);
               return py::make_tuple(o.v_points, o.v_quat, o.v_scale, o.v_opacity,
                                     o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), opt(o.v_ray_o),
                                     opt(o.v_ray_d));
@@ -667,17 +690,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("ray_origins"), py::arg("ray_directions"), py::arg("tile_size_x"), py::arg("tile_size_y"),
           py::arg("tile_offsets"), py::arg("flatten_ids"), py::arg("render_alpha"), py::arg("last_ids"),
           py::arg("v_render_colors"), py::arg("v_render_depth"), py::arg("v_render_alpha"),
-          py::arg("ray_grads") = true);
+          py::arg("ray_grads") = true, py::arg("forward_workspace") = py::none());
     m.def("rasterize_eval3d_dynamic_bwd",
           [](const Tensor& points, const Tensor& vel, const Tensor& scale, const Tensor& quat, const Tensor& opacity,
              const OptT& colors, const Tensor& ray_o, const Tensor& ray_d, const Tensor& ray_t, int64_t tsx,
              int64_t tsy, const Tensor& offsets, const Tensor& flatten, const Tensor& render_alpha,
              const Tensor& last_ids, const OptT& v_colors, const Tensor& v_depth, const Tensor& v_alpha,
-             bool ray_grads) {
+             bool ray_grads, const OptT& fwd_ws) {
               check_tensor(vel, "velocity", points);
               check_tensor(ray_t, "ray_time_delta", points);
               BwdOut o = raster_bwd(points, vel, scale, quat, opacity, colors, ray_o, ray_d, ray_t, tsx, tsy, offsets,
-                                    flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha, ray_grads);
+                                    flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha, ray_grads, fwd_ws);
               return py::make_tuple(o.v_points, o.v_velocity, o.v_quat, o.v_scale, o.v_opacity,
                                     o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), opt(o.v_ray_o),
                                     opt(o.v_ray_d), opt(o.v_time));
@@ -686,7 +709,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("colors"), py::arg("ray_origins"), py::arg("ray_directions"), py::arg("ray_time_delta"),
           py::arg("tile_size_x"), py::arg("tile_size_y"), py::arg("tile_offsets"), py::arg("flatten_ids"),
           py::arg("render_alpha"), py::arg("last_ids"), py::arg("v_render_colors"), py::arg("v_render_depth"),
-          py::arg("v_render_alpha"), py::arg("ray_grads") = true);
+          py::arg("v_render_alpha"), py::arg("ray_grads") = true, py::arg("forward_workspace") = py::none());
 
     m.def("spherical_harmonics_fused_fwd", &sh_fwd, py::arg("degree_to_use"), py::arg("origin"),
           py::arg("positions"), py::arg("coeffs"), py::arg("mask"), py::arg("layout_3kn"),

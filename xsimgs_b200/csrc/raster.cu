@@ -1093,7 +1093,7 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
                       const float* v_renders, const float* v_depths, const float* v_alphas, float* v_means,
                       float* v_velocity, float* v_quats, float* v_scales, float* v_colors, float* v_opacities,
                       float* v_ray_o, float* v_ray_d, float* v_ray_time_delta, void* workspace, size_t ws_bytes,
-                      xsg_stream_t stream) {
+                      int workspace_from_forward, xsg_stream_t stream) {
     int rc = check_common(n_gauss, W, H, tsx, tsy, tiles_w, tiles_h, n_isects, cdim);
     if (rc != XSG_OK) return rc;
     const bool dyn = velocity != nullptr;
@@ -1111,21 +1111,26 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     Arena ar(workspace, ws_bytes);
     float4* rec = ar.take<float4>(size_t(n_gauss) * kRecF4);
     float4* ext = ar.take<float4>(size_t(n_gauss) * 3);
+    const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
+    // same layout as the forward's (records, view constants, tile order), then the accumulator
+    int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
     // Acc<CDIM, kDyn, kRayGrad>::N
     const int na = (!dyn && !ray_grads) ? (cdim == 4 ? 24 : 20) : ((dyn || cdim == 4) ? 20 : 16);
     float* G = ar.take<float>(size_t(n_gauss) * na);
-    const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
-    int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
     if (n_gauss > 0 && (!rec || !ext || !G)) return set_error(XSG_ERR_WORKSPACE, "rasterize_bwd: workspace too small");
     if (dyn) ext = nullptr;  // moving Gaussians: no per-view constants
     // every pixel of the image belongs to exactly one tile thread, which
     // writes its v_ray_o / v_ray_d (/ v_ray_time_delta): no pre-zeroing
-    if (order) launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
+    // the forward's workspace already holds the tile order, records and view constants
+    const bool reuse = workspace_from_forward != 0;
+    if (order && !reuse)
+        launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
     if (n_gauss > 0) {
         XSG_CUDA(cudaMemsetAsync(G, 0, size_t(n_gauss) * na * sizeof(float), st));
         if (cdim > 4) XSG_CUDA(cudaMemsetAsync(v_colors, 0, size_t(n_gauss) * cdim * sizeof(float), st));
-        launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales, opacities,
-               n_gauss, rec, ray_o, ext);
+        if (!reuse)
+            launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales,
+                   opacities, n_gauss, rec, ray_o, ext);
     }
     RasterArgs a{};
     a.rec = rec; a.ext = n_gauss > 0 ? ext : nullptr; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;

@@ -14,6 +14,9 @@ class UTGSRasterize(torch.autograd.Function):
     def forward(ctx, positions, rotation, scale, density, colors, ray_o, ray_d,
                 isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int):
         height, width = ray_o.shape[:2]
+        channels = colors.shape[-1] if colors is not None else 0
+        ws = torch.empty(_C.rasterize_workspace_size(positions.shape[0], channels), dtype=torch.uint8,
+                         device=positions.device)
         out_rgb, out_depth, out_alpha, last_ids = _C.rasterize_eval3d_fwd(
             means=positions,
             quats=rotation,
@@ -28,7 +31,10 @@ class UTGSRasterize(torch.autograd.Function):
             tile_size_height=tile_size_y,
             tile_offsets=isect_offsets,
             flatten_ids=flatten_ids,
+            workspace=ws,
         )
+        # the backward reuses the forward's packed records and tile order
+        ctx.workspace = ws
         ctx.tile_size_x = tile_size_x
         ctx.tile_size_y = tile_size_y
         ctx.save_for_backward(positions, rotation, scale, density, colors, ray_o, ray_d,
@@ -48,6 +54,7 @@ class UTGSRasterize(torch.autograd.Function):
             grad_rgb.contiguous() if grad_rgb is not None else None,
             grad_depth.contiguous(),
             grad_alpha.contiguous(),
+            forward_workspace=ctx.workspace,
             ray_grads=bool(ctx.needs_input_grad[5] or ctx.needs_input_grad[6]),
         )
         return apply_grad_mask(ctx, list(grads) + [None, None, None, None])
