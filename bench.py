@@ -236,21 +236,28 @@ def gpu_arm(args, world, rank, local):
 
     import xsimgs_b200 as X
     from xsimgs_b200 import capi, scenes, roofline
-    from xsimgs_b200.multiview import GradientAllReduce, assign_views
+    from xsimgs_b200.multiview import GradientAllReduce, assign_views, multiview_colors
 
     specs, n_default, scaling = workload_views(args.workload)
     n_gauss = args.gaussians if args.gaussians else n_default
     sc = scenes.street_scene(n_gauss).to(dev)
     if scaling == "weak":
-        mine = [0]          # every rank renders the workload's one view
+        assignment = [[0]] * world   # every rank renders the workload's one view
         px_per_step = world * specs[0].width * specs[0].height
     else:
-        mine = assign_views([s.width * s.height for s in specs], world)[rank]
+        assignment = assign_views([s.width * s.height for s in specs], world)
         px_per_step = sum(s.width * s.height for s in specs)
+    mine = assignment[rank]
+    # with a view on every rank, ranks exchange per-view colour gradients and
+    # rebuild the SH-coefficient gradient locally (MultiViewSH) instead of
+    # all-reducing it
+    mvsh = world > 1 and min(len(v) for v in assignment) >= 1
+    k_max = max(len(v) for v in assignment)
     views = [(specs[i], specs[i].make(dev)) for i in mine]
     leaves = {k: v.clone().requires_grad_(True) for k, v in sc.params().items()}
     # backward finishes the compositing's leaves first, then the SH backward's
-    red = GradientAllReduce([leaves[k] for k in ("quats", "scales", "opacities", "means", "sh")])
+    red = GradientAllReduce([leaves[k] for k in ("quats", "scales", "opacities", "means")] +
+                            ([] if mvsh else [leaves["sh"]]))
     upstream = [tuple(t.to(dev) for t in scenes.upstream_grads(sp.height, sp.width, 3, seed=1 + rank * 16 + k))
                 for k, (sp, _) in enumerate(views)]
 
@@ -258,8 +265,11 @@ def gpu_arm(args, world, rank, local):
         for v in leaves.values():
             v.grad = None
         loss = torch.zeros((), device=dev)
-        for (sp, cam), (gr, gd, ga) in zip(views, grads):
-            colors = X.spherical_harmonics_fused(leaves["sh"], leaves["means"], cam.t0, DEG_C2)
+        if mvsh:
+            cols = multiview_colors(leaves["sh"], leaves["means"], torch.stack([cam.t0 for _, cam in views]),
+                                    DEG_C2, k_max)
+        for v, ((sp, cam), (gr, gd, ga)) in enumerate(zip(views, grads)):
+            colors = cols[v] if mvsh else X.spherical_harmonics_fused(leaves["sh"], leaves["means"], cam.t0, DEG_C2)
             color, depth, alpha, _ = X.ut_gs_render(cam, leaves["means"], leaves["scales"], leaves["quats"],
                                                     leaves["opacities"], sp.width, sp.height, colors=colors)
             loss = loss + (torch.dot(color.reshape(-1), gr.reshape(-1)) + torch.dot(depth.reshape(-1), gd.reshape(-1))
@@ -448,6 +458,9 @@ def gpu_arm(args, world, rank, local):
                    "views_per_gpu": len(views) if scaling == "weak" else
                    [len(v) for v in assign_views([s.width * s.height for s in specs], world)],
                    "parallelism": f"view-sharded dp{world} + NCCL all-reduce of grads",
+                   "gradient_exchange": ("all-reduce of the geometry gradients + all-gather of the per-view colour "
+                                         "gradients, SH-coefficient gradient rebuilt on every rank") if mvsh else
+                                        ("all-reduce of every Gaussian gradient" if world > 1 else "none"),
                    "gaussians": n_gauss, "pixels_per_step": px_per_step, "tile": 16,
                    "l2": f"inputs larger than L2: Gaussian params {gbytes / 1e6:.0f} MB > 126 MB L2"},
         "e2e": {"value": round(e2e, 2), "unit": "Mpix/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},

@@ -258,6 +258,24 @@ int xsg_sh_bwd_noalloc(int degree, const float* origin, const float* positions, 
                        const float* d_out, float* d_coeffs, float* d_coeffs_dc, float* d_positions,
                        float* d_origin, xsg_stream_t stream);
 
+/* Spherical-harmonics backward split for multi-view training (no
+ * counterpart in the reference, which renders one view per call).  The
+ * coefficient gradient summed over views j is sum_j Y(dir_j) (x) d_out_j, so a
+ * multi-GPU step can exchange the per-view colour gradients d_out [n, 3] and
+ * origins instead of the [n, K, 3] coefficient gradients.  Layout [n, K, 3]
+ * with band 0 in `coeffs`, no mask, degree 0..4, K <= 64.
+ *   xsg_sh_positions_bwd:    d_positions [n, 3] = position gradient summed
+ *                            over the n_views views (origins [n_views, 3],
+ *                            d_out [n_views, n, 3]); overwrites.
+ *   xsg_sh_coeffs_bwd_multi: d_coeffs [n, K, 3] = coefficient gradient summed
+ *                            over the n_views views; overwrites; bands past
+ *                            the degree get zero. */
+int xsg_sh_positions_bwd(int degree, int n_views, const float* origins, const float* positions,
+                         const float* coeffs, int64_t n, int dim, const float* d_out, float* d_positions,
+                         xsg_stream_t stream);
+int xsg_sh_coeffs_bwd_multi(int degree, int n_views, const float* origins, const float* positions, int64_t n,
+                            int dim, const float* d_out, float* d_coeffs, xsg_stream_t stream);
+
 /* ------------------------------------------------------------- SMPL ---- *
  * 24-joint SMPL kinematic chain (parents as csrc/nodes/smpl_local_to_global
  * .cu:42-46).  Quaternions (w, x, y, z), 16-byte aligned arrays.  Bodies are

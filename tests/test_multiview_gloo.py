@@ -136,3 +136,91 @@ def test_gradient_allreduce_two_gloo_ranks(target):
         for r in range(world):
             for got, want in zip(results[r], ref):
                 torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-6)
+
+
+def _torch_ops():
+    """CPU stand-ins for the three _C ops MultiViewSH calls (the CUDA ones are
+    checked against the oracle in tests/test_gpu_multiview_sh.py)."""
+    from tests.test_oracle import _torch_sh
+
+    def cols(deg, origin, means, sh):
+        d = means - origin
+        return _torch_sh(deg, d / d.norm(dim=-1, keepdim=True), sh).float()
+
+    def fwd(deg, origin, means, sh, mask, layout):
+        return cols(deg, origin, means, sh)
+
+    def pos_bwd(deg, origins, means, sh, d_out):
+        with torch.enable_grad():
+            m = means.detach().double().requires_grad_(True)
+            sum((cols(deg, origins[v].double(), m, sh.detach().double()) * d_out[v]).sum()
+                for v in range(origins.shape[0])).backward()
+        return m.grad.float()
+
+    def coeff_bwd(deg, origins, means, d_out, dim):
+        with torch.enable_grad():
+            s = torch.zeros(means.shape[0], dim, 3, dtype=torch.float64, requires_grad=True)
+            sum((cols(deg, origins[v].double(), means.detach().double(), s) * d_out[v]).sum()
+                for v in range(origins.shape[0])).backward()
+        return s.grad.float()
+
+    return fwd, pos_bwd, coeff_bwd
+
+
+def _mvsh_setup(rank):
+    g = torch.Generator().manual_seed(5)           # replicated scene
+    means = torch.randn(40, 3, generator=g) * 4
+    sh = torch.randn(40, 16, 3, generator=g)
+    views = [2, 1][rank]                            # uneven views per rank
+    gr = torch.Generator().manual_seed(50 + rank)
+    origins = torch.randn(views, 3, generator=gr)
+    d_cols = torch.randn(views, 40, 3, generator=gr)
+    return means, sh, origins, d_cols
+
+
+def _worker_mvsh(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        from datetime import timedelta
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        from xsimgs_b200._native import _C
+        from xsimgs_b200.multiview import multiview_colors
+        _C.spherical_harmonics_fused_fwd, _C.spherical_harmonics_positions_bwd, \
+            _C.spherical_harmonics_coeffs_bwd_multi = _torch_ops()
+        means, sh, origins, d_cols = _mvsh_setup(rank)
+        means.requires_grad_(True)
+        sh.requires_grad_(True)
+        cols = multiview_colors(sh, means, origins, 3, k_max=2)
+        (cols * d_cols).sum().backward()
+        q.put((rank, (means.grad.clone(), sh.grad.clone())))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def test_multiview_sh_exchange_two_gloo_ranks():
+    """The SH gradient each rank gets is the sum over every view of every
+    rank (uneven view counts, padded), the means gradient its own views'."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_mvsh, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(not isinstance(v, str) for v in res.values()), res
+    fwd, pos_bwd, coeff_bwd = _torch_ops()
+    all_o, all_d = [], []
+    for r in range(world):
+        means, sh, origins, d_cols = _mvsh_setup(r)
+        all_o.append(origins)
+        all_d.append(d_cols)
+        torch.testing.assert_close(res[r][0], pos_bwd(3, origins, means, sh, d_cols), rtol=1e-5, atol=1e-5)
+    want_sh = coeff_bwd(3, torch.cat(all_o), means, torch.cat(all_d), 16)
+    for r in range(world):
+        torch.testing.assert_close(res[r][1], want_sh, rtol=1e-5, atol=1e-5)

@@ -488,6 +488,34 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> sh_bwd(int64_t degree, const Tensor& 
     return {d_coeffs, d_dc, d_pos, d_origin};
 }
 
+// ------------------------------------------------- multi-view SH split --
+// Not in the reference: the SH backward split used by the multi-GPU step
+// (xsimgs_b200.multiview), [N, K, 3] coefficients, no mask.
+Tensor sh_positions_bwd(int64_t degree, const Tensor& origins, const Tensor& positions, const Tensor& coeffs,
+                        const Tensor& d_outputs) {
+    for (auto* t : {&origins, &positions, &coeffs, &d_outputs}) check_tensor(*t, "spherical harmonics input", positions);
+    TORCH_CHECK(coeffs.dim() == 3 && coeffs.size(2) == 3, "coeffs must be [N, K, 3]");
+    const int64_t n = positions.size(0), views = origins.size(0);
+    TORCH_CHECK(d_outputs.numel() == views * n * 3, "d_outputs must be [views, N, 3]");
+    c10::cuda::CUDAGuard g(positions.device());
+    Tensor d_pos = at::empty_like(positions);
+    check(xsg_sh_positions_bwd(int(degree), int(views), fptr(origins), fptr(positions), fptr(coeffs), n,
+                               int(coeffs.size(1)), fptr(d_outputs), fptr_mut(d_pos), stream()));
+    return d_pos;
+}
+
+Tensor sh_coeffs_bwd_multi(int64_t degree, const Tensor& origins, const Tensor& positions, const Tensor& d_outputs,
+                           int64_t dim) {
+    for (auto* t : {&origins, &positions, &d_outputs}) check_tensor(*t, "spherical harmonics input", positions);
+    const int64_t n = positions.size(0), views = origins.size(0);
+    TORCH_CHECK(d_outputs.numel() == views * n * 3, "d_outputs must be [views, N, 3]");
+    c10::cuda::CUDAGuard g(positions.device());
+    Tensor d_coeffs = at::empty({n, dim, 3}, positions.options());
+    check(xsg_sh_coeffs_bwd_multi(int(degree), int(views), fptr(origins), fptr(positions), n, int(dim),
+                                  fptr(d_outputs), fptr_mut(d_coeffs), stream()));
+    return d_coeffs;
+}
+
 // ----------------------------------------------------------------- SMPL --
 // csrc/nodes/smpl_local_to_global.cu:91-337, smpl_lbs_skinning.cu:94-352,
 // smpl.cu:52-95.  Id tensors are 32-bit (int32 or uint32), read as uint32.
@@ -717,6 +745,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("spherical_harmonics_fused_bwd", &sh_bwd, py::arg("degree_to_use"), py::arg("origin"),
           py::arg("positions"), py::arg("coeffs"), py::arg("mask"), py::arg("layout_3kn"), py::arg("d_output"),
           py::arg("coeffs_dc") = py::none());
+    m.def("spherical_harmonics_positions_bwd", &sh_positions_bwd, py::arg("degree_to_use"), py::arg("origins"),
+          py::arg("positions"), py::arg("coeffs"), py::arg("d_outputs"));
+    m.def("spherical_harmonics_coeffs_bwd_multi", &sh_coeffs_bwd_multi, py::arg("degree_to_use"), py::arg("origins"),
+          py::arg("positions"), py::arg("d_outputs"), py::arg("dim"));
     m.def("smpl_local_to_global_fwd", &smpl_local_to_global_fwd, py::arg("local_q_ids"), py::arg("local_q"),
           py::arg("joints"), py::arg("a0_inv_q"), py::arg("a0_inv_t"));
     m.def("smpl_local_to_global_bwd", &smpl_local_to_global_bwd, py::arg("local_q_ids"), py::arg("local_q"),

@@ -104,3 +104,66 @@ class GradientAllReduce:
         for h in self.handles:
             h.remove()
         self.handles = []
+
+
+class MultiViewSH(torch.autograd.Function):
+    """Colours of one Gaussian set seen from each of this rank's views, with a
+    backward that exchanges colour gradients instead of SH-coefficient
+    gradients.
+
+    forward(sh [N, K, 3], means [N, 3], origins [k, 3]) -> colours [k, N, 3]
+    (one spherical_harmonics_fused per view).  The coefficient gradient summed
+    over every view of every rank is sum_j Y(dir_j) (x) dcolour_j, so the
+    backward all-gathers the k colour gradients [N, 3] and origins of every
+    rank (3 floats per Gaussian and view, instead of an all-reduce of
+    3 x (deg+1)^2 floats per Gaussian) and rebuilds that sum locally; the
+    returned `sh` gradient is therefore already the sum over ranks and must
+    not be all-reduced again.  The `means` gradient covers this rank's views
+    only (sum it over ranks with the other geometry gradients).
+
+    Every rank of `group` must call it with the same k_max >= its own k
+    (ranks pad to k_max), and with at least one view, in the same order
+    relative to its other collectives.  Coefficients [N, K, 3] with band 0
+    included; no mask."""
+
+    @staticmethod
+    def forward(ctx, sh, means, origins, degree: int, k_max: int, group=None):
+        from ._native import _C
+        cols = torch.stack([_C.spherical_harmonics_fused_fwd(degree, origins[v].contiguous(), means, sh, None, False)
+                            for v in range(origins.shape[0])])
+        ctx.degree, ctx.k_max, ctx.group = degree, k_max, group
+        ctx.save_for_backward(sh, means, origins)
+        return cols
+
+    @staticmethod
+    def backward(ctx, d_cols):
+        from ._native import _C
+        sh, means, origins = ctx.saved_tensors
+        d_cols = d_cols.contiguous()
+        k, n = origins.shape[0], means.shape[0]
+        distributed = dist.is_available() and dist.is_initialized() and dist.get_world_size(ctx.group) > 1
+        if distributed:
+            world = dist.get_world_size(ctx.group)
+            kmax = ctx.k_max
+            pad_d = torch.zeros(kmax, n, 3, device=d_cols.device, dtype=d_cols.dtype)
+            pad_d[:k] = d_cols
+            # padded views carry zero gradient from a real origin (finite basis)
+            pad_o = origins[:1].expand(kmax, 3).clone()
+            pad_o[:k] = origins
+            all_d = torch.empty(world * kmax, n, 3, device=d_cols.device, dtype=d_cols.dtype)
+            all_o = torch.empty(world * kmax, 3, device=d_cols.device, dtype=d_cols.dtype)
+            w_d = dist.all_gather_into_tensor(all_d, pad_d, group=ctx.group, async_op=True)
+            w_o = dist.all_gather_into_tensor(all_o, pad_o, group=ctx.group, async_op=True)
+        else:
+            all_d, all_o = d_cols, origins
+        d_means = _C.spherical_harmonics_positions_bwd(ctx.degree, origins, means, sh, d_cols)
+        if distributed:
+            w_d.wait()
+            w_o.wait()
+        d_sh = _C.spherical_harmonics_coeffs_bwd_multi(ctx.degree, all_o, means, all_d, sh.shape[1])
+        return d_sh, d_means, None, None, None, None
+
+
+def multiview_colors(sh, means, origins, degree: int, k_max: int, group=None):
+    """[k, N, 3] colours of this rank's k views (see MultiViewSH)."""
+    return MultiViewSH.apply(sh.contiguous(), means.contiguous(), origins.contiguous(), degree, k_max, group)
