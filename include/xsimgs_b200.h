@@ -342,6 +342,58 @@ int xsg_smpl_ids_compaction(const uint32_t* instance_ids, int64_t n, const uint8
                             int64_t n_instances, uint32_t* out_ids, int64_t* count, int64_t* n_out_host,
                             xsg_stream_t stream);
 
+/* ------------------------------------------------- scene assembly ---- *
+ * Replaces copy_gs_rigid_transform_fwd (csrc/nodes/container.cu:157-199).
+ * For each particle p whose instance k = instance_ids[p] is enabled
+ * (inst_mask[k] != 0), at container row r = buffer_offset + p, or
+ * buffer_offset + per_instance_offsets[k] + gs_inst_offsets[p] when both
+ * offset arrays are given: out_positions[r] = R(inst_q[k]) positions[p] +
+ * inst_t[k], out_rotations[r] = inst_q[k] (x) rotations[p],
+ * out_velocities[r] = inst_v[k] + inst_w[k] x R(inst_q[k]) positions[p] (if
+ * given), out_mask[r] = 1 (if given).  Rows outside [0, container_size) and
+ * ids >= n_instances are skipped. */
+int xsg_rigid_transform_fwd(int64_t n, const float* positions, const float* rotations,
+                            const uint32_t* instance_ids, const float* inst_q, const float* inst_t,
+                            const float* inst_v, const float* inst_w, const uint8_t* inst_mask,
+                            int64_t n_instances, int64_t buffer_offset, const uint32_t* per_instance_offsets,
+                            const uint32_t* gs_inst_offsets, int64_t container_size, float* out_positions,
+                            float* out_rotations, float* out_velocities, uint8_t* out_mask, xsg_stream_t stream);
+/* Replaces copy_gs_rigid_transform_bwd (container.cu:202-250).  grad_q,
+ * grad_t [K, .] (and grad_v, grad_w when v_velocities is given) are
+ * ACCUMULATED; grad_positions / grad_rotations are written for the enabled
+ * particles (zero the rest first). */
+int xsg_rigid_transform_bwd(int64_t n, const float* positions, const float* rotations,
+                            const uint32_t* instance_ids, const float* inst_q, const float* inst_w,
+                            const uint8_t* inst_mask, int64_t n_instances, int64_t buffer_offset,
+                            const uint32_t* per_instance_offsets, const uint32_t* gs_inst_offsets,
+                            int64_t container_size, const float* v_positions, const float* v_rotations,
+                            const float* v_velocities, float* grad_positions, float* grad_rotations,
+                            float* grad_q, float* grad_t, float* grad_v, float* grad_w, xsg_stream_t stream);
+
+/* Replaces packed_mask_from_instances (csrc/nodes/gs_masking.cu:27-43):
+ * out u32[ceil(n/32)], bit i = 1 when instance_ids[i] < 0 (not an
+ * instance) or instance_mask[instance_ids[i]] != 0; bits past n are 0. */
+int xsg_packed_mask_from_instances(const int32_t* instance_ids, int64_t n, const uint8_t* instance_mask,
+                                   int64_t n_instances, uint32_t* out, xsg_stream_t stream);
+
+/* Replaces interpolate_smpl_poses_fwd (csrc/nodes/smpl_interpolate.cu:60-98):
+ * poses [N, frames, joints, 4], pose_times [N, frames] (ascending),
+ * query_time [1] (device) -> out [N, joints, 4]: joint 0 = root_q[instance_ids[n]],
+ * the others slerp(std(pose at the last key before the query),
+ * std(pose at the first key at or after it), saturated weight). */
+int xsg_interpolate_smpl_poses_fwd(int64_t n_objects, int frames, int joints, const float* query_time,
+                                   const float* poses, const float* pose_times, const float* root_q,
+                                   const uint32_t* instance_ids, int64_t n_instances, float* out,
+                                   xsg_stream_t stream);
+/* Replaces interpolate_smpl_poses_bwd (smpl_interpolate.cu:198-226): d_poses
+ * written at the two bracketing keys (zero it first), d_root_q and
+ * d_query_time [1] ACCUMULATED.  As in the reference, a zero key interval
+ * uses weight 0.5 in the backward. */
+int xsg_interpolate_smpl_poses_bwd(int64_t n_objects, int frames, int joints, const float* query_time,
+                                   const float* poses, const float* pose_times, const uint32_t* instance_ids,
+                                   int64_t n_instances, const float* grad_out, float* d_poses, float* d_root_q,
+                                   float* d_query_time, xsg_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -292,3 +292,66 @@ def smpl_ids_compaction(instance_ids, instance_mask):
     out = np.zeros(ids.shape[0], np.uint32)
     c = lib().xsgo_smpl_ids_compaction(_p(ids), C.c_int64(ids.shape[0]), _p(mask), _p(out))
     return out[:c]
+
+
+# ---------------------------------------------------------- scene nodes --
+def _opt_u32(a):
+    return None if a is None else _u32(a)
+
+
+def rigid_transform_fwd(pos, rot, inst_id, iq, it, iv, iw, imask, offset, size, per_inst=None, gs_off=None):
+    pos, rot, iq, it, iv, iw = (_f32(a) for a in (pos, rot, iq, it, iv, iw))
+    inst_id, per_inst, gs_off = _u32(inst_id), _opt_u32(per_inst), _opt_u32(gs_off)
+    imask = np.ascontiguousarray(imask, dtype=np.uint8)
+    out_p = np.zeros((size, 3), np.float32)
+    out_r = np.zeros((size, 4), np.float32)
+    out_v = np.zeros((size, 3), np.float32)
+    out_m = np.zeros(size, np.uint8)
+    lib().xsgo_rigid_transform_fwd(C.c_int64(pos.shape[0]), _p(pos), _p(rot), _p(inst_id), _p(iq), _p(it), _p(iv),
+                                   _p(iw), _p(imask), C.c_int64(offset), _p(per_inst), _p(gs_off), _p(out_p),
+                                   _p(out_r), _p(out_v), _p(out_m))
+    return out_p, out_r, out_v, out_m
+
+
+def rigid_transform_bwd(pos, rot, inst_id, iq, iw, imask, offset, v_pos, v_rot, v_vel=None, per_inst=None,
+                        gs_off=None):
+    pos, rot, iq, iw, v_pos, v_rot, v_vel = (_f32(a) for a in (pos, rot, iq, iw, v_pos, v_rot, v_vel))
+    inst_id, per_inst, gs_off = _u32(inst_id), _opt_u32(per_inst), _opt_u32(gs_off)
+    imask = np.ascontiguousarray(imask, dtype=np.uint8)
+    g = dict(positions=np.zeros_like(pos), rotations=np.zeros_like(rot), q=np.zeros_like(iq),
+             t=np.zeros_like(iw), v=np.zeros_like(iw), w=np.zeros_like(iw))
+    lib().xsgo_rigid_transform_bwd(C.c_int64(pos.shape[0]), _p(pos), _p(rot), _p(inst_id), _p(iq), _p(iw),
+                                   _p(imask), C.c_int64(offset), _p(per_inst), _p(gs_off), _p(v_pos), _p(v_rot),
+                                   _p(v_vel), _p(g["positions"]), _p(g["rotations"]), _p(g["q"]), _p(g["t"]),
+                                   _p(g["v"]), _p(g["w"]))
+    return g
+
+
+def packed_mask_from_instances(ids, mask):
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    mask = np.ascontiguousarray(mask, dtype=np.uint8)
+    out = np.zeros((ids.shape[0] + 31) // 32, np.uint32)
+    lib().xsgo_packed_mask_from_instances(C.c_int64(ids.shape[0]), _p(ids), _p(mask), _p(out))
+    return out
+
+
+def interpolate_smpl_fwd(poses, times, root_q, inst_ids, query):
+    poses, times, root_q = _f32(poses), _f32(times), _f32(root_q)
+    inst_ids = _u32(inst_ids)
+    n, frames, joints, _ = poses.shape
+    out = np.zeros((n, joints, 4), np.float32)
+    lib().xsgo_interpolate_smpl_fwd(C.c_int64(n), C.c_int(frames), C.c_int(joints), C.c_float(query), _p(poses),
+                                    _p(times), _p(root_q), _p(inst_ids), _p(out))
+    return out
+
+
+def interpolate_smpl_bwd(poses, times, inst_ids, query, g_out, n_instances):
+    poses, times, g_out = _f32(poses), _f32(times), _f32(g_out)
+    inst_ids = _u32(inst_ids)
+    n, frames, joints, _ = poses.shape
+    d_poses = np.zeros_like(poses)
+    d_root = np.zeros((n_instances, 4), np.float32)
+    d_q = np.zeros(1, np.float32)
+    lib().xsgo_interpolate_smpl_bwd(C.c_int64(n), C.c_int(frames), C.c_int(joints), C.c_float(query), _p(poses),
+                                    _p(times), _p(inst_ids), _p(g_out), _p(d_poses), _p(d_root), _p(d_q))
+    return d_poses, d_root, float(d_q[0])

@@ -622,6 +622,96 @@ Tensor smpl_ids_compaction(const Tensor& instance_ids, const Tensor& instance_ma
     return out.slice(0, 0, n_out);
 }
 
+// -------------------------------------------------------- scene nodes --
+// csrc/nodes/container.cu:157-301, gs_masking.cu:27-48,
+// smpl_interpolate.cu:60-248.
+const uint32_t* opt_u32(const OptT& t, const char* name) { return has(t) ? u32ptr(*t, name) : nullptr; }
+
+void rigid_transform_fwd(const Tensor& positions, const Tensor& rotations, const Tensor& instance_id,
+                         const Tensor& inst_q, const Tensor& inst_t, const Tensor& inst_v, const Tensor& inst_w,
+                         const Tensor& inst_mask, const Tensor& out_positions, const Tensor& out_rotations,
+                         const OptT& out_velocities, const OptT& out_mask, int64_t buffer_offset,
+                         const OptT& per_instance_offsets, const OptT& gs_inst_offsets) {
+    for (auto* t : {&positions, &rotations, &instance_id, &inst_q, &inst_t, &inst_v, &inst_w, &inst_mask,
+                    &out_positions, &out_rotations})
+        check_tensor(*t, "copy_gs_rigid_transform_fwd input", positions);
+    if (has(out_velocities)) check_tensor(*out_velocities, "out_velocities", positions);
+    if (has(out_mask)) check_tensor(*out_mask, "out_mask", positions);
+    c10::cuda::CUDAGuard g(positions.device());
+    check(xsg_rigid_transform_fwd(
+        positions.size(0), fptr(positions), fptr(rotations), u32ptr(instance_id, "instance_id"), fptr(inst_q),
+        fptr(inst_t), fptr(inst_v), fptr(inst_w), reinterpret_cast<const uint8_t*>(inst_mask.data_ptr()),
+        inst_q.size(0), buffer_offset, opt_u32(per_instance_offsets, "per_instance_offsets"),
+        opt_u32(gs_inst_offsets, "gs_inst_offsets"), out_positions.size(0), fptr_mut(out_positions),
+        fptr_mut(out_rotations), has(out_velocities) ? fptr_mut(*out_velocities) : nullptr,
+        has(out_mask) ? reinterpret_cast<uint8_t*>(out_mask->data_ptr()) : nullptr, stream()));
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> rigid_transform_bwd(
+    const Tensor& positions, const Tensor& rotations, const Tensor& instance_id, const Tensor& inst_q,
+    const Tensor& inst_w, const Tensor& inst_mask, int64_t buffer_offset, const OptT& per_instance_offsets,
+    const OptT& gs_inst_offsets, const Tensor& v_positions, const Tensor& v_rotations, const OptT& v_velocities) {
+    for (auto* t : {&positions, &rotations, &instance_id, &inst_q, &inst_w, &inst_mask, &v_positions, &v_rotations})
+        check_tensor(*t, "copy_gs_rigid_transform_bwd input", positions);
+    if (has(v_velocities)) check_tensor(*v_velocities, "v_velocities", positions);
+    c10::cuda::CUDAGuard g(positions.device());
+    Tensor gp = at::zeros_like(positions), gr = at::zeros_like(rotations);
+    Tensor gq = at::zeros_like(inst_q), gt = at::zeros_like(inst_w), gv = at::zeros_like(inst_w),
+           gw = at::zeros_like(inst_w);
+    check(xsg_rigid_transform_bwd(
+        positions.size(0), fptr(positions), fptr(rotations), u32ptr(instance_id, "instance_id"), fptr(inst_q),
+        fptr(inst_w), reinterpret_cast<const uint8_t*>(inst_mask.data_ptr()), inst_q.size(0), buffer_offset,
+        opt_u32(per_instance_offsets, "per_instance_offsets"), opt_u32(gs_inst_offsets, "gs_inst_offsets"),
+        v_positions.size(0), fptr(v_positions), fptr(v_rotations), has(v_velocities) ? fptr(*v_velocities) : nullptr,
+        fptr_mut(gp), fptr_mut(gr), fptr_mut(gq), fptr_mut(gt), fptr_mut(gv), fptr_mut(gw), stream()));
+    return {gp, gr, gq, gt, gv, gw};
+}
+
+Tensor packed_mask_from_instances(const Tensor& instance_ids, const Tensor& instance_mask) {
+    check_tensor(instance_ids, "instance_ids", instance_ids);
+    check_tensor(instance_mask, "instance_mask", instance_ids);
+    TORCH_CHECK(instance_ids.element_size() == 4 && !instance_ids.is_floating_point(),
+                "instance_ids must be a 32-bit integer tensor");
+    TORCH_CHECK(instance_mask.element_size() == 1, "instance_mask must be a bool or uint8 tensor");
+    c10::cuda::CUDAGuard g(instance_ids.device());
+    const int64_t n = instance_ids.numel();
+    Tensor out = at::empty({(n + 31) / 32}, instance_ids.options().dtype(at::kUInt32));
+    check(xsg_packed_mask_from_instances(reinterpret_cast<const int32_t*>(instance_ids.data_ptr()), n,
+                                         reinterpret_cast<const uint8_t*>(instance_mask.data_ptr()),
+                                         instance_mask.numel(), reinterpret_cast<uint32_t*>(out.data_ptr()),
+                                         stream()));
+    return out;
+}
+
+Tensor interpolate_smpl_fwd(const Tensor& poses, const Tensor& times, const Tensor& root_q, const Tensor& inst_ids,
+                            const Tensor& query_time) {
+    for (auto* t : {&poses, &times, &root_q, &inst_ids, &query_time})
+        check_tensor(*t, "interpolate_smpl_poses_fwd input", poses);
+    TORCH_CHECK(poses.dim() == 4 && poses.size(3) == 4, "smpl_poses must be [N, frames, joints, 4]");
+    TORCH_CHECK(poses.size(2) == 24, "num_joints only 24 supported now");
+    c10::cuda::CUDAGuard g(poses.device());
+    Tensor out = at::empty({poses.size(0), poses.size(2), 4}, poses.options());
+    check(xsg_interpolate_smpl_poses_fwd(poses.size(0), int(poses.size(1)), int(poses.size(2)), fptr(query_time),
+                                         fptr(poses), fptr(times), fptr(root_q), u32ptr(inst_ids, "instance_ids"),
+                                         root_q.size(0), fptr_mut(out), stream()));
+    return out;
+}
+
+std::tuple<Tensor, Tensor, Tensor> interpolate_smpl_bwd(const Tensor& poses, const Tensor& times,
+                                                        const Tensor& root_q, const Tensor& inst_ids,
+                                                        const Tensor& query_time, const Tensor& grad_out) {
+    for (auto* t : {&poses, &times, &root_q, &inst_ids, &query_time, &grad_out})
+        check_tensor(*t, "interpolate_smpl_poses_bwd input", poses);
+    TORCH_CHECK(poses.size(2) == 24, "num_joints only 24 supported now");
+    c10::cuda::CUDAGuard g(poses.device());
+    Tensor d_poses = at::zeros_like(poses), d_root = at::zeros_like(root_q), d_q = at::zeros_like(query_time);
+    check(xsg_interpolate_smpl_poses_bwd(poses.size(0), int(poses.size(1)), int(poses.size(2)), fptr(query_time),
+                                         fptr(poses), fptr(times), u32ptr(inst_ids, "instance_ids"), root_q.size(0),
+                                         fptr(grad_out), fptr_mut(d_poses), fptr_mut(d_root), fptr_mut(d_q),
+                                         stream()));
+    return {d_poses, d_root, d_q};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -763,4 +853,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("global_offset"), py::arg("num_instances"), py::arg("grad_out_vertices"),
           py::arg("grad_out_quats"), py::arg("grad_out_velocities") = py::none());
     m.def("smpl_ids_compaction", &smpl_ids_compaction, py::arg("instance_ids"), py::arg("instance_mask"));
+    m.def("copy_gs_rigid_transform_fwd", &rigid_transform_fwd, py::arg("positions"), py::arg("rotations"),
+          py::arg("instance_id"), py::arg("inst_q"), py::arg("inst_t"), py::arg("inst_v"), py::arg("inst_w"),
+          py::arg("inst_mask"), py::arg("out_positions"), py::arg("out_rotations"), py::arg("out_velocities"),
+          py::arg("out_mask"), py::arg("buffer_offset"), py::arg("per_instance_offsets") = py::none(),
+          py::arg("gs_inst_offsets") = py::none());
+    m.def("copy_gs_rigid_transform_bwd", &rigid_transform_bwd, py::arg("positions"), py::arg("rotations"),
+          py::arg("instance_id"), py::arg("inst_q"), py::arg("inst_w"), py::arg("inst_mask"),
+          py::arg("buffer_offset"), py::arg("per_instance_offsets"), py::arg("gs_inst_offsets"),
+          py::arg("v_positions"), py::arg("v_rotations"), py::arg("v_velocities"));
+    m.def("packed_mask_from_instances", &packed_mask_from_instances, py::arg("instance_ids"),
+          py::arg("instance_mask"));
+    m.def("interpolate_smpl_poses_fwd", &interpolate_smpl_fwd, py::arg("smpl_poses"), py::arg("smpl_poses_time"),
+          py::arg("root_q"), py::arg("instance_ids"), py::arg("query_time"));
+    m.def("interpolate_smpl_poses_bwd", &interpolate_smpl_bwd, py::arg("smpl_poses"), py::arg("smpl_poses_time"),
+          py::arg("root_q"), py::arg("instance_ids"), py::arg("query_time"), py::arg("grad_out_quats"));
 }

@@ -16,6 +16,25 @@ from .._native import _C
 from ..utils import apply_grad_mask
 
 
+class InterpolateSMPLPoses(torch.autograd.Function):
+    """Joint rotations of each body at `query_time`, slerped between its two
+    bracketing keyframes (joint 0 taken from root_q[instance_ids]); gradients
+    flow to the keyframe rotations, root_q and the query time
+    (smpl.py:18-43)."""
+
+    @staticmethod
+    def forward(ctx, smpl_poses, smpl_poses_time, root_q, instance_ids, query_time):
+        ctx.save_for_backward(smpl_poses, smpl_poses_time, root_q, instance_ids, query_time)
+        return _C.interpolate_smpl_poses_fwd(smpl_poses, smpl_poses_time, root_q, instance_ids, query_time)
+
+    @staticmethod
+    def backward(ctx, grad_quat_out):
+        smpl_poses, smpl_poses_time, root_q, instance_ids, query_time = ctx.saved_tensors
+        d_poses, d_root, d_query = _C.interpolate_smpl_poses_bwd(smpl_poses, smpl_poses_time, root_q, instance_ids,
+                                                                 query_time, grad_quat_out.contiguous())
+        return apply_grad_mask(ctx, [d_poses, None, d_root, None, d_query])
+
+
 class SMPLLocalToGlobalPose(torch.autograd.Function):
     """(local_q_ids [B], local_q [N,24,4], joints [N,24,3], a0_inv_q [N,24,4],
     a0_inv_t [N,24,3]) -> (global_q [B,24,4], global_t [B,24,3]); gradients
@@ -94,3 +113,9 @@ def valid_instances_indices(instance_ids: torch.Tensor, instance_mask: torch.Ten
         return _C.smpl_ids_compaction(instance_ids, instance_mask)
     idxs = torch.arange(len(instance_ids), device=instance_ids.device)
     return idxs[instance_mask[instance_ids.long()]]
+
+
+def interpolate_smpl_poses(smpl_poses, smpl_poses_time, root_q, instance_ids, query_time):
+    """[N, 24, 4] joint rotations at query_time (smpl.py:206-216)."""
+    return InterpolateSMPLPoses.apply(smpl_poses.contiguous(), smpl_poses_time.contiguous(), root_q.contiguous(),
+                                      instance_ids.contiguous(), query_time)
