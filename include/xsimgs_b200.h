@@ -95,6 +95,35 @@ int xsg_pixel_time(int camera_type, const float* pack, int width, int height, in
 int xsg_pixel_time_from_uv(int camera_type, const float* pack, const float* uv, int64_t n,
                            int delta, float* out, xsg_stream_t stream);
 
+/* Camera-parameter gradients.  Each call writes d_pack (one float per pack
+ * word, xsg_camera_pack_words(camera_type) of them) in full: the gradient of
+ * sum(d_out * out) with respect to the pack, zero for the padding word, the
+ * lidar table address and the spherical/lidar angle limits (the reference
+ * gives the limits no gradient).  Deterministic: per-CTA partial sums go to
+ * `workspace` and are added in a fixed order.
+ * Workspace: xsg_camera_grad_workspace_size() bytes (a constant). */
+size_t xsg_camera_grad_workspace_size(void);
+/* Backward of xsg_camera_rays; d_ray_o may be NULL (no origin gradient), and
+ * is ignored when world_space == 0.  Replaces launch_camera_ray_bwd /
+ * camera_ray_backward_kernel_cuda, include/cameras/ray_kernels.h:61-155, with
+ * the impl backward of perspective.cu:18-34 and fisheye_opencv.cu:77-141. */
+int xsg_camera_rays_bwd(int camera_type, const float* pack, int width, int height,
+                        int world_space, int normalized, const float* d_ray_o,
+                        const float* d_ray_d, float* d_pack, void* workspace,
+                        size_t workspace_bytes, xsg_stream_t stream);
+/* Backward of xsg_pixel_time (grad [H, W]).  Replaces pixel_time_bwd /
+ * pixel_time_delta_bwd, include/cameras/time_kernels.h:115-145, 177-204, 239-267, 299-327. */
+int xsg_pixel_time_bwd(int camera_type, const float* pack, int width, int height, int delta,
+                       const float* grad, float* d_pack, void* workspace,
+                       size_t workspace_bytes, xsg_stream_t stream);
+/* Backward of xsg_pixel_time_from_uv (grad [n]); also writes d_uv [n, 2]
+ * (may be NULL) = grad * rolling_time.  uv and d_uv 8-byte aligned.
+ * Replaces pixel_time_from_uv_bwd / pixel_time_delta_from_uv_bwd,
+ * include/cameras/time_kernels.h:147-175, 206-237, 269-297, 329-361. */
+int xsg_pixel_time_from_uv_bwd(int camera_type, const float* pack, const float* uv, int64_t n,
+                               int delta, const float* grad, float* d_pack, float* d_uv,
+                               void* workspace, size_t workspace_bytes, xsg_stream_t stream);
+
 /* Rolling-shutter point projection, out uvdt [n, 4] and mask [n] (u8).
  * force_no_jacobian selects the fixed-point iteration (projection_nojac).
  * Replaces camera_projection_fwd, include/cameras/projection_kernels.h:259-309. */

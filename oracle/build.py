@@ -1,7 +1,8 @@
 """Build recipe for the CPU oracle (test infrastructure, not a product path).
 
 Compiles oracle/xsg_oracle.cpp (render path), oracle/xsg_oracle_smpl.cpp
-(SMPL skinning) and oracle/xsg_oracle_nodes.cpp (scene assembly) with g++
+(SMPL skinning), oracle/xsg_oracle_nodes.cpp (scene assembly) and
+oracle/xsg_oracle_camgrad.cpp (camera-parameter gradients) with g++
 into oracle/_build/libxsg_oracle.so.
 -ffp-contract=off and no -march flag keep every float operation rounded as
 written, so the oracle is the plain scalar restatement of the reference's
@@ -13,7 +14,8 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-SRCS = [os.path.join(HERE, f) for f in ("xsg_oracle.cpp", "xsg_oracle_smpl.cpp", "xsg_oracle_nodes.cpp")]
+SRCS = [os.path.join(HERE, f) for f in ("xsg_oracle.cpp", "xsg_oracle_smpl.cpp", "xsg_oracle_nodes.cpp",
+                                             "xsg_oracle_camgrad.cpp")]
 OUT_DIR = os.path.join(HERE, "_build")
 OUT = os.path.join(OUT_DIR, "libxsg_oracle.so")
 

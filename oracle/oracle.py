@@ -355,3 +355,34 @@ def interpolate_smpl_bwd(poses, times, inst_ids, query, g_out, n_instances):
     lib().xsgo_interpolate_smpl_bwd(C.c_int64(n), C.c_int(frames), C.c_int(joints), C.c_float(query), _p(poses),
                                     _p(times), _p(inst_ids), _p(g_out), _p(d_poses), _p(d_root), _p(d_q))
     return d_poses, d_root, float(d_q[0])
+
+
+WORDS = {"pinhole": 22, "fisheye": 26, "spherical": 22, "lidar": 24}
+
+
+def camera_rays_bwd(cam, pack, W, H, d_ray_o, d_ray_d, world_space=True, normalized=True, elev=None):
+    """Gradient (float64, one per pack word) of sum(d_ray_o . ray_o + d_ray_d . ray_d)."""
+    pack = _f32(pack).reshape(-1)
+    out = np.zeros(WORDS[cam], np.float64)
+    lib().xsgo_camera_rays_bwd(C.c_int(CAM[cam]), _p(pack), _p(_f32(elev)), C.c_int(W), C.c_int(H),
+                               C.c_int(int(world_space)), C.c_int(int(normalized)), _p(_f32(d_ray_o)),
+                               _p(_f32(d_ray_d)), C.c_int(out.size), _p(out))
+    return out
+
+
+def pixel_time_bwd(cam, pack, grad, delta, W=None, H=None, uv=None, elev=None):
+    """(d_pack float64, d_uv or None) of sum(grad * pixel_time[_delta]); pixel grid
+    when uv is None, else the given uv [n, 2]."""
+    pack = _f32(pack).reshape(-1)
+    grad = _f32(grad).reshape(-1)
+    out = np.zeros(WORDS[cam], np.float64)
+    d_uv = None
+    if uv is not None:
+        uv = _f32(uv).reshape(-1, 2)
+        d_uv = np.zeros_like(uv)
+        n, W, H = uv.shape[0], 1, 1
+    else:
+        n = W * H
+    lib().xsgo_pixel_time_bwd(C.c_int(CAM[cam]), _p(pack), _p(_f32(elev)), C.c_int(W), C.c_int(H), _p(uv),
+                              C.c_int64(n), C.c_int(int(delta)), _p(grad), C.c_int(out.size), _p(out), _p(d_uv))
+    return out, d_uv

@@ -39,6 +39,7 @@ struct CamBase {
 struct Pinhole : CamBase {
     static constexpr int kType = XSG_CAM_PINHOLE;
     static constexpr bool kJacobian = true;
+    static constexpr int kWords = 22;
     float2 f, c;
     __device__ __forceinline__ void load(const float* p) {
         load_base(p);
@@ -52,6 +53,16 @@ struct Pinhole : CamBase {
         return mk3((uv.x - c.x) / f.x, (uv.y - c.y) / f.y, 1.0f);
     }
     __device__ __forceinline__ bool ray_valid(float2) const { return true; }
+    // d(ray_cs)/d(f, c) applied to d_ray, added to pack words 18..21
+    // (perspective.cu:18-34).
+    template <int P>
+    __device__ __forceinline__ void ray_cs_bwd(float2 uv, v3 d, float (&acc)[P]) const {
+        const float ifx = 1.0f / f.x, ify = 1.0f / f.y;
+        acc[18] -= d.x * (uv.x - c.x) * ifx * ifx;
+        acc[19] -= d.y * (uv.y - c.y) * ify * ify;
+        acc[20] -= d.x * ifx;
+        acc[21] -= d.y * ify;
+    }
     __device__ __forceinline__ v3 to_uvd(int, v3 p) const {
         return mk3(p.x * f.x / p.z + c.x, p.y * f.y / p.z + c.y, p.z);
     }
@@ -64,6 +75,7 @@ struct Pinhole : CamBase {
 struct Fisheye : CamBase {
     static constexpr int kType = XSG_CAM_FISHEYE;
     static constexpr bool kJacobian = false;
+    static constexpr int kWords = 26;
     float2 f, c;
     float4 k;
     __device__ __forceinline__ void load(const float* p) {
@@ -123,6 +135,39 @@ struct Fisheye : CamBase {
         const float th = solve(delta, res);
         return (fabsf(res) < 1e-5f) && (distort_deriv(th) > 0.0f);
     }
+    // Backward of ray_cs into f, c (words 18..21) and k1..k4 (22..25),
+    // fisheye_opencv.cu:77-141.  theta(delta, k) is implicit in
+    // distort(theta) = delta, so dtheta/ddelta = 1/distort' and
+    // dtheta/dk_i = -theta^(2i+3)/distort'; rays whose re-solve did not
+    // converge, or sit on the axis, get no gradient.
+    template <int P>
+    __device__ __forceinline__ void ray_cs_bwd(float2 uv, v3 d, float (&acc)[P]) const {
+        const float ux = (uv.x - c.x) / f.x, uy = (uv.y - c.y) / f.y;
+        const float delta = sqrtf(ux * ux + uy * uy);
+        float res;
+        const float th = solve(delta, res);
+        const float der = distort_deriv(th);
+        if (!((th > 0.0f) && (delta > 1e-8f) && (fabsf(res) < 1e-5f) && (der > 1e-3f))) return;
+        float sn, cs;
+        sincosf(th, &sn, &cs);
+        const float idl = 1.0f / delta;
+        const float s = sn * idl;
+        const float d_s = d.x * ux + d.y * uy;
+        const float d_th = d_s * cs * idl - d.z * sn;
+        const float d_ths = d_th / der;
+        const float t2 = th * th, t3 = t2 * th;
+        acc[22] -= d_ths * t3;
+        acc[23] -= d_ths * t3 * t2;
+        acc[24] -= d_ths * t3 * t2 * t2;
+        acc[25] -= d_ths * t3 * t2 * t2 * t2;
+        const float d_dl = -d_s * sn * idl * idl + d_ths;
+        const float dux = s * d.x + d_dl * ux * idl;
+        const float duy = s * d.y + d_dl * uy * idl;
+        acc[18] -= dux * ux / f.x;
+        acc[19] -= duy * uy / f.y;
+        acc[20] -= dux / f.x;
+        acc[21] -= duy / f.y;
+    }
     __device__ __forceinline__ v3 to_uvd(int, v3 p) const {
         const float norm = fmaxf(1e-6f, hypotf(p.x, p.y));
         const float th = atan2f(norm, p.z);
@@ -140,6 +185,7 @@ template <bool kLidar>
 struct Spherical : CamBase {
     static constexpr int kType = kLidar ? XSG_CAM_LIDAR : XSG_CAM_SPHERICAL;
     static constexpr bool kJacobian = true;
+    static constexpr int kWords = kLidar ? 24 : 22;
     float phi_min, phi_range, theta_min, theta_range;
     const float* elev;
     __device__ __forceinline__ void load(const float* p) {
@@ -165,6 +211,10 @@ struct Spherical : CamBase {
         const float xy = 1.0f * ec;
         return mk3(xy * as, xy * ac, 1.0f * es);
     }
+    // The reference gives the angle limits no ray gradient (spherical.h:34-100
+    // keeps BaseCameraImpl's empty pixel_to_camera_ray_backward).
+    template <int P>
+    __device__ __forceinline__ void ray_cs_bwd(float2, v3, float (&)[P]) const {}
     __device__ __forceinline__ bool ray_valid(float2) const { return true; }
     __device__ __forceinline__ float2 angles_to_uv(int mode, float phi, float theta) const {
         float u = (phi - phi_min) / phi_range;

@@ -99,30 +99,129 @@ void validate_pack(const CameraSpec& spec, const Tensor& pack) {
     require_cuda(pack, "camera pack");
 }
 
+using torch::autograd::AutogradContext;
+using torch::autograd::variable_list;
+
+Tensor grad_workspace(const Tensor& like) { return workspace(xsg_camera_grad_workspace_size(), like); }
+
+// camera_rays with the camera-parameter gradient (CameraRaysFunction,
+// include/cameras/ray_kernels.h:158-223): backward returns d_pack only.
+struct CameraRaysFn : public torch::autograd::Function<CameraRaysFn> {
+    static variable_list forward(AutogradContext* ctx, const Tensor& pack, int64_t type, int64_t width,
+                                 int64_t height, bool world_space, bool normalized, bool return_origins,
+                                 bool return_valid) {
+        c10::cuda::CUDAGuard g(pack.device());
+        auto opt = pack.options();
+        // Outputs not asked for are empty tensors (autograd outputs must be
+        // defined); camera_rays() hands them to Python as None / drops them.
+        Tensor ray_o = at::empty(return_origins ? at::IntArrayRef{height, width, 3} : at::IntArrayRef{0}, opt);
+        Tensor ray_d = at::empty({height, width, 3}, opt);
+        Tensor valid = at::empty(return_valid ? at::IntArrayRef{height, width} : at::IntArrayRef{0},
+                                 opt.dtype(at::kBool));
+        check(xsg_camera_rays(int(type), fptr(pack), int(width), int(height), world_space, normalized,
+                              return_origins ? fptr_mut(ray_o) : nullptr, fptr_mut(ray_d),
+                              return_valid ? reinterpret_cast<uint8_t*>(valid.data_ptr()) : nullptr, stream()));
+        ctx->save_for_backward({pack});
+        ctx->saved_data["type"] = type;
+        ctx->saved_data["width"] = width;
+        ctx->saved_data["height"] = height;
+        ctx->saved_data["world_space"] = world_space;
+        ctx->saved_data["normalized"] = normalized;
+        ctx->set_materialize_grads(false);
+        ctx->mark_non_differentiable({valid});
+        return {ray_o, ray_d, valid};
+    }
+    static variable_list backward(AutogradContext* ctx, variable_list grads) {
+        const Tensor pack = ctx->get_saved_variables()[0];
+        c10::cuda::CUDAGuard g(pack.device());
+        const int64_t W = ctx->saved_data["width"].toInt(), H = ctx->saved_data["height"].toInt();
+        Tensor d_pack = at::empty(pack.sizes(), pack.options());
+        Tensor go = (grads[0].defined() && grads[0].numel() == H * W * 3) ? grads[0].contiguous() : Tensor();
+        Tensor gd = grads[1].defined() ? grads[1].contiguous() : at::zeros({H, W, 3}, pack.options());
+        Tensor ws = grad_workspace(pack);
+        check(xsg_camera_rays_bwd(int(ctx->saved_data["type"].toInt()), fptr(pack), int(W), int(H),
+                                  ctx->saved_data["world_space"].toBool(), ctx->saved_data["normalized"].toBool(),
+                                  go.defined() ? fptr(go) : nullptr, fptr(gd), fptr_mut(d_pack), ws.data_ptr(),
+                                  size_t(ws.nbytes()), stream()));
+        return {d_pack, Tensor(), Tensor(), Tensor(), Tensor(), Tensor(), Tensor(), Tensor()};
+    }
+};
+
 py::object camera_rays(const CameraSpec& spec, const Tensor& pack, int64_t width, int64_t height,
                        bool world_space, bool normalized, bool return_origins, bool return_valid) {
     validate_pack(spec, pack);
-    c10::cuda::CUDAGuard g(pack.device());
-    auto opt = pack.options();
-    Tensor ray_o = return_origins ? at::empty({height, width, 3}, opt) : Tensor();
-    Tensor ray_d = at::empty({height, width, 3}, opt);
-    Tensor valid = return_valid ? at::empty({height, width}, opt.dtype(at::kBool)) : Tensor();
-    check(xsg_camera_rays(spec.type, fptr(pack), int(width), int(height), world_space, normalized,
-                          return_origins ? fptr_mut(ray_o) : nullptr, fptr_mut(ray_d),
-                          return_valid ? reinterpret_cast<uint8_t*>(valid.data_ptr()) : nullptr, stream()));
-    py::list out;
-    out.append(return_origins ? py::cast(ray_o) : py::none());
-    out.append(py::cast(ray_d));
-    if (return_valid) out.append(py::cast(valid));
-    return std::move(out);
+    TORCH_CHECK(width > 0 && height > 0, "camera_rays: width and height must be positive");
+    variable_list out = CameraRaysFn::apply(pack, int64_t(spec.type), width, height, world_space, normalized,
+                                            return_origins, return_valid);
+    py::list res;
+    res.append(return_origins ? py::cast(out[0]) : py::none());
+    res.append(py::cast(out[1]));
+    if (return_valid) res.append(py::cast(out[2]));
+    return std::move(res);
 }
+
+// pixel_time / pixel_time_delta with their backward (CameraPixelTimeFunction
+// and CameraPixelTimeDeltaFunction, include/cameras/time_kernels.h:364-460).
+struct PixelTimeFn : public torch::autograd::Function<PixelTimeFn> {
+    static Tensor forward(AutogradContext* ctx, const Tensor& pack, int64_t type, int64_t width, int64_t height,
+                          bool delta) {
+        c10::cuda::CUDAGuard g(pack.device());
+        Tensor out = at::empty({height, width}, pack.options());
+        check(xsg_pixel_time(int(type), fptr(pack), int(width), int(height), delta, fptr_mut(out), stream()));
+        ctx->save_for_backward({pack});
+        ctx->saved_data["type"] = type;
+        ctx->saved_data["delta"] = delta;
+        return out;
+    }
+    static variable_list backward(AutogradContext* ctx, variable_list grads) {
+        const Tensor pack = ctx->get_saved_variables()[0];
+        c10::cuda::CUDAGuard g(pack.device());
+        Tensor grad = grads[0].contiguous();
+        Tensor d_pack = at::empty(pack.sizes(), pack.options());
+        Tensor ws = grad_workspace(pack);
+        check(xsg_pixel_time_bwd(int(ctx->saved_data["type"].toInt()), fptr(pack), int(grad.size(1)),
+                                 int(grad.size(0)), ctx->saved_data["delta"].toBool(), fptr(grad), fptr_mut(d_pack),
+                                 ws.data_ptr(), size_t(ws.nbytes()), stream()));
+        return {d_pack, Tensor(), Tensor(), Tensor(), Tensor()};
+    }
+};
+
+// The uv variants (CameraPixelTimeFromUVFunction and
+// CameraPixelTimeDeltaFromUVFunction, time_kernels.h:398-492): gradients for
+// the pack and for uv.
+struct PixelTimeFromUVFn : public torch::autograd::Function<PixelTimeFromUVFn> {
+    static Tensor forward(AutogradContext* ctx, const Tensor& pack, const Tensor& uv, int64_t type, bool delta) {
+        c10::cuda::CUDAGuard g(pack.device());
+        Tensor u = uv.contiguous();
+        auto sizes = u.sizes().vec();
+        sizes.pop_back();
+        Tensor out = at::empty(sizes, u.options());
+        check(xsg_pixel_time_from_uv(int(type), fptr(pack), fptr(u), u.numel() / 2, delta, fptr_mut(out), stream()));
+        ctx->save_for_backward({pack, u});
+        ctx->saved_data["type"] = type;
+        ctx->saved_data["delta"] = delta;
+        return out;
+    }
+    static variable_list backward(AutogradContext* ctx, variable_list grads) {
+        const auto saved = ctx->get_saved_variables();
+        const Tensor pack = saved[0], u = saved[1];
+        c10::cuda::CUDAGuard g(pack.device());
+        Tensor grad = grads[0].contiguous();
+        Tensor d_pack = at::empty(pack.sizes(), pack.options());
+        Tensor d_uv = ctx->needs_input_grad(1) ? at::empty_like(u) : Tensor();
+        Tensor ws = grad_workspace(pack);
+        check(xsg_pixel_time_from_uv_bwd(int(ctx->saved_data["type"].toInt()), fptr(pack), fptr(u), u.numel() / 2,
+                                         ctx->saved_data["delta"].toBool(), fptr(grad), fptr_mut(d_pack),
+                                         d_uv.defined() ? fptr_mut(d_uv) : nullptr, ws.data_ptr(),
+                                         size_t(ws.nbytes()), stream()));
+        return {d_pack, d_uv, Tensor(), Tensor()};
+    }
+};
 
 Tensor pixel_time(const CameraSpec& spec, const Tensor& pack, int64_t width, int64_t height, bool delta) {
     validate_pack(spec, pack);
-    c10::cuda::CUDAGuard g(pack.device());
-    Tensor out = at::empty({height, width}, pack.options());
-    check(xsg_pixel_time(spec.type, fptr(pack), int(width), int(height), delta, fptr_mut(out), stream()));
-    return out;
+    TORCH_CHECK(width > 0 && height > 0, "pixel_time: width and height must be positive");
+    return PixelTimeFn::apply(pack, int64_t(spec.type), width, height, delta);
 }
 
 Tensor pixel_time_from_uv(const CameraSpec& spec, const Tensor& pack, const Tensor& uv, bool delta) {
@@ -130,13 +229,7 @@ Tensor pixel_time_from_uv(const CameraSpec& spec, const Tensor& pack, const Tens
     TORCH_CHECK(uv.size(-1) == 2, "UV coordinates last dimension must be 2");
     TORCH_CHECK(uv.device() == pack.device(), "Camera and UV-s must be on the same device");
     TORCH_CHECK(uv.scalar_type() == at::kFloat, "UV coordinates must be float32 tensor");
-    c10::cuda::CUDAGuard g(pack.device());
-    Tensor u = uv.contiguous();
-    auto sizes = u.sizes().vec();
-    sizes.pop_back();
-    Tensor out = at::empty(sizes, u.options());
-    check(xsg_pixel_time_from_uv(spec.type, fptr(pack), fptr(u), u.numel() / 2, delta, fptr_mut(out), stream()));
-    return out;
+    return PixelTimeFromUVFn::apply(pack, uv, int64_t(spec.type), delta);
 }
 
 std::tuple<Tensor, Tensor> projection(const CameraSpec& spec, bool nojac, const Tensor& pack, const Tensor& points,

@@ -189,7 +189,7 @@ int xsg_pixel_time(int type, const float* pack, int W, int H, int delta, float* 
 
 int xsg_pixel_time_from_uv(int type, const float* pack, const float* uv, int64_t n, int delta,
                            float* out, xsg_stream_t stream) {
-    XSG_REQUIRE(pack && uv && out && n >= 0, "pixel_time_from_uv: bad arguments");
+    XSG_REQUIRE(pack && n >= 0 && (n == 0 || (uv && out)), "pixel_time_from_uv: bad arguments");
     if (n == 0) return XSG_OK;
     int rc = dispatch_camera(type, [&](auto cam) {
         using Cam = decltype(cam);
@@ -203,7 +203,7 @@ int xsg_pixel_time_from_uv(int type, const float* pack, const float* uv, int64_t
 int xsg_projection(int type, const float* pack, const float* pts, const float* vel, int64_t n,
                    float thr, float max_res, float margin, int mode, int force_nojac, float* uvdt,
                    uint8_t* mask, xsg_stream_t stream) {
-    XSG_REQUIRE(pack && pts && uvdt && mask && n >= 0, "projection: bad arguments");
+    XSG_REQUIRE(pack && n >= 0 && (n == 0 || (pts && uvdt && mask)), "projection: bad arguments");
     XSG_REQUIRE(mode >= 0 && mode <= 2, "projection: bad projection mode");
     if (n == 0) return XSG_OK;
     int rc = dispatch_camera(type, [&](auto cam) {
@@ -224,7 +224,7 @@ int xsg_projection_utgs(int type, const float* pack, const float* pts, const flo
                         float W, float H, float ua, float ub, float uk, float thr, float max_res,
                         float margin, int phm, uint8_t* flags, float* radii, float* means2d,
                         float* depths, xsg_stream_t stream) {
-    XSG_REQUIRE(pack && pts && scales && quats && flags && radii && means2d && depths && n >= 0,
+    XSG_REQUIRE(pack && n >= 0 && (n == 0 || (pts && scales && quats && flags && radii && means2d && depths)),
                 "projection_utgs: bad arguments");
     XSG_REQUIRE(reinterpret_cast<uintptr_t>(quats) % 16 == 0, "projection_utgs: quats must be 16-byte aligned");
     if (n == 0) return XSG_OK;
@@ -252,9 +252,10 @@ int xsg_projection_utgs(int type, const float* pack, const float* pts, const flo
 
 int xsg_mask_radii(const uint8_t* mask, const uint32_t* packed, int64_t n, float* radii,
                    xsg_stream_t stream) {
-    XSG_REQUIRE((mask == nullptr) != (packed == nullptr), "mask_radii: pass exactly one mask");
-    XSG_REQUIRE(radii && n >= 0, "mask_radii: bad arguments");
+    XSG_REQUIRE(n >= 0, "mask_radii: bad arguments");
     if (n == 0) return XSG_OK;
+    XSG_REQUIRE((mask == nullptr) != (packed == nullptr), "mask_radii: pass exactly one mask");
+    XSG_REQUIRE(radii, "mask_radii: bad arguments");
     launch(mask_radii_kernel, blocks_for(n, kThreads), kThreads, 0, as_cuda(stream), 
         mask, packed, n, reinterpret_cast<float2*>(radii));
     return check_launch("mask_radii");
