@@ -47,15 +47,18 @@ enum xsg_status {
  *     SPHERICAL phi_min phi_range theta_min theta_range             -> 22 words
  *     LIDAR     the same 4 limits + 2 words holding the 64-bit device
  *               address of the per-row elevation table (beam_v)      -> 24 words
+ *     DISTORTED f.x f.y c.x c.y, k1 k2 p1 p2, k3 k4 k5 k6 (OpenCV
+ *               rational + tangential model), max_radius^2           -> 31 words
  * Reference: Camera<Impl> (include/cameras/camera.h:67-183) with the impls in
- * csrc/cameras/perspective.cu:7-71, fisheye_opencv.cu:5-188 and
- * spherical.h:34-100.  The lidar address words follow
+ * csrc/cameras/perspective.cu:7-71, fisheye_opencv.cu:5-188,
+ * spherical.h:34-100 and distorted_perspective.cu:6-230.  The lidar address words follow
  * src/xsimgs/cameras/ext/lidar.py:14-19. */
 enum xsg_camera_type {
     XSG_CAM_PINHOLE = 0,
     XSG_CAM_FISHEYE = 1,
     XSG_CAM_SPHERICAL = 2,
     XSG_CAM_LIDAR = 3,
+    XSG_CAM_DISTORTED = 4,
 };
 int xsg_camera_pack_words(int camera_type);
 
@@ -94,6 +97,14 @@ int xsg_pixel_time(int camera_type, const float* pack, int width, int height, in
 /* The same from normalised uv [n, 2]; time_kernels.h:30-112. */
 int xsg_pixel_time_from_uv(int camera_type, const float* pack, const float* uv, int64_t n,
                            int delta, float* out, xsg_stream_t stream);
+
+/* Distortion lookup of the DISTORTED camera: out [H, W, 2] = the distorted
+ * normalised uv of each pixel centre, mapped to [-1, 1] (grid_sample's
+ * range) unless normalized_range != 0.  Other camera types:
+ * XSG_ERR_UNSUPPORTED.  Replaces undistort_map,
+ * include/cameras/distortion.h:33-56. */
+int xsg_undistort_map(int camera_type, const float* pack, int width, int height,
+                      int normalized_range, float* out, xsg_stream_t stream);
 
 /* Camera-parameter gradients.  Each call writes d_pack (one float per pack
  * word, xsg_camera_pack_words(camera_type) of them) in full: the gradient of

@@ -31,7 +31,7 @@ def lib():
     return _lib
 
 
-CAM = {"pinhole": 0, "fisheye": 1, "spherical": 2, "lidar": 3}
+CAM = {"pinhole": 0, "fisheye": 1, "spherical": 2, "lidar": 3, "distorted": 4}
 
 
 def _p(a):
@@ -357,7 +357,7 @@ def interpolate_smpl_bwd(poses, times, inst_ids, query, g_out, n_instances):
     return d_poses, d_root, float(d_q[0])
 
 
-WORDS = {"pinhole": 22, "fisheye": 26, "spherical": 22, "lidar": 24}
+WORDS = {"pinhole": 22, "fisheye": 26, "spherical": 22, "lidar": 24, "distorted": 31}
 
 
 def camera_rays_bwd(cam, pack, W, H, d_ray_o, d_ray_d, world_space=True, normalized=True, elev=None):
@@ -386,3 +386,11 @@ def pixel_time_bwd(cam, pack, grad, delta, W=None, H=None, uv=None, elev=None):
     lib().xsgo_pixel_time_bwd(C.c_int(CAM[cam]), _p(pack), _p(_f32(elev)), C.c_int(W), C.c_int(H), _p(uv),
                               C.c_int64(n), C.c_int(int(delta)), _p(grad), C.c_int(out.size), _p(out), _p(d_uv))
     return out, d_uv
+
+
+def undistort_map(pack, W, H, normalized_range=False):
+    """Distorted uv of every pixel centre of a "distorted" camera, [H, W, 2]."""
+    pack = _f32(pack).reshape(-1)
+    out = np.zeros((H, W, 2), np.float32)
+    lib().xsgo_undistort_map(_p(pack), C.c_int(W), C.c_int(H), C.c_int(int(normalized_range)), _p(out))
+    return out

@@ -138,13 +138,14 @@ inline void quat_to_rows(quat q, f3 rows[3]) {
 //   [0:4) q0 wxyz  [4:7) t0  [7:10) v  [10:13) w  [13] pad
 //   [14:16) rolling_time  [16] trigger_time  [17] pose_time  [18:) intrinsics
 // The reference's field order is camera.h:71-79.
-enum CamType { CAM_PINHOLE = 0, CAM_FISHEYE = 1, CAM_SPHERICAL = 2, CAM_LIDAR = 3 };
+enum CamType { CAM_PINHOLE = 0, CAM_FISHEYE = 1, CAM_SPHERICAL = 2, CAM_LIDAR = 3, CAM_DISTORTED = 4 };
 enum ProjMode { MODE_CENTRAL = 0, MODE_NEG = 1, MODE_POS = 2 };
 
 struct Cam {
     int type;
     quat q0; f3 t0, v, w; f2 rolling; float trigger, pose;
     f2 f, c; f4 dist;                                       // pinhole / fisheye
+    f4 d0, d1; float max_r2;                                 // distorted pinhole
     float phi_min, phi_range, theta_min, theta_range;        // spherical / lidar
     const float* elev;                                       // lidar beam v table
 
@@ -158,10 +159,15 @@ struct Cam {
         k.rolling = {p[14], p[15]};
         k.trigger = p[16];
         k.pose = p[17];
-        if (type == CAM_PINHOLE || type == CAM_FISHEYE) {
+        if (type == CAM_PINHOLE || type == CAM_FISHEYE || type == CAM_DISTORTED) {
             k.f = {p[18], p[19]};
             k.c = {p[20], p[21]};
             if (type == CAM_FISHEYE) k.dist = {p[22], p[23], p[24], p[25]};
+            if (type == CAM_DISTORTED) {
+                k.d0 = {p[22], p[23], p[24], p[25]};
+                k.d1 = {p[26], p[27], p[28], p[29]};
+                k.max_r2 = p[30];
+            }
         } else {
             k.phi_min = p[18]; k.phi_range = p[19];
             k.theta_min = p[20]; k.theta_range = p[21];
@@ -170,7 +176,56 @@ struct Cam {
         return k;
     }
 
-    bool has_jacobian() const { return type != CAM_FISHEYE; }
+    bool has_jacobian() const { return type != CAM_FISHEYE && type != CAM_DISTORTED; }
+
+    // DistortedPerspectiveCameraImpl::DistortionState at (u, v)
+    // (distorted_perspective.cu:11-78): D(x) = x scale + delta and its
+    // symmetric Jacobian.
+    struct DState { float scale, denom, dx, dy, juu, juv, jvv; };
+    DState dstate(float u, float v) const {
+        const float r2 = u * u + v * v;
+        const float num = 1.0f + r2 * (d0.x + r2 * (d0.y + r2 * d1.x));
+        const float den = 1.0f + r2 * (d1.y + r2 * (d1.z + r2 * d1.w));
+        const float sc = num / den;
+        const float dn = d0.x + r2 * (2.0f * d0.y + 3.0f * d1.x * r2);
+        const float dd = d1.y + r2 * (2.0f * d1.z + 3.0f * d1.w * r2);
+        const float dsc = (dn * den - num * dd) / (den * den);
+        return {sc, den,
+                2.0f * d0.z * u * v + d0.w * (r2 + 2.0f * u * u),
+                d0.z * (r2 + 2.0f * v * v) + 2.0f * d0.w * u * v,
+                sc + 2.0f * u * u * dsc + 2.0f * d0.z * v + 6.0f * d0.w * u,
+                2.0f * u * v * dsc + 2.0f * d0.z * u + 2.0f * d0.w * v,
+                sc + 2.0f * v * v * dsc + 6.0f * d0.z * v + 2.0f * d0.w * u};
+    }
+    // undistort_uv, distorted_perspective.cu:80-99 (st = the state at the
+    // start of the last step)
+    f2 undistort(f2 xd, DState& st) const {
+        f2 x = xd;
+        for (int j = 0; j < 5; ++j) {
+            st = dstate(x.x, x.y);
+            const float rx = x.x * st.scale + st.dx - xd.x;
+            const float ry = x.y * st.scale + st.dy - xd.y;
+            const float det = st.juu * st.jvv - st.juv * st.juv;
+            if (std::fabs(det) > 1e-3f) {
+                x.x -= (st.jvv * rx - st.juv * ry) / det;
+                x.y -= (st.juu * ry - st.juv * rx) / det;
+            } else {
+                x = {(xd.x - st.dx) / st.scale, (xd.y - st.dy) / st.scale};
+            }
+        }
+        return x;
+    }
+    // uv_distortion, distortion.h:8-30, applied to x
+    f2 distort(f2 x) const {
+        const float uu = x.x * x.x, vv = x.y * x.y;
+        const float r2 = uu + vv;
+        const float num = 1.0f + r2 * (d0.x + r2 * (d0.y + r2 * d1.x));
+        const float den = 1.0f + r2 * (d1.y + r2 * (d1.z + r2 * d1.w));
+        const float sc = num / den;
+        const float uv2 = 2.0f * x.x * x.y;
+        return {x.x * sc + (d0.z * uv2 + d0.w * (r2 + 2.0f * uu)),
+                x.y * sc + (d0.z * (r2 + 2.0f * vv) + d0.w * uv2)};
+    }
 
     // base_camera_impl.h:9-14; lidar rows from the beam table, spherical.h:77-82
     f2 pixel_to_uv(int px, int py, int W, int H) const {
@@ -221,6 +276,11 @@ struct Cam {
 
     // perspective.cu:13-16, fisheye_opencv.cu:49-64, spherical.h:40-46
     f3 pixel_to_camera_ray(f2 uv) const {
+        if (type == CAM_DISTORTED) {  // distorted_perspective.cu:101-106
+            DState st;
+            const f2 x = undistort((uv - c) / f, st);
+            return {x.x, x.y, 1.0f};
+        }
         if (type == CAM_PINHOLE) {
             const f2 uc = (uv - c) / f;
             return {uc.x, uc.y, 1.0f};
@@ -239,6 +299,15 @@ struct Cam {
 
     // camera.h:117-123, fisheye_opencv.cu:66-74
     bool ray_valid(f2 uv) const {
+        if (type == CAM_DISTORTED) {  // distorted_perspective.cu:108-118
+            DState st;
+            const f2 xd = (uv - c) / f;
+            const f2 x = undistort(xd, st);
+            const float rx = x.x * st.scale + st.dx - xd.x;
+            const float ry = x.y * st.scale + st.dy - xd.y;
+            const float r2 = x.x * x.x + x.y * x.y;
+            return (r2 <= max_r2) && (std::fabs(rx) < 1e-5f) && (std::fabs(ry) < 1e-5f);
+        }
         if (type != CAM_FISHEYE) return true;
         const float delta = length((uv - c) / f);
         if (delta <= 1e-8f) return true;
@@ -265,6 +334,12 @@ struct Cam {
 
     // perspective.cu:54-60, fisheye_opencv.cu:143-153, spherical.h:127-131
     f3 point_to_uvd(int mode, f3 p) const {
+        if (type == CAM_DISTORTED) {  // distorted_perspective.cu:192-199
+            const f2 x{p.x / p.z, p.y / p.z};
+            const f2 xd = distort(x);
+            const float r2 = x.x * x.x + x.y * x.y;
+            return {xd.x * f.x + c.x, xd.y * f.y + c.y, (r2 <= max_r2) ? p.z : 0.0f};
+        }
         if (type == CAM_PINHOLE)
             return {p.x * f.x / p.z + c.x, p.y * f.y / p.z + c.y, p.z};
         if (type == CAM_FISHEYE) {
@@ -551,6 +626,20 @@ void xsgo_pixel_time_from_uv(int type, const float* pack, const float* uv, int64
     for (int64_t i = 0; i < n; ++i) {
         const f2 u{uv[2 * i], uv[2 * i + 1]};
         out[i] = delta ? k.pixel_time_delta(u) : k.pixel_time(u);
+    }
+}
+
+// undistort_map, distortion.h:33-56: distorted uv of every pixel centre,
+// mapped to [-1, 1] unless normalized_range.
+void xsgo_undistort_map(const float* pack, int W, int H, int normalized_range, float* out) {
+    const Cam k = Cam::load(CAM_DISTORTED, pack, nullptr);
+    for (int64_t idx = 0; idx < int64_t(W) * H; ++idx) {
+        const f2 uv = k.pixel_to_uv(int(idx % W), int(idx / W), W, H);
+        const f2 xd = k.distort((uv - k.c) / k.f);
+        f2 r{xd.x * k.f.x + k.c.x, xd.y * k.f.y + k.c.y};
+        if (!normalized_range) r = {r.x * 2.0f - 1.0f, r.y * 2.0f - 1.0f};
+        out[2 * idx] = r.x;
+        out[2 * idx + 1] = r.y;
     }
 }
 

@@ -39,7 +39,45 @@ inline D3 qrot(DQ q, D3 p) {
     return p + q.w * t + cross(q.v, t);
 }
 
-enum { CAM_PINHOLE = 0, CAM_FISHEYE = 1, CAM_SPHERICAL = 2, CAM_LIDAR = 3 };
+enum { CAM_PINHOLE = 0, CAM_FISHEYE = 1, CAM_SPHERICAL = 2, CAM_LIDAR = 3, CAM_DISTORTED = 4 };
+
+// OpenCV 8-coefficient distortion D(x) = x scale(r2) + delta(x) in double,
+// with its symmetric Jacobian (distorted_perspective.cu:43-78); k = pack
+// words 22..29 = k1 k2 p1 p2 k3 k4 k5 k6.
+struct DistD {
+    double scale, denom, dx, dy, juu, juv, jvv;
+    double det() const { return juu * jvv - juv * juv; }
+};
+inline DistD dist_state(const float* k, double u, double v) {
+    const double k1 = k[0], k2 = k[1], p1 = k[2], p2 = k[3], k3 = k[4], k4 = k[5], k5 = k[6], k6 = k[7];
+    const double r2 = u * u + v * v;
+    const double num = 1 + r2 * (k1 + r2 * (k2 + r2 * k3));
+    const double den = 1 + r2 * (k4 + r2 * (k5 + r2 * k6));
+    const double sc = num / den;
+    const double dsc = ((k1 + r2 * (2 * k2 + 3 * k3 * r2)) * den - num * (k4 + r2 * (2 * k5 + 3 * k6 * r2))) /
+                       (den * den);
+    return {sc, den, 2 * p1 * u * v + p2 * (r2 + 2 * u * u), p1 * (r2 + 2 * v * v) + 2 * p2 * u * v,
+            sc + 2 * u * u * dsc + 2 * p1 * v + 6 * p2 * u, 2 * u * v * dsc + 2 * p1 * u + 2 * p2 * v,
+            sc + 2 * v * v * dsc + 6 * p1 * v + 2 * p2 * u};
+}
+// Newton on D(x) = xd (a fixed-point step where |det J| <= 1e-3), run to
+// double precision.
+inline void undistort_d(const float* k, double xdu, double xdv, double& u, double& v) {
+    u = xdu;
+    v = xdv;
+    for (int j = 0; j < 12; ++j) {
+        const DistD s = dist_state(k, u, v);
+        const double rx = u * s.scale + s.dx - xdu, ry = v * s.scale + s.dy - xdv;
+        const double det = s.det();
+        if (std::fabs(det) > 1e-3) {
+            u -= (s.jvv * rx - s.juv * ry) / det;
+            v -= (s.juu * ry - s.juv * rx) / det;
+        } else {
+            u = (xdu - s.dx) / s.scale;
+            v = (xdv - s.dy) / s.scale;
+        }
+    }
+}
 
 // The float32 fisheye re-solve of the forward (fisheye_opencv.cu:14-47),
 // used only for the convergence / validity decision.
@@ -93,6 +131,11 @@ struct RayGrad {
     D3 ray(Pixel uv, double& theta_out) const {
         const double u = uv.u, v = uv.v;
         if (type == CAM_PINHOLE) return {(u - p[20]) / p[18], (v - p[21]) / p[19], 1.0};
+        if (type == CAM_DISTORTED) {
+            double x, y;
+            undistort_d(p + 22, (u - p[20]) / p[18], (v - p[21]) / p[19], x, y);
+            return {x, y, 1.0};
+        }
         if (type == CAM_FISHEYE) {
             const float uxf = (uv.u - p[20]) / p[18], uyf = (uv.v - p[21]) / p[19];
             float res;
@@ -123,6 +166,37 @@ struct RayGrad {
             acc[19] += -d.y * (uv.v - p[21]) / (fy * fy);
             acc[20] += -d.x / fx;
             acc[21] += -d.y / fy;
+            return;
+        }
+        if (type == CAM_DISTORTED) {  // distorted_perspective.cu:115-190
+            const double fx = p[18], fy = p[19];
+            const double xdu = (uv.u - p[20]) / fx, xdv = (uv.v - p[21]) / fy;
+            double x, y;
+            undistort_d(p + 22, xdu, xdv, x, y);
+            const DistD s = dist_state(p + 22, x, y);
+            const double det = s.det();
+            double gx, gy;  // J^-T d.xy
+            if (std::fabs(det) <= 1e-3) {
+                gx = d.x / s.scale;
+                gy = d.y / s.scale;
+            } else {
+                gx = (s.jvv * d.x - s.juv * d.y) / det;
+                gy = (s.juu * d.y - s.juv * d.x) / det;
+            }
+            acc[18] += -gx * xdu / fx;
+            acc[19] += -gy * xdv / fy;
+            acc[20] += -gx / fx;
+            acc[21] += -gy / fy;
+            const double r2 = x * x + y * y, r4 = r2 * r2, r6 = r4 * r2;
+            const double rad = -(gx * x + gy * y) / s.denom, rad_den = -rad * s.scale;
+            acc[22] += rad * r2;
+            acc[23] += rad * r4;
+            acc[24] += -(gx * 2 * x * y + gy * (r2 + 2 * y * y));
+            acc[25] += -(gx * (r2 + 2 * x * x) + gy * 2 * x * y);
+            acc[26] += rad * r6;
+            acc[27] += rad_den * r2;
+            acc[28] += rad_den * r4;
+            acc[29] += rad_den * r6;
             return;
         }
         if (type != CAM_FISHEYE) return;

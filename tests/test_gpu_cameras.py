@@ -32,15 +32,19 @@ def _specs():
                            intrinsics=np.array([120.0 / 400, 120.0 / 300, 0.5, 0.5], np.float32),
                            distortion=np.array([0.03, -0.02, 0.01, -0.004], np.float32),
                            rolling_time=(0.02, 0.0), **motion)
+    di = scenes.CameraSpec("distorted", 480, 272, look_at_quat(EYE, (1.0, -0.4, 1.4)), np.asarray(EYE, np.float32),
+                           intrinsics=np.array([300.0 / 480, 300.0 / 272, 0.52, 0.48], np.float32),
+                           distortion=np.array([-0.25, 0.07, 3e-4, -2e-4, -0.008, 0.03, 0.002, 0.0005], np.float32),
+                           rolling_time=(0.0, 0.03), **motion)
     sp = scenes.CameraSpec("spherical", 512, 256, np.array([1, 0, 0, 0], np.float32), np.asarray(EYE, np.float32),
                            rolling_time=(0.1, 0.0), **motion)
     li = scenes.c4_lidar(beams=64, columns=512)
     li.rolling_time, li.trigger_time, li.pose_time = (0.1, 0.0), 0.0, 0.05
     li.v, li.w = (4.0, 0.0, 0.0), (0.0, 0.0, 0.2)
-    return {"pinhole": ph, "fisheye": fe, "spherical": sp, "lidar": li}
+    return {"pinhole": ph, "fisheye": fe, "distorted": di, "spherical": sp, "lidar": li}
 
 
-KINDS = ["pinhole", "fisheye", "spherical", "lidar"]
+KINDS = ["pinhole", "fisheye", "distorted", "spherical", "lidar"]
 
 
 @pytest.fixture(scope="module")
@@ -93,6 +97,16 @@ def test_camera_rays_and_pixel_time(specs, cuda, kind):
         np.testing.assert_allclose(t, want, atol=1e-7, rtol=1e-6)
 
 
+@pytest.mark.parametrize("normalized_range", [False, True])
+def test_undistort_map(specs, cuda, normalized_range):
+    spec = specs["distorted"]
+    cam, pack, _ = camera_inputs(spec, cuda)
+    got = to_np(cam.undistort_map(spec.width, spec.height, normalized_range=normalized_range))
+    np.testing.assert_allclose(got, O.undistort_map(pack, spec.width, spec.height, normalized_range), atol=2e-6)
+    from xsimgs_b200 import _C
+    assert not hasattr(_C.PerspectiveCamera, "undistort_map")  # only the distorted camera has one
+
+
 def _pixel_time_from_uv(kind, pack, uv, delta):
     import ctypes as C
     pack = np.ascontiguousarray(pack, np.float32)
@@ -140,7 +154,8 @@ def _project(cam, spec, shell, cuda, phm=False, with_vel=False):
 
 
 @pytest.mark.parametrize("kind,phm,with_vel", [("pinhole", False, False), ("pinhole", False, True),
-                                               ("fisheye", False, True), ("spherical", False, True),
+                                               ("fisheye", False, True), ("distorted", False, True),
+                                               ("spherical", False, True),
                                                ("spherical", True, True), ("lidar", False, True),
                                                ("lidar", True, False)])
 def test_ut_projection(specs, shell, cuda, kind, phm, with_vel):
@@ -172,7 +187,7 @@ def _tiles(cam, kind, spec, shell, cuda, proj, with_vel, tsx=16, tsy=16):
     flags, radii, m2, dep = proj
     W, H = spec.width, spec.height
     g = lambda t: t.to(cuda).contiguous()
-    if kind in ("pinhole", "fisheye"):
+    if kind in ("pinhole", "fisheye", "distorted"):
         return _C.isect_regular_tiles(m2, radii, dep, W, H, tsx, tsy), None
     kw = dict(camera_pack=cam.pack, points=g(shell["means"]), points_velocity=g(shell["vel"]) if with_vel else None,
               scale=g(shell["scales"]), quat=g(shell["quats"]), opacity=g(shell["opac"]), flag=flags,
@@ -185,7 +200,7 @@ def _tiles(cam, kind, spec, shell, cuda, proj, with_vel, tsx=16, tsy=16):
 
 def _oracle_tiles(kind, pack, elev, spec, shell, proj, eb, with_vel, tsx=16, tsy=16):
     flags, radii, m2, dep = map(to_np, proj)
-    if kind in ("pinhole", "fisheye"):
+    if kind in ("pinhole", "fisheye", "distorted"):
         return O.isect_regular(m2, radii, dep, spec.width, spec.height, tsx, tsy)
     return O.isect_spherical(kind == "lidar", pack, elev, shell["means"].numpy(),
                              shell["vel"].numpy() if with_vel else None, shell["scales"].numpy(),
@@ -211,7 +226,8 @@ def _assert_tiles_match(got, ref, flags):
         np.testing.assert_array_equal(flat, rfl)
 
 
-@pytest.mark.parametrize("kind,phm", [("pinhole", False), ("fisheye", False), ("spherical", False),
+@pytest.mark.parametrize("kind,phm", [("pinhole", False), ("fisheye", False), ("distorted", False),
+                                      ("spherical", False),
                                       ("spherical", True), ("lidar", False), ("lidar", True)])
 def test_tiling_matches_oracle(specs, shell, cuda, kind, phm):
     """With PHM the range-image projection marks Gaussians that straddle the

@@ -19,7 +19,7 @@ from tests.test_gpu_cameras import KINDS, _specs
 
 pytestmark = pytest.mark.gpu
 
-GROUPS = [(0, 4), (4, 7), (7, 10), (10, 13), (14, 16), (16, 17), (17, 18), (18, 22), (22, 26)]
+GROUPS = [(0, 4), (4, 7), (7, 10), (10, 13), (14, 16), (16, 17), (17, 18), (18, 22), (22, 26), (26, 30)]
 
 
 @pytest.fixture(scope="module")
@@ -100,7 +100,7 @@ def test_ray_gradients_full_hd(cuda):
     check_pack_grad(p.grad, O.camera_rays_bwd("pinhole", pack, 1920, 1080, go, gd), "pinhole 1080p")
 
 
-@pytest.mark.parametrize("kind", ["pinhole", "fisheye"])
+@pytest.mark.parametrize("kind", ["pinhole", "fisheye", "distorted"])
 def test_camera_tensors_receive_gradients(specs, cuda, kind):
     """Leaf camera tensors -> differentiable pack -> rays; also with the
     origins not returned (ray_d gradient only)."""
@@ -108,7 +108,7 @@ def test_camera_tensors_receive_gradients(specs, cuda, kind):
     cam, pack, _ = camera_inputs(spec, cuda)
     W, H = spec.width, spec.height
     leaves = [cam.q0, cam.t0, cam.v, cam.w, cam.rolling_time, cam.trigger_time, cam.pose_time,
-              cam.normalized_intrinsics] + ([cam.distortion] if kind == "fisheye" else [])
+              cam.normalized_intrinsics] + ([cam.distortion] if kind != "pinhole" else [])
     for t in leaves:
         t.requires_grad_(True)
     go, gd = _upstream(H, W, 13, kind, pack)
@@ -124,8 +124,11 @@ def test_camera_tensors_receive_gradients(specs, cuda, kind):
         loss.backward()
         want = O.camera_rays_bwd(kind, pack, W, H, go if return_origins else None, gd)
         got = np.concatenate([to_np(t.grad).reshape(-1) for t in leaves[:4]] + [[0.0]] +
-                             [to_np(t.grad).reshape(-1) for t in leaves[4:]])
+                             [to_np(t.grad).reshape(-1) for t in leaves[4:]] +
+                             ([[0.0]] if kind == "distorted" else []))  # max_radius^2: no gradient
         check_pack_grad(got, want, f"{kind} leaves origins={return_origins}")
+        if kind == "distorted":
+            assert want[30] == 0.0
 
 
 @pytest.mark.parametrize("kind", KINDS)

@@ -15,6 +15,47 @@ import torch
 from oracle import oracle as O
 
 
+DIST8 = (-0.25, 0.07, 3e-4, -2e-4, -0.008, 0.03, 0.002, 0.0005)  # k1 k2 p1 p2 k3 k4 k5 k6
+
+
+def distort_t(x, y, k):
+    """OpenCV rational + tangential distortion of (x, y) (torch, any dtype)."""
+    k1, k2, p1, p2, k3, k4, k5, k6 = (k[i] for i in range(8))
+    r2 = x * x + y * y
+    sc = (1 + r2 * (k1 + r2 * (k2 + r2 * k3))) / (1 + r2 * (k4 + r2 * (k5 + r2 * k6)))
+    return (x * sc + 2 * p1 * x * y + p2 * (r2 + 2 * x * x), y * sc + p1 * (r2 + 2 * y * y) + 2 * p2 * x * y)
+
+
+def undistort_t(xd, yd, k):
+    """D(x) = xd solved by Newton with a differentiable last step: the step
+    at the converged root has the implicit-function derivative in k and xd."""
+    with torch.no_grad():
+        x, y = xd.clone(), yd.clone()
+        kd = k.detach()
+        for _ in range(20):
+            x.requires_grad_(True)
+            y.requires_grad_(True)
+            with torch.enable_grad():
+                fx, fy = distort_t(x, y, kd)
+                jxx, jxy = torch.autograd.grad(fx.sum(), (x, y), retain_graph=True)
+                jyx, jyy = torch.autograd.grad(fy.sum(), (x, y))
+            det = jxx * jyy - jxy * jyx
+            rx, ry = fx.detach() - xd, fy.detach() - yd
+            x = (x - (jyy * rx - jxy * ry) / det).detach()
+            y = (y - (jxx * ry - jyx * rx) / det).detach()
+    x.requires_grad_(True)
+    y.requires_grad_(True)
+    with torch.enable_grad():
+        fx, fy = distort_t(x, y, kd)
+        jxx, jxy = torch.autograd.grad(fx.sum(), (x, y), retain_graph=True)
+        jyx, jyy = torch.autograd.grad(fy.sum(), (x, y))
+    x, y = x.detach(), y.detach()
+    det = jxx * jyy - jxy * jyx
+    rx, ry = distort_t(x, y, k)
+    rx, ry = rx - xd, ry - yd
+    return x - (jyy * rx - jxy * ry) / det, y - (jxx * ry - jyx * rx) / det
+
+
 def _base(words, w=(0.01, -0.02, 0.3), q0=(0.9, 0.1, -0.3, 0.2)):
     p = np.zeros(words, np.float32)
     p[0:4] = q0
@@ -29,10 +70,14 @@ def _base(words, w=(0.01, -0.02, 0.3), q0=(0.9, 0.1, -0.3, 0.2)):
 
 def camera_pack(kind, w=(0.01, -0.02, 0.3), q0=(0.9, 0.1, -0.3, 0.2)):
     p = _base(O.WORDS[kind], w, q0)
-    if kind in ("pinhole", "fisheye"):
+    if kind in ("pinhole", "fisheye", "distorted"):
         p[18:22] = (0.45, 0.6, 0.52, 0.47)
         if kind == "fisheye":
             p[22:26] = (0.03, -0.02, 0.01, -0.004)
+        if kind == "distorted":
+            p[18:20] = (0.9, 1.2)  # the image stays inside the model's monotone range
+            p[22:30] = DIST8
+            p[30] = 4.0
     else:
         p[18:22] = (0.1, 6.0, -0.4, 0.9)  # phi_min, phi_range, theta_min, theta_range
     return p
@@ -95,10 +140,13 @@ def _qmul(a, b):
 def torch_rays(kind, pk, W, H, world, normalized, elev=None):
     U, V = _grid_uv(kind, W, H, elev)
     Ut, Vt = torch.tensor(U, dtype=torch.float64), torch.tensor(V, dtype=torch.float64)
-    if kind in ("pinhole", "fisheye"):
+    if kind in ("pinhole", "fisheye", "distorted"):
         ux, uy = (Ut - pk[20]) / pk[18], (Vt - pk[21]) / pk[19]
         if kind == "pinhole":
             ray = torch.stack([ux, uy, torch.ones_like(ux)], -1)
+        elif kind == "distorted":
+            x, y = undistort_t(ux, uy, pk[22:30])
+            ray = torch.stack([x, y, torch.ones_like(x)], -1)
         else:
             k = pk[22:26]
             p32 = pk.detach().numpy().astype(np.float32)
@@ -150,7 +198,8 @@ def _elev(H):
 
 def _check(got, want, what):
     """Per camera tensor: |got - want| <= 1e-6 * (|want| + max|want| of the tensor)."""
-    groups = [(0, 4), (4, 7), (7, 10), (10, 13), (13, 14), (14, 16), (16, 17), (17, 18), (18, 22), (22, 26)]
+    groups = [(0, 4), (4, 7), (7, 10), (10, 13), (13, 14), (14, 16), (16, 17), (17, 18), (18, 22), (22, 26),
+              (26, 30), (30, 31)]
     for a, b in groups:
         if a >= len(want):
             break
@@ -159,7 +208,7 @@ def _check(got, want, what):
         assert (np.abs(g - w) <= bound).all(), f"{what} words {a}:{b}: {g} vs {w}"
 
 
-@pytest.mark.parametrize("kind", ["pinhole", "fisheye", "spherical", "lidar"])
+@pytest.mark.parametrize("kind", ["pinhole", "fisheye", "spherical", "lidar", "distorted"])
 @pytest.mark.parametrize("world,normalized", [(True, True), (False, True), (True, False), (False, False)])
 def test_oracle_ray_backward_is_autograd(kind, world, normalized):
     W, H = 24, 16

@@ -193,6 +193,75 @@ class FisheyeCamera(FusedRSCamera):
         return self
 
 
+def max_valid_radius(normalized_intrinsics, distortion, margin: float = 1.5, search_limit: float = 16.0,
+                     num_samples: int = 8192) -> torch.Tensor:
+    """Largest camera-space radius r = |xy| / z at which an 8-coefficient
+    calibration is trusted (cameras/torch/distortion_utils.py:96-164): the
+    smaller of the first r where the radial map rho(r) = r * scale(r) stops
+    increasing (past it two ray angles share an image point) and `margin`
+    times the radius of the farthest image corner, found by inverting rho on
+    its running maximum.  Both are read off the same grid of `num_samples`
+    radii in [0, search_limit].  Returns a [..., 1] tensor."""
+    dist = distortion.reshape(-1, 8)
+    intr = normalized_intrinsics.reshape(-1, 4)
+    r = torch.linspace(0.0, search_limit, num_samples, device=dist.device, dtype=dist.dtype)
+    r2 = (r * r)[None, :]
+    k = [dist[:, i:i + 1] for i in range(8)]  # k1 k2 p1 p2 k3 k4 k5 k6
+    rho = r[None, :] * ((1.0 + r2 * (k[0] + r2 * (k[1] + r2 * k[4]))) /
+                        (1.0 + r2 * (k[5] + r2 * (k[6] + r2 * k[7]))))
+    falls = rho[:, 1:] < rho[:, :-1]
+    first_fall = torch.where(falls.any(dim=-1), falls.to(torch.uint8).argmax(dim=-1),
+                             torch.full((dist.shape[0],), num_samples - 1, dtype=torch.long, device=dist.device))
+    corners = torch.tensor([[0.0, 0.0], [1.0, 0.0], [0.0, 1.0], [1.0, 1.0]], device=dist.device, dtype=dist.dtype)
+    reach = ((corners[None] - intr[:, None, 2:]) / intr[:, None, :2]).norm(dim=-1).amax(dim=-1)
+    at_corner = torch.searchsorted(rho.cummax(dim=-1).values.contiguous(), reach[:, None])[:, 0]
+    at_corner = at_corner.clamp(max=num_samples - 1)
+    radius = torch.minimum(r[first_fall], margin * r[at_corner])
+    return radius.reshape(*distortion.shape[:-1], 1)
+
+
+class DistortedPerspectiveCamera(PerspectiveCamera):
+    """Pinhole with the OpenCV 8-coefficient model: `distortion` =
+    (k1, k2, p1, p2, k3, k4, k5, k6); intrinsics normalised by the image size
+    (cameras/ext/distorted_perspective.py, cameras/torch/distorted_perspective.py).
+    The pack also carries max_radius^2 (`max_radius`, derived from the
+    coefficients and intrinsics, `max_radius_margin` past the image corner):
+    points beyond it do not project, rays beyond it are not valid."""
+    ext_cls = _C.DistortedPerspectiveCamera
+    max_radius_margin: float = 1.5
+
+    def __init__(self, q0, t0, normalized_intrinsics, distortion, **kw):
+        super().__init__(q0, t0, normalized_intrinsics, **kw)
+        self.distortion = _vec(distortion, 8, self.device)
+        self._max_radius = None
+
+    @property
+    def max_radius(self) -> torch.Tensor:
+        if self._max_radius is None:
+            self._max_radius = max_valid_radius(self.normalized_intrinsics.detach(), self.distortion.detach(),
+                                                margin=self.max_radius_margin)
+        return self._max_radius
+
+    @property
+    def _pack_data(self):
+        return super()._pack_data + [self.distortion, self.max_radius.reshape(1).square().contiguous()]
+
+    def undistort_map(self, width: int, height: int, normalized_range: bool = False):
+        return self.ext_cls.undistort_map(self.pack, width=width, height=height, normalized_range=normalized_range)
+
+    def undistort(self) -> PerspectiveCamera:
+        """The same camera without distortion."""
+        return PerspectiveCamera(self.q0, self.t0, self.normalized_intrinsics, v=self.v, w=self.w,
+                                 rolling_time=self.rolling_time, trigger_time=self.trigger_time,
+                                 pose_time=self.pose_time, camera_name=self.camera_name)
+
+    def to(self, device):
+        super().to(device)
+        self.distortion = self.distortion.to(device)
+        self._max_radius = None
+        return self
+
+
 class SphericalCamera(FusedRSCamera):
     """Equirectangular range image; limits [phi_min, phi_range, theta_min, theta_range]."""
     ext_cls = _C.SphericalCamera

@@ -181,6 +181,148 @@ struct Fisheye : CamBase {
     __device__ __forceinline__ void to_uvd_jac(int, v3, v3, v3&, float2&) const {}
 };
 
+// OpenCV 8-coefficient pinhole (k1 k2 p1 p2 | k3 k4 k5 k6, rational radial
+// model + tangential), DistortedPerspectiveCameraImpl,
+// csrc/cameras/distorted_perspective.cu:6-230 and include/cameras/distortion.h:8-30.
+// Pack words 18..30: f.x f.y c.x c.y, k1 k2 p1 p2, k3 k4 k5 k6, max_radius^2.
+struct Distorted : CamBase {
+    static constexpr int kType = XSG_CAM_DISTORTED;
+    static constexpr bool kJacobian = false;
+    static constexpr int kWords = 31;
+    static constexpr float kMinDet = 1e-3f;
+    float2 f, c;
+    float4 d0, d1;  // (k1, k2, p1, p2), (k3, k4, k5, k6)
+    float max_r2;
+    __device__ __forceinline__ void load(const float* p) {
+        load_base(p);
+        f = make_float2(p[18], p[19]);
+        c = make_float2(p[20], p[21]);
+        d0 = make_float4(p[22], p[23], p[24], p[25]);
+        d1 = make_float4(p[26], p[27], p[28], p[29]);
+        max_r2 = p[30];
+    }
+    __device__ __forceinline__ float2 pixel_to_uv(int px, int py, int W, int H) const {
+        return make_float2((float(px) + 0.5f) / float(W), (float(py) + 0.5f) / float(H));
+    }
+    // Distortion D(x) = x * scale(r2) + delta(x) at x, with its (symmetric)
+    // Jacobian; DistortionState, distorted_perspective.cu:11-78.
+    struct State {
+        float scale, denom, dx, dy, juu, juv, jvv;
+        __device__ __forceinline__ float det() const { return juu * jvv - juv * juv; }
+    };
+    __device__ __forceinline__ State state_at(float u, float v) const {
+        const float r2 = u * u + v * v;
+        const float num = 1.0f + r2 * (d0.x + r2 * (d0.y + r2 * d1.x));
+        const float den = 1.0f + r2 * (d1.y + r2 * (d1.z + r2 * d1.w));
+        const float sc = num / den;
+        const float dn = d0.x + r2 * (2.0f * d0.y + 3.0f * d1.x * r2);
+        const float dd = d1.y + r2 * (2.0f * d1.z + 3.0f * d1.w * r2);
+        const float dsc = (dn * den - num * dd) / (den * den);
+        State st;
+        st.scale = sc;
+        st.denom = den;
+        st.dx = 2.0f * d0.z * u * v + d0.w * (r2 + 2.0f * u * u);
+        st.dy = d0.z * (r2 + 2.0f * v * v) + 2.0f * d0.w * u * v;
+        st.juu = sc + 2.0f * u * u * dsc + 2.0f * d0.z * v + 6.0f * d0.w * u;
+        st.juv = 2.0f * u * v * dsc + 2.0f * d0.z * u + 2.0f * d0.w * v;
+        st.jvv = sc + 2.0f * v * v * dsc + 6.0f * d0.z * v + 2.0f * d0.w * u;
+        return st;
+    }
+    // Five Newton steps on D(x) = xd (a fixed-point step where the Jacobian
+    // is near singular); `st` is left at the last step's starting point.
+    __device__ __forceinline__ float2 undistort(float2 xd, State& st) const {
+        float2 x = xd;
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            st = state_at(x.x, x.y);
+            const float rx = x.x * st.scale + st.dx - xd.x;
+            const float ry = x.y * st.scale + st.dy - xd.y;
+            const float det = st.det();
+            if (fabsf(det) > kMinDet) {
+                x.x -= (st.jvv * rx - st.juv * ry) / det;
+                x.y -= (st.juu * ry - st.juv * rx) / det;
+            } else {
+                x = make_float2((xd.x - st.dx) / st.scale, (xd.y - st.dy) / st.scale);
+            }
+        }
+        return x;
+    }
+    __device__ __forceinline__ v3 ray_cs(float2 uv) const {
+        State st;
+        const float2 x = undistort(make_float2((uv.x - c.x) / f.x, (uv.y - c.y) / f.y), st);
+        return mk3(x.x, x.y, 1.0f);
+    }
+    __device__ __forceinline__ bool ray_valid(float2 uv) const {
+        State st;
+        const float2 xd = make_float2((uv.x - c.x) / f.x, (uv.y - c.y) / f.y);
+        const float2 x = undistort(xd, st);
+        const float rx = x.x * st.scale + st.dx - xd.x;
+        const float ry = x.y * st.scale + st.dy - xd.y;
+        const float r2 = x.x * x.x + x.y * x.y;
+        return (r2 <= max_r2) && (fabsf(rx) < 1e-5f) && (fabsf(ry) < 1e-5f);
+    }
+    // Backward into f, c (18..21) and the eight coefficients (22..29) at the
+    // re-solved point, implicit in D(x; k) = (uv - c) / f:
+    // g_d = J^-T d_ray.xy, dL/dk = -g_d . dD/dk (distorted_perspective.cu:115-190).
+    template <int P>
+    __device__ __forceinline__ void ray_cs_bwd(float2 uv, v3 d, float (&acc)[P]) const {
+        const float ifx = 1.0f / f.x, ify = 1.0f / f.y;
+        const float2 xd = make_float2((uv.x - c.x) * ifx, (uv.y - c.y) * ify);
+        State st;
+        const float2 x = undistort(xd, st);
+        st = state_at(x.x, x.y);
+        const float det = st.det();
+        float gx, gy;
+        if (fabsf(det) <= kMinDet) {
+            gx = d.x / st.scale;
+            gy = d.y / st.scale;
+        } else {
+            gx = (st.jvv * d.x - st.juv * d.y) / det;
+            gy = (st.juu * d.y - st.juv * d.x) / det;
+        }
+        acc[18] -= gx * xd.x * ifx;
+        acc[19] -= gy * xd.y * ify;
+        acc[20] -= gx * ifx;
+        acc[21] -= gy * ify;
+        const float r2 = x.x * x.x + x.y * x.y, r4 = r2 * r2, r6 = r4 * r2;
+        const float rad = -(gx * x.x + gy * x.y) / st.denom;
+        const float rad_den = -rad * st.scale;
+        acc[22] += rad * r2;
+        acc[23] += rad * r4;
+        acc[24] -= gx * 2.0f * x.x * x.y + gy * (r2 + 2.0f * x.y * x.y);
+        acc[25] -= gx * (r2 + 2.0f * x.x * x.x) + gy * 2.0f * x.x * x.y;
+        acc[26] += rad * r6;
+        acc[27] += rad_den * r2;
+        acc[28] += rad_den * r4;
+        acc[29] += rad_den * r6;
+    }
+    // uv_distortion (distortion.h:8-30) applied to x.
+    __device__ __forceinline__ float2 distort(float2 x) const {
+        const float uu = x.x * x.x, vv = x.y * x.y;
+        const float r2 = uu + vv;
+        const float num = 1.0f + r2 * (d0.x + r2 * (d0.y + r2 * d1.x));
+        const float den = 1.0f + r2 * (d1.y + r2 * (d1.z + r2 * d1.w));
+        const float sc = num / den;
+        const float uv2 = 2.0f * x.x * x.y;
+        return make_float2(x.x * sc + (d0.z * uv2 + d0.w * (r2 + 2.0f * uu)),
+                           x.y * sc + (d0.z * (r2 + 2.0f * vv) + d0.w * uv2));
+    }
+    // camera_point_to_uvd, distorted_perspective.cu:192-199: depth 0 beyond
+    // the trusted radius.
+    __device__ __forceinline__ v3 to_uvd(int, v3 p) const {
+        const float2 x = make_float2(p.x / p.z, p.y / p.z);
+        const float2 xd = distort(x);
+        const float r2 = x.x * x.x + x.y * x.y;
+        return mk3(xd.x * f.x + c.x, xd.y * f.y + c.y, (r2 <= max_r2) ? p.z : 0.0f);
+    }
+    __device__ __forceinline__ void to_uvd_jac(int, v3, v3, v3&, float2&) const {}
+    // distort_uv, distorted_perspective.cu:201-205
+    __device__ __forceinline__ float2 distort_uv(float2 uv) const {
+        const float2 xd = distort(make_float2((uv.x - c.x) / f.x, (uv.y - c.y) / f.y));
+        return make_float2(xd.x * f.x + c.x, xd.y * f.y + c.y);
+    }
+};
+
 template <bool kLidar>
 struct Spherical : CamBase {
     static constexpr int kType = kLidar ? XSG_CAM_LIDAR : XSG_CAM_SPHERICAL;
@@ -385,6 +527,7 @@ int dispatch_camera(int type, F&& f) {
         case XSG_CAM_FISHEYE: f(Fisheye{}); return XSG_OK;
         case XSG_CAM_SPHERICAL: f(Spherical<false>{}); return XSG_OK;
         case XSG_CAM_LIDAR: f(Spherical<true>{}); return XSG_OK;
+        case XSG_CAM_DISTORTED: f(Distorted{}); return XSG_OK;
         default: return set_error(XSG_ERR_INVALID_ARGUMENT, "unknown camera type");
     }
 }

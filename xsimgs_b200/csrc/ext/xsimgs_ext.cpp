@@ -273,7 +273,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> projection_utgs(const CameraSpec& spe
 }
 
 template <typename Cls>
-void bind_camera(py::module& m, const char* name, CameraSpec spec, bool with_phm) {
+py::class_<Cls> bind_camera(py::module& m, const char* name, CameraSpec spec, bool with_phm) {
     auto cls = py::class_<Cls>(m, name);
     cls.def_static("pack", [spec](const std::vector<Tensor>& tensors) { return camera_pack(spec, tensors); },
                    py::arg("tensors"));
@@ -322,12 +322,25 @@ void bind_camera(py::module& m, const char* name, CameraSpec spec, bool with_phm
                        py::arg("residual_thr_early_stop") = kResidualEarlyStop,
                        py::arg("max_residual") = kResidualMax, py::arg("max_margin") = kMaxMargin);
     }
+    return cls;
 }
 
 struct PerspectiveCamera {};
 struct OpenCVFisheyeCamera {};
 struct SphericalCamera {};
 struct LidarCamera {};
+struct DistortedPerspectiveCamera {};
+
+Tensor undistort_map(const CameraSpec& spec, const Tensor& pack, int64_t width, int64_t height,
+                     bool normalized_range) {
+    validate_pack(spec, pack);
+    TORCH_CHECK(width > 0 && height > 0, "undistort_map: width and height must be positive");
+    c10::cuda::CUDAGuard g(pack.device());
+    Tensor out = at::empty({height, width, 2}, pack.options());
+    check(xsg_undistort_map(spec.type, fptr(pack), int(width), int(height), normalized_range, fptr_mut(out),
+                            stream()));
+    return out;
+}
 
 // --------------------------------------------------------------- tiling --
 std::tuple<Tensor, Tensor, Tensor> isect_regular_tiles(const Tensor& means2d, const Tensor& radii,
@@ -820,6 +833,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     bind_camera<OpenCVFisheyeCamera>(m, "OpenCVFisheyeCamera", {XSG_CAM_FISHEYE, "OpenCVFisheyeCamera", {4, 4}}, false);
     bind_camera<SphericalCamera>(m, "SphericalCamera", {XSG_CAM_SPHERICAL, "SphericalCamera", {4}}, true);
     bind_camera<LidarCamera>(m, "LidarCamera", {XSG_CAM_LIDAR, "LidarCamera", {4, 2}}, true);
+    {
+        const CameraSpec spec{XSG_CAM_DISTORTED, "DistortedPerspectiveCamera", {4, 8, 1}};
+        bind_camera<DistortedPerspectiveCamera>(m, "DistortedPerspectiveCamera", spec, false)
+            .def_static("undistort_map",
+                        [spec](const Tensor& pack, int64_t width, int64_t height, bool normalized_range) {
+                            return undistort_map(spec, pack, width, height, normalized_range);
+                        },
+                        py::arg("pack"), py::arg("width"), py::arg("height"), py::arg("normalized_range") = false);
+    }
 
     m.def("isect_regular_tiles", &isect_regular_tiles, py::arg("means2d"), py::arg("radii"), py::arg("depth"),
           py::arg("img_width"), py::arg("img_height"), py::arg("tile_size_x"), py::arg("tile_size_y"),

@@ -56,6 +56,18 @@ __global__ void pixel_time_kernel(const float* __restrict__ pack, int W, int H, 
     out[idx] = delta ? t - k.pose : t;
 }
 
+// undistort_map, distortion.h:33-56 (the reference maps to [-1, 1] when
+// normalized_range is false)
+__global__ void undistort_map_kernel(const float* __restrict__ pack, int W, int H, int normalized_range,
+                                     float2* __restrict__ out) {
+    const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= int64_t(W) * H) return;
+    Distorted k;
+    k.load(pack);
+    const float2 r = k.distort_uv(k.pixel_to_uv(int(idx % W), int(idx / W), W, H));
+    out[idx] = normalized_range ? r : make_float2(r.x * 2.0f - 1.0f, r.y * 2.0f - 1.0f);
+}
+
 // camera_projection_fwd, projection_kernels.h:259-309
 template <typename Cam, bool kJac>
 __global__ void projection_kernel(const float* __restrict__ pack, const float* __restrict__ pts,
@@ -157,6 +169,7 @@ int xsg_camera_pack_words(int type) {
         case XSG_CAM_FISHEYE: return 26;
         case XSG_CAM_SPHERICAL: return 22;
         case XSG_CAM_LIDAR: return 24;
+        case XSG_CAM_DISTORTED: return 31;
         default: return -1;
     }
 }
@@ -198,6 +211,16 @@ int xsg_pixel_time_from_uv(int type, const float* pack, const float* uv, int64_t
     });
     if (rc != XSG_OK) return rc;
     return check_launch("pixel_time_from_uv");
+}
+
+int xsg_undistort_map(int type, const float* pack, int W, int H, int normalized_range, float* out,
+                      xsg_stream_t stream) {
+    XSG_REQUIRE(pack && out && W > 0 && H > 0, "undistort_map: bad arguments");
+    if (type != XSG_CAM_DISTORTED) return set_error(XSG_ERR_UNSUPPORTED, "undistort_map: camera has no distortion");
+    const int64_t n = int64_t(W) * H;
+    launch(undistort_map_kernel, blocks_for(n, kThreads), kThreads, 0, as_cuda(stream), pack, W, H,
+           normalized_range, reinterpret_cast<float2*>(out));
+    return check_launch("undistort_map");
 }
 
 int xsg_projection(int type, const float* pack, const float* pts, const float* vel, int64_t n,

@@ -91,7 +91,7 @@ def street_scene(n: int = 1_000_000, seed: int = 0, sh_degree: int = 3) -> Gauss
 
 @dataclass
 class CameraSpec:
-    kind: str            # "pinhole" | "fisheye" | "lidar" | "spherical"
+    kind: str            # "pinhole" | "fisheye" | "distorted" | "lidar" | "spherical"
     width: int
     height: int
     q0: np.ndarray       # camera->world wxyz
@@ -108,7 +108,7 @@ class CameraSpec:
     w: tuple = (0.0, 0.0, 0.0)
 
     def make(self, device):
-        from .cameras import PerspectiveCamera, FisheyeCamera, LidarCamera, SphericalCamera
+        from .cameras import DistortedPerspectiveCamera, PerspectiveCamera, FisheyeCamera, LidarCamera, SphericalCamera
         kw = dict(v=self.v, w=self.w, rolling_time=self.rolling_time, trigger_time=self.trigger_time,
                   pose_time=self.pose_time, device=device)
         q0 = torch.as_tensor(self.q0, dtype=torch.float32, device=device)
@@ -117,6 +117,8 @@ class CameraSpec:
             return PerspectiveCamera(q0, t0, self.intrinsics, **kw)
         if self.kind == "fisheye":
             return FisheyeCamera(q0, t0, self.intrinsics, self.distortion, **kw)
+        if self.kind == "distorted":
+            return DistortedPerspectiveCamera(q0, t0, self.intrinsics, self.distortion, **kw)
         if self.kind == "lidar":
             cam = LidarCamera.create(q0, t0, torch.as_tensor(self.beam_angles, dtype=torch.float32),
                                      self.phi_min, self.phi_range, **kw)
