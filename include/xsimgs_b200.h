@@ -410,6 +410,22 @@ int xsg_rigid_transform_bwd(int64_t n, const float* positions, const float* rota
                             const float* v_velocities, float* grad_positions, float* grad_rotations,
                             float* grad_q, float* grad_t, float* grad_v, float* grad_w, xsg_stream_t stream);
 
+/* Float RGB image [n_pixels, 3] -> bytes, each channel
+ * (uint8)(saturate(x) * 255) (NaN -> 0):
+ *   XSG_IMG_HWC_RGB  out [n_pixels, 3]
+ *   XSG_IMG_HWC_RGBA out [n_pixels, 4], alpha 255
+ *   XSG_IMG_CHW_RGB  out [3, n_pixels] (planar)
+ * image 4-byte aligned; 16-byte aligned image and output take the vector
+ * path.  Replaces image_to_hwc_rgb_byte / image_to_hwc_rgba_byte /
+ * image_to_chw_rgb_byte, csrc/nodes/img_layout.cu:9-115. */
+enum xsg_image_layout {
+    XSG_IMG_HWC_RGB = 0,
+    XSG_IMG_HWC_RGBA = 1,
+    XSG_IMG_CHW_RGB = 2,
+};
+int xsg_image_to_bytes(int layout, const float* image, int64_t n_pixels, uint8_t* out,
+                       xsg_stream_t stream);
+
 /* Replaces packed_mask_from_instances (csrc/nodes/gs_masking.cu:27-43):
  * out u32[ceil(n/32)], bit i = 1 when instance_ids[i] < 0 (not an
  * instance) or instance_mask[instance_ids[i]] != 0; bits past n are 0. */

@@ -394,3 +394,16 @@ def undistort_map(pack, W, H, normalized_range=False):
     out = np.zeros((H, W, 2), np.float32)
     lib().xsgo_undistort_map(_p(pack), C.c_int(W), C.c_int(H), C.c_int(int(normalized_range)), _p(out))
     return out
+
+
+IMAGE_LAYOUTS = {"hwc_rgb": 0, "hwc_rgba": 1, "chw_rgb": 2}
+
+
+def image_to_bytes(image, layout):
+    """float32 [H, W, 3] -> uint8 [H, W, 3] / [H, W, 4] / [3, H, W]."""
+    image = _f32(image)
+    H, W = image.shape[:2]
+    shape = {"hwc_rgb": (H, W, 3), "hwc_rgba": (H, W, 4), "chw_rgb": (3, H, W)}[layout]
+    out = np.zeros(shape, np.uint8)
+    lib().xsgo_image_to_bytes(C.c_int(IMAGE_LAYOUTS[layout]), C.c_int64(H * W), _p(image), _p(out))
+    return out

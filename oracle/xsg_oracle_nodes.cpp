@@ -253,4 +253,24 @@ void xsgo_interpolate_smpl_bwd(int64_t n_obj, int frames, int joints, float quer
     *d_query = float(dqt);
 }
 
+// image_to_{hwc_rgb,hwc_rgba,chw_rgb}_byte, csrc/nodes/img_layout.cu:9-54:
+// (uint8)(saturate(x) * 255) per channel, saturate(NaN) = 0; layout 0 = HWC
+// RGB, 1 = HWC RGBA (alpha 255), 2 = planar CHW RGB.
+void xsgo_image_to_bytes(int layout, int64_t n, const float* in, uint8_t* out) {
+    auto byte = [](float x) {
+        const float s = x > 0.0f ? (x < 1.0f ? x : 1.0f) : 0.0f;
+        return static_cast<uint8_t>(s * 255.0f);
+    };
+    for (int64_t i = 0; i < n; ++i) {
+        const uint8_t r = byte(in[3 * i]), g = byte(in[3 * i + 1]), b = byte(in[3 * i + 2]);
+        if (layout == 0) {
+            out[3 * i] = r; out[3 * i + 1] = g; out[3 * i + 2] = b;
+        } else if (layout == 1) {
+            out[4 * i] = r; out[4 * i + 1] = g; out[4 * i + 2] = b; out[4 * i + 3] = 255;
+        } else {
+            out[i] = r; out[n + i] = g; out[2 * n + i] = b;
+        }
+    }
+}
+
 }  // extern "C"

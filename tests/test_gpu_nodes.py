@@ -96,3 +96,43 @@ def test_interpolation_matches_oracle(cuda, query):
     assert_grads_close(d_poses, r_poses, "d_poses", rtol=2e-4)
     np.testing.assert_allclose(to_np(d_root), r_root, atol=1e-5)
     np.testing.assert_allclose(float(to_np(d_q)[0]), r_q, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("layout", ["hwc_rgb", "hwc_rgba", "chw_rgb"])
+@pytest.mark.parametrize("hw", [(1, 1), (7, 5), (48, 64), (1080, 1920), (3, 1)])
+def test_image_layouts_match_oracle(cuda, layout, hw):
+    """Bit-exact against the oracle, including NaN / inf / out-of-range values
+    and exact k/255 levels, for pixel counts that are and are not multiples
+    of four (vector and tail kernels)."""
+    from tests.test_oracle_nodes import _image_values
+    from xsimgs_b200 import nodes
+    fn = {"hwc_rgb": nodes.image_to_hwc_rgb_byte, "hwc_rgba": nodes.image_to_hwc_rgba_byte,
+          "chw_rgb": nodes.image_to_chw_rgb_byte}[layout]
+    img = _image_values(np.random.default_rng(hw[0] * 7 + hw[1]), (*hw, 3))
+    got = fn(torch.from_numpy(img).to(cuda))
+    assert got.dtype == torch.uint8 and got.is_cuda
+    np.testing.assert_array_equal(to_np(got), O.image_to_bytes(img, layout))
+    # the reference's host-memory path gives the same bytes on finite values
+    fin = np.nan_to_num(img, nan=0.0, posinf=2.0, neginf=-1.0)
+    np.testing.assert_array_equal(to_np(fn(torch.from_numpy(fin).to(cuda))), to_np(fn(torch.from_numpy(fin))))
+
+
+@pytest.mark.parametrize("layout", ["hwc_rgb", "hwc_rgba", "chw_rgb"])
+def test_image_layouts_unaligned_and_strided(cuda, layout):
+    from xsimgs_b200 import _C
+    fn = getattr(_C, f"image_to_{layout}_byte")
+    rng = np.random.default_rng(3)
+    H, W = 37, 53
+    base = torch.from_numpy(rng.uniform(-0.2, 1.2, size=H * W * 3 + 1).astype(np.float32)).to(cuda)
+    img = base[1:].view(H, W, 3)  # 4-byte but not 16-byte aligned: the per-pixel kernel
+    assert img.data_ptr() % 16 != 0
+    np.testing.assert_array_equal(to_np(fn(img)), O.image_to_bytes(to_np(img), layout))
+    big = torch.from_numpy(rng.uniform(-0.2, 1.2, size=(H, 2 * W, 3)).astype(np.float32)).to(cuda)
+    view = big[:, ::2]  # non-contiguous: made contiguous first
+    np.testing.assert_array_equal(to_np(fn(view)), O.image_to_bytes(to_np(view), layout))
+    empty = torch.zeros(0, 4, 3, device=cuda)
+    assert fn(empty).numel() == 0
+    with pytest.raises(RuntimeError, match="must have dimensions"):
+        fn(torch.zeros(4, 4, 4, device=cuda))
+    with pytest.raises(RuntimeError, match="float32"):
+        fn(torch.zeros(4, 4, 3, device=cuda, dtype=torch.float16))

@@ -118,3 +118,26 @@ def test_oracle_interpolation_is_autograd(query):
     np.testing.assert_allclose(d_root, tr.grad.numpy(), atol=1e-6)
     want_q = float(tqt.grad[0]) if tqt.grad is not None else 0.0  # outside every key range: no gradient
     np.testing.assert_allclose(d_q, want_q, rtol=1e-3, atol=1e-3)
+
+
+def _image_values(rng, shape):
+    img = rng.uniform(-0.3, 1.3, size=shape).astype(np.float32)
+    flat = img.reshape(-1)
+    special = np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 1.0, 1.0 + 1e-7, 1.0 - 1e-7, 0.5 / 255, 1 / 255,
+                        254.9999 / 255, 128 / 255], np.float32)
+    k = min(special.size, flat.size)
+    flat[:k] = special[:k]
+    levels = (np.arange(min(256, flat.size - k)) / 255.0).astype(np.float32)
+    flat[k:k + levels.size] = levels
+    return img
+
+
+@pytest.mark.parametrize("layout", ["hwc_rgb", "hwc_rgba", "chw_rgb"])
+def test_oracle_image_layouts(layout):
+    """Against numpy: saturate (NaN -> 0), times 255 in float32, truncate."""
+    img = _image_values(np.random.default_rng(1), (7, 9, 3))
+    s = np.where(np.isnan(img), np.float32(0), np.clip(img, np.float32(0), np.float32(1))).astype(np.float32)
+    b = (s * np.float32(255)).astype(np.uint8)
+    want = {"hwc_rgb": b, "hwc_rgba": np.concatenate([b, np.full((7, 9, 1), 255, np.uint8)], -1),
+            "chw_rgb": b.transpose(2, 0, 1)}[layout]
+    np.testing.assert_array_equal(O.image_to_bytes(img, layout), want)

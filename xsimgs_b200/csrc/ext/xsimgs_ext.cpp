@@ -773,6 +773,23 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> rigid_transform_bwd(
     return {gp, gr, gq, gt, gv, gw};
 }
 
+// image_to_*_byte, csrc/nodes/img_layout.cu:57-115: the same checks and
+// messages; a non-contiguous image is made contiguous first.
+Tensor image_to_bytes(const Tensor& image_in, int layout) {
+    if (!image_in.is_cuda()) throw std::runtime_error("image is not a CUDA tensor");
+    if (image_in.dim() != 3) throw std::runtime_error("image must have dimensions [H, W, 3]");
+    if (image_in.scalar_type() != at::kFloat) throw std::runtime_error("image must have float32 dtype");
+    if (image_in.size(-1) != 3) throw std::runtime_error("image must have dimensions [H, W, 3]");
+    Tensor image = image_in.contiguous();
+    c10::cuda::CUDAGuard g(image.device());
+    const int64_t H = image.size(0), W = image.size(1);
+    auto opt = image.options().dtype(at::kByte);
+    Tensor out = layout == XSG_IMG_CHW_RGB ? at::empty({3, H, W}, opt)
+                                           : at::empty({H, W, layout == XSG_IMG_HWC_RGBA ? 4 : 3}, opt);
+    check(xsg_image_to_bytes(layout, fptr(image), H * W, out.data_ptr<uint8_t>(), stream()));
+    return out;
+}
+
 Tensor packed_mask_from_instances(const Tensor& instance_ids, const Tensor& instance_mask) {
     check_tensor(instance_ids, "instance_ids", instance_ids);
     check_tensor(instance_mask, "instance_mask", instance_ids);
@@ -977,6 +994,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("instance_id"), py::arg("inst_q"), py::arg("inst_w"), py::arg("inst_mask"),
           py::arg("buffer_offset"), py::arg("per_instance_offsets"), py::arg("gs_inst_offsets"),
           py::arg("v_positions"), py::arg("v_rotations"), py::arg("v_velocities"));
+    m.def("image_to_hwc_rgb_byte", [](const Tensor& image) { return image_to_bytes(image, XSG_IMG_HWC_RGB); },
+          py::arg("image"));
+    m.def("image_to_hwc_rgba_byte", [](const Tensor& image) { return image_to_bytes(image, XSG_IMG_HWC_RGBA); },
+          py::arg("image"));
+    m.def("image_to_chw_rgb_byte", [](const Tensor& image) { return image_to_bytes(image, XSG_IMG_CHW_RGB); },
+          py::arg("image"));
     m.def("packed_mask_from_instances", &packed_mask_from_instances, py::arg("instance_ids"),
           py::arg("instance_mask"));
     m.def("interpolate_smpl_poses_fwd", &interpolate_smpl_fwd, py::arg("smpl_poses"), py::arg("smpl_poses_time"),

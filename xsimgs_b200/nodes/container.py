@@ -13,6 +13,8 @@ import torch
 from .._native import _C
 from ..utils import apply_grad_mask
 
+packed_mask_from_instances = _C.packed_mask_from_instances
+
 
 class RigidTransformAndPut(torch.autograd.Function):
     @staticmethod
