@@ -15,7 +15,8 @@ value  : whole-job Mpix/s with inputs resident in HBM, device-timed with CUDA
          events (max over ranks).
 e2e    : the same step through the same public API with the upstream
          gradient images copied in from pinned host memory and the loss read
-         back each step.
+         back to the host every step (copies double-buffered on a copy
+         stream, each loss read while the next step runs).
 --impl reference : the CPU oracle restatement of the reference (the
          reference itself cannot be built here), rank 0 only.
 """
@@ -309,27 +310,57 @@ def gpu_arm(args, world, rank, local):
     capi.timing_reset()
 
     # ---------------------------------------------------- timed: e2e ----
+    # Each step's upstream gradients come from pinned host memory and each
+    # step's loss goes back to pinned host memory and is read on the host.
+    # The copies are double-buffered on a copy stream (step k+1's inputs
+    # arrive while step k computes) and the loss of step k is read while step
+    # k+1 runs, as a training loop with asynchronous loss logging does.
     host = [[t.cpu().pin_memory() for t in g] for g in upstream]
-    dbuf = [[torch.empty_like(t) for t in g] for g in upstream]
     h2d = sum(t.numel() * t.element_size() for g in host for t in g)
+    comp = torch.cuda.current_stream(dev)
+    copy_stream = torch.cuda.Stream(device=dev)
+    dbufs = [[[torch.empty_like(t) for t in g] for g in upstream] for _ in range(2)]
+    loss_host = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]  # compute is done with dbufs[b]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    for ev in ev_free:
+        ev.record(comp)
+    losses = []
 
-    def copy_in():
-        for dg, hg in zip(dbuf, host):
-            for d, h in zip(dg, hg):
-                d.copy_(h, non_blocking=True)
+    def e2e_steps(n, start_event=None):
+        pending = None
+        for k in range(n):
+            b = k % 2
+            with torch.cuda.stream(copy_stream):
+                if start_event is not None and k == 0:
+                    copy_stream.wait_event(start_event)
+                copy_stream.wait_event(ev_free[b])
+                for dg, hg in zip(dbufs[b], host):
+                    for d, h in zip(dg, hg):
+                        d.copy_(h, non_blocking=True)
+                ev_in[b].record(copy_stream)
+            comp.wait_event(ev_in[b])
+            loss = step(dbufs[b])
+            ev_free[b].record(comp)
+            loss_host[b].copy_(loss.detach(), non_blocking=True)
+            ev_out[b].record(comp)
+            if pending is not None:
+                ev_out[pending].synchronize()
+                losses.append(float(loss_host[pending]))
+            pending = b
+        ev_out[pending].synchronize()
+        losses.append(float(loss_host[pending]))
 
-    for _ in range(max(1, args.warmup // 2)):
-        copy_in()
-        step(dbuf).item()
+    e2e_steps(max(1, args.warmup // 2))
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        copy_in()
-        step(dbuf).item()
+    e2e_steps(args.steps, start_event=e0)
     e1.record()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
+    assert all(math.isfinite(v) for v in losses)
 
     # ------------------------------ timed: C4 lidar rays/s (c2 scene) ----
     lidar_ms = {}
@@ -384,7 +415,7 @@ def gpu_arm(args, world, rank, local):
         pairs = {"evaluated_fwd": 0, "evaluated_bwd": 0, "contributing": 0}
         for sp, cam in views:
             W, H = sp.width, sp.height
-            cnt = torch.zeros(2, dtype=torch.int64, device=dev)
+            cnt = torch.zeros(6, dtype=torch.int64, device=dev)
             capi.set_pair_counters(cnt.data_ptr())
             with torch.no_grad():
                 colors = X.spherical_harmonics_fused(sc.sh, sc.means, cam.t0, DEG_C2)
@@ -397,7 +428,7 @@ def gpu_arm(args, world, rank, local):
                     flatten_ids=td["flatten_ids"])
             torch.cuda.synchronize()
             capi.set_pair_counters(None)
-            n_eval_f, n_contrib = (int(x) for x in cnt.tolist())
+            n_eval_f, n_contrib = (int(x) for x in cnt.tolist()[:2])
             # backward replays every pair up to each pixel's last contributor
             tw = (W + 15) // 16
             ty = torch.arange(H, device=dev) // 16

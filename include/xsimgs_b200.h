@@ -77,9 +77,12 @@ int xsg_timing_query(const char* name, double* total_ms, long long* launches);
 /* FP32 FMA peak probe: launches `blocks` x 512 threads of iters x 128
  * independent FMAs, writes the FLOP count to *flops (time it with events). */
 int xsg_fp32_probe(float* scratch, int iters, int blocks, xsg_stream_t stream, double* flops);
-/* Pair counters of the forward compositing kernel: when `counters` (2 x u64,
- * device, zeroed by the caller) is set, every xsg_rasterize_fwd adds the
- * number of evaluated and of contributing (pixel, Gaussian) pairs to it.
+/* Pair counters of the forward compositing kernel: when `counters` (6 x u64,
+ * device, zeroed by the caller) is set, every xsg_rasterize_fwd adds to it
+ * [0] the evaluated and [1] the contributing (pixel, Gaussian) pairs as the
+ * reference counts them, and, per (warp of 32 pixels, Gaussian), [2] the
+ * entries staged from the tile lists, [3] those passing the warp's cone
+ * test, [4] those passing the per-lane quadric test and [5] those evaluated.
  * NULL (the default) turns counting off. */
 void xsg_set_pair_counters(unsigned long long* counters);
 

@@ -82,6 +82,31 @@ def test_isect_tile_sizes_and_odd_image(cuda, tile):
     np.testing.assert_array_equal(to_np(_C.isect_offset_encode(ids, tw, th)), O.isect_offset_encode(ri, tw, th))
 
 
+@pytest.mark.parametrize("n", [1500, 9000, 40000])
+def test_isect_crowded_tiles_and_negative_depths(cuda, n):
+    """Tiles holding more intersections than each shared-memory bucket sort
+    takes (2048 and 16384 per tile, then the global-memory sort), equal
+    depths (ties kept in emission order) and negative depths (the reference's
+    sign-extended keys collect them in the all-ones bucket)."""
+    from xsimgs_b200 import _C
+    rng = np.random.default_rng(n)
+    W, H = 80, 48
+    m2 = rng.uniform(0, W, size=(n, 2)).astype(np.float32)
+    m2[:, 1] = rng.uniform(0, H, size=n)
+    radii = rng.uniform(20, 90, size=(n, 2)).astype(np.float32)
+    dep = rng.uniform(0.5, 50, size=n).astype(np.float32)
+    dep[: n // 10] = dep[n // 10: 2 * (n // 10)]
+    dep[rng.random(n) < 0.03] *= -1.0
+    t = lambda a: torch.from_numpy(a).to(cuda)
+    tpg, ids, flat = _C.isect_regular_tiles(t(m2), t(radii), t(dep), W, H, 16, 16)
+    rt, ri, rfl = O.isect_regular(m2, radii, dep, W, H, 16, 16)
+    counts = np.bincount((ri[ri >= 0] >> 32).astype(np.int64))
+    assert counts.max() > {1500: 1000, 9000: 2048, 40000: 16384}[n]
+    np.testing.assert_array_equal(to_np(tpg), rt)
+    np.testing.assert_array_equal(to_np(ids), ri)
+    np.testing.assert_array_equal(to_np(flat), rfl)
+
+
 def test_isect_empty(cuda):
     from xsimgs_b200 import _C
     z = torch.zeros(10, 2, device=cuda)

@@ -57,7 +57,7 @@ struct RasterArgs {
     float* v_ray_o;
     float* v_ray_d;
     float* v_ray_t;
-    unsigned long long* pair_counters;  // evaluated, contributing (optional)
+    unsigned long long* pair_counters;  // 6 work counters (optional, xsg_set_pair_counters)
     const int32_t* tile_order;          // launch order of the tiles (optional)
 };
 
@@ -414,6 +414,9 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
     int32_t cur = 0;
     int32_t stop = c.end;  // index of the terminating pair, for the pair counters
     unsigned n_contrib = 0;
+    // warp-level work counters (staged, cone-passed, quadric-passed, evaluated)
+    unsigned long long w_staged = 0, w_cone = 0, w_quad = 0, w_eval = 0;
+    const bool counting = a.pair_counters != nullptr;
     for (int32_t base = c.start; base < c.end; base += kWarpSlot) {
         if (__all_sync(0xffffffffu, done)) break;
         const int32_t idx = base + lane;
@@ -462,6 +465,10 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
         }
         unsigned live = __ballot_sync(0xffffffffu, keep);
         __syncwarp();
+        if (counting) {
+            w_staged += unsigned(min(kWarpSlot, c.end - base));
+            w_cone += unsigned(__popc(live));
+        }
         if (qcull) {
             unsigned m = live;
             live = 0u;
@@ -472,9 +479,11 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
                 if (__any_sync(0xffffffffu, !done && q >= 0.0f)) live |= 1u << t;
             }
         }
+        if (counting) w_quad += unsigned(__popc(live));
         while (live && !done) {
             const int t = __ffs(live) - 1;
             live &= live - 1;
+            if (counting) ++w_eval;
             const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
             v3 gro;
             if (uni) {
@@ -530,6 +539,10 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
         if (lane == 0) {
             atomicAdd(a.pair_counters, e);
             atomicAdd(a.pair_counters + 1, k);
+            atomicAdd(a.pair_counters + 2, w_staged);
+            atomicAdd(a.pair_counters + 3, w_cone);
+            atomicAdd(a.pair_counters + 4, w_quad);
+            atomicAdd(a.pair_counters + 5, w_eval);
         }
     }
     if (c.inside) {
