@@ -225,10 +225,16 @@ int xsg_raster_supported_channels(int* out, int cap);
 /* Forward compositing.  velocity/ray_time_delta non-NULL selects the dynamic
  * variant.  colors [N, cdim] may be NULL with cdim = 0.  Outputs renders
  * [H, W, cdim], depths/alphas [H, W], last_ids i32[H, W].
- * Workspace: xsg_rasterize_workspace_size(n_gauss, cdim).
+ * Workspace: xsg_rasterize_workspace_size(n_gauss, cdim, n_isects, n_tiles,
+ * tile_size_x * tile_size_y) bytes, or with n_isects = n_tiles = 0 the
+ * minimum.  The larger size also holds per-warp contributor masks that the
+ * forward writes and that a backward given the same workspace
+ * (workspace_from_forward) uses to visit only the list entries some pixel
+ * of the warp composited.
  * Replaces rasterize_eval3d_fwd, csrc/rasterization/eval3d_fwd.cu:248-308,
  * and rasterize_eval3d_dynamic_fwd, eval3d_dynamic_fwd.cu:259-323. */
-size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim);
+size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim, int64_t n_isects, int64_t n_tiles,
+                                    int tile_pixels);
 int xsg_rasterize_fwd(const float* means, const float* velocity, const float* quats,
                       const float* scales, const float* colors, int cdim,
                       const float* opacities, int64_t n_gauss, int width, int height,

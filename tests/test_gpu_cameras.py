@@ -314,6 +314,25 @@ def test_composite_fwd_bwd_per_camera(specs, shell, cuda, kind, dynamic):
         if not key.startswith("v_ray"):
             assert_grads_close(got, ref[key], f"{kind} {key} (no ray grads)")
     assert n == to_np(out[0]).shape[0]
+    # the forward's workspace handed to the backward: records, tile order and
+    # contributor masks reused (the backward visits only composited entries)
+    ws = torch.empty(_C.rasterize_workspace_size(n, 3, n_isects=flat.numel(), n_tiles=off.numel(), tile_pixels=256),
+                     dtype=torch.uint8, device=cuda)
+    if dynamic:
+        _C.rasterize_eval3d_dynamic_fwd(velocity=g(shell["vel"]), ray_time_delta=rt, workspace=ws, **args)
+    else:
+        _C.rasterize_eval3d_fwd(workspace=ws, **args)
+    for rg in (True, False):
+        if dynamic:
+            reused = _C.rasterize_eval3d_dynamic_bwd(bwd_args[0], g(shell["vel"]), *bwd_args[1:], rt, 16, 16, *tail,
+                                                     ray_grads=rg, forward_workspace=ws)
+        else:
+            reused = _C.rasterize_eval3d_bwd(*bwd_args, 16, 16, *tail, ray_grads=rg, forward_workspace=ws)
+        for got, key in zip(reused, names):
+            if rg or not key.startswith("v_ray"):
+                if key == "v_ray_t":
+                    got = to_np(got).reshape(H, W)
+                assert_grads_close(got, ref[key], f"{kind} {key} (forward workspace, ray grads {rg})")
 
 
 def test_mask_radii_match_oracle(cuda):

@@ -26,7 +26,7 @@ def lib() -> C.CDLL:
         _lib.xsg_isect_workspace_size.restype = C.c_size_t
         _lib.xsg_isect_workspace_size.argtypes = [C.c_int64, C.c_int64]
         _lib.xsg_rasterize_workspace_size.restype = C.c_size_t
-        _lib.xsg_rasterize_workspace_size.argtypes = [C.c_int64, C.c_int]
+        _lib.xsg_rasterize_workspace_size.argtypes = [C.c_int64, C.c_int, C.c_int64, C.c_int64, C.c_int]
         _lib.xsg_sh_bwd_workspace_size.restype = C.c_size_t
         _lib.xsg_sh_bwd_workspace_size.argtypes = [C.c_int64]
         _lib.xsg_timing_query.argtypes = [C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_longlong)]

@@ -469,7 +469,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> raster_fwd(const Tensor& means, const
     Tensor depths = at::empty({H, W}, opt);
     Tensor alphas = at::empty({H, W}, opt);
     Tensor last_ids = at::empty({H, W}, opt.dtype(at::kInt));
-    const size_t ws_need = xsg_rasterize_workspace_size(n, int(channels));
+    const size_t ws_need = xsg_rasterize_workspace_size(n, int(channels), 0, 0, 0);
     Tensor ws;
     if (has(workspace_in)) {
         check_tensor(*workspace_in, "workspace", means);
@@ -524,7 +524,7 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
         o.v_velocity = at::empty_like(*velocity);
         if (ray_grads) o.v_time = at::empty_like(*ray_t);
     }
-    const size_t ws_need = xsg_rasterize_workspace_size(n, int(cdim));
+    const size_t ws_need = xsg_rasterize_workspace_size(n, int(cdim), 0, 0, 0);
     Tensor ws;
     if (has(fwd_ws)) {
         check_tensor(*fwd_ws, "forward_workspace", points);
@@ -898,10 +898,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("eval3d_supported_ndims", &eval3d_supported_ndims);
     // bytes of the scratch a rasterize call uses: a caller that passes the
     // forward's `workspace` on to the backward as `forward_workspace` lets
-    // the backward reuse the forward's packed records (not in the reference)
+    // the backward reuse the forward's packed records and, when the size
+    // was asked with the intersection and tile counts, its per-warp
+    // contributor masks (not in the reference)
     m.def("rasterize_workspace_size",
-          [](int64_t n_gauss, int64_t channels) { return int64_t(xsg_rasterize_workspace_size(n_gauss, int(channels))); },
-          py::arg("n_gauss"), py::arg("channels"));
+          [](int64_t n_gauss, int64_t channels, int64_t n_isects, int64_t n_tiles, int64_t tile_pixels) {
+              return int64_t(xsg_rasterize_workspace_size(n_gauss, int(channels), n_isects, n_tiles, int(tile_pixels)));
+          },
+          py::arg("n_gauss"), py::arg("channels"), py::arg("n_isects") = 0, py::arg("n_tiles") = 0,
+          py::arg("tile_pixels") = 256);
     m.def("rasterize_eval3d_fwd",
           [](const Tensor& means, const Tensor& quats, const Tensor& scales, const OptT& colors, const Tensor& opac,
              int64_t W, int64_t H, int64_t tsx, int64_t tsy, const Tensor& ray_o, const Tensor& ray_d,

@@ -7,20 +7,22 @@
 // Design (B200):
 //  * A pack kernel turns each Gaussian into one 64-byte record
 //      {M row 0, mu.x} {M row 1, mu.y} {M row 2, mu.z} {opacity, velocity}
-//    with M = S^-1 R^T computed exactly as the reference does per load, so
-//    the tile loops fetch one aligned record (4 x 16 B) per intersection
-//    instead of gathering five arrays.
-//  * One CTA per image tile (one thread per pixel), batches of records staged
-//    in shared memory, block-wide early exit when every pixel is saturated.
-//  * Static scenes whose tile shares one ray origin (global shutter: every
-//    pixel of the tile has bitwise the same ray_o) compute M (o - mu) once per
-//    Gaussian while staging instead of once per pixel — the same arithmetic,
-//    so the same bits.
-//  * Backward: per (warp, Gaussian) the 16 gradient values are reduced with a
-//    transpose butterfly (16 shuffles instead of 80), pre-reduced across the
-//    CTA's warps in shared memory, and flushed once per (tile, Gaussian) with
-//    vector reductions (red.global.add.v4.f32) into a 16-float-per-Gaussian
-//    accumulator; a final pass scatters that into the output layout.
+//    with M = S^-1 R^T computed exactly as the reference does per load, and,
+//    for static scenes, 48 bytes of view constants for the rays that start
+//    at pixel 0's origin (M (o - mu), the quadric pre-test, the cone radius).
+//  * One CTA per image tile, heaviest tiles first; each warp owns an 8 x 4
+//    block of pixels and works on its own (no block barriers): it stages the
+//    tile's records 32 at a time in its slice of shared memory, skips the
+//    Gaussians no ray of its cone can see and, per lane, those whose quadric
+//    test fails for every pixel, and stops when all its pixels saturate.
+//  * The forward records per warp and batch of 32 list entries which ones
+//    some pixel composited (contributor masks); a backward given the
+//    forward's workspace visits exactly those, back to front.
+//  * Backward: per (warp, Gaussian) event the 16 gradient values are reduced
+//    with a transpose butterfly (16 shuffles) and added with four
+//    red.global.add.v4.f32 into a per-Gaussian accumulator; dL/dM is summed
+//    there and turned into quaternion / scale gradients once per Gaussian by
+//    a finalize pass.
 #include "common.cuh"
 
 namespace xsg {
@@ -59,7 +61,17 @@ struct RasterArgs {
     float* v_ray_t;
     unsigned long long* pair_counters;  // 6 work counters (optional, xsg_set_pair_counters)
     const int32_t* tile_order;          // launch order of the tiles (optional)
+    // contributor masks (optional): word ((start >> 5) + tile + k) * warps_per_tile + warp has
+    // bit i set when list entry start + 32 k + i reached alpha >= 1/255 at one of the warp's
+    // pixels before it saturated; the forward writes them, the backward visits only those entries
+    uint32_t* masks;
 };
+
+// Index of the contributor mask of batch k of a warp (tiles' batch ranges
+// [(start >> 5) + tile, + ceil(len / 32)) never overlap).
+__device__ __forceinline__ int64_t mask_index(int32_t start, int tile, int32_t k, int wpt, int wid) {
+    return (int64_t(start >> 5) + tile + k) * wpt + wid;
+}
 
 static unsigned long long* g_pair_counters = nullptr;
 // tile-order scratch is sized for images up to this many tiles (16k x 16k at 16x16)
@@ -480,6 +492,7 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
             }
         }
         if (counting) w_quad += unsigned(__popc(live));
+        unsigned lmask = 0u;  // entries this lane composited (for the contributor mask)
         while (live && !done) {
             const int t = __ffs(live) - 1;
             live &= live - 1;
@@ -523,7 +536,11 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
             cur = base + t;
             T = nT;
             ++n_contrib;
+            lmask |= 1u << t;
         }
+        const unsigned cmask = a.masks ? __reduce_or_sync(0xffffffffu, lmask) : 0u;
+        if (a.masks && lane == 0)
+            a.masks[mask_index(c.start, c.tile, (base - c.start) >> 5, int(blockDim.x >> 5), wid)] = cmask;
         __syncwarp();
     }
     if (a.pair_counters) {
@@ -536,6 +553,8 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
             e += __shfl_xor_sync(0xffffffffu, e, o_);
             k += __shfl_xor_sync(0xffffffffu, k, o_);
         }
+        // lanes leave the evaluation loop when they saturate: the warp's count is the longest
+        w_eval = __reduce_max_sync(0xffffffffu, unsigned(w_eval));
         if (lane == 0) {
             atomicAdd(a.pair_counters, e);
             atomicAdd(a.pair_counters + 1, k);
@@ -690,205 +709,244 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     int32_t wmax = bin_final;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
-    for (int32_t top = min(c.end - 1, wmax); top >= c.start; top -= kWarpSlot) {
-        const int32_t idx = top - lane;
-        bool keep = false;
-        if (idx >= c.start) {
-            const int32_t g = a.flatten[idx];
-            const float4* r = a.rec + int64_t(kRecF4) * g;
-            const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
-            Quad qd = quad_keep_all();
-            if (gref) {
-                const float4* e = a.ext + 3 * int64_t(g);
-                const float4 e0 = e[0], e1 = e[1];
-                sgro[lane] = e[2];  // M (o - mu)
-                keep = cone_may_hit_r(cone, e1.w, mk3(r0.w, r1.w, r2.w), mk3(0.f, 0.f, 0.f), false);
-                if (keep) {
-                    qd.a = e0;
-                    qd.b = make_float4(e1.x, e1.y, e1.z, 0.f);
-                }
-            } else {
-                keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
-                if (qcull && keep) {
-                    v3 mu = mk3(r0.w, r1.w, r2.w);
-                    if (kDyn) mu = mu + rt0 * mk3(r3.y, r3.z, r3.w);
-                    qd = make_quad(r0, r1, r2, r3.x, mu, o0);
-                }
-            }
-            sqa[lane] = qd.a;
-            sqb[lane] = qd.b;
-            s0[lane] = r0; s1[lane] = r1; s2[lane] = r2; s3[lane] = r3;
-            if constexpr (kStageColor) {
-                float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
-                const float* cp = a.colors + int64_t(g) * CDIM;
-                cc.x = cp[0];
-                if (CDIM > 1) cc.y = cp[1];
-                if (CDIM > 2) cc.z = cp[2];
-                if (CDIM > 3) cc.w = cp[3];
-                sc[lane] = cc;
-            }
-            sid[lane] = g;
+    // one entry of the staged batch (slot t, list index gidx) for all lanes of the warp
+    auto process = [&](int t, int32_t gidx) {
+        bool valid = inside && (gidx <= bin_final);
+        const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
+        v3 mu = mk3(r0.w, r1.w, r2.w);
+        const v3 vel = mk3(r3.y, r3.z, r3.w);
+        if (kDyn) mu = mu + rt * vel;
+        const v3 omm = o - mu;
+        v3 gro;
+        if (gref) {
+            const float4 ge = sgro[t];
+            gro = mk3(ge.x, ge.y, ge.z);
+        } else {
+            gro = mrows(r0, r1, r2, omm);
         }
-        unsigned live = __ballot_sync(0xffffffffu, keep);
-        __syncwarp();
-        if (qcull) {
-            unsigned m = live;
-            live = 0u;
-            while (m) {
-                const int t = __ffs(m) - 1;
-                m &= m - 1;
-                const float q = eval_quad(sqa[t], sqb[t], dq);
-                if (__any_sync(0xffffffffu, inside && (top - t <= bin_final) && q >= 0.0f)) live |= 1u << t;
-            }
-        }
-        while (live) {
-            const int t = __ffs(live) - 1;
-            live &= live - 1;
-            bool valid = inside && (top - t <= bin_final);
-            const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
-            v3 mu = mk3(r0.w, r1.w, r2.w);
-            const v3 vel = mk3(r3.y, r3.z, r3.w);
-            if (kDyn) mu = mu + rt * vel;
-            const v3 omm = o - mu;
-            v3 gro;
-            if (gref) {
-                const float4 ge = sgro[t];
-                gro = mk3(ge.x, ge.y, ge.z);
-            } else {
-                gro = mrows(r0, r1, r2, omm);
-            }
-            const v3 grd = mrows(r0, r1, r2, d);
-            const float l = dot3(grd, grd);
-            const v3 gn = l > 0.0f ? grd * rsqrtf(l) : grd;
-            const v3 gc = cross3(gn, gro);
-            const float power = -0.5f * dot3(gc, gc);
-            const float vis = __expf(power);
-            const float op = r3.x;
-            const float alpha = fminf(0.99f, op * vis);
-            if (alpha < 1.f / 255.f) valid = false;
-            if (!__any_sync(0xffffffffu, valid)) continue;
+        const v3 grd = mrows(r0, r1, r2, d);
+        const float l = dot3(grd, grd);
+        const v3 gn = l > 0.0f ? grd * rsqrtf(l) : grd;
+        const v3 gc = cross3(gn, gro);
+        const float power = -0.5f * dot3(gc, gc);
+        const float vis = __expf(power);
+        const float op = r3.x;
+        const float alpha = fminf(0.99f, op * vis);
+        if (alpha < 1.f / 255.f) valid = false;
+        if (!__any_sync(0xffffffffu, valid)) return;
 
-            float gv[16];
+        float gv[16];
 #pragma unroll
-            for (int k = 0; k < 16; ++k) gv[k] = 0.f;
-            float gvel[3] = {0.f, 0.f, 0.f};
-            float gcol[CSZ];
+        for (int k = 0; k < 16; ++k) gv[k] = 0.f;
+        float gvel[3] = {0.f, 0.f, 0.f};
+        float gcol[CSZ];
 #pragma unroll
-            for (int k = 0; k < CSZ; ++k) gcol[k] = 0.f;
-            if (valid) {
-                const float od = dot3(gro, grd);
-                const float hit_t = __fdividef(-od, l);
-                const float ra = __fdividef(1.0f, fmaxf(1e-6f, 1.0f - alpha));
-                T *= ra;
-                const float fac = alpha * T;
-                float rgb[CSZ];
-                if constexpr (kStageColor) {
-                    const float4 cc = sc[t];
-                    rgb[0] = cc.x;
-                    if (CDIM > 1) rgb[1] = cc.y;
-                    if (CDIM > 2) rgb[2] = cc.z;
-                    if (CDIM > 3) rgb[3] = cc.w;
-                } else if constexpr (CDIM > 0) {
-                    const float* cp = a.colors + int64_t(sid[t]) * CDIM;
-#pragma unroll 4
-                    for (int k = 0; k < CDIM; ++k) rgb[k] = cp[k];
-                }
-                float v_alpha = 0.f;
-#pragma unroll
-                for (int k = 0; k < CDIM; ++k) {
-                    gcol[k] = vc[k] * fac;
-                    v_alpha += (rgb[k] * T - buf[k] * ra) * vc[k];
-                }
-                v_alpha += (hit_t * T - dbuf * ra) * vd;
-                v_alpha += T_final * ra * va;
-                // hit distance t* = -(gro . grd) / (grd . grd)
-                const float dLdt = vd * fac;
-                const float il2 = __fdividef(1.0f, l);
-                v3 v_gro = (-dLdt * il2) * grd;
-                v3 v_grd = (dLdt * il2 * il2) * (2.0f * od * grd - l * gro);
-                if (op * vis <= 0.99f) {
-                    const float v_vis = op * v_alpha;
-                    const float v_dist = -0.5f * vis * v_vis;
-                    const v3 v_gc = 2.0f * v_dist * gc;
-                    const v3 v_gn = -1.0f * cross3(v_gc, gro);
-                    v_gro = v_gro + cross3(v_gc, gn);
-                    if (l > 0.0f) {
-                        const float il = rsqrtf(l);
-                        const float il3 = il * il * il;
-                        v_grd = v_grd + (il * v_gn - il3 * dot3(v_gn, grd) * grd);
-                    } else {
-                        v_grd = v_grd + v_gn;
-                    }
-                    if (kRayGrad || kDyn || !fact) {
-                        // v_(o - mu) = M^T v_gro
-                        const v3 v_omm = mk3(r0.x * v_gro.x + r1.x * v_gro.y + r2.x * v_gro.z,
-                                             r0.y * v_gro.x + r1.y * v_gro.y + r2.y * v_gro.z,
-                                             r0.z * v_gro.x + r1.z * v_gro.y + r2.z * v_gro.z);
-                        gv[0] = -v_omm.x; gv[1] = -v_omm.y; gv[2] = -v_omm.z;
-                        if constexpr (kRayGrad) {
-                            // v_ray_d = M^T v_grd
-                            const v3 v_d = mk3(r0.x * v_grd.x + r1.x * v_grd.y + r2.x * v_grd.z,
-                                               r0.y * v_grd.x + r1.y * v_grd.y + r2.y * v_grd.z,
-                                               r0.z * v_grd.x + r1.z * v_grd.y + r2.z * v_grd.z);
-                            vro = vro + v_omm;
-                            vrd = vrd + v_d;
-                            if (kDyn) vtime += -dot3(v_omm, vel);
-                        }
-                        if (kDyn) {
-                            gvel[0] = -v_omm.x * rt; gvel[1] = -v_omm.y * rt; gvel[2] = -v_omm.z * rt;
-                        }
-                    } else {
-                        gv[0] = v_gro.x; gv[1] = v_gro.y; gv[2] = v_gro.z;
-                    }
-                    gv[3] = vis * v_alpha;
-                    // dL/dM row i = v_grd[i] d + v_gro[i] (o - mu); in factored
-                    // warps the finalize pass adds the second term
-                    v3 vM0 = v_grd.x * d, vM1 = v_grd.y * d, vM2 = v_grd.z * d;
-                    if (!fact) {
-                        vM0 = vM0 + v_gro.x * omm;
-                        vM1 = vM1 + v_gro.y * omm;
-                        vM2 = vM2 + v_gro.z * omm;
-                    }
-                    gv[4] = vM0.x; gv[5] = vM0.y; gv[6] = vM0.z;
-                    gv[7] = vM1.x; gv[8] = vM1.y; gv[9] = vM1.z;
-                    gv[10] = vM2.x; gv[11] = vM2.y; gv[12] = vM2.z;
-                }
-#pragma unroll
-                for (int k = 0; k < CDIM; ++k) buf[k] += rgb[k] * fac;
-                dbuf += fac * hit_t;
-            }
+        for (int k = 0; k < CSZ; ++k) gcol[k] = 0.f;
+        if (valid) {
+            const float od = dot3(gro, grd);
+            const float hit_t = __fdividef(-od, l);
+            const float ra = __fdividef(1.0f, fmaxf(1e-6f, 1.0f - alpha));
+            T *= ra;
+            const float fac = alpha * T;
+            float rgb[CSZ];
             if constexpr (kStageColor) {
+                const float4 cc = sc[t];
+                rgb[0] = cc.x;
+                if (CDIM > 1) rgb[1] = cc.y;
+                if (CDIM > 2) rgb[2] = cc.z;
+                if (CDIM > 3) rgb[3] = cc.w;
+            } else if constexpr (CDIM > 0) {
+                const float* cp = a.colors + int64_t(sid[t]) * CDIM;
+#pragma unroll 4
+                for (int k = 0; k < CDIM; ++k) rgb[k] = cp[k];
+            }
+            float v_alpha = 0.f;
 #pragma unroll
-                for (int k = 0; k < (CDIM < 3 ? CDIM : 3); ++k) gv[13 + k] = gcol[k];
+            for (int k = 0; k < CDIM; ++k) {
+                gcol[k] = vc[k] * fac;
+                v_alpha += (rgb[k] * T - buf[k] * ra) * vc[k];
             }
-            butterfly16(gv, lane);
-            // lanes 8k+0/2/4/6 hold values 4k..4k+3: gather them into lane 8k
-            const float g1 = __shfl_down_sync(0xffffffffu, gv[0], 2);
-            const float g2 = __shfl_down_sync(0xffffffffu, gv[0], 4);
-            const float g3 = __shfl_down_sync(0xffffffffu, gv[0], 6);
-            float* dst = a.G + int64_t(sid[t]) * NA;
-            // a factored warp's first group (sum of v_gro, v_opacity) goes to its own slots
-            const int slot = (fact && lane == 0) ? AC::kFactSlot : (lane >> 1);
-            if ((lane & 7) == 0) red_add_v4(dst + slot, gv[0], g1, g2, g3);
-            if constexpr (CDIM == 4 || kDyn) {
-                float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
-                if constexpr (CDIM == 4) e0 = warp_sum(gcol[3]);
-                if constexpr (kDyn) {
-                    const float x0 = warp_sum(gvel[0]), x1 = warp_sum(gvel[1]), x2 = warp_sum(gvel[2]);
-                    if (AC::kVel == 16) { e0 = x0; e1 = x1; e2 = x2; }
-                    else { e1 = x0; e2 = x1; e3 = x2; }
+            v_alpha += (hit_t * T - dbuf * ra) * vd;
+            v_alpha += T_final * ra * va;
+            // hit distance t* = -(gro . grd) / (grd . grd)
+            const float dLdt = vd * fac;
+            const float il2 = __fdividef(1.0f, l);
+            v3 v_gro = (-dLdt * il2) * grd;
+            v3 v_grd = (dLdt * il2 * il2) * (2.0f * od * grd - l * gro);
+            if (op * vis <= 0.99f) {
+                const float v_vis = op * v_alpha;
+                const float v_dist = -0.5f * vis * v_vis;
+                const v3 v_gc = 2.0f * v_dist * gc;
+                const v3 v_gn = -1.0f * cross3(v_gc, gro);
+                v_gro = v_gro + cross3(v_gc, gn);
+                if (l > 0.0f) {
+                    const float il = rsqrtf(l);
+                    const float il3 = il * il * il;
+                    v_grd = v_grd + (il * v_gn - il3 * dot3(v_gn, grd) * grd);
+                } else {
+                    v_grd = v_grd + v_gn;
                 }
-                if (lane == 0) red_add_v4(dst + 16, e0, e1, e2, e3);
+                if (kRayGrad || kDyn || !fact) {
+                    // v_(o - mu) = M^T v_gro
+                    const v3 v_omm = mk3(r0.x * v_gro.x + r1.x * v_gro.y + r2.x * v_gro.z,
+                                         r0.y * v_gro.x + r1.y * v_gro.y + r2.y * v_gro.z,
+                                         r0.z * v_gro.x + r1.z * v_gro.y + r2.z * v_gro.z);
+                    gv[0] = -v_omm.x; gv[1] = -v_omm.y; gv[2] = -v_omm.z;
+                    if constexpr (kRayGrad) {
+                        // v_ray_d = M^T v_grd
+                        const v3 v_d = mk3(r0.x * v_grd.x + r1.x * v_grd.y + r2.x * v_grd.z,
+                                           r0.y * v_grd.x + r1.y * v_grd.y + r2.y * v_grd.z,
+                                           r0.z * v_grd.x + r1.z * v_grd.y + r2.z * v_grd.z);
+                        vro = vro + v_omm;
+                        vrd = vrd + v_d;
+                        if (kDyn) vtime += -dot3(v_omm, vel);
+                    }
+                    if (kDyn) {
+                        gvel[0] = -v_omm.x * rt; gvel[1] = -v_omm.y * rt; gvel[2] = -v_omm.z * rt;
+                    }
+                } else {
+                    gv[0] = v_gro.x; gv[1] = v_gro.y; gv[2] = v_gro.z;
+                }
+                gv[3] = vis * v_alpha;
+                // dL/dM row i = v_grd[i] d + v_gro[i] (o - mu); in factored
+                // warps the finalize pass adds the second term
+                v3 vM0 = v_grd.x * d, vM1 = v_grd.y * d, vM2 = v_grd.z * d;
+                if (!fact) {
+                    vM0 = vM0 + v_gro.x * omm;
+                    vM1 = vM1 + v_gro.y * omm;
+                    vM2 = vM2 + v_gro.z * omm;
+                }
+                gv[4] = vM0.x; gv[5] = vM0.y; gv[6] = vM0.z;
+                gv[7] = vM1.x; gv[8] = vM1.y; gv[9] = vM1.z;
+                gv[10] = vM2.x; gv[11] = vM2.y; gv[12] = vM2.z;
             }
-            if constexpr (!kStageColor && CDIM > 0) {
-                // wide colours: warp-reduced straight into the output
-                for (int k = 0; k < CDIM; ++k) {
-                    const float sv = warp_sum(gcol[k]);
-                    if (lane == 0 && sv != 0.f) atomicAdd(a.v_colors_direct + int64_t(sid[t]) * CDIM + k, sv);
-                }
+#pragma unroll
+            for (int k = 0; k < CDIM; ++k) buf[k] += rgb[k] * fac;
+            dbuf += fac * hit_t;
+        }
+        if constexpr (kStageColor) {
+#pragma unroll
+            for (int k = 0; k < (CDIM < 3 ? CDIM : 3); ++k) gv[13 + k] = gcol[k];
+        }
+        butterfly16(gv, lane);
+        // lanes 8k+0/2/4/6 hold values 4k..4k+3: gather them into lane 8k
+        const float g1 = __shfl_down_sync(0xffffffffu, gv[0], 2);
+        const float g2 = __shfl_down_sync(0xffffffffu, gv[0], 4);
+        const float g3 = __shfl_down_sync(0xffffffffu, gv[0], 6);
+        float* dst = a.G + int64_t(sid[t]) * NA;
+        // a factored warp's first group (sum of v_gro, v_opacity) goes to its own slots
+        const int slot = (fact && lane == 0) ? AC::kFactSlot : (lane >> 1);
+        if ((lane & 7) == 0) red_add_v4(dst + slot, gv[0], g1, g2, g3);
+        if constexpr (CDIM == 4 || kDyn) {
+            float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
+            if constexpr (CDIM == 4) e0 = warp_sum(gcol[3]);
+            if constexpr (kDyn) {
+                const float x0 = warp_sum(gvel[0]), x1 = warp_sum(gvel[1]), x2 = warp_sum(gvel[2]);
+                if (AC::kVel == 16) { e0 = x0; e1 = x1; e2 = x2; }
+                else { e1 = x0; e2 = x1; e3 = x2; }
+            }
+            if (lane == 0) red_add_v4(dst + 16, e0, e1, e2, e3);
+        }
+        if constexpr (!kStageColor && CDIM > 0) {
+            // wide colours: warp-reduced straight into the output
+            for (int k = 0; k < CDIM; ++k) {
+                const float sv = warp_sum(gcol[k]);
+                if (lane == 0 && sv != 0.f) atomicAdd(a.v_colors_direct + int64_t(sid[t]) * CDIM + k, sv);
             }
         }
-        __syncwarp();
+    };
+    if (a.masks) {
+        // the forward's contributor masks: visit only entries some lane of
+        // this warp composited, without the cone and quadric pre-tests
+        const int wpt = int(blockDim.x >> 5);
+        for (int32_t k = wmax >= c.start ? (wmax - c.start) >> 5 : -1; k >= 0; --k) {
+            const uint32_t cm = a.masks[mask_index(c.start, c.tile, k, wpt, wid)];
+            if (!cm) continue;
+            const int32_t base = c.start + (k << 5);
+            if ((cm >> lane) & 1u) {
+                const int32_t g = a.flatten[base + lane];
+                const float4* r = a.rec + int64_t(kRecF4) * g;
+                s0[lane] = r[0]; s1[lane] = r[1]; s2[lane] = r[2]; s3[lane] = r[3];
+                if (gref) sgro[lane] = a.ext[3 * int64_t(g) + 2];  // M (o - mu)
+                if constexpr (kStageColor) {
+                    float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float* cp = a.colors + int64_t(g) * CDIM;
+                    cc.x = cp[0];
+                    if (CDIM > 1) cc.y = cp[1];
+                    if (CDIM > 2) cc.z = cp[2];
+                    if (CDIM > 3) cc.w = cp[3];
+                    sc[lane] = cc;
+                }
+                sid[lane] = g;
+            }
+            __syncwarp();
+            unsigned live = cm;
+            while (live) {
+                const int t = 31 - __clz(live);
+                live &= ~(1u << t);
+                process(t, base + t);
+            }
+            __syncwarp();
+        }
+    } else {
+        for (int32_t top = min(c.end - 1, wmax); top >= c.start; top -= kWarpSlot) {
+            const int32_t idx = top - lane;
+            bool keep = false;
+            if (idx >= c.start) {
+                const int32_t g = a.flatten[idx];
+                const float4* r = a.rec + int64_t(kRecF4) * g;
+                const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
+                Quad qd = quad_keep_all();
+                if (gref) {
+                    const float4* e = a.ext + 3 * int64_t(g);
+                    const float4 e0 = e[0], e1 = e[1];
+                    sgro[lane] = e[2];  // M (o - mu)
+                    keep = cone_may_hit_r(cone, e1.w, mk3(r0.w, r1.w, r2.w), mk3(0.f, 0.f, 0.f), false);
+                    if (keep) {
+                        qd.a = e0;
+                        qd.b = make_float4(e1.x, e1.y, e1.z, 0.f);
+                    }
+                } else {
+                    keep = cone_may_hit(cone, r0, r1, r2, r3, kDyn);
+                    if (qcull && keep) {
+                        v3 mu = mk3(r0.w, r1.w, r2.w);
+                        if (kDyn) mu = mu + rt0 * mk3(r3.y, r3.z, r3.w);
+                        qd = make_quad(r0, r1, r2, r3.x, mu, o0);
+                    }
+                }
+                sqa[lane] = qd.a;
+                sqb[lane] = qd.b;
+                s0[lane] = r0; s1[lane] = r1; s2[lane] = r2; s3[lane] = r3;
+                if constexpr (kStageColor) {
+                    float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float* cp = a.colors + int64_t(g) * CDIM;
+                    cc.x = cp[0];
+                    if (CDIM > 1) cc.y = cp[1];
+                    if (CDIM > 2) cc.z = cp[2];
+                    if (CDIM > 3) cc.w = cp[3];
+                    sc[lane] = cc;
+                }
+                sid[lane] = g;
+            }
+            unsigned live = __ballot_sync(0xffffffffu, keep);
+            __syncwarp();
+            if (qcull) {
+                unsigned m = live;
+                live = 0u;
+                while (m) {
+                    const int t = __ffs(m) - 1;
+                    m &= m - 1;
+                    const float q = eval_quad(sqa[t], sqb[t], dq);
+                    if (__any_sync(0xffffffffu, inside && (top - t <= bin_final) && q >= 0.0f)) live |= 1u << t;
+                }
+            }
+            while (live) {
+                const int t = __ffs(live) - 1;
+                live &= live - 1;
+                process(t, top - t);
+            }
+            __syncwarp();
+        }
     }
     if (kRayGrad && inside) {
         st3(a.v_ray_o + 3 * c.pix, vro);
@@ -1028,6 +1086,13 @@ static int check_common(int64_t n_gauss, int W, int H, int tsx, int tsy, int til
     return XSG_OK;
 }
 
+// words of the contributor masks: one per (batch of 32 list entries, warp),
+// tile batch ranges start at (start >> 5) + tile (see mask_index)
+static int64_t mask_words(int64_t n_isects, int64_t n_tiles, int tile_pixels) {
+    if (n_isects <= 0 || n_tiles <= 0 || tile_pixels < 32) return 0;
+    return (n_isects / 32 + n_tiles + 2) * (tile_pixels / 32);
+}
+
 }  // namespace xsg
 
 using namespace xsg;
@@ -1042,14 +1107,17 @@ int xsg_raster_supported_channels(int* out, int cap) {
     return n;
 }
 
-size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim) {
+size_t xsg_rasterize_workspace_size(int64_t n_gauss, int cdim, int64_t n_isects, int64_t n_tiles,
+                                    int tile_pixels) {
     (void)cdim;
     if (n_gauss < 0) n_gauss = 0;
-    // packed records + the (dynamic-sized) gradient accumulator
+    // packed records, view constants, tile order, contributor masks (when the
+    // intersection and tile counts are given) and the gradient accumulator
     return Arena::round(size_t(n_gauss) * kRecF4 * sizeof(float4)) +
            Arena::round(size_t(n_gauss) * 3 * sizeof(float4)) +
-           Arena::round(size_t(n_gauss) * kMaxAcc * sizeof(float)) +
-           Arena::round(size_t(kMaxTiles) * sizeof(int32_t));
+           Arena::round(size_t(kMaxTiles) * sizeof(int32_t)) +
+           Arena::round(size_t(mask_words(n_isects, n_tiles, tile_pixels)) * sizeof(uint32_t)) +
+           Arena::round(size_t(n_gauss) * kMaxAcc * sizeof(float));
 }
 
 int xsg_rasterize_fwd(const float* means, const float* velocity, const float* quats, const float* scales,
@@ -1070,6 +1138,11 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
     float4* ext = ar.take<float4>(size_t(n_gauss) * 3);
     const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
     int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
+    // contributor masks for the backward, when the workspace was sized for them
+    const int64_t nmw = mask_words(n_isects, n_tiles, tsx * tsy);
+    const bool with_masks =
+        nmw > 0 && ws_bytes >= xsg_rasterize_workspace_size(n_gauss, cdim, n_isects, n_tiles, tsx * tsy);
+    uint32_t* masks = with_masks ? ar.take<uint32_t>(size_t(nmw)) : nullptr;
     if ((n_gauss > 0 && (!rec || !ext)) || (n_gauss > 0 && !workspace))
         return set_error(XSG_ERR_WORKSPACE, "rasterize_fwd: workspace too small");
     const bool dyn = velocity != nullptr;
@@ -1086,6 +1159,7 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
     a.out_rgb = renders; a.out_depth = depths; a.out_alpha = alphas; a.out_last = last_ids;
     a.pair_counters = g_pair_counters;
     a.tile_order = order;
+    a.masks = masks;
     const int bs = tsx * tsy;
 #define XSG_FWD_CASE(C)                                                             \
     case C:                                                                         \
@@ -1127,6 +1201,12 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     const int64_t n_tiles = int64_t(tiles_w) * tiles_h;
     // same layout as the forward's (records, view constants, tile order), then the accumulator
     int32_t* order = n_tiles <= kMaxTiles ? ar.take<int32_t>(size_t(kMaxTiles)) : nullptr;
+    // the forward's contributor masks (same layout and condition as there)
+    const bool reuse = workspace_from_forward != 0;
+    const int64_t nmw = mask_words(n_isects, n_tiles, tsx * tsy);
+    const bool with_masks = reuse && nmw > 0 &&
+                            ws_bytes >= xsg_rasterize_workspace_size(n_gauss, cdim, n_isects, n_tiles, tsx * tsy);
+    uint32_t* masks = with_masks ? ar.take<uint32_t>(size_t(nmw)) : nullptr;
     // Acc<CDIM, kDyn, kRayGrad>::N
     const int na = (!dyn && !ray_grads) ? (cdim == 4 ? 24 : 20) : ((dyn || cdim == 4) ? 20 : 16);
     float* G = ar.take<float>(size_t(n_gauss) * na);
@@ -1135,7 +1215,6 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     // every pixel of the image belongs to exactly one tile thread, which
     // writes its v_ray_o / v_ray_d (/ v_ray_time_delta): no pre-zeroing
     // the forward's workspace already holds the tile order, records and view constants
-    const bool reuse = workspace_from_forward != 0;
     if (order && !reuse)
         launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
     if (n_gauss > 0) {
@@ -1154,6 +1233,7 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     a.v_rgb = v_renders; a.v_depth = v_depths; a.v_alpha = v_alphas;
     a.G = G; a.v_colors_direct = v_colors;
     a.tile_order = order;
+    a.masks = masks;  // written by the forward into the same workspace
     a.v_ray_o = v_ray_o; a.v_ray_d = v_ray_d; a.v_ray_t = v_ray_time_delta;
     const int bs = tsx * tsy;
     FinalizeOut fin{v_means, v_velocity, v_quats, v_scales, v_opacities, v_colors};

@@ -15,7 +15,9 @@ class UTGSRasterize(torch.autograd.Function):
                 isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int):
         height, width = ray_o.shape[:2]
         channels = colors.shape[-1] if colors is not None else 0
-        ws = torch.empty(_C.rasterize_workspace_size(positions.shape[0], channels), dtype=torch.uint8,
+        ws = torch.empty(_C.rasterize_workspace_size(positions.shape[0], channels, n_isects=flatten_ids.numel(),
+                                                     n_tiles=isect_offsets.numel(),
+                                                     tile_pixels=tile_size_x * tile_size_y), dtype=torch.uint8,
                          device=positions.device)
         out_rgb, out_depth, out_alpha, last_ids = _C.rasterize_eval3d_fwd(
             means=positions,
