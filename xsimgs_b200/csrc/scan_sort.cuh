@@ -1,5 +1,5 @@
-// Device-wide exclusive scan and a stable LSD radix sort of (u32 key, u32
-// value) pairs, written for this library (no CUB).  Used by tile
+// Device-wide exclusive scan and stable counting-sort passes of (u32 key,
+// u32 value) pairs, written for this library (no CUB).  Used by tile
 // intersection: a depth presort of the visible Gaussians and a stable bucket
 // sort of intersections by tile.
 #pragma once
@@ -45,9 +45,13 @@ __device__ __forceinline__ int64_t block_excl_scan(int64_t v, int64_t* total) {
 
 // Phase 1: per-block sums of `in` (T = int32 or int64), optionally of a
 // predicate (in[i] > 0).
+// n_dev (optional) holds the element count on the device; the grid is then
+// sized for its upper bound n.
 template <typename T, bool kPred>
 __global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(const T* __restrict__ in, int64_t n,
-                                                                   int64_t* __restrict__ block_sums) {
+                                                                   int64_t* __restrict__ block_sums,
+                                                                   const int64_t* __restrict__ n_dev) {
+    if (n_dev) n = *n_dev;
     const int64_t base = int64_t(blockIdx.x) * kScanChunk;
     int64_t s = 0;
 #pragma unroll
@@ -67,7 +71,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(const T* __re
 template <typename T, bool kPred>
 __global__ void __launch_bounds__(kScanThreads)
     scan_apply_kernel(const T* __restrict__ in, int64_t n, const int64_t* __restrict__ block_offsets,
-                      int64_t* __restrict__ out, int64_t* __restrict__ total) {
+                      int64_t* __restrict__ out, int64_t* __restrict__ total, const int64_t* __restrict__ n_dev) {
+    if (n_dev) n = *n_dev;
     const int64_t base = int64_t(blockIdx.x) * kScanChunk + int64_t(threadIdx.x) * kScanItems;
     int64_t vals[kScanItems];
     int64_t s = 0;
@@ -113,126 +118,22 @@ inline size_t scan_workspace_bytes(int64_t n) {
 
 // Exclusive scan of n values into out (int64).  `total` (device, may be
 // null) receives the sum.  tmp needs scan_workspace_bytes(n).
+// With n_dev the count is read on the device (at most n; out is written
+// for the first *n_dev elements only).
 template <typename T, bool kPred = false>
 int exclusive_scan(const T* in, int64_t n, int64_t* out, int64_t* total, void* tmp,
-                   cudaStream_t st) {
+                   cudaStream_t st, const int64_t* n_dev = nullptr) {
     if (n == 0) {
         if (total) XSG_CUDA(cudaMemsetAsync(total, 0, sizeof(int64_t), st));
         return XSG_OK;
     }
     const int64_t nb = (n + kScanChunk - 1) / kScanChunk;
     int64_t* bs = static_cast<int64_t*>(tmp);
-    launch(scan_reduce_kernel<T, kPred>, unsigned(nb), kScanThreads, 0, st, in, n, bs);
+    launch(scan_reduce_kernel<T, kPred>, unsigned(nb), kScanThreads, 0, st, in, n, bs, n_dev);
     launch(scan_small_kernel, 1, 1024, 0, st, bs, nb);
-    launch(scan_apply_kernel<T, kPred>, unsigned(nb), kScanThreads, 0, st, in, n, bs, out, total);
+    launch(scan_apply_kernel<T, kPred>, unsigned(nb), kScanThreads, 0, st, in, n, static_cast<const int64_t*>(bs),
+           out, total, n_dev);
     return check_launch("exclusive_scan");
-}
-
-// ---------------------------------------------------------------- radix --
-// Stable LSD radix sort, 8-bit digits, warp-granular: the input is cut into
-// warp chunks of 32 x R consecutive keys (R = 16 or 64).  Per pass:
-//   1. hist:     every warp counts the digits of its chunk in its own
-//                shared-memory counters -> counts[digit][chunk];
-//   2. row scan: one CTA per digit scans its row over the chunks ->
-//                offsets[digit][chunk] (within the digit) and totals[digit];
-//   3. scatter:  every warp walks its chunk in order, 32 keys at a time,
-//                ranks equal digits among its lanes and keeps its own
-//                per-digit cursor in shared memory; the digit bases come
-//                from a scan of the 256 totals.  No block-wide barrier
-//                inside the loop; keys are prefetched 16 rounds at a time.
-// Warp chunks are processed in input order inside each digit, so the sort
-// is stable.
-constexpr int kSortThreads = 256;
-constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kRadixBits = 8;
-constexpr int kRadixBins = 1 << kRadixBits;
-constexpr int kRxBatch = 16;  // rounds prefetched together
-
-inline int sort_rounds(int64_t n) { return n > (int64_t(4) << 20) ? 64 : 16; }
-inline int64_t sort_chunks(int64_t n) {
-    const int64_t per = int64_t(32) * sort_rounds(n);
-    return (n + per - 1) / per;
-}
-
-// Lanes of the warp holding the same digit (0..255, or 256 for a lane past
-// the end): nine ballots, constant time whatever the digits are.
-__device__ __forceinline__ unsigned match_digit(int digit) {
-    unsigned m = 0xffffffffu;
-#pragma unroll
-    for (int b = 0; b < kRadixBits + 1; ++b) {
-        const bool bit = (digit >> b) & 1;
-        const unsigned bal = __ballot_sync(0xffffffffu, bit);
-        m &= bit ? bal : ~bal;
-    }
-    return m;
-}
-
-__global__ void __launch_bounds__(kSortThreads)
-    radix_hist_kernel(const uint32_t* __restrict__ keys, int64_t n, int shift, int rounds,
-                      int32_t* __restrict__ counts, int64_t nchunks) {
-    __shared__ int32_t h[kSortWarps][kRadixBins];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t c = int64_t(blockIdx.x) * kSortWarps + w;
-    if (c >= nchunks) return;  // warp-uniform; no block barrier below
-#pragma unroll
-    for (int k = 0; k < kRadixBins / 32; ++k) h[w][lane + 32 * k] = 0;
-    __syncwarp();
-    const int64_t base = c * 32 * rounds;
-    for (int b = 0; b < rounds; b += kRxBatch) {
-        int dg[kRxBatch];
-#pragma unroll
-        for (int r = 0; r < kRxBatch; ++r) {
-            const int64_t i = base + int64_t(b + r) * 32 + lane;
-            dg[r] = i < n ? int((keys[i] >> shift) & (kRadixBins - 1)) : kRadixBins;
-        }
-#pragma unroll
-        for (int r = 0; r < kRxBatch; ++r) {
-            const unsigned peers = match_digit(dg[r]);
-            if (dg[r] < kRadixBins && lane == __ffs(peers) - 1) h[w][dg[r]] += __popc(peers);
-            __syncwarp();
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < kRadixBins / 32; ++k) {
-        const int d = lane + 32 * k;
-        counts[int64_t(d) * nchunks + c] = h[w][d];
-    }
-}
-
-// One CTA per digit: exclusive scan of counts[d][*] -> offsets[d][*], eight
-// consecutive chunks per thread.
-constexpr int kRowItems = 8;
-__global__ void __launch_bounds__(1024)
-    radix_rowscan_kernel(const int32_t* __restrict__ counts, int64_t nchunks, int32_t* __restrict__ offsets,
-                         int64_t* __restrict__ totals) {
-    __shared__ int64_t carry;
-    const int64_t d = blockIdx.x;
-    if (threadIdx.x == 0) carry = 0;
-    __syncthreads();
-    const int32_t* row = counts + d * nchunks;
-    int32_t* orow = offsets + d * nchunks;
-    const int64_t span = int64_t(blockDim.x) * kRowItems;
-    for (int64_t b = 0; b < nchunks; b += span) {
-        const int64_t i0 = b + int64_t(threadIdx.x) * kRowItems;
-        int32_t v[kRowItems];
-        int64_t s = 0;
-#pragma unroll
-        for (int k = 0; k < kRowItems; ++k) {
-            v[k] = (i0 + k < nchunks) ? row[i0 + k] : 0;
-            s += v[k];
-        }
-        int64_t tot;
-        int64_t run = block_excl_scan(s, &tot) + carry;
-#pragma unroll
-        for (int k = 0; k < kRowItems; ++k) {
-            if (i0 + k < nchunks) orow[i0 + k] = int32_t(run);
-            run += v[k];
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) carry += tot;
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) totals[d] = carry;
 }
 
 // Output mode of the final scatter of the tile sort: keys become the
@@ -243,56 +144,170 @@ struct IsectEpilogue {
     int32_t* flatten_ids;    // out
 };
 
-template <bool kIsect>
-__global__ void __launch_bounds__(kSortThreads)
-    radix_scatter_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, int64_t n,
-                         int shift, int rounds, const int32_t* __restrict__ offsets,
-                         const int64_t* __restrict__ totals, int64_t nchunks, uint32_t* __restrict__ keys_out,
-                         uint32_t* __restrict__ vals_out, IsectEpilogue ep) {
-    __shared__ int64_t dbase[kRadixBins];
-    __shared__ int64_t cur[kSortWarps][kRadixBins];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    // digit bases: exclusive scan of the 256 digit totals (one per thread)
-    {
-        int64_t tot;
-        dbase[threadIdx.x] = block_excl_scan(totals[threadIdx.x], &tot);
+// ------------------------------------------------------ counting pass --
+// One stable counting-sort pass of (u32 key, u32 value) pairs on a digit of
+// the key (at most kCsMaxBins values).  Warp w (one warp per CTA) owns the
+// contiguous input range [w * per, (w + 1) * per):
+//   1. hist:    it counts its digits in its own shared-memory bins;
+//   2. offsets: every (bin, warp) gets its first output position;
+//   3. scatter: the warp walks its range 32 keys at a time, in order: lanes
+//               with equal digits are grouped with a match and ranked by
+//               lane, and the group's leader advances the bin's cursor.
+// Ranges are visited in order inside every bin, so the pass is stable.
+// Narrow digits (<= kCsNarrowBins values) use many short ranges and a
+// bin-major count array scanned as a whole; wide digits use fewer, longer
+// ranges, a warp-major array, a column scan per bin and a scan of the bin
+// totals.  The element count may live on the device (n_dev, at most n).
+constexpr int kCsMaxBins = 8192;
+constexpr int kCsNarrowBins = 256;
+
+struct CsPlan {
+    int max_warps, min_per;
+};
+__host__ __device__ constexpr CsPlan cs_plan(int nbins) {
+    return nbins <= kCsNarrowBins ? CsPlan{148 * 32, 512} : CsPlan{4 * 148, 2048};
+}
+
+struct CsDigit {
+    int shift;
+    uint32_t mask;
+    __device__ __forceinline__ int operator()(uint32_t k) const { return int((k >> shift) & mask); }
+};
+
+__device__ __forceinline__ void cs_range(int64_t n, int64_t& i0, int64_t& i1) {
+    const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+    i0 = int64_t(blockIdx.x) * per;
+    i1 = min(n, i0 + per);
+}
+
+// counts[b * G + w] (bin-major) or counts[w * nbins + b] (warp-major)
+template <bool kBinMajor>
+__global__ void __launch_bounds__(32)
+    cs_hist_kernel(const uint32_t* __restrict__ keys, int64_t n, const int64_t* __restrict__ n_dev, CsDigit dg,
+                   int nbins, int32_t* __restrict__ counts) {
+    extern __shared__ int32_t h[];
+    const int lane = threadIdx.x;
+    if (n_dev) n = *n_dev;
+    for (int b = lane; b < nbins; b += 32) h[b] = 0;
+    __syncwarp();
+    int64_t i0, i1;
+    cs_range(n, i0, i1);
+    for (int64_t i = i0 + lane; i < i1; i += 32) atomicAdd(h + dg(keys[i]), 1);
+    __syncwarp();
+    for (int b = lane; b < nbins; b += 32)
+        counts[kBinMajor ? int64_t(b) * gridDim.x + blockIdx.x : int64_t(blockIdx.x) * nbins + b] = h[b];
+}
+
+// Wide digits: block (32 bins) x (32 warp groups); thread (g, c) owns warps
+// [g R, (g + 1) R) of bin b0 + c (coalesced across c), sums them, the 32
+// group sums of a bin are scanned in shared memory, then the warps' offsets
+// inside the bin (offs, warp-major) and the bin totals are written.
+constexpr int kCsColRows = (4 * 148 + 31) / 32;
+__global__ void __launch_bounds__(1024)
+    cs_colscan_kernel(const int32_t* __restrict__ counts, int G, int nbins, int32_t* __restrict__ offs,
+                      int64_t* __restrict__ totals) {
+    __shared__ int32_t part[32][33];
+    const int c = threadIdx.x & 31, g = threadIdx.x >> 5;
+    const int b = blockIdx.x * 32 + c;
+    const int R = (G + 31) / 32;
+    const int w0 = g * R, w1 = min(G, w0 + R);
+    int32_t v[kCsColRows];
+    int32_t sum = 0;
+#pragma unroll
+    for (int r = 0; r < kCsColRows; ++r) {
+        const int w = w0 + r;
+        v[r] = (r < R && w < w1 && b < nbins) ? counts[int64_t(w) * nbins + b] : 0;
+        sum += v[r];
+    }
+    part[g][c] = sum;
+    __syncthreads();
+    if (g == 0) {
+        int32_t run = 0;
+        for (int k = 0; k < 32; ++k) {
+            const int32_t t = part[k][c];
+            part[k][c] = run;
+            run += t;
+        }
+        if (b < nbins) totals[b] = run;
     }
     __syncthreads();
-    const int64_t c = int64_t(blockIdx.x) * kSortWarps + w;
-    if (c >= nchunks) return;  // warp-uniform; no block barrier below
+    int32_t run = part[g][c];
 #pragma unroll
-    for (int k = 0; k < kRadixBins / 32; ++k) {
-        const int d = lane + 32 * k;
-        cur[w][d] = dbase[d] + offsets[int64_t(d) * nchunks + c];
+    for (int r = 0; r < kCsColRows; ++r) {
+        const int w = w0 + r;
+        if (r < R && w < w1 && b < nbins) offs[int64_t(w) * nbins + b] = run;
+        run += v[r];
     }
+}
+
+// starts[b] = totals[< b]; one CTA.
+__global__ void __launch_bounds__(1024) cs_starts_kernel(const int64_t* __restrict__ totals, int nbins,
+                                                         int64_t* __restrict__ starts) {
+    __shared__ int64_t carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int base = 0; base < nbins; base += blockDim.x) {
+        const int b = base + threadIdx.x;
+        int64_t tot;
+        const int64_t ex = block_excl_scan(b < nbins ? totals[b] : 0, &tot);
+        const int64_t c = carry;
+        if (b < nbins) starts[b] = c + ex;
+        __syncthreads();
+        if (threadIdx.x == 0) carry = c + tot;
+        __syncthreads();
+    }
+}
+
+// Cursor of (bin b, this warp): pos0[b * G + w] (narrow digits) or
+// starts[b] + offs[w * nbins + b] (wide digits).
+template <bool kBinMajor, bool kIsect>
+__global__ void __launch_bounds__(32)
+    cs_scatter_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int64_t n,
+                      const int64_t* __restrict__ n_dev, CsDigit dg, int nbins, const int64_t* __restrict__ pos0,
+                      const int32_t* __restrict__ offs, const int64_t* __restrict__ starts,
+                      uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, IsectEpilogue ep) {
+    extern __shared__ int32_t cur[];  // positions < n < 2^31
+    const int lane = threadIdx.x;
+    if (n_dev) n = *n_dev;
+    for (int b = lane; b < nbins; b += 32)
+        cur[b] = kBinMajor ? int32_t(pos0[int64_t(b) * gridDim.x + blockIdx.x])
+                           : int32_t(starts[b]) + offs[int64_t(blockIdx.x) * nbins + b];
     __syncwarp();
+    int64_t i0, i1;
+    cs_range(n, i0, i1);
     const unsigned lt = (1u << lane) - 1u;
-    const int64_t base = c * 32 * rounds;
-    for (int b = 0; b < rounds; b += kRxBatch) {
-        uint32_t kk[kRxBatch], vv[kRxBatch];
+    constexpr int kB = 16;  // rounds whose loads are issued together
+    for (int64_t base = i0; base < i1; base += 32 * kB) {
+        uint32_t kk[kB], vv[kB];
+        float dd[kB];
 #pragma unroll
-        for (int r = 0; r < kRxBatch; ++r) {
-            const int64_t i = base + int64_t(b + r) * 32 + lane;
-            kk[r] = i < n ? keys_in[i] : 0u;
-            vv[r] = i < n ? vals_in[i] : 0u;
+        for (int r = 0; r < kB; ++r) {
+            const int64_t i = base + 32 * r + lane;
+            const bool ok = i < i1;
+            kk[r] = ok ? keys[i] : 0u;
+            vv[r] = ok ? vals[i] : 0u;
+        }
+        if constexpr (kIsect) {
+#pragma unroll
+            for (int r = 0; r < kB; ++r) dd[r] = (base + 32 * r + lane < i1) ? ep.depths[vv[r]] : 0.f;
         }
 #pragma unroll
-        for (int r = 0; r < kRxBatch; ++r) {
-            const int64_t i = base + int64_t(b + r) * 32 + lane;
-            const bool ok = i < n;
-            const int digit = ok ? int((kk[r] >> shift) & (kRadixBins - 1)) : kRadixBins;
-            const unsigned peers = match_digit(digit);
+        for (int r = 0; r < kB; ++r) {
+            const bool ok = base + 32 * r + lane < i1;
+            const int d = ok ? dg(kk[r]) : nbins;
+            const unsigned peers = __match_any_sync(0xffffffffu, d);
             const int leader = __ffs(peers) - 1;
-            int64_t p0 = 0;
-            if (ok && lane == leader) p0 = cur[w][digit];
+            int32_t p0 = 0;
+            if (ok && lane == leader) {
+                p0 = cur[d];
+                cur[d] = p0 + __popc(peers);
+            }
             p0 = __shfl_sync(0xffffffffu, p0, leader);
-            if (ok && lane == leader) cur[w][digit] = p0 + __popc(peers);
             __syncwarp();
             if (ok) {
-                const int64_t pos = p0 + __popc(peers & lt);
+                const int32_t pos = p0 + __popc(peers & lt);
                 if constexpr (kIsect) {
-                    const int32_t bits = __float_as_int(ep.depths[vv[r]]);
-                    // negative depths: the sign extension fills the tile bits
+                    const int32_t bits = __float_as_int(dd[r]);
                     const uint64_t hi = bits < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(kk[r]) << 32);
                     ep.isect_ids[pos] = int64_t(hi | uint64_t(uint32_t(bits)));
                     ep.flatten_ids[pos] = int32_t(vv[r]);
@@ -305,58 +320,81 @@ __global__ void __launch_bounds__(kSortThreads)
     }
 }
 
-// largest chunk count of any sort of at most n keys
-inline int64_t sort_chunks_max(int64_t n) {
-    const int64_t small = n < (int64_t(4) << 20) ? n : (int64_t(4) << 20);
-    const int64_t a = sort_chunks(n), b = sort_chunks(small);
-    return a > b ? a : b;
+inline int cs_warps(int64_t n, int nbins) {
+    const CsPlan pl = cs_plan(nbins);
+    const int64_t want = (n + pl.min_per - 1) / pl.min_per;
+    return int(want < 1 ? 1 : (want > pl.max_warps ? pl.max_warps : want));
 }
 
-inline size_t radix_workspace_bytes(int64_t n) {
-    const int64_t nc = sort_chunks_max(n);
-    return 2 * Arena::round(size_t(nc) * kRadixBins * sizeof(int32_t)) +
-           Arena::round(size_t(kRadixBins) * sizeof(int64_t));
+// Scratch of a pass over at most n keys with nbins bins.
+inline size_t cs_workspace_bytes(int64_t n, int nbins) {
+    const int64_t mat = int64_t(cs_warps(n, nbins)) * nbins;
+    if (nbins <= kCsNarrowBins)
+        return Arena::round(size_t(mat) * sizeof(int32_t)) + Arena::round(size_t(mat + 1) * sizeof(int64_t)) +
+               scan_workspace_bytes(mat);
+    return 2 * Arena::round(size_t(mat) * sizeof(int32_t)) + 2 * Arena::round(size_t(nbins + 1) * sizeof(int64_t));
 }
 
-// Stable ascending sort of (key, value) pairs on key bits [0, bits).
-// keys/vals and keys_alt/vals_alt are ping-pong buffers; the sorted result
-// is returned in *keys_res / *vals_res (one of the two).  With `ep` given the
-// final pass writes 64-bit isect ids and flatten ids instead.
-inline int radix_sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
-                            int64_t n, int bits, void* tmp, size_t tmp_bytes, cudaStream_t st,
-                            const IsectEpilogue* ep, uint32_t** keys_res, uint32_t** vals_res) {
-    if (keys_res) *keys_res = keys;
-    if (vals_res) *vals_res = vals;
-    if (n == 0) return XSG_OK;
-    if (n >= (int64_t(1) << 31)) return set_error(XSG_ERR_UNSUPPORTED, "radix sort: 2^31 or more keys");
-    const int64_t nc = sort_chunks(n);
-    const int rounds = sort_rounds(n);
-    Arena a(tmp, tmp_bytes);
-    int32_t* counts = a.take<int32_t>(size_t(nc) * kRadixBins);
-    int32_t* offs = a.take<int32_t>(size_t(nc) * kRadixBins);
-    int64_t* totals = a.take<int64_t>(kRadixBins);
-    if (!counts || !offs || !totals) return set_error(XSG_ERR_WORKSPACE, "radix sort: workspace too small");
-    const unsigned grid = unsigned((nc + kSortWarps - 1) / kSortWarps);
-    const int passes = (bits + kRadixBits - 1) / kRadixBits;
-    IsectEpilogue none{};
-    for (int p = 0; p < passes; ++p) {
-        const int shift = p * kRadixBits;
-        launch(radix_hist_kernel, grid, kSortThreads, 0, st, keys, n, shift, rounds, counts, nc);
-        launch(radix_rowscan_kernel, kRadixBins, 1024, 0, st, counts, nc, offs, totals);
-        const bool last = (p == passes - 1);
-        if (last && ep) {
-            launch(radix_scatter_kernel<true>, grid, kSortThreads, 0, st, keys, vals, n, shift, rounds, offs,
-                   totals, nc, nullptr, nullptr, *ep);
-        } else {
-            launch(radix_scatter_kernel<false>, grid, kSortThreads, 0, st, keys, vals, n, shift, rounds, offs,
-                   totals, nc, keys_alt, vals_alt, none);
-            uint32_t* t = keys; keys = keys_alt; keys_alt = t;
-            t = vals; vals = vals_alt; vals_alt = t;
-        }
+// One stable pass of `n` (upper bound; the count itself at n_dev when given)
+// pairs on digit dg with nbins values into keys_out / vals_out, or with `ep`
+// into the 64-bit isect ids and flatten ids.
+inline int counting_pass(const uint32_t* keys, const uint32_t* vals, uint32_t* keys_out, uint32_t* vals_out,
+                         int64_t n, const int64_t* n_dev, CsDigit dg, int nbins, void* tmp, size_t tmp_bytes,
+                         cudaStream_t st, const IsectEpilogue* ep) {
+    if (n <= 0) return XSG_OK;
+    if (nbins > kCsMaxBins) return set_error(XSG_ERR_UNSUPPORTED, "counting pass: too many bins");
+    static bool attrs_set[64] = {};
+    int dev = 0;
+    XSG_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !attrs_set[dev]) {
+        const int sm = int(kCsMaxBins * sizeof(int32_t));
+        XSG_CUDA(cudaFuncSetAttribute(cs_hist_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+        XSG_CUDA(cudaFuncSetAttribute(cs_scatter_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      sm));
+        XSG_CUDA(cudaFuncSetAttribute(cs_scatter_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      sm));
+        attrs_set[dev] = true;
     }
-    if (keys_res) *keys_res = keys;
-    if (vals_res) *vals_res = vals;
-    return check_launch("radix_sort_pairs");
+    const int G = cs_warps(n, nbins);
+    const int64_t mat = int64_t(G) * nbins;
+    const size_t smem = size_t(nbins) * sizeof(int32_t);
+    Arena a(tmp, tmp_bytes);
+    IsectEpilogue none{};
+    const IsectEpilogue& e = ep ? *ep : none;
+    int32_t* counts = a.take<int32_t>(size_t(mat));
+    if (nbins <= kCsNarrowBins) {
+        int64_t* pos0 = a.take<int64_t>(size_t(mat + 1));
+        void* stmp = a.take<char>(scan_workspace_bytes(mat));
+        if (!counts || !pos0 || !stmp) return set_error(XSG_ERR_WORKSPACE, "counting pass: workspace too small");
+        launch(cs_hist_kernel<true>, G, 32, smem, st, keys, n, n_dev, dg, nbins, counts);
+        int rc = exclusive_scan<int32_t>(counts, mat, pos0, nullptr, stmp, st);
+        if (rc != XSG_OK) return rc;
+        const int64_t* p0 = pos0;
+        if (ep)
+            launch(cs_scatter_kernel<true, true>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins, p0,
+                   static_cast<const int32_t*>(nullptr), static_cast<const int64_t*>(nullptr), nullptr, nullptr, e);
+        else
+            launch(cs_scatter_kernel<true, false>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins, p0,
+                   static_cast<const int32_t*>(nullptr), static_cast<const int64_t*>(nullptr), keys_out, vals_out, e);
+        return check_launch("counting_pass");
+    }
+    int32_t* offs = a.take<int32_t>(size_t(mat));
+    int64_t* totals = a.take<int64_t>(size_t(nbins + 1));
+    int64_t* starts = a.take<int64_t>(size_t(nbins + 1));
+    if (!counts || !offs || !totals || !starts) return set_error(XSG_ERR_WORKSPACE, "counting pass: workspace too small");
+    launch(cs_hist_kernel<false>, G, 32, smem, st, keys, n, n_dev, dg, nbins, counts);
+    launch(cs_colscan_kernel, unsigned((nbins + 31) / 32), 1024, 0, st, static_cast<const int32_t*>(counts), G,
+           nbins, offs, totals);
+    launch(cs_starts_kernel, 1, 1024, 0, st, static_cast<const int64_t*>(totals), nbins, starts);
+    const int32_t* of = offs;
+    const int64_t* sts = starts;
+    if (ep)
+        launch(cs_scatter_kernel<false, true>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins,
+               static_cast<const int64_t*>(nullptr), of, sts, nullptr, nullptr, e);
+    else
+        launch(cs_scatter_kernel<false, false>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins,
+               static_cast<const int64_t*>(nullptr), of, sts, keys_out, vals_out, e);
+    return check_launch("counting_pass");
 }
 
 }  // namespace xsg

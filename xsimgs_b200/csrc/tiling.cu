@@ -7,14 +7,17 @@
 // the emission order, which is Gaussian index then tile row-major):
 //   sorted by (tile, depth bits as u32, Gaussian index, tile row-major).
 // It is produced here without sorting 64-bit keys:
-//   1. the visible Gaussians are compacted and radix-sorted by depth bits
-//      (stable, so ties keep Gaussian order);
+//   1. the visible Gaussians are compacted and sorted by depth bits with
+//      three stable counting passes (so ties keep Gaussian order);
 //   2. their intersections are emitted in that order, keyed by tile only;
-//   3. a stable LSD radix sort on the tile bits moves them into tile order,
-//      and its last pass writes the 64-bit ids and the flatten ids.
+//   3. stable counting passes on the tile bits move them into tile order,
+//      and the last one writes the 64-bit ids and the flatten ids.
+// The number of visible Gaussians stays on the device throughout.
 // Negative depths (never produced by the projections) would make the
 // reference's sign-extended key fill the tile bits; they are keyed with the
 // all-ones tile value so the order still matches.
+#include <algorithm>
+
 #include "cameras.cuh"
 #include "scan_sort.cuh"
 
@@ -95,9 +98,9 @@ __global__ void __launch_bounds__(kTileThreads)
                         int bucket_neg, const uint32_t* __restrict__ order,
                         const int64_t* __restrict__ offsets, uint32_t* __restrict__ bucket_keys,
                         uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
-                        int32_t* __restrict__ flatten_ids) {
+                        int32_t* __restrict__ flatten_ids, const int64_t* __restrict__ n_dev) {
     const int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (p >= n_items) return;
+    if (p >= (n_dev ? *n_dev : n_items)) return;
     const uint32_t g = kSorted ? order[p] : uint32_t(p);
     Rect rc;
     if (!regular_rect(means2d[g], radii[g], ts, ntx, nty, rc)) return;
@@ -130,9 +133,9 @@ __global__ void compact_visible_kernel(const int32_t* __restrict__ counts, const
 }
 
 __global__ void gather_counts_kernel(const int32_t* __restrict__ counts, const uint32_t* __restrict__ order,
-                                     int64_t n, int32_t* __restrict__ out) {
+                                     int64_t n, int32_t* __restrict__ out, const int64_t* __restrict__ n_dev) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < n) out[i] = counts[order[i]];
+    if (i < (n_dev ? *n_dev : n)) out[i] = counts[order[i]];
 }
 
 // isect_offset_encode_kernel semantics (tiling_common.cu:25-71): offsets[t]
@@ -344,6 +347,13 @@ struct IsectWs {
     int32_t* fcopy;         // max_isects
 };
 
+// Scratch of the counting passes: 11-bit digits over n Gaussians or m
+// intersections (depth words), up to 8-bit digits over m (tile bits).
+static size_t sort_scratch_bytes(int64_t n, int64_t m) {
+    const int64_t big = n > m ? n : m;
+    return std::max(cs_workspace_bytes(big, 2048), cs_workspace_bytes(m, 256));
+}
+
 static size_t isect_ws_layout(int64_t n, int64_t m, void* base, size_t cap, IsectWs* ws) {
     Arena a(base, cap);
     const int64_t big = n > m ? n : m;
@@ -356,7 +366,7 @@ static size_t isect_ws_layout(int64_t n, int64_t m, void* base, size_t cap, Isec
     w.cnt_sorted = a.take<int32_t>(size_t(n));
     w.bk = a.take<uint32_t>(size_t(m)); w.bv = a.take<uint32_t>(size_t(m));
     w.bk2 = a.take<uint32_t>(size_t(m)); w.bv2 = a.take<uint32_t>(size_t(m));
-    w.sort_tmp_bytes = radix_workspace_bytes(big);
+    w.sort_tmp_bytes = sort_scratch_bytes(n, m);
     w.sort_tmp = a.take<char>(w.sort_tmp_bytes);
     w.kcopy = a.take<int64_t>(size_t(m));
     w.fcopy = a.take<int32_t>(size_t(m));
@@ -365,7 +375,7 @@ static size_t isect_ws_layout(int64_t n, int64_t m, void* base, size_t cap, Isec
     size_t need = 0;
     need += Arena::round(8) + Arena::round(size_t(n + 1) * 8) + scan_workspace_bytes(big + 1);
     need += 4 * Arena::round(size_t(n) * 4) + Arena::round(size_t(n) * 4);
-    need += 4 * Arena::round(size_t(m) * 4) + radix_workspace_bytes(big);
+    need += 4 * Arena::round(size_t(m) * 4) + sort_scratch_bytes(n, m);
     need += Arena::round(size_t(m) * 8) + Arena::round(size_t(m) * 4);
     return need;
 }
@@ -397,18 +407,41 @@ __global__ void permute_isects_kernel(const int64_t* __restrict__ kin, const int
     fout[j] = fin[p];
 }
 
+// Stable LSD sort of (u32 key, u32 value) pairs on key bits [0, bits) with
+// counting passes of up to `digit` bits; the result is returned in *keys_res /
+// *vals_res (one of the two buffer pairs).  With `ep` the last pass writes the
+// 64-bit isect ids and flatten ids instead.
+static int counting_sort(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int64_t n, const int64_t* n_dev,
+                         int bits, int digit, const IsectWs& w, cudaStream_t st, const IsectEpilogue* ep,
+                         uint32_t** keys_res, uint32_t** vals_res) {
+    const int np = (bits + digit - 1) / digit;
+    const int per = (bits + np - 1) / np;
+    for (int p = 0; p < np; ++p) {
+        const int lo = p * per, b = std::min(per, bits - lo);
+        const bool last = p == np - 1;
+        const int rc = counting_pass(k0, v0, k1, v1, n, n_dev, CsDigit{lo, uint32_t((uint64_t(1) << b) - 1)}, 1 << b,
+                                     w.sort_tmp, w.sort_tmp_bytes, st, last ? ep : nullptr);
+        if (rc != XSG_OK) return rc;
+        std::swap(k0, k1);
+        std::swap(v0, v1);
+    }
+    if (keys_res) *keys_res = k0;
+    if (vals_res) *vals_res = v0;
+    return XSG_OK;
+}
+
 // Stable sort of emitted (64-bit id, flatten id) pairs on id bits
 // [0, 32 + tb), in place: by the depth word, then stably by the tile bits.
 static int sort_isect_pairs_inplace(int64_t* ids, int32_t* flat, int64_t n, int tb, const struct IsectWs& w,
                                     cudaStream_t st) {
     launch(split_key_kernel, blocks_for(n, 256), 256, 0, st, ids, n, w.bk, w.bv);
     uint32_t *ks, *vs;
-    int rc = radix_sort_pairs(w.bk, w.bv, w.bk2, w.bv2, n, 32, w.sort_tmp, w.sort_tmp_bytes, st, nullptr, &ks, &vs);
+    int rc = counting_sort(w.bk, w.bv, w.bk2, w.bv2, n, nullptr, 32, 11, w, st, nullptr, &ks, &vs);
     if (rc != XSG_OK) return rc;
     uint32_t* k2 = (ks == w.bk) ? w.bk2 : w.bk;
     uint32_t* v2 = (vs == w.bv) ? w.bv2 : w.bv;
     launch(gather_hi_kernel, blocks_for(n, 256), 256, 0, st, ids, vs, n, tb, k2, v2);
-    rc = radix_sort_pairs(k2, v2, ks, vs, n, tb, w.sort_tmp, w.sort_tmp_bytes, st, nullptr, &ks, &vs);
+    rc = counting_sort(k2, v2, ks, vs, n, nullptr, tb, 8, w, st, nullptr, &ks, &vs);
     if (rc != XSG_OK) return rc;
     XSG_CUDA(cudaMemcpyAsync(w.kcopy, ids, size_t(n) * 8, cudaMemcpyDeviceToDevice, st));
     XSG_CUDA(cudaMemcpyAsync(w.fcopy, flat, size_t(n) * 4, cudaMemcpyDeviceToDevice, st));
@@ -418,33 +451,33 @@ static int sort_isect_pairs_inplace(int64_t* ids, int32_t* flat, int64_t n, int 
 
 // Sorted emission shared by regular and spherical tilings: presort the
 // visible Gaussians by depth, scan their counts in that order and let
-// `emit(order, offsets, n_vis)` write tile-keyed pairs, then bucket-sort.
+// `emit(order, offsets, n_vis_upper, n_vis_dev)` write tile-keyed pairs, then
+// bucket them stably by tile.  The number of visible Gaussians stays on the
+// device (grids are sized for all n), so there is no host round trip here.
 template <typename Emit>
 static int sorted_isects(const int32_t* counts, const float* depths, int64_t n, int64_t n_isects,
                          int64_t n_tiles, const IsectWs& w, int64_t* isect_ids, int32_t* flatten_ids,
                          cudaStream_t st, Emit&& emit) {
-    // 1. compact visible Gaussians (count > 0)
+    // 1. compact visible Gaussians (count > 0); their number goes to scan_out[n]
     int rc = exclusive_scan<int32_t, true>(counts, n, w.scan_out, w.scan_out + n, w.scan_tmp, st);
     if (rc != XSG_OK) return rc;
-    int64_t n_vis = 0;
-    XSG_CUDA(cudaMemcpyAsync(&n_vis, w.scan_out + n, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
-    XSG_CUDA(cudaStreamSynchronize(st));
-    launch(compact_visible_kernel, blocks_for(n, 256), 256, 0, st, counts, w.scan_out, depths, n, w.gk, w.gv);
-    // 2. stable sort by depth bits
-    uint32_t *ks, *vs;
-    rc = radix_sort_pairs(w.gk, w.gv, w.gk2, w.gv2, n_vis, 32, w.sort_tmp, w.sort_tmp_bytes, st, nullptr,
-                          &ks, &vs);
+    const int64_t* n_vis = w.scan_out + n;
+    launch(compact_visible_kernel, blocks_for(n, 256), 256, 0, st, counts, static_cast<const int64_t*>(w.scan_out),
+           depths, n, w.gk, w.gv);
+    // 2. stable sort by the 32 depth bits: three counting passes (11 + 11 + 10 bits)
+    uint32_t* order = nullptr;
+    rc = counting_sort(w.gk, w.gv, w.gk2, w.gv2, n, n_vis, 32, 11, w, st, nullptr, nullptr, &order);
     if (rc != XSG_OK) return rc;
     // 3. counts in depth order -> emission offsets
-    launch(gather_counts_kernel, blocks_for(n_vis, 256), 256, 0, st, counts, vs, n_vis, w.cnt_sorted);
-    rc = exclusive_scan<int32_t>(w.cnt_sorted, n_vis, w.scan_out, nullptr, w.scan_tmp, st);
+    launch(gather_counts_kernel, blocks_for(n, 256), 256, 0, st, counts, order, n, w.cnt_sorted, n_vis);
+    rc = exclusive_scan<int32_t>(w.cnt_sorted, n, w.scan_out, nullptr, w.scan_tmp, st, n_vis);
     if (rc != XSG_OK) return rc;
-    emit(vs, w.scan_out, n_vis);
-    // 4. stable bucket sort by tile; the last pass writes the outputs
-    const int tb = tile_bits_for(n_tiles);
+    emit(order, static_cast<const int64_t*>(w.scan_out), n, n_vis);
+    // 4. stable counting passes on the tile bits (up to 8 bits each), the
+    //    last of which writes the outputs
     IsectEpilogue ep{depths, isect_ids, flatten_ids};
-    return radix_sort_pairs(w.bk, w.bv, w.bk2, w.bv2, n_isects, tb, w.sort_tmp, w.sort_tmp_bytes, st, &ep,
-                            nullptr, nullptr);
+    return counting_sort(w.bk, w.bv, w.bk2, w.bv2, n_isects, nullptr, tile_bits_for(n_tiles), 8, w, st, &ep,
+                         nullptr, nullptr);
 }
 
 }  // namespace xsg
@@ -499,16 +532,17 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
         int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
         if (rc != XSG_OK) return rc;
         launch(regular_emit_kernel<false>, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
-            m2, r2, depths, n, ts, ntx, nty, 0, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids);
+            m2, r2, depths, n, ts, ntx, nty, 0, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
+            static_cast<const int64_t*>(nullptr));
         return check_launch("isect_regular_emit");
     }
     const int64_t n_tiles = int64_t(ntx) * nty;
     const int bucket_neg = int((int64_t(1) << tile_bits_for(n_tiles)) - 1);
     return sorted_isects(counts, depths, n, n_isects, n_tiles, w, isect_ids, flatten_ids, st,
-                         [&](const uint32_t* order, const int64_t* offs, int64_t n_vis) {
-                             launch(regular_emit_kernel<true>, blocks_for(n_vis, kTileThreads), kTileThreads, 0, st, 
-                                 m2, r2, depths, n_vis, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv,
-                                 nullptr, nullptr);
+                         [&](const uint32_t* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
+                             launch(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st,
+                                 m2, r2, depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv,
+                                 nullptr, nullptr, n_vis);
                          });
 }
 
