@@ -48,9 +48,9 @@ def bwd_flops(n_eval_bwd: int, n_contrib: int, cdim: int, ray_grads: bool = True
     return float(BWD_EVAL * n_eval_bwd + bwd_contrib(cdim, ray_grads) * n_contrib)
 
 
-# DRAM bytes per launch of the compositing backward (no ray gradients) on the
-# C2 view (1M Gaussians, 1920x1080, 16x16 tiles), dram__bytes_read.sum +
-# dram__bytes_write.sum from one capture:
+# DRAM bytes per launch of the compositing backward (no ray gradients, the
+# forward's contributor masks) on the C2 view (1M Gaussians, 1920x1080,
+# 16x16 tiles), dram__bytes_read.sum + dram__bytes_write.sum from one capture:
 #   ncu --set full --clock-control none -k regex:raster_bwd_kernel -s 1 -c 1 \
 #       python bench.py --steps 2 --warmup 1 --no-cpu-baseline --no-lidar
-BWD_DRAM_BYTES_C2 = 346.77e6 + 44.06e6
+BWD_DRAM_BYTES_C2 = 265.65e6 + 37.29e6
