@@ -15,8 +15,8 @@ value  : whole-job Mpix/s with inputs resident in HBM, device-timed with CUDA
          events (max over ranks).
 e2e    : the same step through the same public API with the upstream
          gradient images copied in from pinned host memory and the loss read
-         back to the host every step (copies double-buffered on a copy
-         stream, each loss read while the next step runs).
+         back to the host every step (copies buffered on a copy stream,
+         each loss read while the next steps run).
 --impl reference : the CPU oracle restatement of the reference (the
          reference itself cannot be built here), rank 0 only.
 """
@@ -312,26 +312,31 @@ def gpu_arm(args, world, rank, local):
     # ---------------------------------------------------- timed: e2e ----
     # Each step's upstream gradients come from pinned host memory and each
     # step's loss goes back to pinned host memory and is read on the host.
-    # The copies are double-buffered on a copy stream (step k+1's inputs
-    # arrive while step k computes) and the loss of step k is read while step
-    # k+1 runs, as a training loop with asynchronous loss logging does.
+    # The copies are buffered on a copy stream (later steps' inputs arrive
+    # while step k computes) and the loss of step k is read while the next
+    # steps run, as a training loop with asynchronous loss logging does.
     host = [[t.cpu().pin_memory() for t in g] for g in upstream]
     h2d = sum(t.numel() * t.element_size() for g in host for t in g)
     comp = torch.cuda.current_stream(dev)
     copy_stream = torch.cuda.Stream(device=dev)
-    dbufs = [[[torch.empty_like(t) for t in g] for g in upstream] for _ in range(2)]
-    loss_host = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(2)]
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_free = [torch.cuda.Event() for _ in range(2)]  # compute is done with dbufs[b]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
+    NB = 3  # buffers: the host reads step k's loss while steps k+1 and k+2 are queued
+    dbufs = [[[torch.empty_like(t) for t in g] for g in upstream] for _ in range(NB)]
+    loss_host = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(NB)]
+    ev_in = [torch.cuda.Event() for _ in range(NB)]
+    ev_free = [torch.cuda.Event() for _ in range(NB)]  # compute is done with dbufs[b]
+    ev_out = [torch.cuda.Event() for _ in range(NB)]
     for ev in ev_free:
         ev.record(comp)
     losses = []
 
     def e2e_steps(n, start_event=None):
-        pending = None
+        pending = []
         for k in range(n):
-            b = k % 2
+            b = k % NB
+            if len(pending) == NB - 1:  # buffer b's previous loss must be read before it is reused
+                p = pending.pop(0)
+                ev_out[p].synchronize()
+                losses.append(float(loss_host[p]))
             with torch.cuda.stream(copy_stream):
                 if start_event is not None and k == 0:
                     copy_stream.wait_event(start_event)
@@ -345,12 +350,10 @@ def gpu_arm(args, world, rank, local):
             ev_free[b].record(comp)
             loss_host[b].copy_(loss.detach(), non_blocking=True)
             ev_out[b].record(comp)
-            if pending is not None:
-                ev_out[pending].synchronize()
-                losses.append(float(loss_host[pending]))
-            pending = b
-        ev_out[pending].synchronize()
-        losses.append(float(loss_host[pending]))
+            pending.append(b)
+        for p in pending:
+            ev_out[p].synchronize()
+            losses.append(float(loss_host[p]))
 
     e2e_steps(max(1, args.warmup // 2))
     barrier()
