@@ -104,9 +104,40 @@ constexpr int kShThreads = kShWarps * 32;
 // rows (row length S, padded row stride S + 1), eight loads in flight per
 // lane.  Row/column of element j come from a float reciprocal: (j + 0.5) / S
 // is at least 0.5 / S away from an integer, far more than its rounding error.
+// Rows of S floats between global memory (dense) and a warp's shared
+// staging area (rows padded to S + 1 floats against bank conflicts).  With a
+// 16-byte aligned global pointer and S a multiple of 4 the copy moves float4
+// words (a word never straddles two rows).
+__device__ __forceinline__ bool stage_vec_ok(const float* g, int total, int S) {
+    return (reinterpret_cast<uintptr_t>(g) & 15u) == 0 && (S & 3) == 0 && (total & 3) == 0;
+}
+
 __device__ __forceinline__ void stage_rows_in(const float* __restrict__ src, int total, int S, float* wb,
                                               int lane) {
     const float invS = 1.0f / float(S);
+    if (stage_vec_ok(src, total, S)) {
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        const int t4 = total >> 2;
+        for (int base = 0; base < t4; base += 32 * 4) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int q = base + u * 32 + lane;
+                v[u] = q < t4 ? s4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int q = base + u * 32 + lane;
+                if (q < t4) {
+                    const int j = q << 2;
+                    const int row = int((float(j) + 0.5f) * invS);
+                    float* d = wb + row * (S + 1) + (j - row * S);
+                    d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w;
+                }
+            }
+        }
+        return;
+    }
     for (int base = 0; base < total; base += 32 * 8) {
         float v[8];
 #pragma unroll
@@ -128,6 +159,17 @@ __device__ __forceinline__ void stage_rows_in(const float* __restrict__ src, int
 __device__ __forceinline__ void stage_rows_out(float* __restrict__ dst, int total, int S, const float* wb,
                                                int lane) {
     const float invS = 1.0f / float(S);
+    if (stage_vec_ok(dst, total, S)) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        const int t4 = total >> 2;
+        for (int q = lane; q < t4; q += 32) {
+            const int j = q << 2;
+            const int row = int((float(j) + 0.5f) * invS);
+            const float* sp = wb + row * (S + 1) + (j - row * S);
+            d4[q] = make_float4(sp[0], sp[1], sp[2], sp[3]);
+        }
+        return;
+    }
     for (int base = 0; base < total; base += 32 * 8) {
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
