@@ -100,25 +100,52 @@ __global__ void __launch_bounds__(kTileThreads)
                         uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
                         int32_t* __restrict__ flatten_ids, const int64_t* __restrict__ n_dev) {
     const int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (p >= (n_dev ? *n_dev : n_items)) return;
-    const uint32_t g = kSorted ? order[p] : uint32_t(p);
-    Rect rc;
-    if (!regular_rect(means2d[g], radii[g], ts, ntx, nty, rc)) return;
-    int64_t off = offsets[p];
-    const int32_t bits = __float_as_int(depths[g]);
-    for (int y = rc.y0; y < rc.y1; ++y)
-        for (int x = rc.x0; x < rc.x1; ++x) {
-            const uint32_t tile = uint32_t(y) * uint32_t(ntx) + uint32_t(x);
-            if constexpr (kSorted) {
-                bucket_keys[off] = bits < 0 ? uint32_t(bucket_neg) : tile;
-                bucket_vals[off] = g;
-            } else {
-                const uint64_t hi = bits < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(tile) << 32);
-                isect_ids[off] = int64_t(hi | uint64_t(uint32_t(bits)));
-                flatten_ids[off] = int32_t(g);
-            }
-            ++off;
+    const int lane = threadIdx.x & 31;
+    const bool in = p < (n_dev ? *n_dev : n_items);
+    uint32_t g = 0;
+    Rect rc{0, 0, 0, 0};
+    bool has = false;
+    if (in) {
+        g = kSorted ? order[p] : uint32_t(p);
+        has = regular_rect(means2d[g], radii[g], ts, ntx, nty, rc);
+    }
+    const int cnt = has ? rc.count() : 0;
+    const int64_t off0 = cnt > 0 ? offsets[p] : 0;
+    const int32_t bits = has ? __float_as_int(depths[g]) : 0;
+    auto put = [&](int64_t off, int x, int y, int32_t b, uint32_t gg) {
+        const uint32_t tile = uint32_t(y) * uint32_t(ntx) + uint32_t(x);
+        if constexpr (kSorted) {
+            bucket_keys[off] = b < 0 ? uint32_t(bucket_neg) : tile;
+            bucket_vals[off] = gg;
+        } else {
+            const uint64_t hi = b < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(tile) << 32);
+            isect_ids[off] = int64_t(hi | uint64_t(uint32_t(b)));
+            flatten_ids[off] = int32_t(gg);
         }
+    };
+    // Gaussians with many tiles (close to the camera) are written by the
+    // whole warp, one tile per lane, in the same row-major order; the rest by
+    // their own lane
+    constexpr int kCoop = 16;
+    unsigned big = __ballot_sync(0xffffffffu, cnt > kCoop);
+    while (big) {
+        const int L = __ffs(big) - 1;
+        big &= big - 1;
+        const int lx0 = __shfl_sync(0xffffffffu, rc.x0, L), ly0 = __shfl_sync(0xffffffffu, rc.y0, L);
+        const int lw = __shfl_sync(0xffffffffu, rc.x1 - rc.x0, L), lc = __shfl_sync(0xffffffffu, cnt, L);
+        const int64_t lo = __shfl_sync(0xffffffffu, off0, L);
+        const int32_t lb = __shfl_sync(0xffffffffu, bits, L);
+        const uint32_t lg = __shfl_sync(0xffffffffu, g, L);
+        for (int j = lane; j < lc; j += 32) {
+            const int yy = j / lw;
+            put(lo + j, lx0 + (j - yy * lw), ly0 + yy, lb, lg);
+        }
+    }
+    if (cnt > 0 && cnt <= kCoop) {
+        int64_t off = off0;
+        for (int y = rc.y0; y < rc.y1; ++y)
+            for (int x = rc.x0; x < rc.x1; ++x) put(off++, x, y, bits, g);
+    }
 }
 
 // Visible (count > 0) Gaussians -> (depth bits, index) pairs, in index order.
