@@ -191,10 +191,58 @@ __device__ __forceinline__ TileCtx tile_ctx(const RasterArgs& a) {
     return c;
 }
 
+// ------------------------------------------------- evaluation arithmetic --
+// The alpha of a (ray, Gaussian) pair (eval3d_fwd.cu:111-124: grd = M d,
+// gn = grd / |grd|, gc = gn x gro with gro = M (o - mu), power = -|gc|^2 / 2)
+// as a fixed sequence of explicitly rounded products and FMAs, nothing left
+// to the compiler's contraction.  The forward evaluates two list entries at a
+// time with the paired FP32 instructions of sm_100 (fma / mul .f32x2, one
+// entry per half) and the backward one entry at a time with the scalar form;
+// both get bit-identical alpha and so take the same alpha >= 1/255 decisions.
+__device__ __forceinline__ float fx_dot(v3 a, v3 b) {
+    return __fmaf_rn(a.z, b.z, __fmaf_rn(a.y, b.y, __fmul_rn(a.x, b.x)));
+}
 // M v with M rows (r0,r1,r2).xyz, in glm's mat3 * vec3 order
-__device__ __forceinline__ v3 mrows(float4 r0, float4 r1, float4 r2, v3 v) {
-    return mk3(r0.x * v.x + r0.y * v.y + r0.z * v.z, r1.x * v.x + r1.y * v.y + r1.z * v.z,
-               r2.x * v.x + r2.y * v.y + r2.z * v.z);
+__device__ __forceinline__ v3 fx_mrows(float4 r0, float4 r1, float4 r2, v3 v) {
+    return mk3(fx_dot(mk3(r0.x, r0.y, r0.z), v), fx_dot(mk3(r1.x, r1.y, r1.z), v),
+               fx_dot(mk3(r2.x, r2.y, r2.z), v));
+}
+// glm::cross component order
+__device__ __forceinline__ v3 fx_cross(v3 a, v3 b) {
+    return mk3(__fmaf_rn(a.y, b.z, -__fmul_rn(b.y, a.z)), __fmaf_rn(a.z, b.x, -__fmul_rn(b.z, a.x)),
+               __fmaf_rn(a.x, b.y, -__fmul_rn(b.x, a.y)));
+}
+// (o - mu) of a moving Gaussian: mu + rt vel
+__device__ __forceinline__ v3 fx_moved(v3 mu, v3 vel, float rt) {
+    return mk3(__fmaf_rn(rt, vel.x, mu.x), __fmaf_rn(rt, vel.y, mu.y), __fmaf_rn(rt, vel.z, mu.z));
+}
+struct EvalTerms {
+    v3 grd, gn, gc;
+    float l, vis;  // |grd|^2, exp(power)
+};
+__device__ __forceinline__ EvalTerms fx_eval(float4 r0, float4 r1, float4 r2, v3 gro, v3 d) {
+    EvalTerms e;
+    e.grd = fx_mrows(r0, r1, r2, d);
+    e.l = fx_dot(e.grd, e.grd);
+    const float il = e.l > 0.0f ? rsqrtf(e.l) : 1.0f;
+    e.gn = mk3(__fmul_rn(e.grd.x, il), __fmul_rn(e.grd.y, il), __fmul_rn(e.grd.z, il));
+    e.gc = fx_cross(e.gn, gro);
+    e.vis = __expf(__fmul_rn(-0.5f, fx_dot(e.gc, e.gc)));
+    return e;
+}
+
+// The same operations on two entries at once: .x entry A, .y entry B.
+struct p3 {
+    float2 x, y, z;
+};
+__device__ __forceinline__ float2 pdup(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 pneg(float2 a) { return make_float2(-a.x, -a.y); }
+__device__ __forceinline__ float2 pdot(p3 a, p3 b) {
+    return __ffma2_rn(a.z, b.z, __ffma2_rn(a.y, b.y, __fmul2_rn(a.x, b.x)));
+}
+__device__ __forceinline__ p3 pcross(p3 a, p3 b) {
+    return {__ffma2_rn(a.y, b.z, pneg(__fmul2_rn(b.y, a.z))), __ffma2_rn(a.z, b.x, pneg(__fmul2_rn(b.z, a.x))),
+            __ffma2_rn(a.x, b.y, pneg(__fmul2_rn(b.x, a.y)))};
 }
 
 // ------------------------------------------------------- warp culling ----
@@ -348,7 +396,7 @@ __device__ __forceinline__ Quad make_quad(float4 r0, float4 r1, float4 r2, float
 __device__ __forceinline__ void view_consts(float4 r0, float4 r1, float4 r2, float4 r3, v3 o, float4* e) {
     const v3 mu = mk3(r0.w, r1.w, r2.w);
     const Quad q = make_quad(r0, r1, r2, r3.x, mu, o);
-    const v3 gro = mrows(r0, r1, r2, o - mu);
+    const v3 gro = fx_mrows(r0, r1, r2, o - mu);
     e[0] = q.a;
     e[1] = make_float4(q.b.x, q.b.y, q.b.z, cone_radius(r0, r1, r2, r3));
     e[2] = make_float4(gro.x, gro.y, gro.z, 0.f);
@@ -368,32 +416,55 @@ __device__ __forceinline__ float eval_quad(const float4& A, const float4& B, con
 }
 
 // ------------------------------------------------------------ forward ----
-// Warp-independent: each warp owns 32 pixels (two rows of a 16-wide tile),
-// stages the tile's records 32 at a time in its own slice of shared memory
-// and stops as soon as all its pixels are saturated.  There is no block-wide
-// barrier; the CTA only groups a tile's warps on one SM so they share L1.
+// Warp-independent: each warp owns 32 pixels (an 8 x 4 block of a tile),
+// takes the tile's list 32 entries at a time and stops as soon as all its
+// pixels are saturated.  There is no block-wide barrier; the CTA only groups
+// a tile's warps on one SM so they share L1.
+//
+// Per batch, lane i stages entry i: it loads the record, runs the warp-cone
+// test and leaves the quadric terms in shared memory, and the quadric loop
+// keeps the entries some lane may see.  The staging lanes of those then write
+// their records, in list order, as pairs: kept entry 2j in the low and 2j+1
+// in the high half of pair j's float2 components.  The evaluation loop reads
+// one pair at a time, computes both alphas with the paired FP32 instructions
+// and composites the two entries in order.
 constexpr int kWarpSlot = 32;
+constexpr int kPairs = kWarpSlot / 2;
+constexpr uint16_t kNoSlot = 0xffffu;
 
-// shared memory per warp: 4 record float4 + 1 colour float4 per slot, ids
-// per slot: 4 record float4, 1 colour float4, 2 quadric float4, the id
-__host__ __device__ constexpr size_t warp_stage_bytes() {
-    return size_t(kWarpSlot) * (7 * sizeof(float4) + sizeof(int32_t));
+// float2 components of a staged pair: 0-8 M row-major, 9-11 M (o - mu) when
+// the warp has one ray origin and -mu otherwise, 12 opacity, then -velocity
+// (dynamic) and the colour channels (CDIM <= 4)
+template <int CDIM, bool kDyn>
+struct PairLayout {
+    static constexpr bool kColor = CDIM > 0 && CDIM <= 4;
+    static constexpr int kVel = 13;
+    static constexpr int kCol = kDyn ? 16 : 13;
+    static constexpr int kComps = kCol + (kColor ? CDIM : 0);
+    static constexpr int kWords = (kComps + 1) / 2;  // float4 words a pair uses
+    static constexpr int kStride = kWords + 1;       // padded: pairs start in different banks
+    // float4 per warp: quadric terms (2 per entry), pairs, Gaussian ids and pair slots
+    static constexpr int kWarpF4 = 2 * kWarpSlot + kPairs * kStride + (kWarpSlot * 6) / 16;
+};
+
+// component C of a pair (float2: entry A, entry B) out of its float4 words
+template <int C>
+__device__ __forceinline__ float2 pc(const float4* w) {
+    return (C & 1) ? make_float2(w[C >> 1].z, w[C >> 1].w) : make_float2(w[C >> 1].x, w[C >> 1].y);
 }
 
 template <int CDIM, bool kDyn>
 __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
-    constexpr bool kStageColor = CDIM > 0 && CDIM <= 4;
+    using PL = PairLayout<CDIM, kDyn>;
+    constexpr bool kStageColor = PL::kColor;
     constexpr int CSZ = CDIM > 0 ? CDIM : 1;
     extern __shared__ float4 smem4[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    float4* s0 = smem4 + wid * (7 * kWarpSlot);
-    float4* s1 = s0 + kWarpSlot;
-    float4* s2 = s1 + kWarpSlot;
-    float4* s3 = s2 + kWarpSlot;
-    float4* sc = s3 + kWarpSlot;
-    float4* sqa = sc + kWarpSlot;
+    float4* sqa = smem4 + wid * PL::kWarpF4;
     float4* sqb = sqa + kWarpSlot;
-    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 7 * kWarpSlot) + wid * kWarpSlot;
+    float4* sp = sqb + kWarpSlot;  // [kPairs][kStride]
+    int32_t* sid = reinterpret_cast<int32_t*>(sp + kPairs * PL::kStride);
+    uint16_t* sslot = reinterpret_cast<uint16_t*>(sid + kWarpSlot);
 
     const TileCtx c = tile_ctx(a);
     const v3 o = c.inside ? ld3(a.ray_o + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
@@ -417,6 +488,7 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
                       __float_as_uint(o0.y) == __float_as_uint(a.ray_o[1]) &&
                       __float_as_uint(o0.z) == __float_as_uint(a.ray_o[2]);
     const DirQ dq = dir_q(d);
+    const p3 d2 = {pdup(d.x), pdup(d.y), pdup(d.z)};
 
     bool done = !c.inside;
     float T = 1.0f, depth = 0.0f;
@@ -433,11 +505,11 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
         if (__all_sync(0xffffffffu, done)) break;
         const int32_t idx = base + lane;
         bool keep = false;
+        float4 r0 = make_float4(0.f, 0.f, 0.f, 0.f), r1 = r0, r2 = r0, r3 = r0, cc = r0;
         if (idx < c.end) {
             const int32_t g = a.flatten[idx];
             const float4* r = a.rec + int64_t(kRecF4) * g;
-            float4 r0 = r[0], r1 = r[1], r2 = r[2];
-            const float4 r3 = r[3];
+            r0 = r[0]; r1 = r[1]; r2 = r[2]; r3 = r[3];
             Quad qd = quad_keep_all();
             if (gref) {
                 const float4* e = a.ext + 3 * int64_t(g);
@@ -456,21 +528,20 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
                     qd = make_quad(r0, r1, r2, r3.x, mu, o0);
                 }
                 if (uni) {
-                    const v3 gro = mrows(r0, r1, r2, o0 - mk3(r0.w, r1.w, r2.w));
+                    const v3 gro = fx_mrows(r0, r1, r2, o0 - mk3(r0.w, r1.w, r2.w));
                     r0.w = gro.x; r1.w = gro.y; r2.w = gro.z;
+                } else {
+                    r0.w = -r0.w; r1.w = -r1.w; r2.w = -r2.w;  // -mu
                 }
             }
             sqa[lane] = qd.a;
             sqb[lane] = qd.b;
-            s0[lane] = r0; s1[lane] = r1; s2[lane] = r2; s3[lane] = r3;
             if constexpr (kStageColor) {
-                float4 cc = make_float4(0.f, 0.f, 0.f, 0.f);
                 const float* cp = a.colors + int64_t(g) * CDIM;
                 cc.x = cp[0];
                 if (CDIM > 1) cc.y = cp[1];
                 if (CDIM > 2) cc.z = cp[2];
                 if (CDIM > 3) cc.w = cp[3];
-                sc[lane] = cc;
             } else {
                 sid[lane] = g;
             }
@@ -491,43 +562,48 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
                 if (__any_sync(0xffffffffu, !done && q >= 0.0f)) live |= 1u << t;
             }
         }
-        if (counting) w_quad += unsigned(__popc(live));
-        unsigned lmask = 0u;  // entries this lane composited (for the contributor mask)
-        while (live && !done) {
-            const int t = __ffs(live) - 1;
-            live &= live - 1;
-            if (counting) ++w_eval;
-            const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
-            v3 gro;
-            if (uni) {
-                gro = mk3(r0.w, r1.w, r2.w);
-            } else {
-                v3 mu = mk3(r0.w, r1.w, r2.w);
-                if (kDyn) mu = mu + rt * mk3(r3.y, r3.z, r3.w);
-                gro = mrows(r0, r1, r2, o - mu);
+        const int n_live = __popc(live);
+        if (counting) w_quad += unsigned(n_live);
+        // kept entries, ranked in list order, into the pair layout
+        if ((live >> lane) & 1u) {
+            const int rank = __popc(live & ((1u << lane) - 1u));
+            float* p = reinterpret_cast<float*>(sp + (rank >> 1) * PL::kStride) + (rank & 1);
+            auto put = [&](int comp, float v) { p[(comp >> 1) * 4 + (comp & 1) * 2] = v; };
+            put(0, r0.x); put(1, r0.y); put(2, r0.z);
+            put(3, r1.x); put(4, r1.y); put(5, r1.z);
+            put(6, r2.x); put(7, r2.y); put(8, r2.z);
+            put(9, r0.w); put(10, r1.w); put(11, r2.w);
+            put(12, r3.x);
+            if (kDyn) {
+                put(PL::kVel, -r3.y); put(PL::kVel + 1, -r3.z); put(PL::kVel + 2, -r3.w);
             }
-            const v3 grd = mrows(r0, r1, r2, d);
-            const float l = dot3(grd, grd);
-            const v3 gn = l > 0.0f ? grd * rsqrtf(l) : grd;
-            const v3 gc = cross3(gn, gro);
-            const float power = -0.5f * dot3(gc, gc);
-            const float alpha = fminf(0.999f, r3.x * __expf(power));
-            if (alpha < 1.f / 255.f) continue;
-            const float hit_t = __fdividef(-dot3(gro, grd), l);
+            if constexpr (kStageColor) {
+                put(PL::kCol, cc.x);
+                if (CDIM > 1) put(PL::kCol + 1, cc.y);
+                if (CDIM > 2) put(PL::kCol + 2, cc.z);
+                if (CDIM > 3) put(PL::kCol + 3, cc.w);
+            }
+            sslot[rank] = uint16_t(lane);
+            if (rank == n_live - 1 && !(rank & 1)) sslot[rank + 1] = kNoSlot;  // odd count: B is empty
+        }
+        __syncwarp();
+        unsigned lmask = 0u;  // entries this lane composited (for the contributor mask)
+        // one entry of the current pair; true when the pixel saturated on it
+        auto composite = [&](float ov, float od, float l, int t, const float (&col)[4]) -> bool {
+            const float alpha = fminf(0.999f, ov);
+            if (alpha < 1.f / 255.f) return false;
+            const float hit_t = __fdividef(-od, l);
             const float nT = T * (1.0f - alpha);
             if (nT <= 1e-4f) {
                 done = true;
                 stop = base + t;
-                break;
+                return true;
             }
             const float vis = alpha * T;
             depth += vis * hit_t;
             if constexpr (kStageColor) {
-                const float4 cc = sc[t];
-                acc[0] += cc.x * vis;
-                if (CDIM > 1) acc[1] += cc.y * vis;
-                if (CDIM > 2) acc[2] += cc.z * vis;
-                if (CDIM > 3) acc[3] += cc.w * vis;
+#pragma unroll
+                for (int k = 0; k < CDIM; ++k) acc[k] += col[k] * vis;
             } else if constexpr (CDIM > 0) {
                 const float* cp = a.colors + int64_t(sid[t]) * CDIM;
 #pragma unroll 4
@@ -537,6 +613,48 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
             T = nT;
             ++n_contrib;
             lmask |= 1u << t;
+            return false;
+        };
+        const int n_pairs = (n_live + 1) >> 1;
+        for (int j = 0; j < n_pairs && !done; ++j) {
+            float4 w[PL::kWords];
+#pragma unroll
+            for (int k = 0; k < PL::kWords; ++k) w[k] = sp[j * PL::kStride + k];
+            const uint32_t slots = reinterpret_cast<const uint32_t*>(sslot)[j];
+            const int tA = int(slots & 0xffffu), tB = int(slots >> 16);
+            if (counting) w_eval += (tB == kNoSlot) ? 1 : 2;
+            p3 gro = {pc<9>(w), pc<10>(w), pc<11>(w)};
+            if (!uni) {
+                // the pair holds -mu: gro = M (o - mu) for this lane's origin
+                p3 nmu = gro;
+                if (kDyn) {
+                    const float2 r2 = pdup(rt);
+                    nmu = {__ffma2_rn(r2, pc<PL::kVel>(w), nmu.x), __ffma2_rn(r2, pc<PL::kVel + 1>(w), nmu.y),
+                           __ffma2_rn(r2, pc<PL::kVel + 2>(w), nmu.z)};
+                }
+                const p3 omm = {__fadd2_rn(pdup(o.x), nmu.x), __fadd2_rn(pdup(o.y), nmu.y),
+                                __fadd2_rn(pdup(o.z), nmu.z)};
+                gro = {pdot({pc<0>(w), pc<1>(w), pc<2>(w)}, omm), pdot({pc<3>(w), pc<4>(w), pc<5>(w)}, omm),
+                       pdot({pc<6>(w), pc<7>(w), pc<8>(w)}, omm)};
+            }
+            const p3 grd = {pdot({pc<0>(w), pc<1>(w), pc<2>(w)}, d2), pdot({pc<3>(w), pc<4>(w), pc<5>(w)}, d2),
+                            pdot({pc<6>(w), pc<7>(w), pc<8>(w)}, d2)};
+            const float2 l = pdot(grd, grd);
+            const float2 il = make_float2(l.x > 0.0f ? rsqrtf(l.x) : 1.0f, l.y > 0.0f ? rsqrtf(l.y) : 1.0f);
+            const p3 gn = {__fmul2_rn(grd.x, il), __fmul2_rn(grd.y, il), __fmul2_rn(grd.z, il)};
+            const p3 gc = pcross(gn, gro);
+            const float2 pw = __fmul2_rn(pdup(-0.5f), pdot(gc, gc));
+            const float2 ov = __fmul2_rn(pc<12>(w), make_float2(__expf(pw.x), __expf(pw.y)));
+            const float2 od = pdot(gro, grd);
+            float colA[4] = {0.f, 0.f, 0.f, 0.f}, colB[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (kStageColor) {
+                colA[0] = pc<PL::kCol>(w).x; colB[0] = pc<PL::kCol>(w).y;
+                if constexpr (CDIM > 1) { colA[1] = pc<PL::kCol + 1>(w).x; colB[1] = pc<PL::kCol + 1>(w).y; }
+                if constexpr (CDIM > 2) { colA[2] = pc<PL::kCol + 2>(w).x; colB[2] = pc<PL::kCol + 2>(w).y; }
+                if constexpr (CDIM > 3) { colA[3] = pc<PL::kCol + 3>(w).x; colB[3] = pc<PL::kCol + 3>(w).y; }
+            }
+            if (composite(ov.x, od.x, l.x, tA, colA)) break;
+            if (tB != kNoSlot && composite(ov.y, od.y, l.y, tB, colB)) break;
         }
         const unsigned cmask = a.masks ? __reduce_or_sync(0xffffffffu, lmask) : 0u;
         if (a.masks && lane == 0)
@@ -715,21 +833,19 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
         const float4 r0 = s0[t], r1 = s1[t], r2 = s2[t], r3 = s3[t];
         v3 mu = mk3(r0.w, r1.w, r2.w);
         const v3 vel = mk3(r3.y, r3.z, r3.w);
-        if (kDyn) mu = mu + rt * vel;
+        if (kDyn) mu = fx_moved(mu, vel, rt);
         const v3 omm = o - mu;
         v3 gro;
         if (gref) {
             const float4 ge = sgro[t];
             gro = mk3(ge.x, ge.y, ge.z);
         } else {
-            gro = mrows(r0, r1, r2, omm);
+            gro = fx_mrows(r0, r1, r2, omm);
         }
-        const v3 grd = mrows(r0, r1, r2, d);
-        const float l = dot3(grd, grd);
-        const v3 gn = l > 0.0f ? grd * rsqrtf(l) : grd;
-        const v3 gc = cross3(gn, gro);
-        const float power = -0.5f * dot3(gc, gc);
-        const float vis = __expf(power);
+        // the forward's arithmetic: same alpha, same decisions
+        const EvalTerms ev = fx_eval(r0, r1, r2, gro, d);
+        const v3 grd = ev.grd, gn = ev.gn, gc = ev.gc;
+        const float l = ev.l, vis = ev.vis;
         const float op = r3.x;
         const float alpha = fminf(0.99f, op * vis);
         if (alpha < 1.f / 255.f) valid = false;
@@ -743,7 +859,7 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
 #pragma unroll
         for (int k = 0; k < CSZ; ++k) gcol[k] = 0.f;
         if (valid) {
-            const float od = dot3(gro, grd);
+            const float od = fx_dot(gro, grd);
             const float hit_t = __fdividef(-od, l);
             const float ra = __fdividef(1.0f, fmaxf(1e-6f, 1.0f - alpha));
             T *= ra;
@@ -1032,13 +1148,15 @@ __global__ void grads_finalize_kernel(const float* __restrict__ G, const float* 
 
 static const int kSupported[] = {0, 1, 2, 3, 4, 5, 8, 9, 16, 17, 32, 33, 64, 65, 128, 129, 256, 257, 512, 513};
 
-static size_t fwd_smem(int bs) { return size_t(bs / 32) * warp_stage_bytes(); }
-// the backward stages one more float4 per Gaussian (M (o - mu) of view-constant warps)
-static size_t bwd_smem(int bs, int) { return size_t(bs / 32) * (warp_stage_bytes() + kWarpSlot * sizeof(float4)); }
+template <int CDIM, bool kDyn>
+static size_t fwd_smem(int bs) { return size_t(bs / 32) * PairLayout<CDIM, kDyn>::kWarpF4 * sizeof(float4); }
+// the backward stages per slot 4 record words, the colour, the quadric terms
+// and M (o - mu) of view-constant warps (8 float4), and the Gaussian id
+static size_t bwd_smem(int bs) { return size_t(bs / 32) * kWarpSlot * (8 * sizeof(float4) + sizeof(int32_t)); }
 
 template <int CDIM, bool kDyn>
 static int launch_fwd(const RasterArgs& a, int bs, cudaStream_t st) {
-    const size_t sm = fwd_smem(bs);
+    const size_t sm = fwd_smem<CDIM, kDyn>(bs);
     auto fn = raster_fwd_kernel<CDIM, kDyn>;
     if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
     {
@@ -1054,7 +1172,7 @@ struct FinalizeOut {
 
 template <int CDIM, bool kDyn, bool kRayGrad>
 static int launch_bwd(const RasterArgs& a, int bs, cudaStream_t st, int64_t n_gauss, FinalizeOut fin) {
-    const size_t sm = bwd_smem(bs, Acc<CDIM, kDyn, kRayGrad>::N);
+    const size_t sm = bwd_smem(bs);
     auto fn = raster_bwd_kernel<CDIM, kDyn, kRayGrad>;
     if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
     {
