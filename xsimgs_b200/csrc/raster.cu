@@ -975,7 +975,9 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
         // the forward's contributor masks: visit only entries some lane of
         // this warp composited, without the cone and quadric pre-tests
         const int wpt = int(blockDim.x >> 5);
-        for (int32_t k = wmax >= c.start ? (wmax - c.start) >> 5 : -1; k >= 0; --k) {
+        // a pixel without contributors has last id 0: stay inside the tile's list
+        const int32_t wlast = min(wmax, c.end - 1);
+        for (int32_t k = wlast >= c.start ? (wlast - c.start) >> 5 : -1; k >= 0; --k) {
             const uint32_t cm = a.masks[mask_index(c.start, c.tile, k, wpt, wid)];
             if (!cm) continue;
             const int32_t base = c.start + (k << 5);
@@ -1068,6 +1070,255 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
         st3(a.v_ray_o + 3 * c.pix, vro);
         st3(a.v_ray_d + 3 * c.pix, vrd);
         if (kDyn) a.v_ray_t[c.pix] = vtime;
+    }
+}
+
+// ------------------------------------------ backward, two pixels a lane --
+// The static-scene backward without ray gradients (the training call), when
+// the forward's contributor masks are at hand, with two pixels per lane: a
+// warp owns two of the forward's 8 x 4 pixel blocks (pixel A of lane l is
+// lane l of the forward's warp 2w, pixel B lane l of warp 2w + 1), visits the
+// union of their masks back to front, evaluates every entry for both pixels
+// at once with the paired FP32 instructions (.x pixel A, .y pixel B; the
+// Gaussian's values are staged duplicated, so each is a ready pair) and adds
+// the two pixels' gradient values before the butterfly, which so runs once
+// per 64 pixels.  The alpha arithmetic is the forward's (fx_eval, per half).
+//
+// The colour and depth terms of v_alpha are carried as one running sum per
+// pixel: with X = sum_k rgb_k vc_k + hit_t vd, the reference's
+//   v_alpha = sum_k (rgb_k T - buf_k ra) vc_k + (hit_t T - dbuf ra) vd + T_final ra va
+// equals T X - ra Z with Z = sum_k buf_k vc_k + dbuf vd - T_final va, and
+// every contributing entry adds fac X to Z.
+template <int CDIM>
+struct Px2 {
+    // duplicated float2 components of a staged entry: 0-8 M row-major,
+    // 9-11 -mu, 12 opacity, 13-15 M (o - mu) for rays from pixel 0's origin,
+    // then the colour channels
+    static constexpr int kNmu = 9, kOp = 12, kGro = 13, kCol = 16;
+    static constexpr int kWords = (kCol + CDIM + 1) / 2;  // float4 per entry
+    static constexpr size_t warp_bytes() { return size_t(kWarpSlot) * (kWords * sizeof(float4) + sizeof(int32_t)); }
+};
+
+__device__ __forceinline__ p3 pscale(p3 a, float2 s) {
+    return {__fmul2_rn(a.x, s), __fmul2_rn(a.y, s), __fmul2_rn(a.z, s)};
+}
+__device__ __forceinline__ float hsum(float2 a) { return a.x + a.y; }
+
+template <int CDIM>
+__global__ void __launch_bounds__(128, 4) raster_bwd_px2_kernel(RasterArgs a) {
+    using L = Px2<CDIM>;
+    using AC = Acc<CDIM, false, false>;
+    constexpr int NA = AC::N;
+    constexpr int CSZ = CDIM > 0 ? CDIM : 1;
+    extern __shared__ float4 smem4[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    float4* sw = smem4 + wid * (L::kWords * kWarpSlot);  // [kWords][32]
+    int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * L::kWords * kWarpSlot) + wid * kWarpSlot;
+
+    const int tile = a.tile_order ? a.tile_order[blockIdx.x] : int(blockIdx.x);
+    const int ty = tile / a.ntx, tx = tile - ty * a.ntx;
+    const int wc = a.tsx >> 3;
+    const int fA = 2 * wid, fB = 2 * wid + 1;  // the forward's warps
+    const int pxA = tx * a.tsx + (fA % wc) * 8 + (lane & 7), pyA = ty * a.tsy + (fA / wc) * 4 + (lane >> 3);
+    const int pxB = tx * a.tsx + (fB % wc) * 8 + (lane & 7), pyB = ty * a.tsy + (fB / wc) * 4 + (lane >> 3);
+    const bool inA = pxA < a.W && pyA < a.H, inB = pxB < a.W && pyB < a.H;
+    const int64_t pixA = int64_t(pyA) * a.W + pxA, pixB = int64_t(pyB) * a.W + pxB;
+    const int32_t start = a.offsets[tile];
+    const int32_t end = (tile == a.ntx * a.nty - 1) ? int32_t(a.n_isects) : a.offsets[tile + 1];
+
+    // pixels outside the image get a harmless ray and never contribute
+    const v3 o_ref = ld3(a.ray_o);
+    const v3 oA = inA ? ld3(a.ray_o + 3 * pixA) : o_ref, oB = inB ? ld3(a.ray_o + 3 * pixB) : o_ref;
+    const v3 dA = inA ? ld3(a.ray_d + 3 * pixA) : mk3(0.f, 0.f, 1.f);
+    const v3 dB = inB ? ld3(a.ray_d + 3 * pixB) : mk3(0.f, 0.f, 1.f);
+    auto same = [](v3 u, v3 v) {
+        return __float_as_uint(u.x) == __float_as_uint(v.x) && __float_as_uint(u.y) == __float_as_uint(v.y) &&
+               __float_as_uint(u.z) == __float_as_uint(v.z);
+    };
+    // every pixel has pixel 0's ray origin: factored accumulation, view constants
+    const bool fact = __all_sync(0xffffffffu, same(oA, o_ref) && same(oB, o_ref));
+    const bool gref = fact && a.ext;
+    const p3 o2 = {make_float2(oA.x, oB.x), make_float2(oA.y, oB.y), make_float2(oA.z, oB.z)};
+    const p3 d2 = {make_float2(dA.x, dB.x), make_float2(dA.y, dB.y), make_float2(dA.z, dB.z)};
+    const int32_t binA = inA ? a.last_ids[pixA] : -1, binB = inB ? a.last_ids[pixB] : -1;
+    float2 T = make_float2(inA ? 1.0f - a.render_alpha[pixA] : 1.0f, inB ? 1.0f - a.render_alpha[pixB] : 1.0f);
+    float2 vc[CSZ];
+#pragma unroll
+    for (int k = 0; k < CSZ; ++k) vc[k] = make_float2(0.f, 0.f);
+    if (a.v_rgb) {
+#pragma unroll
+        for (int k = 0; k < CDIM; ++k)
+            vc[k] = make_float2(inA ? a.v_rgb[pixA * CDIM + k] : 0.f, inB ? a.v_rgb[pixB * CDIM + k] : 0.f);
+    }
+    const float2 vd = make_float2(inA ? a.v_depth[pixA] : 0.f, inB ? a.v_depth[pixB] : 0.f);
+    const float2 va = make_float2(inA ? a.v_alpha[pixA] : 0.f, inB ? a.v_alpha[pixB] : 0.f);
+    float2 nZ = __fmul2_rn(T, va);  // -Z = T_final va before any entry
+    // each forward warp's last contributor, inside the tile's list: the
+    // forward wrote that warp's masks for every batch up to it, and no others
+    int32_t wA = binA, wB = binB;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        wA = max(wA, __shfl_xor_sync(0xffffffffu, wA, off));
+        wB = max(wB, __shfl_xor_sync(0xffffffffu, wB, off));
+    }
+    wA = min(wA, end - 1);
+    wB = min(wB, end - 1);
+    const int32_t kA = wA >= start ? (wA - start) >> 5 : -1, kB = wB >= start ? (wB - start) >> 5 : -1;
+
+    auto process = [&](int t, int32_t gidx) {
+        float4 w[L::kWords];
+#pragma unroll
+        for (int k = 0; k < L::kWords; ++k) w[k] = sw[k * kWarpSlot + t];
+        const p3 M0 = {pc<0>(w), pc<1>(w), pc<2>(w)}, M1 = {pc<3>(w), pc<4>(w), pc<5>(w)},
+                 M2 = {pc<6>(w), pc<7>(w), pc<8>(w)};
+        p3 omm = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)}, gro;
+        if (gref) {
+            gro = {pc<L::kGro>(w), pc<L::kGro + 1>(w), pc<L::kGro + 2>(w)};
+        } else {
+            omm = {__fadd2_rn(o2.x, pc<L::kNmu>(w)), __fadd2_rn(o2.y, pc<L::kNmu + 1>(w)),
+                   __fadd2_rn(o2.z, pc<L::kNmu + 2>(w))};
+            gro = {pdot(M0, omm), pdot(M1, omm), pdot(M2, omm)};
+        }
+        const p3 grd = {pdot(M0, d2), pdot(M1, d2), pdot(M2, d2)};
+        const float2 l = pdot(grd, grd);
+        const float2 il = make_float2(l.x > 0.0f ? rsqrtf(l.x) : 1.0f, l.y > 0.0f ? rsqrtf(l.y) : 1.0f);
+        const p3 gn = pscale(grd, il);
+        const p3 gc = pcross(gn, gro);
+        const float2 pw = __fmul2_rn(pdup(-0.5f), pdot(gc, gc));
+        const float2 vis = make_float2(__expf(pw.x), __expf(pw.y));
+        const float2 op = pc<L::kOp>(w);
+        const float2 ov = __fmul2_rn(op, vis);
+        const float alA = fminf(0.99f, ov.x), alB = fminf(0.99f, ov.y);
+        const bool vA = inA && gidx <= binA && !(alA < 1.f / 255.f);
+        const bool vB = inB && gidx <= binB && !(alB < 1.f / 255.f);
+        if (!__any_sync(0xffffffffu, vA || vB)) return;
+
+        const float2 od = pdot(gro, grd);
+        const float hA = __fdividef(-od.x, l.x), hB = __fdividef(-od.y, l.y);
+        const float2 ra = make_float2(__fdividef(1.0f, fmaxf(1e-6f, 1.0f - alA)),
+                                      __fdividef(1.0f, fmaxf(1e-6f, 1.0f - alB)));
+        T = make_float2(vA ? T.x * ra.x : T.x, vB ? T.y * ra.y : T.y);
+        const float2 nfac = make_float2(vA ? -(alA * T.x) : 0.f, vB ? -(alB * T.y) : 0.f);
+        // X = sum_k rgb_k vc_k + hit_t vd
+        float2 X = __fmul2_rn(make_float2(hA, hB), vd);
+        if constexpr (CDIM > 0) X = __ffma2_rn(pc<L::kCol>(w), vc[0], X);
+        if constexpr (CDIM > 1) X = __ffma2_rn(pc<L::kCol + 1>(w), vc[1], X);
+        if constexpr (CDIM > 2) X = __ffma2_rn(pc<L::kCol + 2>(w), vc[2], X);
+        if constexpr (CDIM > 3) X = __ffma2_rn(pc<L::kCol + 3>(w), vc[3], X);
+        const float2 v_alpha = __ffma2_rn(T, X, __fmul2_rn(ra, nZ));  // T X - ra Z
+        nZ = __ffma2_rn(nfac, X, nZ);                                 // Z += fac X
+
+        // the alpha-dependent gradients: zero where the pixel does not
+        // contribute or its alpha was clamped
+        const bool kA = vA && ov.x <= 0.99f, kB = vB && ov.y <= 0.99f;
+        const float2 il2 = make_float2(__fdividef(1.0f, l.x), __fdividef(1.0f, l.y));
+        const float2 ndl = __fmul2_rn(vd, nfac);  // -dL/dt* = -vd fac
+        const float2 c1 = make_float2(kA ? ndl.x * il2.x : 0.f, kB ? ndl.y * il2.y : 0.f);
+        const float2 vae = make_float2(kA ? v_alpha.x : 0.f, kB ? v_alpha.y : 0.f);
+        // hit distance t* = -(gro . grd) / l: v_gro = -dLdt / l grd,
+        // v_grd = dLdt / l^2 (2 od grd - l gro) = (c1 / l) (l gro - 2 od grd)
+        p3 v_gro = pscale(grd, c1);
+        const float2 c2 = __fmul2_rn(c1, il2);
+        const float2 ntod = __fmul2_rn(od, pdup(-2.0f));
+        p3 v_grd = {__fmul2_rn(c2, __ffma2_rn(ntod, grd.x, __fmul2_rn(l, gro.x))),
+                    __fmul2_rn(c2, __ffma2_rn(ntod, grd.y, __fmul2_rn(l, gro.y))),
+                    __fmul2_rn(c2, __ffma2_rn(ntod, grd.z, __fmul2_rn(l, gro.z)))};
+        // power = -|gc|^2 / 2: v_gc = -(vis op v_alpha) gc
+        const float2 q = pneg(__fmul2_rn(vis, __fmul2_rn(op, vae)));
+        const p3 v_gc = pscale(gc, q);
+        const p3 v_gn = pcross(gro, v_gc);
+        const p3 xg = pcross(v_gc, gn);
+        v_gro = {__fadd2_rn(v_gro.x, xg.x), __fadd2_rn(v_gro.y, xg.y), __fadd2_rn(v_gro.z, xg.z)};
+        // normalisation: v_grd += il v_gn - il^3 (v_gn . grd) grd
+        const float2 s = pneg(__fmul2_rn(__fmul2_rn(__fmul2_rn(il, il), il), pdot(v_gn, grd)));
+        v_grd = {__ffma2_rn(s, grd.x, __ffma2_rn(il, v_gn.x, v_grd.x)),
+                 __ffma2_rn(s, grd.y, __ffma2_rn(il, v_gn.y, v_grd.y)),
+                 __ffma2_rn(s, grd.z, __ffma2_rn(il, v_gn.z, v_grd.z))};
+
+        float gv[16];
+        if (fact) {
+            gv[0] = hsum(v_gro.x); gv[1] = hsum(v_gro.y); gv[2] = hsum(v_gro.z);
+        } else {
+            // v_mean = -M^T v_gro
+            gv[0] = -hsum(__ffma2_rn(M2.x, v_gro.z, __ffma2_rn(M1.x, v_gro.y, __fmul2_rn(M0.x, v_gro.x))));
+            gv[1] = -hsum(__ffma2_rn(M2.y, v_gro.z, __ffma2_rn(M1.y, v_gro.y, __fmul2_rn(M0.y, v_gro.x))));
+            gv[2] = -hsum(__ffma2_rn(M2.z, v_gro.z, __ffma2_rn(M1.z, v_gro.y, __fmul2_rn(M0.z, v_gro.x))));
+        }
+        gv[3] = hsum(__fmul2_rn(vis, vae));
+        // dL/dM row i = v_grd[i] d (+ v_gro[i] (o - mu) when not factored)
+        const float2 vg[3] = {v_grd.x, v_grd.y, v_grd.z};
+        const float2 vo[3] = {v_gro.x, v_gro.y, v_gro.z};
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            float2 m0 = __fmul2_rn(vg[i], d2.x), m1 = __fmul2_rn(vg[i], d2.y), m2 = __fmul2_rn(vg[i], d2.z);
+            if (!fact) {
+                m0 = __ffma2_rn(vo[i], omm.x, m0);
+                m1 = __ffma2_rn(vo[i], omm.y, m1);
+                m2 = __ffma2_rn(vo[i], omm.z, m2);
+            }
+            gv[4 + 3 * i] = hsum(m0);
+            gv[5 + 3 * i] = hsum(m1);
+            gv[6 + 3 * i] = hsum(m2);
+        }
+        float gc3 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) gv[13 + k] = k < CDIM ? -hsum(__fmul2_rn(vc[k < CSZ ? k : 0], nfac)) : 0.f;
+        if constexpr (CDIM == 4) gc3 = -hsum(__fmul2_rn(vc[3], nfac));
+
+        float* dst = a.G + int64_t(sid[t]) * NA;
+        butterfly16(gv, lane);
+        // lanes 8k+0/2/4/6 hold values 4k..4k+3: gather them into lane 8k
+        const float g1 = __shfl_down_sync(0xffffffffu, gv[0], 2);
+        const float g2 = __shfl_down_sync(0xffffffffu, gv[0], 4);
+        const float g3 = __shfl_down_sync(0xffffffffu, gv[0], 6);
+        // a factored warp's first group (sum of v_gro, v_opacity) goes to its own slots
+        const int slot = (fact && lane == 0) ? AC::kFactSlot : (lane >> 1);
+        if ((lane & 7) == 0) red_add_v4(dst + slot, gv[0], g1, g2, g3);
+        if constexpr (CDIM == 4) {
+            const float e0 = warp_sum(gc3);
+            if (lane == 0) red_add_v4(dst + 16, e0, 0.f, 0.f, 0.f);
+        }
+    };
+
+    const int wpt = (a.tsx * a.tsy) >> 5;  // the forward's warps per tile
+    for (int32_t k = max(kA, kB); k >= 0; --k) {
+        const uint32_t cm = (k <= kA ? a.masks[mask_index(start, tile, k, wpt, fA)] : 0u) |
+                            (k <= kB ? a.masks[mask_index(start, tile, k, wpt, fB)] : 0u);
+        if (!cm) continue;
+        const int32_t base = start + (k << 5);
+        if ((cm >> lane) & 1u) {
+            const int32_t g = a.flatten[base + lane];
+            const float4* r = a.rec + int64_t(kRecF4) * g;
+            const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
+            const float4 e2 = gref ? a.ext[3 * int64_t(g) + 2] : make_float4(0.f, 0.f, 0.f, 0.f);  // M (o - mu)
+            float4* s = sw + lane;
+            s[0 * kWarpSlot] = make_float4(r0.x, r0.x, r0.y, r0.y);
+            s[1 * kWarpSlot] = make_float4(r0.z, r0.z, r1.x, r1.x);
+            s[2 * kWarpSlot] = make_float4(r1.y, r1.y, r1.z, r1.z);
+            s[3 * kWarpSlot] = make_float4(r2.x, r2.x, r2.y, r2.y);
+            s[4 * kWarpSlot] = make_float4(r2.z, r2.z, -r0.w, -r0.w);
+            s[5 * kWarpSlot] = make_float4(-r1.w, -r1.w, -r2.w, -r2.w);
+            s[6 * kWarpSlot] = make_float4(r3.x, r3.x, e2.x, e2.x);
+            s[7 * kWarpSlot] = make_float4(e2.y, e2.y, e2.z, e2.z);
+            if constexpr (CDIM > 0) {
+                const float* cp = a.colors + int64_t(g) * CDIM;
+                const float c0 = cp[0], c1 = CDIM > 1 ? cp[1] : 0.f;
+                s[8 * kWarpSlot] = make_float4(c0, c0, c1, c1);
+                if constexpr (CDIM > 2) {
+                    const float c2 = cp[2], c3 = CDIM > 3 ? cp[3] : 0.f;
+                    s[9 * kWarpSlot] = make_float4(c2, c2, c3, c3);
+                }
+            }
+            sid[lane] = g;
+        }
+        __syncwarp();
+        unsigned live = cm;
+        while (live) {
+            const int t = 31 - __clz(live);
+            live &= ~(1u << t);
+            process(t, base + t);
+        }
+        __syncwarp();
     }
 }
 
@@ -1172,10 +1423,23 @@ struct FinalizeOut {
 
 template <int CDIM, bool kDyn, bool kRayGrad>
 static int launch_bwd(const RasterArgs& a, int bs, cudaStream_t st, int64_t n_gauss, FinalizeOut fin) {
-    const size_t sm = bwd_smem(bs);
-    auto fn = raster_bwd_kernel<CDIM, kDyn, kRayGrad>;
-    if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
-    {
+    bool done = false;
+    if constexpr (!kDyn && !kRayGrad && CDIM <= 4) {
+        // two pixels a lane: needs the masks and an even count of 8 x 4 warp blocks per tile
+        if (a.masks && a.tsx % 8 == 0 && a.tsy % 4 == 0 && ((a.tsx * a.tsy) / 32) % 2 == 0) {
+            const size_t sm = size_t(bs / 64) * Px2<CDIM>::warp_bytes();
+            auto fn = raster_bwd_px2_kernel<CDIM>;
+            if (sm > 48 * 1024)
+                XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
+            ScopedTimer tm("rasterize_bwd", st);
+            launch(fn, unsigned(a.ntx * a.nty), bs / 2, sm, st, a);
+            done = true;
+        }
+    }
+    if (!done) {
+        const size_t sm = bwd_smem(bs);
+        auto fn = raster_bwd_kernel<CDIM, kDyn, kRayGrad>;
+        if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
         ScopedTimer tm("rasterize_bwd", st);
         launch(fn, unsigned(a.ntx * a.nty), bs, sm, st, a);
     }
