@@ -418,7 +418,7 @@ def gpu_arm(args, world, rank, local):
         pairs = {"evaluated_fwd": 0, "evaluated_bwd": 0, "contributing": 0}
         for sp, cam in views:
             W, H = sp.width, sp.height
-            cnt = torch.zeros(6, dtype=torch.int64, device=dev)
+            cnt = torch.zeros(8, dtype=torch.int64, device=dev)
             capi.set_pair_counters(cnt.data_ptr())
             with torch.no_grad():
                 colors = X.spherical_harmonics_fused(sc.sh, sc.means, cam.t0, DEG_C2)
@@ -451,7 +451,7 @@ def gpu_arm(args, world, rank, local):
         ach_b = fl_b / (bwd_step * 1e-3) / 1e12
         ach_f = fl_f / (fwd_step * 1e-3) / 1e12
         c2_full = args.workload == "c2" and n_gauss == N_C2
-        roof = {"kernel": "rasterize_bwd (raster_bwd_kernel<3,false,false>, no ray gradients)", "bound": "fp32",
+        roof = {"kernel": "rasterize_bwd (raster_bwd_px2_kernel<3>: static scene, no ray gradients, two pixels a lane)", "bound": "fp32",
                 "achieved": round(ach_b, 2), "peak": round(peak_flops / 1e12, 2), "unit": "TFLOP/s",
                 "frac": round(ach_b / (peak_flops / 1e12), 3),
                 "traffic": roofline.BWD_DRAM_BYTES_C2 if c2_full else None,

@@ -77,12 +77,18 @@ int xsg_timing_query(const char* name, double* total_ms, long long* launches);
 /* FP32 FMA peak probe: launches `blocks` x 512 threads of iters x 128
  * independent FMAs, writes the FLOP count to *flops (time it with events). */
 int xsg_fp32_probe(float* scratch, int iters, int blocks, xsg_stream_t stream, double* flops);
-/* Pair counters of the forward compositing kernel: when `counters` (6 x u64,
+/* Pair counters of the forward compositing kernel: when `counters` (8 x u64,
  * device, zeroed by the caller) is set, every xsg_rasterize_fwd adds to it
  * [0] the evaluated and [1] the contributing (pixel, Gaussian) pairs as the
  * reference counts them, and, per (warp of 32 pixels, Gaussian), [2] the
  * entries staged from the tile lists, [3] those passing the warp's cone
  * test, [4] those passing the per-lane quadric test and [5] those evaluated.
+ * With a workspace sized for contributor masks (static scene, colour channels
+ * <= 4, tile sides multiples of 8 and 4, an even count of 8 x 4 blocks per
+ * tile) it also adds, over the pairs of 8 x 4 pixel blocks (2w, 2w + 1) of
+ * every fourth tile, [6] the union and [7] the sum of the two blocks'
+ * contributor counts per list entry: the backward runs two pixels a lane when
+ * [6] is at most 72 % of [7] for the image.
  * NULL (the default) turns counting off. */
 void xsg_set_pair_counters(unsigned long long* counters);
 

@@ -181,6 +181,88 @@ def test_rasterize_fwd_bwd_match_oracle(c1, cuda):
         assert_grads_close(got, rg[key], key + " (no ray grads)")
 
 
+def test_rasterize_mixed_origins_forward_workspace(c1, cuda):
+    """An image where some 16 x 4 pixel blocks share pixel 0's ray origin and
+    others do not: with the forward's workspace the backward gives the first
+    kind to the two-pixels-a-lane kernel and the second to the per-pixel one;
+    together they must match the oracle on every Gaussian gradient."""
+    from xsimgs_b200 import _C, scenes
+    sc, spec = c1
+    W, H = spec.width, spec.height
+    cam, off, flat, ro, rd = _raster_inputs(sc, spec, cuda)
+    shape = ro.shape
+    ro = ro.clone().view(H, W, 3)
+    ro[20:36, :, 0] += 1e-3          # whole rows of blocks with another origin
+    ro[::7, ::13, 1] -= 2e-3         # scattered pixels spoil other blocks
+    ro = ro.reshape(shape).contiguous()
+    colors = sh_colors(sc.sh, 0)
+    g = lambda t: t.to(cuda).contiguous()
+    args = dict(means=g(sc.means), quats=g(sc.quats), scales=g(sc.scales), colors=g(colors).unsqueeze(0),
+                opacities=g(sc.opacities).view(1, -1), image_width=W, image_height=H, tile_size_width=16,
+                tile_size_height=16, ray_origs=ro, ray_dirs=rd, tile_offsets=off, flatten_ids=flat)
+    n = sc.means.shape[0]
+    ws = torch.empty(_C.rasterize_workspace_size(n, 3, n_isects=flat.numel(), n_tiles=off.numel(), tile_pixels=256),
+                     dtype=torch.uint8, device=cuda)
+    rgb, depth, alpha, last = _C.rasterize_eval3d_fwd(workspace=ws, **args)
+    r = O.rasterize_fwd(sc.means.numpy(), sc.quats.numpy(), sc.scales.numpy(), colors.numpy(),
+                        sc.opacities.numpy(), W, H, 16, 16, to_np(ro), to_np(rd), to_np(off), to_np(flat))
+    near = r[4]
+    vr, vd, va = zero_at(near, *scenes.upstream_grads(H, W, 3))
+    rg = O.rasterize_bwd(sc.means.numpy(), sc.quats.numpy(), sc.scales.numpy(), colors.numpy(),
+                         sc.opacities.numpy(), W, H, 16, 16, to_np(ro), to_np(rd), to_np(off), to_np(flat),
+                         to_np(alpha), to_np(last), vr.numpy(), vd.numpy(), va.numpy())
+    for ray_grads in (False, True):
+        out = _C.rasterize_eval3d_bwd(g(sc.means), g(sc.scales), g(sc.quats), g(sc.opacities), g(colors), ro, rd,
+                                      16, 16, off, flat, alpha, last, g(vr), g(vd), g(va), ray_grads=ray_grads,
+                                      forward_workspace=ws)
+        for got, key in zip(out[:5], ["v_means", "v_quats", "v_scales", "v_opacities", "v_colors"]):
+            assert_grads_close(got, rg[key], f"{key} (mixed origins, ray grads {ray_grads})")
+
+
+def test_rasterize_backward_kernel_choice(c1, cuda):
+    """The forward counts how far the contributor masks of the two 8 x 4
+    blocks of each pair overlap (pair counters 6 and 7); the backward runs two
+    pixels a lane when the union is at most 72 % of the sum, else per pixel.
+    The C1 scene (large Gaussians) and the same scene shrunk 20-fold land on
+    the two sides, and both backward kernels match the oracle."""
+    from xsimgs_b200 import _C, capi, scenes
+    sc, spec = c1
+    W, H = spec.width, spec.height
+    ratios = []
+    for shrink in (1.0, 0.05):
+        sc_s = type(sc)(**{**sc.__dict__, "scales": sc.scales * shrink}) if shrink != 1.0 else sc
+        cam, off, flat, ro, rd = _raster_inputs(sc_s, spec, cuda)
+        colors = sh_colors(sc_s.sh, 0)
+        g = lambda t: t.to(cuda).contiguous()
+        n = sc_s.means.shape[0]
+        ws = torch.empty(_C.rasterize_workspace_size(n, 3, n_isects=flat.numel(), n_tiles=off.numel(),
+                                                     tile_pixels=256), dtype=torch.uint8, device=cuda)
+        cnt = torch.zeros(8, dtype=torch.int64, device=cuda)
+        capi.set_pair_counters(cnt.data_ptr())
+        try:
+            rgb, depth, alpha, last = _C.rasterize_eval3d_fwd(
+                means=g(sc_s.means), quats=g(sc_s.quats), scales=g(sc_s.scales), colors=g(colors).unsqueeze(0),
+                opacities=g(sc_s.opacities).view(1, -1), image_width=W, image_height=H, tile_size_width=16,
+                tile_size_height=16, ray_origs=ro, ray_dirs=rd, tile_offsets=off, flatten_ids=flat, workspace=ws)
+            torch.cuda.synchronize()
+        finally:
+            capi.set_pair_counters(None)
+        c = cnt.tolist()
+        assert c[7] > 0 and c[7] >= c[6] >= c[7] // 2
+        ratios.append(c[6] / c[7])
+        args = (sc_s.means.numpy(), sc_s.quats.numpy(), sc_s.scales.numpy(), colors.numpy(),
+                sc_s.opacities.numpy(), W, H, 16, 16, to_np(ro), to_np(rd), to_np(off), to_np(flat))
+        near = O.rasterize_fwd(*args)[4]
+        vr, vd, va = zero_at(near, *scenes.upstream_grads(H, W, 3))
+        rg = O.rasterize_bwd(*args, to_np(alpha), to_np(last), vr.numpy(), vd.numpy(), va.numpy())
+        out = _C.rasterize_eval3d_bwd(g(sc_s.means), g(sc_s.scales), g(sc_s.quats), g(sc_s.opacities), g(colors),
+                                      ro, rd, 16, 16, off, flat, alpha, last, g(vr), g(vd), g(va), ray_grads=False,
+                                      forward_workspace=ws)
+        for got, key in zip(out[:5], ["v_means", "v_quats", "v_scales", "v_opacities", "v_colors"]):
+            assert_grads_close(got, rg[key], f"{key} (scales x {shrink}, mask overlap {ratios[-1]:.3f})")
+    assert ratios[0] <= 0.72 < ratios[1], ratios
+
+
 @pytest.mark.parametrize("degree", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("layout_3kn", [False, True])
 def test_sh_fwd_bwd_match_oracle(cuda, degree, layout_3kn):

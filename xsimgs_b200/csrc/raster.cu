@@ -65,7 +65,24 @@ struct RasterArgs {
     // bit i set when list entry start + 32 k + i reached alpha >= 1/255 at one of the warp's
     // pixels before it saturated; the forward writes them, the backward visits only those entries
     uint32_t* masks;
+    // after the masks: the union and the sum of the mask bits of each pair of
+    // 8 x 4 blocks (2w, 2w + 1), over the image, counted by the forward; the
+    // backward's choice between its two kernels (px2_chosen)
+    unsigned long long* px2_stats;
 };
+
+// largest union of the block pairs' contributor masks, in percent of the
+// pairs' two counts, for which the backward runs two pixels a lane
+constexpr int kPx2UnionPct = 72;
+
+// The two-pixels-a-lane backward pays a whole paired evaluation for an entry
+// only one block of its pair composited, so it serves an image whose block
+// pairs mostly composite the same Gaussians; the per-pixel backward serves
+// the others (sparse angular sampling: lidar).  Both kernels are launched and
+// read the forward's counts; the one not chosen returns at once.
+__device__ __forceinline__ bool px2_chosen(const unsigned long long* stats) {
+    return stats[0] * 100ull <= (unsigned long long)kPx2UnionPct * stats[1];
+}
 
 // Index of the contributor mask of batch k of a warp (tiles' batch ranges
 // [(start >> 5) + tile, + ceil(len / 32)) never overlap).
@@ -87,8 +104,10 @@ __device__ __forceinline__ void view_consts(float4 r0, float4 r1, float4 r2, flo
 __global__ void pack_records_kernel(const float* __restrict__ means, const float* __restrict__ vel,
                                     const float* __restrict__ quats, const float* __restrict__ scales,
                                     const float* __restrict__ opac, int64_t n, float4* __restrict__ rec,
-                                    const float* __restrict__ o_ref, float4* __restrict__ ext) {
+                                    const float* __restrict__ o_ref, float4* __restrict__ ext,
+                                    unsigned long long* __restrict__ px2_stats) {
     const int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (px2_stats && g < 2) px2_stats[g] = 0ull;  // the forward counts into them
     if (g >= n) return;
     float w = quats[4 * g], x = quats[4 * g + 1], y = quats[4 * g + 2], z = quats[4 * g + 3];
     const float inv_norm = rsqrtf(x * x + y * y + z * z + w * w);
@@ -501,8 +520,10 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
     // warp-level work counters (staged, cone-passed, quadric-passed, evaluated)
     unsigned long long w_staged = 0, w_cone = 0, w_quad = 0, w_eval = 0;
     const bool counting = a.pair_counters != nullptr;
+    int32_t n_batches = 0;  // batches this warp took (and wrote masks for)
     for (int32_t base = c.start; base < c.end; base += kWarpSlot) {
         if (__all_sync(0xffffffffu, done)) break;
+        ++n_batches;
         const int32_t idx = base + lane;
         bool keep = false;
         float4 r0 = make_float4(0.f, 0.f, 0.f, 0.f), r1 = r0, r2 = r0, r3 = r0, cc = r0;
@@ -682,6 +703,41 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
             atomicAdd(a.pair_counters + 5, w_eval);
         }
     }
+    if (a.px2_stats && (c.tile & 3) == 0) {
+        // union and sum of the mask bits of this tile's block pairs, for the
+        // backward's choice of kernel (every fourth tile is a large enough sample)
+        __shared__ int32_t s_nb[32];
+        __shared__ unsigned long long s_cnt[2];
+        if (threadIdx.x < 2) s_cnt[threadIdx.x] = 0ull;
+        if (lane == 0) s_nb[wid] = n_batches;
+        __syncthreads();
+        if (!(wid & 1)) {
+            const int wpt = int(blockDim.x >> 5);
+            const int32_t kA = s_nb[wid] - 1, kB = s_nb[wid + 1] - 1;
+            unsigned u = 0u, both = 0u;
+            for (int32_t k = lane; k <= max(kA, kB); k += 32) {
+                const uint32_t mA = k <= kA ? a.masks[mask_index(c.start, c.tile, k, wpt, wid)] : 0u;
+                const uint32_t mB = k <= kB ? a.masks[mask_index(c.start, c.tile, k, wpt, wid + 1)] : 0u;
+                u += unsigned(__popc(mA | mB));
+                both += unsigned(__popc(mA) + __popc(mB));
+            }
+            u = __reduce_add_sync(0xffffffffu, u);
+            both = __reduce_add_sync(0xffffffffu, both);
+            if (lane == 0) {
+                atomicAdd(&s_cnt[0], (unsigned long long)u);
+                atomicAdd(&s_cnt[1], (unsigned long long)both);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && (s_cnt[0] | s_cnt[1])) {
+            atomicAdd(a.px2_stats, s_cnt[0]);
+            atomicAdd(a.px2_stats + 1, s_cnt[1]);
+            if (a.pair_counters) {
+                atomicAdd(a.pair_counters + 6, s_cnt[0]);
+                atomicAdd(a.pair_counters + 7, s_cnt[1]);
+            }
+        }
+    }
     if (c.inside) {
         a.out_alpha[c.pix] = 1.0f - T;
         a.out_depth[c.pix] = depth;
@@ -783,6 +839,7 @@ __global__ void __launch_bounds__(256, 3) raster_bwd_kernel(RasterArgs a) {
     float4* sgro = sqb + kWarpSlot;
     int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * 8 * kWarpSlot) + wid * kWarpSlot;
 
+    if (a.px2_stats && px2_chosen(a.px2_stats)) return;  // the two-pixels-a-lane kernel has the image
     const TileCtx c = tile_ctx(a);
     const bool inside = c.inside;
     const v3 o = inside ? ld3(a.ray_o + 3 * c.pix) : mk3(0.f, 0.f, 0.f);
@@ -1115,6 +1172,7 @@ __global__ void __launch_bounds__(128, 4) raster_bwd_px2_kernel(RasterArgs a) {
     float4* sw = smem4 + wid * (L::kWords * kWarpSlot);  // [kWords][32]
     int32_t* sid = reinterpret_cast<int32_t*>(smem4 + (blockDim.x >> 5) * L::kWords * kWarpSlot) + wid * kWarpSlot;
 
+    if (!px2_chosen(a.px2_stats)) return;  // the per-pixel kernel has the image
     const int tile = a.tile_order ? a.tile_order[blockIdx.x] : int(blockIdx.x);
     const int ty = tile / a.ntx, tx = tile - ty * a.ntx;
     const int wc = a.tsx >> 3;
@@ -1164,6 +1222,8 @@ __global__ void __launch_bounds__(128, 4) raster_bwd_px2_kernel(RasterArgs a) {
     wA = min(wA, end - 1);
     wB = min(wB, end - 1);
     const int32_t kA = wA >= start ? (wA - start) >> 5 : -1, kB = wB >= start ? (wB - start) >> 5 : -1;
+    const int wpt = (a.tsx * a.tsy) >> 5;  // the forward's warps per tile
+
 
     auto process = [&](int t, int32_t gidx) {
         float4 w[L::kWords];
@@ -1280,7 +1340,6 @@ __global__ void __launch_bounds__(128, 4) raster_bwd_px2_kernel(RasterArgs a) {
         }
     };
 
-    const int wpt = (a.tsx * a.tsy) >> 5;  // the forward's warps per tile
     for (int32_t k = max(kA, kB); k >= 0; --k) {
         const uint32_t cm = (k <= kA ? a.masks[mask_index(start, tile, k, wpt, fA)] : 0u) |
                             (k <= kB ? a.masks[mask_index(start, tile, k, wpt, fB)] : 0u);
@@ -1426,13 +1485,20 @@ static int launch_bwd(const RasterArgs& a, int bs, cudaStream_t st, int64_t n_ga
     bool done = false;
     if constexpr (!kDyn && !kRayGrad && CDIM <= 4) {
         // two pixels a lane: needs the masks and an even count of 8 x 4 warp blocks per tile
-        if (a.masks && a.tsx % 8 == 0 && a.tsy % 4 == 0 && ((a.tsx * a.tsy) / 32) % 2 == 0) {
+        if (a.px2_stats) {
             const size_t sm = size_t(bs / 64) * Px2<CDIM>::warp_bytes();
             auto fn = raster_bwd_px2_kernel<CDIM>;
             if (sm > 48 * 1024)
                 XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
+            // and the per-pixel one: the forward's mask counts choose which works
+            RasterArgs b = a;
+            const size_t sm1 = bwd_smem(bs);
+            auto fn1 = raster_bwd_kernel<CDIM, kDyn, kRayGrad>;
+            if (sm1 > 48 * 1024)
+                XSG_CUDA(cudaFuncSetAttribute(fn1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm1)));
             ScopedTimer tm("rasterize_bwd", st);
-            launch(fn, unsigned(a.ntx * a.nty), bs / 2, sm, st, a);
+            launch(fn, unsigned(a.ntx * a.nty), bs / 2, sm, st, b);
+            launch(fn1, unsigned(a.ntx * a.nty), bs, sm1, st, b);
             done = true;
         }
     }
@@ -1441,7 +1507,9 @@ static int launch_bwd(const RasterArgs& a, int bs, cudaStream_t st, int64_t n_ga
         auto fn = raster_bwd_kernel<CDIM, kDyn, kRayGrad>;
         if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
         ScopedTimer tm("rasterize_bwd", st);
-        launch(fn, unsigned(a.ntx * a.nty), bs, sm, st, a);
+        RasterArgs b = a;
+        b.px2_stats = nullptr;
+        launch(fn, unsigned(a.ntx * a.nty), bs, sm, st, b);
     }
     if (a.G && n_gauss > 0)
         launch(grads_finalize_kernel<CDIM, kDyn, kRayGrad>, blocks_for(n_gauss, 256), 256, 0, st, a.G, a.quats,
@@ -1470,9 +1538,22 @@ static int check_common(int64_t n_gauss, int W, int H, int tsx, int tsy, int til
 
 // words of the contributor masks: one per (batch of 32 list entries, warp),
 // tile batch ranges start at (start >> 5) + tile (see mask_index)
-static int64_t mask_words(int64_t n_isects, int64_t n_tiles, int tile_pixels) {
+static int64_t mask_batch_words(int64_t n_isects, int64_t n_tiles, int tile_pixels) {
     if (n_isects <= 0 || n_tiles <= 0 || tile_pixels < 32) return 0;
     return (n_isects / 32 + n_tiles + 2) * (tile_pixels / 32);
+}
+// ... followed by the two 64-bit block-pair counts (px2_stats)
+static int64_t px2_stats_word(int64_t n_isects, int64_t n_tiles, int tile_pixels) {
+    return (mask_batch_words(n_isects, n_tiles, tile_pixels) + 1) & ~int64_t(1);
+}
+static int64_t mask_words(int64_t n_isects, int64_t n_tiles, int tile_pixels) {
+    return mask_batch_words(n_isects, n_tiles, tile_pixels) ? px2_stats_word(n_isects, n_tiles, tile_pixels) + 4 : 0;
+}
+// the block-pair counts exist (and the backward may run two pixels a lane)
+// for static scenes with staged colours, 8 x 4 warp blocks and an even count
+// of them per tile
+static bool px2_layout(int cdim, bool dyn, int tsx, int tsy) {
+    return !dyn && cdim <= 4 && tsx % 8 == 0 && tsy % 4 == 0 && ((tsx * tsy) / 32) % 2 == 0;
 }
 
 }  // namespace xsg
@@ -1529,10 +1610,14 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
         return set_error(XSG_ERR_WORKSPACE, "rasterize_fwd: workspace too small");
     const bool dyn = velocity != nullptr;
     if (dyn) ext = nullptr;  // moving Gaussians: no per-view constants
+    unsigned long long* px2_stats =
+        (masks && px2_layout(cdim, dyn, tsx, tsy))
+            ? reinterpret_cast<unsigned long long*>(masks + px2_stats_word(n_isects, n_tiles, tsx * tsy))
+            : nullptr;
     if (order) launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
     if (n_gauss > 0)
         launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales, opacities,
-               n_gauss, rec, ray_o, ext);
+               n_gauss, rec, ray_o, ext, px2_stats);
     RasterArgs a{};
     a.rec = rec; a.ext = n_gauss > 0 ? ext : nullptr; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
     a.ray_o = ray_o; a.ray_d = ray_d; a.ray_t = ray_time_delta;
@@ -1542,6 +1627,7 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
     a.pair_counters = g_pair_counters;
     a.tile_order = order;
     a.masks = masks;
+    a.px2_stats = px2_stats;
     const int bs = tsx * tsy;
 #define XSG_FWD_CASE(C)                                                             \
     case C:                                                                         \
@@ -1604,7 +1690,7 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
         if (cdim > 4) XSG_CUDA(cudaMemsetAsync(v_colors, 0, size_t(n_gauss) * cdim * sizeof(float), st));
         if (!reuse)
             launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales,
-                   opacities, n_gauss, rec, ray_o, ext);
+                   opacities, n_gauss, rec, ray_o, ext, nullptr);
     }
     RasterArgs a{};
     a.rec = rec; a.ext = n_gauss > 0 ? ext : nullptr; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
@@ -1616,6 +1702,9 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     a.G = G; a.v_colors_direct = v_colors;
     a.tile_order = order;
     a.masks = masks;  // written by the forward into the same workspace
+    a.px2_stats = (masks && px2_layout(cdim, dyn, tsx, tsy))
+                      ? reinterpret_cast<unsigned long long*>(masks + px2_stats_word(n_isects, n_tiles, tsx * tsy))
+                      : nullptr;
     a.v_ray_o = v_ray_o; a.v_ray_d = v_ray_d; a.v_ray_t = v_ray_time_delta;
     const int bs = tsx * tsy;
     FinalizeOut fin{v_means, v_velocity, v_quats, v_scales, v_opacities, v_colors};

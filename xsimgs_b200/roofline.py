@@ -48,9 +48,10 @@ def bwd_flops(n_eval_bwd: int, n_contrib: int, cdim: int, ray_grads: bool = True
     return float(BWD_EVAL * n_eval_bwd + bwd_contrib(cdim, ray_grads) * n_contrib)
 
 
-# DRAM bytes per launch of the compositing backward (no ray gradients, the
-# forward's contributor masks) on the C2 view (1M Gaussians, 1920x1080,
-# 16x16 tiles), dram__bytes_read.sum + dram__bytes_write.sum from one capture:
-#   ncu --set full --clock-control none -k regex:raster_bwd_kernel -s 1 -c 1 \
+# DRAM bytes per launch of the compositing backward (static scene, no ray
+# gradients, two pixels a lane, the forward's contributor masks) on the C2
+# view (1M Gaussians, 1920x1080, 16x16 tiles), dram__bytes_read.sum +
+# dram__bytes_write.sum from one capture:
+#   ncu --set full --clock-control none -k regex:raster_bwd_px2 -s 1 -c 1 \
 #       python bench.py --steps 2 --warmup 1 --no-cpu-baseline --no-lidar
-BWD_DRAM_BYTES_C2 = 265.65e6 + 37.29e6
+BWD_DRAM_BYTES_C2 = 269.33e6 + 35.51e6
