@@ -28,6 +28,12 @@ def test_assign_views_balanced_and_deterministic():
         assign_views(costs, 0)
 
 
+def _plain(t):
+    # a numpy copy pickles by value: a tensor would travel as a file
+    # descriptor its worker must still hold when the parent reads the queue
+    return t.detach().cpu().numpy().copy()
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -102,7 +108,7 @@ def _worker_values(rank, world, port, q, idle=()):
         if rank not in idle:
             ((sh[:, 0, :] * means.sin()).sum() + (means * w).sum() + (quats ** 2).sum() * (rank + 1)).backward()
         assert red.wait() == 3
-        q.put((rank, [t.grad.clone() for t in (means, quats, sh)]))
+        q.put((rank, [_plain(t.grad) for t in (means, quats, sh)]))
         dist.destroy_process_group()
     except Exception as e:
         q.put((rank, repr(e)))
@@ -124,7 +130,7 @@ def test_gradient_allreduce_two_gloo_ranks(target):
     results = {}
     for _ in range(world):
         r, v = q.get(timeout=120)
-        results[r] = v
+        results[r] = v if isinstance(v, str) else [torch.from_numpy(x) for x in v]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -193,7 +199,7 @@ def _worker_mvsh(rank, world, port, q):
         sh.requires_grad_(True)
         cols = multiview_colors(sh, means, origins, 3, k_max=2)
         (cols * d_cols).sum().backward()
-        q.put((rank, (means.grad.clone(), sh.grad.clone())))
+        q.put((rank, (_plain(means.grad), _plain(sh.grad))))
         dist.destroy_process_group()
     except Exception as e:
         q.put((rank, repr(e)))
@@ -209,7 +215,8 @@ def test_multiview_sh_exchange_two_gloo_ranks():
     procs = [ctx.Process(target=_worker_mvsh, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=120) for _ in range(world))
+    res = {r: (v if isinstance(v, str) else [torch.from_numpy(x) for x in v])
+           for r, v in (q.get(timeout=120) for _ in range(world))}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
