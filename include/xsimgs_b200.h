@@ -38,21 +38,26 @@ enum xsg_status {
     XSG_ERR_WORKSPACE = 4,
 };
 
-/* Camera models; the pack layout (float32 words) is
+/* Camera models; the pack layout (float32 words) is the reference's
+ * Camera<Impl> struct (include/cameras/camera.h:67-183) viewed as floats:
  *   [0:4) q0 (w,x,y,z) camera->world rotation   [4:7) t0   [7:10) v   [10:13) w
  *   [13] padding   [14:16) rolling_time   [16] trigger_time   [17] pose_time
- *   [18:...) intrinsics:
- *     PINHOLE   f.x f.y c.x c.y (normalised by image size)         -> 22 words
- *     FISHEYE   f.x f.y c.x c.y k1 k2 k3 k4                         -> 26 words
- *     SPHERICAL phi_min phi_range theta_min theta_range             -> 22 words
- *     LIDAR     the same 4 limits + 2 words holding the 64-bit device
+ *   then the camera impl, aligned as its struct is (16 bytes when it holds a
+ *   float4, so from word 20 with words 18..19 padding):
+ *     PINHOLE   [18:22) f.x f.y c.x c.y (normalised by image size) -> 22 words
+ *     FISHEYE   [20:28) f.x f.y c.x c.y k1 k2 k3 k4                 -> 28 words
+ *     SPHERICAL [18:22) phi_min phi_range theta_min theta_range     -> 22 words
+ *     LIDAR     [18:22) the same 4 limits, [22:24) the 64-bit device
  *               address of the per-row elevation table (beam_v)      -> 24 words
- *     DISTORTED f.x f.y c.x c.y, k1 k2 p1 p2, k3 k4 k5 k6 (OpenCV
- *               rational + tangential model), max_radius^2           -> 31 words
- * Reference: Camera<Impl> (include/cameras/camera.h:67-183) with the impls in
- * csrc/cameras/perspective.cu:7-71, fisheye_opencv.cu:5-188,
- * spherical.h:34-100 and distorted_perspective.cu:6-230.  The lidar address words follow
- * src/xsimgs/cameras/ext/lidar.py:14-19. */
+ *     DISTORTED [20:32) f.x f.y c.x c.y, k1 k2 p1 p2, k3 k4 k5 k6 (OpenCV
+ *               rational + tangential model), [32] max_radius^2,
+ *               [33:36) padding                                      -> 36 words
+ * Padding words are zero.  The impls are in csrc/cameras/perspective.cu:7-71,
+ * fisheye_opencv.cu:5-188, spherical.h:34-100 and
+ * distorted_perspective.cu:6-230; the lidar address words follow
+ * src/xsimgs/cameras/ext/lidar.py:14-19.  (The layout takes the reference's
+ * pytoast quaternion as four floats without extra alignment, which nothing
+ * in the reference pins.) */
 enum xsg_camera_type {
     XSG_CAM_PINHOLE = 0,
     XSG_CAM_FISHEYE = 1,
@@ -61,6 +66,8 @@ enum xsg_camera_type {
     XSG_CAM_DISTORTED = 4,
 };
 int xsg_camera_pack_words(int camera_type);
+/* First word of the camera impl (intrinsics) in the pack: 18 or 20. */
+int xsg_camera_intrinsics_word(int camera_type);
 
 const char* xsg_last_error(void);
 const char* xsg_version(void);
@@ -303,6 +310,10 @@ int xsg_sh_bwd(int degree, const float* origin, const float* positions, const fl
  *     returns XSG_ERR_INVALID_ARGUMENT.
  *   - The first call on a device looks up the array's device address (with
  *     that device current); make that first call before any stream capture.
+ *     `stream` must belong to the current device (else
+ *     XSG_ERR_INVALID_ARGUMENT).  The looked-up address is cached per device
+ *     ordinal for the life of the process and does not survive a
+ *     cudaDeviceReset.
  *   - All calls share the one array: calls that overlap on the GPU (other
  *     streams, other threads) race and must be serialised by the caller.
  *     Each call writes every partial it reads, so no clearing is needed.

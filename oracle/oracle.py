@@ -357,7 +357,10 @@ def interpolate_smpl_bwd(poses, times, inst_ids, query, g_out, n_instances):
     return d_poses, d_root, float(d_q[0])
 
 
-WORDS = {"pinhole": 22, "fisheye": 26, "spherical": 22, "lidar": 24, "distorted": 31}
+# pack words per camera and the first word of its intrinsics (impls holding a
+# float4 start 16-byte aligned, at word 20)
+WORDS = {"pinhole": 22, "fisheye": 28, "spherical": 22, "lidar": 24, "distorted": 36}
+INTR = {"pinhole": 18, "fisheye": 20, "spherical": 18, "lidar": 18, "distorted": 20}
 
 
 def camera_rays_bwd(cam, pack, W, H, d_ray_o, d_ray_d, world_space=True, normalized=True, elev=None):

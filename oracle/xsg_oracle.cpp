@@ -160,13 +160,16 @@ struct Cam {
         k.trigger = p[16];
         k.pose = p[17];
         if (type == CAM_PINHOLE || type == CAM_FISHEYE || type == CAM_DISTORTED) {
-            k.f = {p[18], p[19]};
-            k.c = {p[20], p[21]};
-            if (type == CAM_FISHEYE) k.dist = {p[22], p[23], p[24], p[25]};
+            // impls holding a float4 start at word 20 (16-byte aligned, as in
+            // the reference's Camera<Impl> struct), the others at word 18
+            const float* in = p + ((type == CAM_PINHOLE) ? 18 : 20);
+            k.f = {in[0], in[1]};
+            k.c = {in[2], in[3]};
+            if (type == CAM_FISHEYE) k.dist = {in[4], in[5], in[6], in[7]};
             if (type == CAM_DISTORTED) {
-                k.d0 = {p[22], p[23], p[24], p[25]};
-                k.d1 = {p[26], p[27], p[28], p[29]};
-                k.max_r2 = p[30];
+                k.d0 = {in[4], in[5], in[6], in[7]};
+                k.d1 = {in[8], in[9], in[10], in[11]};
+                k.max_r2 = in[12];
             }
         } else {
             k.phi_min = p[18]; k.phi_range = p[19];
@@ -369,7 +372,8 @@ struct Cam {
         }
         const float x2y2 = p.x * p.x + p.y * p.y;
         const float r = std::sqrt(x2y2 + p.z * p.z);
-        const float phi = std::atan2(-p.x, -p.y) + float(M_PI);
+        // double M_PI, as spherical.h:140 adds it (one rounding from double)
+        const float phi = float(double(std::atan2(-p.x, -p.y)) + M_PI);
         const float theta = std::asin(p.z / r);
         const f2 uv = angles_to_uv(mode, phi, theta);
         uvd = {uv.x, uv.y, r};

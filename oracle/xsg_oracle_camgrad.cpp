@@ -42,8 +42,8 @@ inline D3 qrot(DQ q, D3 p) {
 enum { CAM_PINHOLE = 0, CAM_FISHEYE = 1, CAM_SPHERICAL = 2, CAM_LIDAR = 3, CAM_DISTORTED = 4 };
 
 // OpenCV 8-coefficient distortion D(x) = x scale(r2) + delta(x) in double,
-// with its symmetric Jacobian (distorted_perspective.cu:43-78); k = pack
-// words 22..29 = k1 k2 p1 p2 k3 k4 k5 k6.
+// with its symmetric Jacobian (distorted_perspective.cu:43-78); k = the
+// eight coefficients k1 k2 p1 p2 k3 k4 k5 k6 (pack words 24..31).
 struct DistD {
     double scale, denom, dx, dy, juu, juv, jvv;
     double det() const { return juu * jvv - juv * juv; }
@@ -245,8 +245,12 @@ extern "C" {
 // with respect to the pack; ray_kernels.h:61-123.
 void xsgo_camera_rays_bwd(int type, const float* pack, const float* elev, int W, int H, int world_space,
                           int normalized, const float* d_ray_o, const float* d_ray_d, int words, double* d_pack) {
-    RayGrad k{pack, type, {0.0f, 0.0f, 0.0f, 0.0f}};
-    if (type == CAM_FISHEYE) k.fe = {pack[22], pack[23], pack[24], pack[25]};
+    // RayGrad indexes the intrinsics from word 18; impls holding a float4
+    // start at word 20 in the pack (the reference's struct alignment), so
+    // those read and accumulate two words further on
+    const int shift = (type == CAM_FISHEYE || type == CAM_DISTORTED) ? 2 : 0;
+    RayGrad k{pack + shift, type, {0.0f, 0.0f, 0.0f, 0.0f}};
+    if (type == CAM_FISHEYE) k.fe = {k.p[22], k.p[23], k.p[24], k.p[25]};
     const double qn = std::sqrt(double(pack[0]) * pack[0] + double(pack[1]) * pack[1] + double(pack[2]) * pack[2] +
                                 double(pack[3]) * pack[3]);
     const double sg = pack[0] < 0.0f ? -1.0 : 1.0;
@@ -309,7 +313,7 @@ void xsgo_camera_rays_bwd(int type, const float* pack, const float* elev, int W,
                 dray = dn;
             }
             if (normalized) dray = normalize_bwd(ray, dray);
-            k.impl_bwd(uv, theta, dray, acc);
+            k.impl_bwd(uv, theta, dray, acc + shift);
         }
     }
     for (int j = 0; j < words; ++j) d_pack[j] = 0.0;

@@ -19,7 +19,8 @@ from tests.test_gpu_cameras import KINDS, _specs
 
 pytestmark = pytest.mark.gpu
 
-GROUPS = [(0, 4), (4, 7), (7, 10), (10, 13), (14, 16), (16, 17), (17, 18), (18, 22), (22, 26), (26, 30)]
+GROUPS = [(0, 4), (4, 7), (7, 10), (10, 13), (14, 16), (16, 17), (17, 18), (18, 20), (20, 22), (22, 24),
+          (24, 28), (28, 32), (32, 36)]
 
 
 @pytest.fixture(scope="module")
@@ -53,7 +54,7 @@ def _upstream(H, W, seed, kind=None, pack=None):
     if kind == "fisheye":
         _, rc, valid = O.camera_rays("fisheye", pack, W, H, world_space=False, normalized=True)
         th = np.arccos(np.clip(rc[..., 2].astype(np.float64), -1.0, 1.0))
-        k1, k2, k3, k4 = (float(x) for x in pack[22:26])
+        k1, k2, k3, k4 = (float(x) for x in pack[24:28])
         t2 = th * th
         der = 1 + t2 * (3 * k1 + t2 * (5 * k2 + t2 * (7 * k3 + t2 * 9 * k4)))
         keep = valid & (der > 0.05)
@@ -123,12 +124,20 @@ def test_camera_tensors_receive_gradients(specs, cuda, kind):
             assert ro is None
         loss.backward()
         want = O.camera_rays_bwd(kind, pack, W, H, go if return_origins else None, gd)
+        # the leaves' gradients laid out as pack words: padding words 13 and
+        # (16-byte aligned impls) 18..19 get none, nor does max_radius^2 (32)
+        # or the distorted pack's tail padding (33..35)
+        aligned = kind in ("fisheye", "distorted")
         got = np.concatenate([to_np(t.grad).reshape(-1) for t in leaves[:4]] + [[0.0]] +
-                             [to_np(t.grad).reshape(-1) for t in leaves[4:]] +
-                             ([[0.0]] if kind == "distorted" else []))  # max_radius^2: no gradient
+                             [to_np(t.grad).reshape(-1) for t in leaves[4:7]] +
+                             ([[0.0, 0.0]] if aligned else []) +
+                             [to_np(t.grad).reshape(-1) for t in leaves[7:]] +
+                             ([[0.0] * 4] if kind == "distorted" else []))
         check_pack_grad(got, want, f"{kind} leaves origins={return_origins}")
+        if aligned:
+            assert not want[18:20].any()
         if kind == "distorted":
-            assert want[30] == 0.0
+            assert not want[32:].any()
 
 
 @pytest.mark.parametrize("kind", KINDS)

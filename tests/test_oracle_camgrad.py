@@ -70,16 +70,17 @@ def _base(words, w=(0.01, -0.02, 0.3), q0=(0.9, 0.1, -0.3, 0.2)):
 
 def camera_pack(kind, w=(0.01, -0.02, 0.3), q0=(0.9, 0.1, -0.3, 0.2)):
     p = _base(O.WORDS[kind], w, q0)
+    i = O.INTR[kind]
     if kind in ("pinhole", "fisheye", "distorted"):
-        p[18:22] = (0.45, 0.6, 0.52, 0.47)
+        p[i:i + 4] = (0.45, 0.6, 0.52, 0.47)
         if kind == "fisheye":
-            p[22:26] = (0.03, -0.02, 0.01, -0.004)
+            p[i + 4:i + 8] = (0.03, -0.02, 0.01, -0.004)
         if kind == "distorted":
-            p[18:20] = (0.9, 1.2)  # the image stays inside the model's monotone range
-            p[22:30] = DIST8
-            p[30] = 4.0
+            p[i:i + 2] = (0.9, 1.2)  # the image stays inside the model's monotone range
+            p[i + 4:i + 12] = DIST8
+            p[i + 12] = 4.0
     else:
-        p[18:22] = (0.1, 6.0, -0.4, 0.9)  # phi_min, phi_range, theta_min, theta_range
+        p[i:i + 4] = (0.1, 6.0, -0.4, 0.9)  # phi_min, phi_range, theta_min, theta_range
     return p
 
 
@@ -140,20 +141,21 @@ def _qmul(a, b):
 def torch_rays(kind, pk, W, H, world, normalized, elev=None):
     U, V = _grid_uv(kind, W, H, elev)
     Ut, Vt = torch.tensor(U, dtype=torch.float64), torch.tensor(V, dtype=torch.float64)
+    i = O.INTR[kind]
     if kind in ("pinhole", "fisheye", "distorted"):
-        ux, uy = (Ut - pk[20]) / pk[18], (Vt - pk[21]) / pk[19]
+        ux, uy = (Ut - pk[i + 2]) / pk[i], (Vt - pk[i + 3]) / pk[i + 1]
         if kind == "pinhole":
             ray = torch.stack([ux, uy, torch.ones_like(ux)], -1)
         elif kind == "distorted":
-            x, y = undistort_t(ux, uy, pk[22:30])
+            x, y = undistort_t(ux, uy, pk[i + 4:i + 12])
             ray = torch.stack([x, y, torch.ones_like(x)], -1)
         else:
-            k = pk[22:26]
+            k = pk[i + 4:i + 8]
             p32 = pk.detach().numpy().astype(np.float32)
-            uxf = (U - p32[20]) / p32[18]
-            uyf = (V - p32[21]) / p32[19]
+            uxf = (U - p32[i + 2]) / p32[i]
+            uyf = (V - p32[i + 3]) / p32[i + 1]
             dlf = np.sqrt(uxf * uxf + uyf * uyf)
-            thf, resf, derf = _fe_solve_f32(dlf, p32[22:26])
+            thf, resf, derf = _fe_solve_f32(dlf, p32[i + 4:i + 8])
             valid = (thf > 0) & (dlf > 1e-8) & (np.abs(resf) < 1e-5) & (derf > 1e-3)
             assert valid.all(), "test camera must converge everywhere"
             delta = torch.sqrt(ux * ux + uy * uy)
@@ -170,7 +172,7 @@ def torch_rays(kind, pk, W, H, world, normalized, elev=None):
             s = torch.sin(th) / delta
             ray = torch.stack([s * ux, s * uy, torch.cos(th)], -1)
     else:
-        lim = pk[18:22].detach()
+        lim = pk[i:i + 4].detach()
         az, el = lim[0] + Ut * lim[1], lim[2] + Vt * lim[3]
         ray = torch.stack([torch.cos(el) * torch.sin(az), torch.cos(el) * torch.cos(az), torch.sin(el)], -1)
     nray = ray / ray.norm(dim=-1, keepdim=True) if normalized else ray
@@ -198,8 +200,8 @@ def _elev(H):
 
 def _check(got, want, what):
     """Per camera tensor: |got - want| <= 1e-6 * (|want| + max|want| of the tensor)."""
-    groups = [(0, 4), (4, 7), (7, 10), (10, 13), (13, 14), (14, 16), (16, 17), (17, 18), (18, 22), (22, 26),
-              (26, 30), (30, 31)]
+    groups = [(0, 4), (4, 7), (7, 10), (10, 13), (13, 14), (14, 16), (16, 17), (17, 18), (18, 20), (20, 22),
+              (22, 24), (24, 28), (28, 32), (32, 33), (33, 36)]
     for a, b in groups:
         if a >= len(want):
             break
@@ -230,6 +232,8 @@ def test_oracle_ray_backward_is_autograd(kind, world, normalized):
     assert got[13] == 0.0
     if kind in ("spherical", "lidar"):
         assert not got[18:].any()
+    if kind in ("fisheye", "distorted"):
+        assert not got[18:20].any()  # padding before the 16-byte aligned impl
 
 
 @pytest.mark.parametrize("w", [(0.0, 0.0, 0.0), (0.01, -0.02, 0.05), (2.0, -1.0, 9.0)])

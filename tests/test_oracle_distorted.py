@@ -34,9 +34,9 @@ def test_rays_invert_the_distortion():
     assert valid.all()
     np.testing.assert_array_equal(rd[..., 2], 1.0)
     U, V = _grid(W, H, pack)
-    xd, yd = distort_np(rd[..., 0].astype(np.float64), rd[..., 1].astype(np.float64), pack[22:30])
-    np.testing.assert_allclose(xd * pack[18] + pack[20], U, atol=2e-6)
-    np.testing.assert_allclose(yd * pack[19] + pack[21], V, atol=2e-6)
+    xd, yd = distort_np(rd[..., 0].astype(np.float64), rd[..., 1].astype(np.float64), pack[24:32])
+    np.testing.assert_allclose(xd * pack[20] + pack[22], U, atol=2e-6)
+    np.testing.assert_allclose(yd * pack[21] + pack[23], V, atol=2e-6)
 
 
 def test_projection_round_trip():
@@ -65,15 +65,15 @@ def test_trusted_radius():
     pack = camera_pack("distorted")
     _, rc, valid = O.camera_rays("distorted", pack, W, H, world_space=False, normalized=False)
     r2 = (rc[..., :2].astype(np.float64) ** 2).sum(-1)
-    pack[30] = np.float32(np.median(r2))
+    pack[32] = np.float32(np.median(r2))
     _, _, valid = O.camera_rays("distorted", pack, W, H, world_space=False, normalized=False)
-    np.testing.assert_array_equal(valid, r2 <= pack[30])
+    np.testing.assert_array_equal(valid, r2 <= pack[32])
     pts = np.concatenate([rc.reshape(-1, 3) * 5.0], 0).astype(np.float32)
     pack[0:4] = (1, 0, 0, 0)
     pack[4:13] = 0.0
     pack[14:16] = 0.0
     uvdt, mask = O.projection("distorted", pack, pts)
-    np.testing.assert_array_equal(mask, (r2 <= pack[30]).reshape(-1))
+    np.testing.assert_array_equal(mask, (r2 <= pack[32]).reshape(-1))
 
 
 @pytest.mark.parametrize("normalized_range", [False, True])
@@ -82,8 +82,8 @@ def test_undistort_map_is_the_distorted_grid(normalized_range):
     pack = camera_pack("distorted")
     got = O.undistort_map(pack, W, H, normalized_range)
     U, V = _grid(W, H, pack)
-    xd, yd = distort_np((U - pack[20]) / pack[18], (V - pack[21]) / pack[19], pack[22:30])
-    want = np.stack([xd * pack[18] + pack[20], yd * pack[19] + pack[21]], -1)
+    xd, yd = distort_np((U - pack[22]) / pack[20], (V - pack[23]) / pack[21], pack[24:32])
+    want = np.stack([xd * pack[20] + pack[22], yd * pack[21] + pack[23]], -1)
     if not normalized_range:
         want = want * 2 - 1
     np.testing.assert_allclose(got, want, atol=3e-6)

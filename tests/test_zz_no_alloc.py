@@ -4,9 +4,12 @@ Some callers of this library cannot allocate device memory: a host runtime
 that only lends the library the buffers it already owns, or code that must
 not call cudaMalloc on its hot path.  For them the library keeps its scratch
 (per-block partial sums of the origin gradient) in a fixed device array.
-This test calls that entry point through the C ABI twice in a row and checks
-each result against the regular xsg_sh_bwd, which takes a caller workspace.
-The second call is smaller than the first, so anything it read from the first
+This test calls that entry point through the C ABI several times in a row
+and checks each result against the regular xsg_sh_bwd, which takes a caller
+workspace.  Both run the same kernels with the same block partition and the
+same summation order, so every output must agree bit for bit.  Later calls
+are smaller than the first (fewer blocks, a size that is not a multiple of
+the block), one with a Gaussian mask, so anything a call read from an earlier
 call's leftovers would show up as a wrong origin gradient.
 
 It lives in its own file named to be collected last, so a run that stops at
@@ -18,7 +21,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.helpers import assert_grads_close, to_np
+from tests.helpers import to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -34,16 +37,22 @@ def _lib():
     return lib
 
 
-def _case(seed, n, degree, dev):
+def _case(seed, n, degree, dev, masked=False):
     rng = np.random.default_rng(seed)
     k = (degree + 1) ** 2
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+    mask = None
+    if masked:
+        bits = np.packbits(rng.random(n) < 0.7, bitorder="little")
+        bits = np.concatenate([bits, np.zeros((-len(bits)) % 4, np.uint8)])
+        mask = torch.from_numpy(bits.view(np.uint32).astype(np.int64).astype(np.int32)).to(dev)
     return dict(pos=t(rng.normal(size=(n, 3)) * 10), origin=t([0.3, -0.7, 1.1]),
-                coeffs=t(rng.normal(size=(n, k, 3))), d_out=t(rng.normal(size=(n, 3))), n=n, k=k, degree=degree)
+                coeffs=t(rng.normal(size=(n, k, 3))), d_out=t(rng.normal(size=(n, 3))), n=n, k=k, degree=degree,
+                mask=mask)
 
 
 def _outputs(c):
-    return (torch.empty_like(c["coeffs"]), torch.empty_like(c["pos"]), torch.empty(3, device=c["pos"].device))
+    return (torch.zeros_like(c["coeffs"]), torch.zeros_like(c["pos"]), torch.zeros(3, device=c["pos"].device))
 
 
 def _ptr(t):
@@ -53,7 +62,8 @@ def _ptr(t):
 def _run(lib, c, noalloc):
     d_coeffs, d_pos, d_origin = _outputs(c)
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    args = [c["degree"], _ptr(c["origin"]), _ptr(c["pos"]), _ptr(c["coeffs"]), None, None, 0, c["n"], c["k"],
+    mask = _ptr(c["mask"]) if c["mask"] is not None else None
+    args = [c["degree"], _ptr(c["origin"]), _ptr(c["pos"]), _ptr(c["coeffs"]), None, mask, 0, c["n"], c["k"],
             _ptr(c["d_out"]), _ptr(d_coeffs), None, _ptr(d_pos), _ptr(d_origin)]
     if noalloc:
         rc = lib.xsg_sh_bwd_noalloc(*args, stream)
@@ -68,15 +78,15 @@ def _run(lib, c, noalloc):
 
 def test_sh_backward_without_allocation_matches_workspace_version(cuda):
     lib = _lib()
-    first = _case(1, 300_000, 3, cuda)
-    second = _case(2, 70_001, 2, cuda)  # fewer blocks than the first call
-    for c in (first, second):
+    cases = [_case(1, 300_000, 3, cuda),                # many blocks
+             _case(2, 70_001, 2, cuda),                 # fewer blocks, ragged last block
+             _case(3, 12_345, 3, cuda, masked=True),    # fewer still, masked Gaussians
+             _case(4, 300_000, 1, cuda, masked=True)]   # back to many blocks
+    for c in cases:
         got = _run(lib, c, noalloc=True)
         ref = _run(lib, c, noalloc=False)
-        np.testing.assert_allclose(to_np(got[0]), to_np(ref[0]), atol=1e-5, rtol=1e-5)
-        assert_grads_close(got[1], ref[1], "d_positions")
-        scale = float(to_np(ref[1]).__abs__().sum())
-        np.testing.assert_allclose(to_np(got[2]), to_np(ref[2]), rtol=1e-3, atol=1e-3 * scale)
+        for name, a, b in zip(("d_coeffs", "d_positions", "d_origin"), got, ref):
+            np.testing.assert_array_equal(to_np(a), to_np(b), err_msg=f"{name} (n={c['n']})")
 
 
 def test_sh_backward_without_allocation_rejects_oversize(cuda):

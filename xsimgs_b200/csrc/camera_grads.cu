@@ -18,7 +18,7 @@ namespace xsg {
 constexpr int kGradThreads = 256;
 constexpr int kGradWarps = kGradThreads / 32;
 constexpr int kGradMaxBlocks = 4 * 148;
-constexpr int kGradStride = 32;  // floats per partial row (>= every pack)
+constexpr int kGradStride = 48;  // floats per partial row (>= every pack, 36 words at most)
 
 // Reduce the CTA's per-thread accumulators (pack words [off, off + P)) to one
 // partial row; words outside that range are written as zero.

@@ -75,14 +75,14 @@ struct Pinhole : CamBase {
 struct Fisheye : CamBase {
     static constexpr int kType = XSG_CAM_FISHEYE;
     static constexpr bool kJacobian = false;
-    static constexpr int kWords = 26;
+    static constexpr int kWords = 28;
     float2 f, c;
     float4 k;
     __device__ __forceinline__ void load(const float* p) {
         load_base(p);
-        f = make_float2(p[18], p[19]);
-        c = make_float2(p[20], p[21]);
-        k = make_float4(p[22], p[23], p[24], p[25]);
+        f = make_float2(p[20], p[21]);
+        c = make_float2(p[22], p[23]);
+        k = make_float4(p[24], p[25], p[26], p[27]);
     }
     __device__ __forceinline__ float2 pixel_to_uv(int px, int py, int W, int H) const {
         return make_float2((float(px) + 0.5f) / float(W), (float(py) + 0.5f) / float(H));
@@ -135,7 +135,7 @@ struct Fisheye : CamBase {
         const float th = solve(delta, res);
         return (fabsf(res) < 1e-5f) && (distort_deriv(th) > 0.0f);
     }
-    // Backward of ray_cs into f, c (words 18..21) and k1..k4 (22..25),
+    // Backward of ray_cs into f, c (words 20..23) and k1..k4 (24..27),
     // fisheye_opencv.cu:77-141.  theta(delta, k) is implicit in
     // distort(theta) = delta, so dtheta/ddelta = 1/distort' and
     // dtheta/dk_i = -theta^(2i+3)/distort'; rays whose re-solve did not
@@ -156,17 +156,17 @@ struct Fisheye : CamBase {
         const float d_th = d_s * cs * idl - d.z * sn;
         const float d_ths = d_th / der;
         const float t2 = th * th, t3 = t2 * th;
-        acc[22] -= d_ths * t3;
-        acc[23] -= d_ths * t3 * t2;
-        acc[24] -= d_ths * t3 * t2 * t2;
-        acc[25] -= d_ths * t3 * t2 * t2 * t2;
+        acc[24] -= d_ths * t3;
+        acc[25] -= d_ths * t3 * t2;
+        acc[26] -= d_ths * t3 * t2 * t2;
+        acc[27] -= d_ths * t3 * t2 * t2 * t2;
         const float d_dl = -d_s * sn * idl * idl + d_ths;
         const float dux = s * d.x + d_dl * ux * idl;
         const float duy = s * d.y + d_dl * uy * idl;
-        acc[18] -= dux * ux / f.x;
-        acc[19] -= duy * uy / f.y;
-        acc[20] -= dux / f.x;
-        acc[21] -= duy / f.y;
+        acc[20] -= dux * ux / f.x;
+        acc[21] -= duy * uy / f.y;
+        acc[22] -= dux / f.x;
+        acc[23] -= duy / f.y;
     }
     __device__ __forceinline__ v3 to_uvd(int, v3 p) const {
         const float norm = fmaxf(1e-6f, hypotf(p.x, p.y));
@@ -188,18 +188,18 @@ struct Fisheye : CamBase {
 struct Distorted : CamBase {
     static constexpr int kType = XSG_CAM_DISTORTED;
     static constexpr bool kJacobian = false;
-    static constexpr int kWords = 31;
+    static constexpr int kWords = 36;
     static constexpr float kMinDet = 1e-3f;
     float2 f, c;
     float4 d0, d1;  // (k1, k2, p1, p2), (k3, k4, k5, k6)
     float max_r2;
     __device__ __forceinline__ void load(const float* p) {
         load_base(p);
-        f = make_float2(p[18], p[19]);
-        c = make_float2(p[20], p[21]);
-        d0 = make_float4(p[22], p[23], p[24], p[25]);
-        d1 = make_float4(p[26], p[27], p[28], p[29]);
-        max_r2 = p[30];
+        f = make_float2(p[20], p[21]);
+        c = make_float2(p[22], p[23]);
+        d0 = make_float4(p[24], p[25], p[26], p[27]);
+        d1 = make_float4(p[28], p[29], p[30], p[31]);
+        max_r2 = p[32];
     }
     __device__ __forceinline__ float2 pixel_to_uv(int px, int py, int W, int H) const {
         return make_float2((float(px) + 0.5f) / float(W), (float(py) + 0.5f) / float(H));
@@ -280,21 +280,21 @@ struct Distorted : CamBase {
             gx = (st.jvv * d.x - st.juv * d.y) / det;
             gy = (st.juu * d.y - st.juv * d.x) / det;
         }
-        acc[18] -= gx * xd.x * ifx;
-        acc[19] -= gy * xd.y * ify;
-        acc[20] -= gx * ifx;
-        acc[21] -= gy * ify;
+        acc[20] -= gx * xd.x * ifx;
+        acc[21] -= gy * xd.y * ify;
+        acc[22] -= gx * ifx;
+        acc[23] -= gy * ify;
         const float r2 = x.x * x.x + x.y * x.y, r4 = r2 * r2, r6 = r4 * r2;
         const float rad = -(gx * x.x + gy * x.y) / st.denom;
         const float rad_den = -rad * st.scale;
-        acc[22] += rad * r2;
-        acc[23] += rad * r4;
-        acc[24] -= gx * 2.0f * x.x * x.y + gy * (r2 + 2.0f * x.y * x.y);
-        acc[25] -= gx * (r2 + 2.0f * x.x * x.x) + gy * 2.0f * x.x * x.y;
-        acc[26] += rad * r6;
-        acc[27] += rad_den * r2;
-        acc[28] += rad_den * r4;
-        acc[29] += rad_den * r6;
+        acc[24] += rad * r2;
+        acc[25] += rad * r4;
+        acc[26] -= gx * 2.0f * x.x * x.y + gy * (r2 + 2.0f * x.y * x.y);
+        acc[27] -= gx * (r2 + 2.0f * x.x * x.x) + gy * 2.0f * x.x * x.y;
+        acc[28] += rad * r6;
+        acc[29] += rad_den * r2;
+        acc[30] += rad_den * r4;
+        acc[31] += rad_den * r6;
     }
     // uv_distortion (distortion.h:8-30) applied to x.
     __device__ __forceinline__ float2 distort(float2 x) const {
@@ -381,7 +381,10 @@ struct Spherical : CamBase {
     __device__ __forceinline__ void to_uvd_jac(int mode, v3 p, v3 dp, v3& uvd, float2& duv) const {
         const float x2y2 = p.x * p.x + p.y * p.y;
         const float r = sqrtf(x2y2 + p.z * p.z);
-        const float phi = atan2f(-p.x, -p.y) + float(M_PI);
+        // the reference adds the double constant M_PI here (spherical.h:140),
+        // so the sum is rounded once from double (cartesian_to_spherical,
+        // used by to_uvd above, adds float(M_PI))
+        const float phi = float(double(atan2f(-p.x, -p.y)) + M_PI);
         const float th = asinf(p.z / r);
         const float2 uv = angles_to_uv(mode, phi, th);
         uvd = mk3(uv.x, uv.y, r);
@@ -465,7 +468,14 @@ __device__ __forceinline__ void project_point(const Cam& k, v3 P, v3 Pv, float t
         // does not depend on the capture time, so every Newton step below
         // projects the same point and has d residual / d t = 1.  Project
         // once and iterate only the time update (same checks, same result).
-        uvd = k.to_uvd(mode, quat_rotate(k.qw, mk3(-k.qx, -k.qy, -k.qz), P - k.t0));
+        // the camera's Jacobian projection where the reference iterates
+        // with it (its uvd can differ in the last bit from to_uvd's)
+        if constexpr (kUseJac && Cam::kJacobian) {
+            float2 duv;
+            k.to_uvd_jac(mode, quat_rotate(k.qw, mk3(-k.qx, -k.qy, -k.qz), P - k.t0), mk3(0.f, 0.f, 0.f), uvd, duv);
+        } else {
+            uvd = k.to_uvd(mode, quat_rotate(k.qw, mk3(-k.qx, -k.qy, -k.qz), P - k.t0));
+        }
         if ((uvd.z <= 0.0f) || (uvd.x < -margin) || (uvd.x > 1.0f + margin) || (uvd.y < -margin) ||
             (uvd.y > 1.0f + margin)) {
             valid = false;

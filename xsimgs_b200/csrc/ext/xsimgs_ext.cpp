@@ -88,8 +88,15 @@ Tensor camera_pack(const CameraSpec& spec, const std::vector<Tensor>& tensors) {
         TORCH_CHECK(t.device() == tensors[0].device(), "Camera tensors must be on the same device");
         parts.push_back(t.reshape({want}));
         if (i == 3) parts.push_back(at::zeros({1}, t.options()));  // padding word 13
+        // the intrinsics start where the reference's Camera<Impl> struct puts
+        // them: word 20 for impls holding a float4 (16-byte aligned)
+        if (i + 1 == kBaseDims.size() && xsg_camera_intrinsics_word(spec.type) > 18)
+            parts.push_back(at::zeros({xsg_camera_intrinsics_word(spec.type) - 18}, t.options()));
     }
-    return at::cat(parts).view({1, -1});
+    Tensor pack = at::cat(parts);
+    const int64_t words = xsg_camera_pack_words(spec.type);
+    if (pack.numel() < words) pack = at::cat({pack, at::zeros({words - pack.numel()}, pack.options())});
+    return pack.view({1, -1});
 }
 
 void validate_pack(const CameraSpec& spec, const Tensor& pack) {

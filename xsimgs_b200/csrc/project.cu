@@ -165,11 +165,22 @@ extern "C" {
 
 int xsg_camera_pack_words(int type) {
     switch (type) {
-        case XSG_CAM_PINHOLE: return 22;
-        case XSG_CAM_FISHEYE: return 26;
-        case XSG_CAM_SPHERICAL: return 22;
-        case XSG_CAM_LIDAR: return 24;
-        case XSG_CAM_DISTORTED: return 31;
+        case XSG_CAM_PINHOLE: return Pinhole::kWords;
+        case XSG_CAM_FISHEYE: return Fisheye::kWords;
+        case XSG_CAM_SPHERICAL: return Spherical<false>::kWords;
+        case XSG_CAM_LIDAR: return Spherical<true>::kWords;
+        case XSG_CAM_DISTORTED: return Distorted::kWords;
+        default: return -1;
+    }
+}
+
+int xsg_camera_intrinsics_word(int type) {
+    switch (type) {
+        case XSG_CAM_FISHEYE:
+        case XSG_CAM_DISTORTED: return 20;
+        case XSG_CAM_PINHOLE:
+        case XSG_CAM_SPHERICAL:
+        case XSG_CAM_LIDAR: return 18;
         default: return -1;
     }
 }

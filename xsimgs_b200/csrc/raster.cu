@@ -214,14 +214,22 @@ __device__ __forceinline__ TileCtx tile_ctx(const RasterArgs& a) {
 // The alpha of a (ray, Gaussian) pair (eval3d_fwd.cu:111-124: grd = M d,
 // gn = grd / |grd|, gc = gn x gro with gro = M (o - mu), power = -|gc|^2 / 2)
 // as a fixed sequence of explicitly rounded products and FMAs, nothing left
-// to the compiler's contraction.  The forward evaluates two list entries at a
-// time with the paired FP32 instructions of sm_100 (fma / mul .f32x2, one
-// entry per half) and the backward one entry at a time with the scalar form;
-// both get bit-identical alpha and so take the same alpha >= 1/255 decisions.
+// to the compiler's contraction.  The sequence is the one the reference's
+// own kernel gets from nvcc (-O3, FMA contraction on) for the same
+// expressions, established by comparing bit patterns of alpha and t* over a
+// million pairs: a 3-term sum of products x0 y0 + x1 y1 + x2 y2 (glm::dot,
+// the rows of mat3 * vec3) is fma(x2, y2, fma(x0, y0, x1 y1)) and a cross
+// component a b - c d is fma(a, b, -(c d)); t* = -(gro . grd) / (grd . grd)
+// is a correctly rounded division.  So the compositing forward returns the
+// reference's images bit for bit on the same tile lists.  The forward
+// evaluates two list entries at a time with the paired FP32 instructions of
+// sm_100 (fma / mul .f32x2, one entry per half) and the backward one entry at
+// a time with the scalar form; both get bit-identical alpha and so take the
+// same alpha >= 1/255 decisions.
 __device__ __forceinline__ float fx_dot(v3 a, v3 b) {
-    return __fmaf_rn(a.z, b.z, __fmaf_rn(a.y, b.y, __fmul_rn(a.x, b.x)));
+    return __fmaf_rn(a.z, b.z, __fmaf_rn(a.x, b.x, __fmul_rn(a.y, b.y)));
 }
-// M v with M rows (r0,r1,r2).xyz, in glm's mat3 * vec3 order
+// M v with M rows (r0,r1,r2).xyz (glm's mat3 * vec3, contracted as fx_dot)
 __device__ __forceinline__ v3 fx_mrows(float4 r0, float4 r1, float4 r2, v3 v) {
     return mk3(fx_dot(mk3(r0.x, r0.y, r0.z), v), fx_dot(mk3(r1.x, r1.y, r1.z), v),
                fx_dot(mk3(r2.x, r2.y, r2.z), v));
@@ -257,7 +265,7 @@ struct p3 {
 __device__ __forceinline__ float2 pdup(float v) { return make_float2(v, v); }
 __device__ __forceinline__ float2 pneg(float2 a) { return make_float2(-a.x, -a.y); }
 __device__ __forceinline__ float2 pdot(p3 a, p3 b) {
-    return __ffma2_rn(a.z, b.z, __ffma2_rn(a.y, b.y, __fmul2_rn(a.x, b.x)));
+    return __ffma2_rn(a.z, b.z, __ffma2_rn(a.x, b.x, __fmul2_rn(a.y, b.y)));
 }
 __device__ __forceinline__ p3 pcross(p3 a, p3 b) {
     return {__ffma2_rn(a.y, b.z, pneg(__fmul2_rn(b.y, a.z))), __ffma2_rn(a.z, b.x, pneg(__fmul2_rn(b.z, a.x))),
@@ -613,7 +621,7 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
         auto composite = [&](float ov, float od, float l, int t, const float (&col)[4]) -> bool {
             const float alpha = fminf(0.999f, ov);
             if (alpha < 1.f / 255.f) return false;
-            const float hit_t = __fdividef(-od, l);
+            const float hit_t = __fdiv_rn(-od, l);
             const float nT = T * (1.0f - alpha);
             if (nT <= 1e-4f) {
                 done = true;

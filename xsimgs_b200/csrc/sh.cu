@@ -300,10 +300,19 @@ static __device__ __align__(256) float g_sh_noalloc_partials[kShNoAllocMaxBlocks
 static std::mutex g_noalloc_mu;
 static float* g_noalloc_ptr[64] = {nullptr};
 
-static int sh_noalloc_scratch(float** out) {
+// The kernels run on the caller's stream, so the array must be the one on
+// that stream's device: a stream of another device is rejected rather than
+// handed this device's address.
+static int sh_noalloc_scratch(cudaStream_t stream, float** out) {
     int dev = -1;
     XSG_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(XSG_ERR_UNSUPPORTED, "spherical_harmonics_bwd_noalloc: device ordinal out of range");
+    int stream_dev = dev;
+    XSG_CUDA(cudaStreamGetDevice(stream, &stream_dev));
+    if (stream_dev != dev)
+        return set_error(XSG_ERR_INVALID_ARGUMENT,
+                         "spherical_harmonics_bwd_noalloc: the stream belongs to device " + std::to_string(stream_dev) +
+                             " but device " + std::to_string(dev) + " is current");
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (!g_noalloc_ptr[dev]) {
         void* p = nullptr;
@@ -341,7 +350,7 @@ int xsg_sh_bwd_noalloc(int degree, const float* origin, const float* pos, const 
     XSG_REQUIRE(origin && pos && d_out && d_coeffs && d_pos && (!dc || d_dc),
                 "spherical_harmonics_bwd_noalloc: null argument");
     float* part = nullptr;
-    rc = sh_noalloc_scratch(&part);
+    rc = sh_noalloc_scratch(st, &part);
     if (rc != XSG_OK) return rc;
     // every block writes its own partial before the final sum reads it, so
     // nothing left from an earlier call is read and nothing needs clearing
