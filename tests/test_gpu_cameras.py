@@ -20,6 +20,8 @@ from tests.helpers import assert_grads_close, assert_images_close, camera_inputs
 
 pytestmark = pytest.mark.gpu
 
+DEPTH_ATOL_CPU = 2e-4
+
 EYE = (0.0, 0.0, 1.6)
 
 
@@ -283,7 +285,11 @@ def test_composite_fwd_bwd_per_camera(specs, shell, cuda, kind, dynamic):
     rrgb, rdep, ralpha, rlast, near = O.rasterize_fwd(*np_in, **dyn_kw)
     assert float(to_np(alpha).mean()) > 0.05, "too little coverage for a meaningful check"
     assert_images_close(rgb, rrgb, near, what="rgb")
-    assert_images_close(depth, rdep, near, atol=1e-4 * max(1.0, float(np.abs(rdep).max())), what="depth")
+    # absolute, not relative: the CPU restatement rounds every product on its
+    # own (no FMA), which puts it up to ~5 ulps of a 30 m depth away from the
+    # reference's GPU kernels; against those kernels this package's depth is
+    # bit-exact (test_gpu_ref_parity.py)
+    assert_images_close(depth, rdep, near, atol=DEPTH_ATOL_CPU, what="depth")
     assert_images_close(alpha, ralpha, near, what="alpha")
     np.testing.assert_array_equal(to_np(last)[~near], rlast[~near])
 
