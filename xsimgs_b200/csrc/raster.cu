@@ -220,7 +220,9 @@ __device__ __forceinline__ TileCtx tile_ctx(const RasterArgs& a) {
 // million pairs: a 3-term sum of products x0 y0 + x1 y1 + x2 y2 (glm::dot,
 // the rows of mat3 * vec3) is fma(x2, y2, fma(x0, y0, x1 y1)) and a cross
 // component a b - c d is fma(a, b, -(c d)); t* = -(gro . grd) / (grd . grd)
-// is a correctly rounded division.  So the compositing forward returns the
+// is the reference's correctly rounded division, computed as a
+// Newton-corrected quotient (div_nr) that gave the same bits on every pair of
+// the full-size test views.  So the compositing forward returns the
 // reference's images bit for bit on the same tile lists.  The forward
 // evaluates two list entries at a time with the paired FP32 instructions of
 // sm_100 (fma / mul .f32x2, one entry per half) and the backward one entry at
@@ -260,9 +262,9 @@ __device__ __forceinline__ EvalTerms fx_eval(float4 r0, float4 r1, float4 r2, v3
 
 // a / b to within about half an ulp (nearly always the correctly rounded
 // quotient): the approximate reciprocal, then one Newton correction of the
-// quotient (Markstein).  The backward's replay of T and its t* use it: far
-// closer to the forward's and the reference's IEEE division than the
-// approximate quotient, at two FMAs more.
+// quotient (Markstein).  The forward's t* and the backward's replay of T use
+// it: it matches the reference's IEEE division where the approximate
+// quotient does not, at two FMAs more and well below the cost of div.rn.
 __device__ __forceinline__ float div_nr(float a, float b) {
     const float r = __fdividef(1.0f, b);
     const float q = __fmul_rn(a, r);
@@ -632,7 +634,7 @@ __global__ void __launch_bounds__(256, 4) raster_fwd_kernel(RasterArgs a) {
         auto composite = [&](float ov, float od, float l, int t, const float (&col)[4]) -> bool {
             const float alpha = fminf(0.999f, ov);
             if (alpha < 1.f / 255.f) return false;
-            const float hit_t = __fdiv_rn(-od, l);
+            const float hit_t = div_nr(-od, l);
             const float nT = T * (1.0f - alpha);
             if (nT <= 1e-4f) {
                 done = true;
