@@ -231,3 +231,77 @@ def test_multiview_sh_exchange_two_gloo_ranks():
     want_sh = coeff_bwd(3, torch.cat(all_o), means, torch.cat(all_d), 16)
     for r in range(world):
         torch.testing.assert_close(res[r][1], want_sh, rtol=1e-5, atol=1e-5)
+
+
+def _worker_mvsh_gated(rank, world, port, q):
+    """The render step's two exchanges together on one group: the geometry
+    all-reduces (GradientAllReduce, gated) and MultiViewSH's all-gathers,
+    with different view counts (so different autograd graphs) per rank."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        from datetime import timedelta
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        from xsimgs_b200._native import _C
+        from xsimgs_b200.multiview import multiview_colors
+        _C.spherical_harmonics_fused_fwd, _C.spherical_harmonics_positions_bwd, \
+            _C.spherical_harmonics_coeffs_bwd_multi = _torch_ops()
+        means, sh, origins, d_cols = _mvsh_setup(rank)
+        g = torch.Generator().manual_seed(7)
+        quats = torch.randn(40, 4, generator=g)
+        w_q, w_m = _gated_weights(rank)
+        for t in (means, sh, quats):
+            t.requires_grad_(True)
+        red = GradientAllReduce([quats, means], gated=True)
+        for _ in range(2):  # hooks registered once, two passes
+            for t in (means, sh, quats):
+                t.grad = None
+            cols = multiview_colors(sh, means, origins, 3, k_max=2, reducer=red)
+            # "compositing": quats and means feed it as well as the colours
+            loss = (cols * d_cols).sum() + (quats * w_q).sum() + (means * w_m).sum()
+            loss.backward()
+            assert red.wait() == 2
+        q.put((rank, (_plain(means.grad), _plain(sh.grad), _plain(quats.grad))))
+        red.remove()
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def _gated_weights(rank):
+    g = torch.Generator().manual_seed(70 + rank)
+    return torch.randn(40, 4, generator=g), torch.randn(40, 3, generator=g)
+
+
+def test_gated_allreduce_with_multiview_exchange_two_gloo_ranks():
+    """Every rank ends with the sum over ranks of the geometry gradients and
+    the SH gradient of every view of every rank, uneven view counts."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_mvsh_gated, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {r: (v if isinstance(v, str) else [torch.from_numpy(x) for x in v])
+           for r, v in (q.get(timeout=120) for _ in range(world))}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(not isinstance(v, str) for v in res.values()), res
+    fwd, pos_bwd, coeff_bwd = _torch_ops()
+    all_o, all_d = [], []
+    want_m = 0
+    want_q = 0
+    for r in range(world):
+        means, sh, origins, d_cols = _mvsh_setup(r)
+        all_o.append(origins)
+        all_d.append(d_cols)
+        w_q, w_m = _gated_weights(r)
+        want_m = want_m + pos_bwd(3, origins, means, sh, d_cols) + w_m
+        want_q = want_q + w_q
+    want_sh = coeff_bwd(3, torch.cat(all_o), means, torch.cat(all_d), 16)
+    for r in range(world):
+        torch.testing.assert_close(res[r][0], want_m, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(res[r][1], want_sh, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(res[r][2], want_q, rtol=1e-5, atol=1e-5)

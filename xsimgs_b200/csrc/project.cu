@@ -265,6 +265,7 @@ int xsg_projection_utgs(int type, const float* pack, const float* pts, const flo
     if (phm && type != XSG_CAM_SPHERICAL && type != XSG_CAM_LIDAR)
         return set_error(XSG_ERR_UNSUPPORTED, "projection_utgs_phm: only spherical and lidar cameras");
     const UTParams p = ut_params(ua, ub, uk, thr, max_res, margin, W, H);
+    ScopedTimer tm(phm ? "projection_utgs_phm" : "projection_utgs", as_cuda(stream));
     int rc = dispatch_camera(type, [&](auto cam) {
         using Cam = decltype(cam);
         auto* f4q = reinterpret_cast<const float4*>(quats);

@@ -214,6 +214,7 @@ int xsg_sh_fwd(int degree, const float* origin, const float* pos, const float* c
     const unsigned nb = blocks_for(n, kShThreads);
     const size_t sm = layout_3kn ? 0 : sh_stage_bytes(dim);
     int rc2 = XSG_OK;
+    ScopedTimer tm("sh_fwd", st);
     auto go = [&](auto kernel) {
         if (sm > 48 * 1024 && cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)) != cudaSuccess)
             rc2 = set_error(XSG_ERR_UNSUPPORTED, "spherical_harmonics_fwd: too many coefficient bands");
@@ -257,6 +258,7 @@ int xsg_sh_bwd(int degree, const float* origin, const float* pos, const float* c
     float* part = static_cast<float*>(workspace);
     const size_t sm = layout_3kn ? 0 : sh_stage_bytes(dim);
     int rc2 = XSG_OK;
+    ScopedTimer tm("sh_bwd", st);
     auto go = [&](auto kernel) {
         if (sm > 48 * 1024 && cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)) != cudaSuccess)
             rc2 = set_error(XSG_ERR_UNSUPPORTED, "spherical_harmonics_bwd: too many coefficient bands");

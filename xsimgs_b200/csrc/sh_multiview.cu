@@ -143,6 +143,7 @@ extern "C" int xsg_sh_positions_bwd(int degree, int n_views, const float* origin
     return sh_mv_launch(degree, [&](auto D) {
         auto k = sh_positions_bwd_kernel<decltype(D)::value>;
         if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
+        ScopedTimer tm("sh_positions_bwd", st);
         launch(k, nb, kShThreads, sm, st, n_views, origins, positions, coeffs, n, dim, d_out, d_positions);
         return check_launch("spherical_harmonics_positions_bwd");
     });
@@ -161,6 +162,7 @@ extern "C" int xsg_sh_coeffs_bwd_multi(int degree, int n_views, const float* ori
     return sh_mv_launch(degree, [&](auto D) {
         auto k = sh_coeffs_bwd_multi_kernel<decltype(D)::value>;
         if (sm > 48 * 1024) XSG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)));
+        ScopedTimer tm("sh_coeffs_bwd_multi", st);
         launch(k, nb, kShThreads, sm, st, n_views, origins, positions, n, dim, d_out, d_coeffs);
         return check_launch("spherical_harmonics_coeffs_bwd_multi");
     });

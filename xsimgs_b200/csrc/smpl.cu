@@ -546,6 +546,7 @@ extern "C" int xsg_smpl_lbs_skinning_fwd(const uint32_t* valid_ids, int64_t n_va
                 "smpl_lbs_skinning: quaternion arrays must be 16-byte aligned");
     SkinIn in{valid_ids, global_q, global_t, vertices, quats, weights, instance_ids,
               n_objects, n_vertices, n_instances, global_offset};
+    ScopedTimer tm("lbs_fwd", as_cuda(stream));
     launch(lbs_fwd_kernel, dim3(blocks_for(n_vertices, kSkinThreads), unsigned(n_valid)), dim3(kSkinThreads), 0,
            as_cuda(stream), in, instance_t, instance_v, out_positions, out_rotations, out_velocities, out_mask);
     return check_launch("smpl_lbs_skinning");
@@ -571,6 +572,7 @@ extern "C" int xsg_smpl_lbs_skinning_bwd(const uint32_t* valid_ids, int64_t n_va
                 "smpl_lbs_skinning_bwd: quaternion arrays must be 16-byte aligned");
     SkinIn in{valid_ids, global_q, global_t, vertices, quats, weights, instance_ids,
               n_objects, n_vertices, n_instances, global_offset};
+    ScopedTimer tm("lbs_bwd", as_cuda(stream));
     launch(lbs_bwd_kernel, dim3(blocks_for(n_vertices, kSkinThreads), unsigned(n_valid)), dim3(kSkinThreads), 0,
            as_cuda(stream), in, grad_positions, grad_rotations, grad_velocities, d_global_q, d_global_t, d_vertices,
            d_quats, d_weights, d_instance_v, d_instance_t);

@@ -528,6 +528,7 @@ int xsg_isect_regular_count(const float* means2d, const float* radii, int64_t n,
     if (ws_bytes < need || !workspace) return set_error(XSG_ERR_WORKSPACE, "isect_regular_tiles: workspace too small");
     XSG_CUDA(cudaMemsetAsync(w.total, 0, sizeof(unsigned long long), st));
     const int ntx = (W + tsx - 1) / tsx, nty = (H + tsy - 1) / tsy;
+    ScopedTimer tm("isect_count", st);
     if (n > 0)
         launch(regular_count_kernel, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
             reinterpret_cast<const float2*>(means2d), reinterpret_cast<const float2*>(radii), n,
@@ -565,6 +566,7 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
     }
     const int64_t n_tiles = int64_t(ntx) * nty;
     const int bucket_neg = int((int64_t(1) << tile_bits_for(n_tiles)) - 1);
+    ScopedTimer tm("isect_emit_sort", st);
     return sorted_isects(counts, depths, n, n_isects, n_tiles, w, isect_ids, flatten_ids, st,
                          [&](const uint32_t* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
                              launch(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st,

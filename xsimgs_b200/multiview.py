@@ -52,11 +52,21 @@ class GradientAllReduce:
     `wait()` issues whatever is left — with a zero gradient for a leaf this
     rank never touched in the pass (a rank without views) — and blocks the
     current stream on all collectives of the pass; call it once per pass,
-    after backward()."""
+    after backward().
 
-    def __init__(self, leaves: Iterable[torch.Tensor], group=None):
+    `gated=True` holds every all-reduce of a pass until `open_gate()` is
+    called (MultiViewSH.backward calls it right after issuing its
+    all-gathers on the same group), so that every rank issues its
+    collectives in the same order whatever order autograd runs the ready
+    nodes in: the view exchange first, then the all-reduces in leaf order.
+    A rank whose graphs differ from its peers' (other view counts) could
+    otherwise interleave the two kinds differently and mismatch the
+    collectives."""
+
+    def __init__(self, leaves: Iterable[torch.Tensor], group=None, gated: bool = False):
         self.leaves = list(leaves)
         self.group = group
+        self.gated = gated
         self.enabled = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
         self.handles = []
         self._reset()
@@ -68,6 +78,12 @@ class GradientAllReduce:
         self.ready = [False] * len(self.leaves)
         self.next = 0
         self.works = []
+        self.gate_open = not self.gated
+
+    def open_gate(self):
+        """Lets the pass's all-reduces go (issuing those already ready)."""
+        self.gate_open = True
+        self._flush()
 
     def _make_hook(self, i):
         def hook(_t):
@@ -82,6 +98,8 @@ class GradientAllReduce:
         self.works.append(dist.all_reduce(t.grad, group=self.group, async_op=True))
 
     def _flush(self):
+        if not self.gate_open:
+            return
         while self.next < len(self.leaves) and self.ready[self.next]:
             self._issue(self.next)
             self.next += 1
@@ -91,12 +109,14 @@ class GradientAllReduce:
         returns how many were issued."""
         if not self.enabled:
             return 0
+        self.gate_open = True
         while self.next < len(self.leaves):
             self._issue(self.next)
             self.next += 1
         n = len(self.works)
         for w in self.works:
             w.wait()
+        timeline.mark("exchange_end")
         self._reset()
         return n
 
@@ -123,15 +143,17 @@ class MultiViewSH(torch.autograd.Function):
 
     Every rank of `group` must call it with the same k_max >= its own k
     (ranks pad to k_max), and with at least one view, in the same order
-    relative to its other collectives.  Coefficients [N, K, 3] with band 0
-    included; no mask."""
+    relative to its other collectives: pass the step's GradientAllReduce
+    (built with gated=True) as `reducer`, and its all-reduces are released
+    only after the all-gathers are issued.  Coefficients [N, K, 3] with band
+    0 included; no mask."""
 
     @staticmethod
-    def forward(ctx, sh, means, origins, degree: int, k_max: int, group=None):
+    def forward(ctx, sh, means, origins, degree: int, k_max: int, group=None, reducer=None):
         from ._native import _C
         cols = torch.stack([_C.spherical_harmonics_fused_fwd(degree, origins[v].contiguous(), means, sh, None, False)
                             for v in range(origins.shape[0])])
-        ctx.degree, ctx.k_max, ctx.group = degree, k_max, group
+        ctx.degree, ctx.k_max, ctx.group, ctx.reducer = degree, k_max, group, reducer
         ctx.save_for_backward(sh, means, origins)
         return cols
 
@@ -156,14 +178,42 @@ class MultiViewSH(torch.autograd.Function):
             w_o = dist.all_gather_into_tensor(all_o, pad_o, group=ctx.group, async_op=True)
         else:
             all_d, all_o = d_cols, origins
+        if ctx.reducer is not None:
+            ctx.reducer.open_gate()
+        timeline.mark("sh_bwd_start")
         d_means = _C.spherical_harmonics_positions_bwd(ctx.degree, origins, means, sh, d_cols)
         if distributed:
             w_d.wait()
             w_o.wait()
+        timeline.mark("sh_gathered")
         d_sh = _C.spherical_harmonics_coeffs_bwd_multi(ctx.degree, all_o, means, all_d, sh.shape[1])
-        return d_sh, d_means, None, None, None, None
+        timeline.mark("sh_bwd_end")
+        return d_sh, d_means, None, None, None, None, None
 
 
-def multiview_colors(sh, means, origins, degree: int, k_max: int, group=None):
+def multiview_colors(sh, means, origins, degree: int, k_max: int, group=None, reducer=None):
     """[k, N, 3] colours of this rank's k views (see MultiViewSH)."""
-    return MultiViewSH.apply(sh.contiguous(), means.contiguous(), origins.contiguous(), degree, k_max, group)
+    return MultiViewSH.apply(sh.contiguous(), means.contiguous(), origins.contiguous(), degree, k_max, group,
+                             reducer)
+
+
+class Timeline:
+    """Optional named CUDA events on the current stream, for per-phase step
+    timing (off unless enabled; marks cost one event record each)."""
+
+    def __init__(self):
+        self.enabled = False
+        self.events: list[tuple[str, torch.cuda.Event]] = []
+
+    def mark(self, name: str):
+        if self.enabled:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.events.append((name, e))
+
+    def take(self) -> list[tuple[str, torch.cuda.Event]]:
+        ev, self.events = self.events, []
+        return ev
+
+
+timeline = Timeline()

@@ -55,3 +55,49 @@ def bwd_flops(n_eval_bwd: int, n_contrib: int, cdim: int, ray_grads: bool = True
 #   ncu --set full --clock-control none -k regex:raster_bwd_px2 -s 1 -c 1 \
 #       python bench.py --steps 2 --warmup 1 --no-cpu-baseline --no-lidar
 BWD_DRAM_BYTES_C2 = 269.33e6 + 35.51e6
+
+
+# The quaternion / scale part of the backward (quat_scale_to_preci_half_vjp,
+# rasterization/utils.h:232-263) is linear in dL/dM for a fixed Gaussian:
+# this package's backward sums dL/dM over the pairs and applies the VJP once
+# per Gaussian in its finalize pass, so of the algorithmic count above it
+# executes 136 FLOP per contributing pair fewer (and 136 per Gaussian more).
+QUAT_SCALE_VJP = 136
+
+
+def bwd_flops_executed(n_eval_bwd: int, n_contrib: int, n_gauss_touched: int, cdim: int,
+                       ray_grads: bool = True) -> float:
+    return bwd_flops(n_eval_bwd, n_contrib, cdim, ray_grads) - QUAT_SCALE_VJP * (n_contrib - n_gauss_touched)
+
+
+# Algorithmic HBM bytes per launch of the memory-bound stages (inputs read
+# once, outputs written once), by the timing names of the C ABI:
+#   projection_utgs   means, scales 12 + 12, quats 16, opacity 4 read;
+#                     flag 1, radii 8, means2d 8, depth 4 written    65 B / Gaussian
+#   isect_count       means2d, radii read, count written             20 B / Gaussian
+#   sh_fwd            position 12 + coefficients 12 K read, colour 12 written
+#   sh_bwd            position, coefficients, colour gradient read; coefficient
+#                     and position gradients written
+#   sh_positions_bwd  position, coefficients, J colour gradients read; position
+#                     gradient written
+#   sh_coeffs_bwd_multi  position, J colour gradients read; coefficient
+#                     gradient written
+#   lbs_fwd           vertex 12, quat 16, 24 weights 96 read; position 12,
+#                     rotation 16, velocity 12, mask 1 written     165 B / element
+#   lbs_bwd           vertex, quat, weights and the position / rotation /
+#                     velocity gradients read; vertex, quat, weight gradients
+#                     written                                      288 B / element
+def stage_bytes(name: str, n: int, sh_bands: int = 16, views: int = 1) -> float | None:
+    k = 12 * sh_bands
+    table = {
+        "projection_utgs": 65, "projection_utgs_phm": 65,
+        "isect_count": 20,
+        "sh_fwd": 12 + k + 12,
+        "sh_bwd": 12 + k + 12 + k + 12,
+        "sh_positions_bwd": 12 + k + 12 * views + 12,
+        "sh_coeffs_bwd_multi": 12 + 12 * views + k,
+        "lbs_fwd": 165,
+        "lbs_bwd": 288,
+    }
+    per = table.get(name)
+    return None if per is None else float(per) * n
