@@ -84,7 +84,7 @@ int xsg_timing_query(const char* name, double* total_ms, long long* launches);
 /* FP32 FMA peak probe: launches `blocks` x 512 threads of iters x 128
  * independent FMAs, writes the FLOP count to *flops (time it with events). */
 int xsg_fp32_probe(float* scratch, int iters, int blocks, xsg_stream_t stream, double* flops);
-/* Pair counters of the forward compositing kernel: when `counters` (8 x u64,
+/* Work counters of the compositing kernels: when `counters` (12 x u64,
  * device, zeroed by the caller) is set, every xsg_rasterize_fwd adds to it
  * [0] the evaluated and [1] the contributing (pixel, Gaussian) pairs as the
  * reference counts them, and, per (warp of 32 pixels, Gaussian), [2] the
@@ -95,8 +95,10 @@ int xsg_fp32_probe(float* scratch, int iters, int blocks, xsg_stream_t stream, d
  * tile) it also adds, over the pairs of 8 x 4 pixel blocks (2w, 2w + 1) of
  * every fourth tile, [6] the union and [7] the sum of the two blocks'
  * contributor counts per list entry: the backward runs two pixels a lane when
- * [6] is at most 72 % of [7] for the image.
- * NULL (the default) turns counting off. */
+ * [6] is at most 72 % of [7] for the image.  The two-pixels-a-lane backward
+ * adds [8] the list entries its warps process, [9] the lanes holding a
+ * contributing pixel summed over them and [10] the entries with at most two
+ * such lanes.  NULL (the default) turns counting off. */
 void xsg_set_pair_counters(unsigned long long* counters);
 
 /* Camera rays: ray_o/ray_d [H, W, 3] (ray_o and valid may be NULL).

@@ -59,7 +59,7 @@ struct RasterArgs {
     float* v_ray_o;
     float* v_ray_d;
     float* v_ray_t;
-    unsigned long long* pair_counters;  // 6 work counters (optional, xsg_set_pair_counters)
+    unsigned long long* pair_counters;  // work counters (optional, xsg_set_pair_counters)
     const int32_t* tile_order;          // launch order of the tiles (optional)
     // contributor masks (optional): word ((start >> 5) + tile + k) * warps_per_tile + warp has
     // bit i set when list entry start + 32 k + i reached alpha >= 1/255 at one of the warp's
@@ -1272,7 +1272,15 @@ __global__ void __launch_bounds__(128, 4) raster_bwd_px2_kernel(RasterArgs a) {
         const float alA = fminf(0.99f, ov.x), alB = fminf(0.99f, ov.y);
         const bool vA = inA && gidx <= binA && !(alA < 1.f / 255.f);
         const bool vB = inB && gidx <= binB && !(alB < 1.f / 255.f);
-        if (!__any_sync(0xffffffffu, vA || vB)) return;
+        const unsigned vmask = __ballot_sync(0xffffffffu, vA || vB);
+        if (!vmask) return;
+        if (a.pair_counters && lane == 0) {
+            // work counters 8-10: entries processed, lanes with a contributing
+            // pixel over them, entries with at most two such lanes
+            atomicAdd(a.pair_counters + 8, 1ull);
+            atomicAdd(a.pair_counters + 9, (unsigned long long)__popc(vmask));
+            if (__popc(vmask) <= 2) atomicAdd(a.pair_counters + 10, 1ull);
+        }
 
         const float2 od = pdot(gro, grd);
         const float hA = div_nr(-od.x, l.x), hB = div_nr(-od.y, l.y);
@@ -1722,6 +1730,7 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     a.v_rgb = v_renders; a.v_depth = v_depths; a.v_alpha = v_alphas;
     a.G = G; a.v_colors_direct = v_colors;
     a.tile_order = order;
+    a.pair_counters = g_pair_counters;
     a.masks = masks;  // written by the forward into the same workspace
     a.px2_stats = (masks && px2_layout(cdim, dyn, tsx, tsy))
                       ? reinterpret_cast<unsigned long long*>(masks + px2_stats_word(n_isects, n_tiles, tsx * tsy))
