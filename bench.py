@@ -65,6 +65,8 @@ def parse():
     p.add_argument("--no-rig", action="store_true", help="skip the C3 / C3-8 rig measurement")
     p.add_argument("--no-c5", action="store_true", help="skip the C5 skinned-actor measurement")
     p.add_argument("--gaussians", type=int, default=0, help="override the workload's Gaussian count")
+    p.add_argument("--exchange", default="bucketed", choices=["bucketed", "per-leaf"],
+                   help="geometry gradients ready together share one all-reduce (bucketed) or not")
     p.add_argument("--workload", default="c2", choices=["c2", "c3", "c3-8", "c5"],
                    help="c2: one C2 view per rank (weak scaling, the default); c3 / c3-8 / c5: the rig's views "
                         "sharded over the ranks (strong scaling)")
@@ -275,7 +277,7 @@ class Workload:
     the gradient exchange and a `step(upstream)` that runs one fwd+bwd pass
     of every view of this rank and the exchange."""
 
-    def __init__(self, name, world, rank, dev, n_gauss=0):
+    def __init__(self, name, world, rank, dev, n_gauss=0, exchange="bucketed"):
         import torch
         import xsimgs_b200 as X
         from xsimgs_b200 import scenes
@@ -300,12 +302,18 @@ class Workload:
         if name == "c5":
             self._setup_c5(dev)
         # with a view on every rank, ranks exchange per-view colour gradients
-        # and rebuild the SH-coefficient gradient locally (MultiViewSH)
+        # and rebuild the SH-coefficient gradient locally (MultiViewSH), on a
+        # communicator of their own: its all-gathers and the all-reduces
+        # below each keep one order on every rank and run side by side
         self.mvsh = world > 1 and name != "c5" and min(len(v) for v in self.assignment) >= 1
+        import torch.distributed as dist
+        self.sh_group = dist.new_group(list(range(world))) if self.mvsh else None
         order = ["quats", "scales", "opacities", "means"] + ([] if self.mvsh else ["sh"])
         order += [k for k in self.leaves if k not in order]
-        # backward finishes the compositing's leaves first, then the SH backward's
-        self.red = GradientAllReduce([self.leaves[k] for k in order], gated=self.mvsh)
+        # backward finishes the compositing's leaves first (quats, scales and
+        # opacities together: one bucket), then the SH backward's
+        buckets = ([3] + [1] * (len(order) - 3)) if exchange == "bucketed" else None
+        self.red = GradientAllReduce([self.leaves[k] for k in order], buckets=buckets)
         self.upstream = [tuple(t.to(dev) for t in scenes.upstream_grads(sp.height, sp.width, 3,
                                                                          seed=1 + rank * 16 + k))
                          for k, (sp, _) in enumerate(self.views)]
@@ -353,7 +361,7 @@ class Workload:
         means, quats, scales, opac, sh, vel = self._scene()
         if self.mvsh:
             cols = self.mvc(sh, means, torch.stack([cam.t0 for _, cam in self.views]), DEG, self.k_max,
-                            reducer=self.red)
+                            group=self.sh_group)
         outs, ups = [], []
         for v, ((sp, cam), g) in enumerate(zip(self.views, grads)):
             colors = cols[v] if self.mvsh else X.spherical_harmonics_fused(sh, means, cam.t0, DEG)
@@ -442,7 +450,61 @@ def phase_times(wl, steps, world):
                 acc[names[k]] = acc.get(names[k], 0.0) + prev.elapsed_time(ev[k])
                 prev = ev[k]
     timeline.enabled = False
-    return {k: round(v / steps, 4) for k, v in acc.items()}
+    mine = {k: v / steps for k, v in acc.items()}
+    if world == 1:
+        return {k: round(v, 4) for k, v in mine.items()}
+    # every rank's phases: the max and min over ranks show the load skew the
+    # collectives wait out
+    import torch
+    import torch.distributed as dist
+    keys = ["forward", "backward_compute", "sh_bwd_exchange_wait", "sh_coeff_rebuild", "backward_rest",
+            "allreduce_tail"]
+    t = torch.tensor([mine.get(k, 0.0) for k in keys], dtype=torch.float64, device=torch.device("cuda"))
+    all_t = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(all_t, t)
+    m = torch.stack(all_t)
+    return {k: {"rank0": round(float(m[0, i]), 4), "max": round(float(m[:, i].max()), 4),
+                "min": round(float(m[:, i].min()), 4)} for i, k in enumerate(keys) if k in mine}
+
+
+def exchange_probe(wl, world, dev, reps=10):
+    """The step's gradient exchange alone (no compute running): the
+    all-gather of one colour gradient per rank and the all-reduces of the
+    geometry gradients, as the step issues them; mean ms over `reps`."""
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return None
+    n = wl.n_gauss
+    geo = [torch.zeros(n, k, device=dev) for k in (4, 3, 1, 3)]
+    d = torch.zeros(n, 3, device=dev)
+    out = torch.empty(world * n, 3, device=dev)
+    flat = torch.zeros(n * 11, device=dev)
+
+    def run(split):
+        w = [dist.all_gather_into_tensor(out, d, async_op=True)] if wl.mvsh else []
+        if split:
+            w += [dist.all_reduce(t, async_op=True) for t in geo]
+        else:
+            w += [dist.all_reduce(flat, async_op=True)]
+        for x in w:
+            x.wait()
+
+    res = {}
+    for split in (True, False):
+        for _ in range(3):
+            run(split)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run(split)
+        e1.record()
+        barrier(world)
+        res["per_leaf" if split else "one_bucket"] = round(e0.elapsed_time(e1) / reps, 4)
+    res["bytes_all_reduced"] = 4 * 11 * n
+    res["bytes_all_gathered_per_rank"] = 12 * n if wl.mvsh else 0
+    return res
 
 
 def gpu_arm(args, world, rank, local):
@@ -457,7 +519,7 @@ def gpu_arm(args, world, rank, local):
     import xsimgs_b200 as X
     from xsimgs_b200 import capi, scenes, roofline
 
-    wl = Workload(args.workload, world, rank, dev, args.gaussians)
+    wl = Workload(args.workload, world, rank, dev, args.gaussians, args.exchange)
     views, leaves = wl.views, wl.leaves
 
     for _ in range(args.warmup):
@@ -539,6 +601,7 @@ def gpu_arm(args, world, rank, local):
 
     # ----------------------------------------------------- phases ----
     phases = phase_times(wl, min(10, args.steps), world)
+    xprobe = exchange_probe(wl, world, dev)
 
     extra = {}
     main_default = args.workload == "c2"
@@ -592,6 +655,7 @@ def gpu_arm(args, world, rank, local):
                         "as in a training loop"},
         "gpu_launches": int(launches), "gpu_launches_per_step": round(launches / args.steps, 1),
         "clocks": clk, "roofline": roof, "cpu_baseline": cpu, "phases": phases, "stages": stages,
+        "exchange_alone_ms": xprobe,
     }
     line.update(extra)
     print(json.dumps(line), flush=True)
@@ -640,7 +704,7 @@ def strong_leg(args, name, world, rank, dev, phases=True):
     """A strong-scaling workload (all views of the rig per step, sharded over
     the ranks) timed like the main line; Mpix/s of the whole job."""
     import torch
-    wl = Workload(name, world, rank, dev)
+    wl = Workload(name, world, rank, dev, exchange=args.exchange)
     steps = max(3, min(args.steps, 20))
     ms = time_steps(wl, steps, max(3, args.warmup), world)
     ph = phase_times(wl, min(5, steps), world) if phases else None

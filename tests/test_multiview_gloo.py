@@ -91,9 +91,10 @@ def _reference_sum(world, idle=()):
     return tot
 
 
-def _worker_values(rank, world, port, q, idle=()):
+def _worker_values(rank, world, port, q, idle=(), buckets=None):
     """`idle` ranks run no backward (a rank without views): they contribute
-    zeros and still take part in every collective."""
+    zeros and still take part in every collective.  With `buckets`, leaves
+    share collectives (their gradients become views of one flat buffer)."""
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -103,28 +104,29 @@ def _worker_values(rank, world, port, q, idle=()):
         means = torch.randn(50, 3, generator=g).requires_grad_(True)
         quats = torch.randn(50, 4, generator=g).requires_grad_(True)
         sh = torch.randn(50, 16, 3, generator=g).requires_grad_(True)
-        red = GradientAllReduce([means, quats, sh])
+        red = GradientAllReduce([means, quats, sh], buckets=buckets)
         w = torch.randn(50, 3, generator=g)
         if rank not in idle:
             ((sh[:, 0, :] * means.sin()).sum() + (means * w).sum() + (quats ** 2).sum() * (rank + 1)).backward()
-        assert red.wait() == 3
+        assert red.wait() == (3 if buckets is None else len(buckets))
         q.put((rank, [_plain(t.grad) for t in (means, quats, sh)]))
         dist.destroy_process_group()
     except Exception as e:
         q.put((rank, repr(e)))
 
 
-@pytest.mark.parametrize("target", ["consistency", "values", "idle_rank"])
+@pytest.mark.parametrize("target", ["consistency", "values", "idle_rank", "buckets", "buckets_idle_rank"])
 def test_gradient_allreduce_two_gloo_ranks(target):
     world = 2
-    idle = (1,) if target == "idle_rank" else ()
+    idle = (1,) if target.endswith("idle_rank") else ()
+    buckets = [2, 1] if target.startswith("buckets") else None
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     if target == "consistency":
         procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     else:
-        procs = [ctx.Process(target=_worker_values, args=(r, world, port, q, idle)) for r in range(world)]
+        procs = [ctx.Process(target=_worker_values, args=(r, world, port, q, idle, buckets)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -233,10 +235,12 @@ def test_multiview_sh_exchange_two_gloo_ranks():
         torch.testing.assert_close(res[r][1], want_sh, rtol=1e-5, atol=1e-5)
 
 
-def _worker_mvsh_gated(rank, world, port, q):
-    """The render step's two exchanges together on one group: the geometry
-    all-reduces (GradientAllReduce, gated) and MultiViewSH's all-gathers,
-    with different view counts (so different autograd graphs) per rank."""
+def _worker_mvsh_gated(rank, world, port, q, own_group=False):
+    """The render step's two exchanges together: the geometry all-reduces
+    (GradientAllReduce) and MultiViewSH's all-gathers, with different view
+    counts (so different autograd graphs) per rank — either on one group
+    with the all-reduces gated behind the all-gathers, or with the view
+    exchange on a group of its own (each group keeps one order)."""
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -252,11 +256,13 @@ def _worker_mvsh_gated(rank, world, port, q):
         w_q, w_m = _gated_weights(rank)
         for t in (means, sh, quats):
             t.requires_grad_(True)
-        red = GradientAllReduce([quats, means], gated=True)
+        sh_group = dist.new_group([0, 1]) if own_group else None
+        red = GradientAllReduce([quats, means], gated=not own_group)
         for _ in range(2):  # hooks registered once, two passes
             for t in (means, sh, quats):
                 t.grad = None
-            cols = multiview_colors(sh, means, origins, 3, k_max=2, reducer=red)
+            cols = (multiview_colors(sh, means, origins, 3, k_max=2, group=sh_group) if own_group else
+                    multiview_colors(sh, means, origins, 3, k_max=2, reducer=red))
             # "compositing": quats and means feed it as well as the colours
             loss = (cols * d_cols).sum() + (quats * w_q).sum() + (means * w_m).sum()
             loss.backward()
@@ -273,14 +279,15 @@ def _gated_weights(rank):
     return torch.randn(40, 4, generator=g), torch.randn(40, 3, generator=g)
 
 
-def test_gated_allreduce_with_multiview_exchange_two_gloo_ranks():
+@pytest.mark.parametrize("own_group", [False, True], ids=["gated", "own_group"])
+def test_allreduce_with_multiview_exchange_two_gloo_ranks(own_group):
     """Every rank ends with the sum over ranks of the geometry gradients and
     the SH gradient of every view of every rank, uneven view counts."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker_mvsh_gated, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker_mvsh_gated, args=(r, world, port, q, own_group)) for r in range(world)]
     for p in procs:
         p.start()
     res = {r: (v if isinstance(v, str) else [torch.from_numpy(x) for x in v])

@@ -52,7 +52,8 @@ class GradientAllReduce:
     `wait()` issues whatever is left — with a zero gradient for a leaf this
     rank never touched in the pass (a rank without views) — and blocks the
     current stream on all collectives of the pass; call it once per pass,
-    after backward().
+    after backward().  It returns the number of collectives issued (one per
+    bucket).
 
     `gated=True` holds every all-reduce of a pass until `open_gate()` is
     called (MultiViewSH.backward calls it right after issuing its
@@ -63,10 +64,22 @@ class GradientAllReduce:
     otherwise interleave the two kinds differently and mismatch the
     collectives."""
 
-    def __init__(self, leaves: Iterable[torch.Tensor], group=None, gated: bool = False):
+    def __init__(self, leaves: Iterable[torch.Tensor], group=None, gated: bool = False,
+                 buckets: Sequence[int] | None = None):
         self.leaves = list(leaves)
         self.group = group
         self.gated = gated
+        # consecutive leaves that get ready together can share one
+        # collective: `buckets` gives the group sizes in leaf order
+        sizes = list(buckets) if buckets is not None else [1] * len(self.leaves)
+        if sum(sizes) != len(self.leaves) or min(sizes, default=1) < 1:
+            raise ValueError("buckets must split the leaves into consecutive non-empty groups")
+        self.bucket_of, self.bucket_leaves = [], []
+        k = 0
+        for b, n in enumerate(sizes):
+            self.bucket_leaves.append(list(range(k, k + n)))
+            self.bucket_of += [b] * n
+            k += n
         self.enabled = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
         self.handles = []
         self._reset()
@@ -76,8 +89,9 @@ class GradientAllReduce:
 
     def _reset(self):
         self.ready = [False] * len(self.leaves)
-        self.next = 0
+        self.next = 0  # next bucket to issue
         self.works = []
+        self.unpack = []
         self.gate_open = not self.gated
 
     def open_gate(self):
@@ -91,16 +105,28 @@ class GradientAllReduce:
             self._flush()
         return hook
 
-    def _issue(self, i):
-        t = self.leaves[i]
-        if t.grad is None:
-            t.grad = torch.zeros_like(t)
-        self.works.append(dist.all_reduce(t.grad, group=self.group, async_op=True))
+    def _issue(self, b):
+        idx = self.bucket_leaves[b]
+        for i in idx:
+            t = self.leaves[i]
+            if t.grad is None:
+                t.grad = torch.zeros_like(t)
+        if len(idx) == 1:
+            self.works.append(dist.all_reduce(self.leaves[idx[0]].grad, group=self.group, async_op=True))
+            return
+        # one flat buffer per bucket; after the collective each leaf's
+        # gradient becomes a view of it
+        flat = torch.cat([self.leaves[i].grad.reshape(-1) for i in idx])
+        self.works.append(dist.all_reduce(flat, group=self.group, async_op=True))
+        self.unpack.append((flat, idx))
+
+    def _bucket_ready(self, b):
+        return all(self.ready[i] for i in self.bucket_leaves[b])
 
     def _flush(self):
         if not self.gate_open:
             return
-        while self.next < len(self.leaves) and self.ready[self.next]:
+        while self.next < len(self.bucket_leaves) and self._bucket_ready(self.next):
             self._issue(self.next)
             self.next += 1
 
@@ -110,12 +136,18 @@ class GradientAllReduce:
         if not self.enabled:
             return 0
         self.gate_open = True
-        while self.next < len(self.leaves):
+        while self.next < len(self.bucket_leaves):
             self._issue(self.next)
             self.next += 1
         n = len(self.works)
         for w in self.works:
             w.wait()
+        for flat, idx in self.unpack:
+            off = 0
+            for i in idx:
+                t = self.leaves[i]
+                t.grad = flat[off:off + t.numel()].view_as(t)
+                off += t.numel()
         timeline.mark("exchange_end")
         self._reset()
         return n
@@ -143,10 +175,12 @@ class MultiViewSH(torch.autograd.Function):
 
     Every rank of `group` must call it with the same k_max >= its own k
     (ranks pad to k_max), and with at least one view, in the same order
-    relative to its other collectives: pass the step's GradientAllReduce
-    (built with gated=True) as `reducer`, and its all-reduces are released
-    only after the all-gathers are issued.  Coefficients [N, K, 3] with band
-    0 included; no mask."""
+    relative to its other collectives on `group`.  Either give it a group of
+    its own (its all-gathers then run beside the gradient all-reduces, each
+    group in one order on every rank), or share the all-reduces' group and
+    pass the step's GradientAllReduce (built with gated=True) as `reducer`:
+    its all-reduces are then released only after the all-gathers are issued.
+    Coefficients [N, K, 3] with band 0 included; no mask."""
 
     @staticmethod
     def forward(ctx, sh, means, origins, degree: int, k_max: int, group=None, reducer=None):
