@@ -201,6 +201,26 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
                            int64_t* isect_ids, int32_t* flatten_ids, void* workspace,
                            size_t workspace_bytes, xsg_stream_t stream);
 
+/* Regular tiling with no host round trip: count, emit, sort and offset
+ * encoding in one call that never synchronises `stream`.  Output buffers are
+ * sized for `capacity` intersections (isect_ids i64[capacity], flatten_ids
+ * i32[capacity], offsets i32[tiles_h * tiles_w]); on the device,
+ * n_isects_dev[0] receives the intersection total and n_isects_dev[1] =
+ * min(total, capacity), the number written.  The lists are the ones
+ * *_count + *_emit(sort = 1) + xsg_isect_offset_encode produce whenever
+ * total <= capacity; when it is larger they hold the first `capacity`
+ * intersections in depth order only, and the caller, reading
+ * n_isects_dev[0] later, must redo the view with a larger capacity.
+ * Pass n_isects_dev + 1 and n_isects = capacity to xsg_rasterize_fwd /
+ * xsg_rasterize_bwd.  Workspace: xsg_isect_workspace_size(n, capacity).
+ * Same reference interface as *_count + *_emit. */
+int xsg_isect_regular_tiles_async(const float* means2d, const float* radii, const float* depths,
+                                  int64_t n, int width, int height, int tile_size_x,
+                                  int tile_size_y, int64_t capacity, int32_t* tiles_per_gauss,
+                                  int64_t* isect_ids, int32_t* flatten_ids, int32_t* offsets,
+                                  int64_t* n_isects_dev, void* workspace, size_t workspace_bytes,
+                                  xsg_stream_t stream);
+
 /* Azimuth/elevation tiling for range images.  lidar != 0: irregular
  * elevation tiles bounded by elev_bounds[n_elev] (every tile_size_y-th beam
  * value); else regular tiles of tile_size_x x tile_size_y.  Gaussians with
@@ -242,7 +262,10 @@ int xsg_raster_supported_channels(int* out, int cap);
  * [H, W, cdim], depths/alphas [H, W], last_ids i32[H, W].
  * Workspace: xsg_rasterize_workspace_size(n_gauss, cdim, n_isects, n_tiles,
  * tile_size_x * tile_size_y) bytes, or with n_isects = n_tiles = 0 the
- * minimum.  The larger size also holds per-warp contributor masks that the
+ * minimum.  n_isects_dev (device, may be NULL) holds the list length when
+ * it is only known on the device; n_isects is then its upper bound (the
+ * capacity the lists were allocated for) and sizes the workspace.  The larger
+ * size also holds per-warp contributor masks that the
  * forward writes and that a backward given the same workspace
  * (workspace_from_forward) uses to visit only the list entries some pixel
  * of the warp composited.
@@ -258,7 +281,7 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
                       const int32_t* tile_offsets, int tiles_w, int tiles_h,
                       const int32_t* flatten_ids, int64_t n_isects, float* renders,
                       float* depths, float* alphas, int32_t* last_ids, void* workspace,
-                      size_t workspace_bytes, xsg_stream_t stream);
+                      size_t workspace_bytes, xsg_stream_t stream, const int64_t* n_isects_dev);
 
 /* Backward compositing.  Gradient outputs are overwritten (zeroed first):
  * v_means/v_velocity [N,3], v_quats [N,4], v_scales [N,3], v_opacities [N],
@@ -283,7 +306,8 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
                       float* v_means, float* v_velocity, float* v_quats, float* v_scales,
                       float* v_colors, float* v_opacities, float* v_ray_o, float* v_ray_d,
                       float* v_ray_time_delta, void* workspace, size_t workspace_bytes,
-                      int workspace_from_forward, xsg_stream_t stream);
+                      int workspace_from_forward, xsg_stream_t stream,
+                      const int64_t* n_isects_dev);
 
 /* Spherical-harmonics colour, degree 0..4; layout_3kn selects [3, K, N]
  * coefficients (else [N, K, 3]); coeffs_dc optionally holds band 0 apart;

@@ -21,7 +21,7 @@ def test_c_abi_rejects_bad_arguments_without_gpu():
     from xsimgs_b200 import capi
     lib = capi.lib()
     # argument validation happens before any CUDA call
-    rc = lib.xsg_rasterize_fwd(*([None] * 7), 7, *([None] * 17))  # unsupported channel count first
+    rc = lib.xsg_rasterize_fwd(*([None] * 7), 7, *([None] * 18))  # unsupported channel count first
     assert rc != 0
     rc = lib.xsg_mask_radii(None, None, ctypes.c_int64(4), None, None)
     assert rc == 1 and b"exactly one mask" in lib.xsg_last_error()

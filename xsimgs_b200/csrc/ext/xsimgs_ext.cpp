@@ -378,6 +378,42 @@ std::tuple<Tensor, Tensor, Tensor> isect_regular_tiles(const Tensor& means2d, co
     return {tiles_per_gauss, isect_ids, flatten_ids};
 }
 
+// Capacity-sized regular tiling with no host synchronisation: returns
+// (tiles_per_gauss, isect_ids[capacity], flatten_ids[capacity],
+// offsets[tiles_h, tiles_w], counts int64[2] = {total, written}).  Lists
+// match isect_regular_tiles + isect_offset_encode when total <= capacity.
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> isect_regular_tiles_async(
+    const Tensor& means2d, const Tensor& radii, const Tensor& depths, int64_t img_width, int64_t img_height,
+    int64_t tile_size_x, int64_t tile_size_y, int64_t capacity, const OptT& workspace_in) {
+    check_tensor(means2d, "means2d", means2d);
+    check_tensor(radii, "radii", means2d);
+    check_tensor(depths, "depth", means2d);
+    TORCH_CHECK(capacity > 0, "isect_regular_tiles_async: capacity must be positive");
+    c10::cuda::CUDAGuard g(means2d.device());
+    const int64_t n = means2d.numel() / 2;
+    auto opt = depths.options();
+    const int64_t ntx = (img_width + tile_size_x - 1) / tile_size_x, nty = (img_height + tile_size_y - 1) / tile_size_y;
+    Tensor tiles_per_gauss = at::empty_like(depths, opt.dtype(at::kInt));
+    Tensor isect_ids = at::empty({capacity}, opt.dtype(at::kLong));
+    Tensor flatten_ids = at::empty({capacity}, opt.dtype(at::kInt));
+    Tensor offsets = at::empty({nty, ntx}, opt.dtype(at::kInt));
+    Tensor counts = at::empty({2}, opt.dtype(at::kLong));
+    const size_t need = xsg_isect_workspace_size(n, capacity);
+    Tensor ws;
+    if (has(workspace_in) && size_t(workspace_in->nbytes()) >= need) {
+        check_tensor(*workspace_in, "workspace", means2d);
+        ws = *workspace_in;
+    } else {
+        ws = workspace(need, means2d);
+    }
+    check(xsg_isect_regular_tiles_async(fptr(means2d), fptr(radii), fptr(depths), n, int(img_width), int(img_height),
+                                        int(tile_size_x), int(tile_size_y), capacity,
+                                        tiles_per_gauss.data_ptr<int32_t>(), isect_ids.data_ptr<int64_t>(),
+                                        flatten_ids.data_ptr<int32_t>(), offsets.data_ptr<int32_t>(),
+                                        counts.data_ptr<int64_t>(), ws.data_ptr(), size_t(ws.nbytes()), stream()));
+    return {tiles_per_gauss, isect_ids, flatten_ids, offsets, counts};
+}
+
 std::tuple<Tensor, Tensor, Tensor> isect_range_tiles(bool lidar, const Tensor& pack, const Tensor& points,
                                                      const OptT& vel, const Tensor& scale, const Tensor& quat,
                                                      const OptT& opacity, const Tensor& flag, const Tensor& means2d,
@@ -451,6 +487,15 @@ void mask_radii_packed(const Tensor& packed_mask, const Tensor& radii) {
 }
 
 // ---------------------------------------------------------- rasteriser ---
+// The device-side list length of a capacity-sized intersection list
+// (isect_regular_tiles_async), or null: the list is then flatten_ids whole.
+const int64_t* n_isects_ptr(const OptT& n_dev, const Tensor& like) {
+    if (!has(n_dev)) return nullptr;
+    check_tensor(*n_dev, "n_isects", like);
+    TORCH_CHECK(n_dev->scalar_type() == at::kLong && n_dev->numel() >= 1, "n_isects must be an int64 device tensor");
+    return n_dev->data_ptr<int64_t>();
+}
+
 std::vector<int64_t> eval3d_supported_ndims() {
     int buf[64];
     const int n = xsg_raster_supported_channels(buf, 64);
@@ -462,7 +507,8 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> raster_fwd(const Tensor& means, const
                                                       const Tensor& opacities, int64_t W, int64_t H, int64_t tsx,
                                                       int64_t tsy, const Tensor& ray_o, const Tensor& ray_d,
                                                       const OptT& ray_t, const Tensor& tile_offsets,
-                                                      const Tensor& flatten_ids, const OptT& workspace_in) {
+                                                      const Tensor& flatten_ids, const OptT& workspace_in,
+                                                      const OptT& n_isects_dev) {
     for (auto* t : {&means, &quats, &scales, &opacities, &ray_o, &ray_d, &tile_offsets, &flatten_ids})
         check_tensor(*t, "rasterize input", means);
     if (has(colors)) check_tensor(*colors, "colors", means);
@@ -490,7 +536,8 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> raster_fwd(const Tensor& means, const
                             fptr(ray_t), tile_offsets.data_ptr<int32_t>(), int(tile_offsets.size(-1)),
                             int(tile_offsets.size(-2)), flatten_ids.data_ptr<int32_t>(), flatten_ids.numel(),
                             channels ? fptr_mut(renders) : nullptr, fptr_mut(depths), fptr_mut(alphas),
-                            last_ids.data_ptr<int32_t>(), ws.data_ptr(), size_t(ws.nbytes()), stream()));
+                            last_ids.data_ptr<int32_t>(), ws.data_ptr(), size_t(ws.nbytes()), stream(),
+                            n_isects_ptr(n_isects_dev, means)));
     return {renders, depths, alphas, last_ids};
 }
 
@@ -504,7 +551,7 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
                   const Tensor& opacity, const OptT& colors, const Tensor& ray_o, const Tensor& ray_d,
                   const OptT& ray_t, int64_t tsx, int64_t tsy, const Tensor& tile_offsets, const Tensor& flatten_ids,
                   const Tensor& render_alpha, const Tensor& last_ids, const OptT& v_colors_in, const Tensor& v_depth,
-                  const Tensor& v_alpha, bool ray_grads, const OptT& fwd_ws) {
+                  const Tensor& v_alpha, bool ray_grads, const OptT& fwd_ws, const OptT& n_isects_dev) {
     if (has(v_colors_in) && !v_colors_in->is_contiguous())
         throw std::runtime_error("v_render_colors must be contiguous");
     for (auto* t : {&points, &scale, &quat, &opacity, &ray_o, &ray_d, &tile_offsets, &flatten_ids, &render_alpha,
@@ -549,7 +596,8 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
                             fptr_mut(o.v_quat), fptr_mut(o.v_scale), has(colors) ? fptr_mut(*o.v_colors) : nullptr,
                             fptr_mut(o.v_opacity), ray_grads ? fptr_mut(o.v_ray_o) : nullptr,
                             ray_grads ? fptr_mut(o.v_ray_d) : nullptr, dyn && ray_grads ? fptr_mut(o.v_time) : nullptr,
-                            ws.data_ptr(), size_t(ws.nbytes()), has(fwd_ws) ? 1 : 0, stream()));
+                            ws.data_ptr(), size_t(ws.nbytes()), has(fwd_ws) ? 1 : 0, stream(),
+                            n_isects_ptr(n_isects_dev, points)));
     return o;
 }
 
@@ -870,6 +918,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("isect_regular_tiles", &isect_regular_tiles, py::arg("means2d"), py::arg("radii"), py::arg("depth"),
           py::arg("img_width"), py::arg("img_height"), py::arg("tile_size_x"), py::arg("tile_size_y"),
           py::arg("sort") = true, py::arg("double_buffer") = true);
+    m.def("isect_regular_tiles_async", &isect_regular_tiles_async, py::arg("means2d"), py::arg("radii"),
+          py::arg("depth"), py::arg("img_width"), py::arg("img_height"), py::arg("tile_size_x"),
+          py::arg("tile_size_y"), py::arg("capacity"), py::arg("workspace") = py::none());
     m.def("isect_lidar_tiles",
           [](const Tensor& pack, const Tensor& points, const OptT& vel, const Tensor& scale, const Tensor& quat,
              const OptT& opacity, const Tensor& flag, const Tensor& means2d, const Tensor& radii, const Tensor& depths,
@@ -917,33 +968,36 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("rasterize_eval3d_fwd",
           [](const Tensor& means, const Tensor& quats, const Tensor& scales, const OptT& colors, const Tensor& opac,
              int64_t W, int64_t H, int64_t tsx, int64_t tsy, const Tensor& ray_o, const Tensor& ray_d,
-             const Tensor& offsets, const Tensor& flatten, const OptT& ws) {
+             const Tensor& offsets, const Tensor& flatten, const OptT& ws, const OptT& n_isects) {
               return raster_fwd(means, std::nullopt, quats, scales, colors, opac, W, H, tsx, tsy, ray_o, ray_d,
-                                std::nullopt, offsets, flatten, ws);
+                                std::nullopt, offsets, flatten, ws, n_isects);
           },
           py::arg("means"), py::arg("quats"), py::arg("scales"), py::arg("colors"), py::arg("opacities"),
           py::arg("image_width"), py::arg("image_height"), py::arg("tile_size_width"), py::arg("tile_size_height"),
           py::arg("ray_origs"), py::arg("ray_dirs"), py::arg("tile_offsets"), py::arg("flatten_ids"),
-          py::arg("workspace") = py::none());
+          py::arg("workspace") = py::none(), py::arg("n_isects") = py::none());
     m.def("rasterize_eval3d_dynamic_fwd",
           [](const Tensor& means, const OptT& vel, const Tensor& quats, const Tensor& scales, const OptT& colors,
              const Tensor& opac, int64_t W, int64_t H, int64_t tsx, int64_t tsy, const Tensor& ray_o,
-             const Tensor& ray_d, const OptT& ray_t, const Tensor& offsets, const Tensor& flatten, const OptT& ws) {
+             const Tensor& ray_d, const OptT& ray_t, const Tensor& offsets, const Tensor& flatten, const OptT& ws,
+             const OptT& n_isects) {
               return raster_fwd(means, vel, quats, scales, colors, opac, W, H, tsx, tsy, ray_o, ray_d, ray_t,
-                                offsets, flatten, ws);
+                                offsets, flatten, ws, n_isects);
           },
           py::arg("means"), py::arg("velocity"), py::arg("quats"), py::arg("scales"), py::arg("colors"),
           py::arg("opacities"), py::arg("image_width"), py::arg("image_height"), py::arg("tile_size_width"),
           py::arg("tile_size_height"), py::arg("ray_origs"), py::arg("ray_dirs"), py::arg("ray_time_delta"),
-          py::arg("tile_offsets"), py::arg("flatten_ids"), py::arg("workspace") = py::none());
+          py::arg("tile_offsets"), py::arg("flatten_ids"), py::arg("workspace") = py::none(),
+          py::arg("n_isects") = py::none());
     m.def("rasterize_eval3d_bwd",
           [](const Tensor& points, const Tensor& scale, const Tensor& quat, const Tensor& opacity, const OptT& colors,
              const Tensor& ray_o, const Tensor& ray_d, int64_t tsx, int64_t tsy, const Tensor& offsets,
              const Tensor& flatten, const Tensor& render_alpha, const Tensor& last_ids, const OptT& v_colors,
-             const Tensor& v_depth, const Tensor& v_alpha, bool ray_grads, const OptT& fwd_ws) {
+             const Tensor& v_depth, const Tensor& v_alpha, bool ray_grads, const OptT& fwd_ws,
+             const OptT& n_isects) {
               BwdOut o = raster_bwd(points, std::nullopt, scale, quat, opacity, colors, ray_o, ray_d, std::nullopt,
                                     tsx, tsy, offsets, flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha,
-                                    ray_grads, fwd_ws);
+                                    ray_grads, fwd_ws, n_isects);
               return py::make_tuple(o.v_points, o.v_quat, o.v_scale, o.v_opacity,
                                     o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), opt(o.v_ray_o),
                                     opt(o.v_ray_d));
@@ -952,17 +1006,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("ray_origins"), py::arg("ray_directions"), py::arg("tile_size_x"), py::arg("tile_size_y"),
           py::arg("tile_offsets"), py::arg("flatten_ids"), py::arg("render_alpha"), py::arg("last_ids"),
           py::arg("v_render_colors"), py::arg("v_render_depth"), py::arg("v_render_alpha"),
-          py::arg("ray_grads") = true, py::arg("forward_workspace") = py::none());
+          py::arg("ray_grads") = true, py::arg("forward_workspace") = py::none(), py::arg("n_isects") = py::none());
     m.def("rasterize_eval3d_dynamic_bwd",
           [](const Tensor& points, const Tensor& vel, const Tensor& scale, const Tensor& quat, const Tensor& opacity,
              const OptT& colors, const Tensor& ray_o, const Tensor& ray_d, const Tensor& ray_t, int64_t tsx,
              int64_t tsy, const Tensor& offsets, const Tensor& flatten, const Tensor& render_alpha,
              const Tensor& last_ids, const OptT& v_colors, const Tensor& v_depth, const Tensor& v_alpha,
-             bool ray_grads, const OptT& fwd_ws) {
+             bool ray_grads, const OptT& fwd_ws, const OptT& n_isects) {
               check_tensor(vel, "velocity", points);
               check_tensor(ray_t, "ray_time_delta", points);
               BwdOut o = raster_bwd(points, vel, scale, quat, opacity, colors, ray_o, ray_d, ray_t, tsx, tsy, offsets,
-                                    flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha, ray_grads, fwd_ws);
+                                    flatten, render_alpha, last_ids, v_colors, v_depth, v_alpha, ray_grads, fwd_ws,
+                                    n_isects);
               return py::make_tuple(o.v_points, o.v_velocity, o.v_quat, o.v_scale, o.v_opacity,
                                     o.v_colors.has_value() ? py::cast(*o.v_colors) : py::none(), opt(o.v_ray_o),
                                     opt(o.v_ray_d), opt(o.v_time));
@@ -971,7 +1026,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("colors"), py::arg("ray_origins"), py::arg("ray_directions"), py::arg("ray_time_delta"),
           py::arg("tile_size_x"), py::arg("tile_size_y"), py::arg("tile_offsets"), py::arg("flatten_ids"),
           py::arg("render_alpha"), py::arg("last_ids"), py::arg("v_render_colors"), py::arg("v_render_depth"),
-          py::arg("v_render_alpha"), py::arg("ray_grads") = true, py::arg("forward_workspace") = py::none());
+          py::arg("v_render_alpha"), py::arg("ray_grads") = true, py::arg("forward_workspace") = py::none(),
+          py::arg("n_isects") = py::none());
 
     m.def("spherical_harmonics_fused_fwd", &sh_fwd, py::arg("degree_to_use"), py::arg("origin"),
           py::arg("positions"), py::arg("coeffs"), py::arg("mask"), py::arg("layout_3kn"),

@@ -42,6 +42,7 @@ struct RasterArgs {
     const int32_t* offsets;   // [tiles]
     const int32_t* flatten;   // [n_isects]
     int64_t n_isects;
+    const int64_t* n_isects_dev;  // the list length on the device (n_isects is then its capacity), or null
     int W, H, tsx, tsy, ntx, nty;
     // forward outputs
     float* out_rgb;
@@ -133,9 +134,11 @@ __global__ void pack_records_kernel(const float* __restrict__ means, const float
 // Heavy tiles first: tiles bucketed by floor(log2(intersection count)),
 // buckets in descending order, tile order kept inside a bucket.  One CTA.
 __global__ void __launch_bounds__(1024) tile_order_kernel(const int32_t* __restrict__ offsets, int n_tiles,
-                                                          int32_t n_isects, int32_t* __restrict__ order) {
+                                                          int32_t n_isects, const int64_t* __restrict__ n_isects_dev,
+                                                          int32_t* __restrict__ order) {
     __shared__ int hist[33];
     __shared__ int base[33];
+    if (n_isects_dev) n_isects = int32_t(*n_isects_dev);
     if (threadIdx.x < 33) hist[threadIdx.x] = 0;
     __syncthreads();
     auto bucket = [&](int t) {
@@ -206,7 +209,8 @@ __device__ __forceinline__ TileCtx tile_ctx(const RasterArgs& a) {
     const int64_t last = int64_t(a.W) * a.H - 1;
     c.pix = lin < last ? lin : last;
     c.start = a.offsets[c.tile];
-    c.end = (c.tile == a.ntx * a.nty - 1) ? int32_t(a.n_isects) : a.offsets[c.tile + 1];
+    c.end = (c.tile == a.ntx * a.nty - 1) ? int32_t(a.n_isects_dev ? *a.n_isects_dev : a.n_isects)
+                                          : a.offsets[c.tile + 1];
     return c;
 }
 
@@ -1203,7 +1207,8 @@ __global__ void __launch_bounds__(128, 4) raster_bwd_px2_kernel(RasterArgs a) {
     const bool inA = pxA < a.W && pyA < a.H, inB = pxB < a.W && pyB < a.H;
     const int64_t pixA = int64_t(pyA) * a.W + pxA, pixB = int64_t(pyB) * a.W + pxB;
     const int32_t start = a.offsets[tile];
-    const int32_t end = (tile == a.ntx * a.nty - 1) ? int32_t(a.n_isects) : a.offsets[tile + 1];
+    const int32_t end = (tile == a.ntx * a.nty - 1) ? int32_t(a.n_isects_dev ? *a.n_isects_dev : a.n_isects)
+                                                    : a.offsets[tile + 1];
 
     // pixels outside the image get a harmless ray and never contribute
     const v3 o_ref = ld3(a.ray_o);
@@ -1617,7 +1622,7 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
                       int tsx, int tsy, const float* ray_o, const float* ray_d, const float* ray_time_delta,
                       const int32_t* tile_offsets, int tiles_w, int tiles_h, const int32_t* flatten_ids,
                       int64_t n_isects, float* renders, float* depths, float* alphas, int32_t* last_ids,
-                      void* workspace, size_t ws_bytes, xsg_stream_t stream) {
+                      void* workspace, size_t ws_bytes, xsg_stream_t stream, const int64_t* n_isects_dev) {
     int rc = check_common(n_gauss, W, H, tsx, tsy, tiles_w, tiles_h, n_isects, cdim);
     if (rc != XSG_OK) return rc;
     XSG_REQUIRE(means && quats && scales && opacities && ray_o && ray_d && tile_offsets && depths && alphas &&
@@ -1643,14 +1648,15 @@ int xsg_rasterize_fwd(const float* means, const float* velocity, const float* qu
         (masks && px2_layout(cdim, dyn, tsx, tsy))
             ? reinterpret_cast<unsigned long long*>(masks + px2_stats_word(n_isects, n_tiles, tsx * tsy))
             : nullptr;
-    if (order) launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
+    if (order)
+        launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), n_isects_dev, order);
     if (n_gauss > 0)
         launch(pack_records_kernel, blocks_for(n_gauss, 256), 256, 0, st, means, velocity, quats, scales, opacities,
                n_gauss, rec, ray_o, ext, px2_stats);
     RasterArgs a{};
     a.rec = rec; a.ext = n_gauss > 0 ? ext : nullptr; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
     a.ray_o = ray_o; a.ray_d = ray_d; a.ray_t = ray_time_delta;
-    a.offsets = tile_offsets; a.flatten = flatten_ids; a.n_isects = n_isects;
+    a.offsets = tile_offsets; a.flatten = flatten_ids; a.n_isects = n_isects; a.n_isects_dev = n_isects_dev;
     a.W = W; a.H = H; a.tsx = tsx; a.tsy = tsy; a.ntx = tiles_w; a.nty = tiles_h;
     a.out_rgb = renders; a.out_depth = depths; a.out_alpha = alphas; a.out_last = last_ids;
     a.pair_counters = g_pair_counters;
@@ -1677,7 +1683,7 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
                       const float* v_renders, const float* v_depths, const float* v_alphas, float* v_means,
                       float* v_velocity, float* v_quats, float* v_scales, float* v_colors, float* v_opacities,
                       float* v_ray_o, float* v_ray_d, float* v_ray_time_delta, void* workspace, size_t ws_bytes,
-                      int workspace_from_forward, xsg_stream_t stream) {
+                      int workspace_from_forward, xsg_stream_t stream, const int64_t* n_isects_dev) {
     int rc = check_common(n_gauss, W, H, tsx, tsy, tiles_w, tiles_h, n_isects, cdim);
     if (rc != XSG_OK) return rc;
     const bool dyn = velocity != nullptr;
@@ -1713,7 +1719,8 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     // writes its v_ray_o / v_ray_d (/ v_ray_time_delta): no pre-zeroing
     // the forward's workspace already holds the tile order, records and view constants
     if (order && !reuse)
-        launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), order);
+        launch(tile_order_kernel, 1, 1024, 0, st, tile_offsets, int(n_tiles), int32_t(n_isects), n_isects_dev,
+               order);
     if (n_gauss > 0) {
         XSG_CUDA(cudaMemsetAsync(G, 0, size_t(n_gauss) * na * sizeof(float), st));
         if (cdim > 4) XSG_CUDA(cudaMemsetAsync(v_colors, 0, size_t(n_gauss) * cdim * sizeof(float), st));
@@ -1724,7 +1731,7 @@ int xsg_rasterize_bwd(const float* means, const float* velocity, const float* qu
     RasterArgs a{};
     a.rec = rec; a.ext = n_gauss > 0 ? ext : nullptr; a.means = means; a.quats = quats; a.scales = scales; a.colors = colors;
     a.ray_o = ray_o; a.ray_d = ray_d; a.ray_t = ray_time_delta;
-    a.offsets = tile_offsets; a.flatten = flatten_ids; a.n_isects = n_isects;
+    a.offsets = tile_offsets; a.flatten = flatten_ids; a.n_isects = n_isects; a.n_isects_dev = n_isects_dev;
     a.W = W; a.H = H; a.tsx = tsx; a.tsy = tsy; a.ntx = tiles_w; a.nty = tiles_h;
     a.render_alpha = render_alphas; a.last_ids = last_ids;
     a.v_rgb = v_renders; a.v_depth = v_depths; a.v_alpha = v_alphas;

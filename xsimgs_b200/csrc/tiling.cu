@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kTileThreads)
                         int bucket_neg, const uint32_t* __restrict__ order,
                         const int64_t* __restrict__ offsets, uint32_t* __restrict__ bucket_keys,
                         uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
-                        int32_t* __restrict__ flatten_ids, const int64_t* __restrict__ n_dev) {
+                        int32_t* __restrict__ flatten_ids, const int64_t* __restrict__ n_dev, int64_t cap) {
     const int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
     const bool in = p < (n_dev ? *n_dev : n_items);
@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(kTileThreads)
     const int64_t off0 = cnt > 0 ? offsets[p] : 0;
     const int32_t bits = has ? __float_as_int(depths[g]) : 0;
     auto put = [&](int64_t off, int x, int y, int32_t b, uint32_t gg) {
+        if (off >= cap) return;  // capacity-bounded output: the rest is dropped, the count says so
         const uint32_t tile = uint32_t(y) * uint32_t(ntx) + uint32_t(x);
         if constexpr (kSorted) {
             bucket_keys[off] = b < 0 ? uint32_t(bucket_neg) : tile;
@@ -187,6 +188,44 @@ __global__ void offset_encode_kernel(const int64_t* __restrict__ ids, int64_t n,
         const int64_t prev = tile_of(ids[idx - 1]);
         for (int64_t t = max(prev + 1, int64_t(0)); t < cur + 1 && t < n_tiles; ++t) offsets[t] = int32_t(idx);
     }
+}
+
+// The same with the intersection count on the device (`n_dev`, at most the
+// capacity the grid is sized for); no intersections -> all offsets 0.
+__global__ void offset_encode_dev_kernel(const int64_t* __restrict__ ids, const int64_t* __restrict__ n_dev,
+                                         int64_t n_tiles, int tb, int32_t* __restrict__ offsets) {
+    const int64_t n = *n_dev;
+    const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (n == 0) {
+        for (int64_t t = idx; t < n_tiles; t += int64_t(gridDim.x) * blockDim.x) offsets[t] = 0;
+        return;
+    }
+    if (idx >= n) return;
+    auto tile_of = [&](int64_t key) {
+        const int64_t hi = key >> 32;
+        return (hi >> tb) * n_tiles + (hi & ((int64_t(1) << tb) - 1));
+    };
+    const int64_t hc = ids[idx] >> 32;
+    const int64_t cur = tile_of(ids[idx]);
+    if (idx == 0)
+        for (int64_t t = 0; t < cur + 1 && t < n_tiles; ++t) offsets[t] = 0;
+    if (idx == n - 1)
+        for (int64_t t = max(cur + 1, int64_t(0)); t < n_tiles; ++t) offsets[t] = int32_t(n);
+    if (idx > 0) {
+        const int64_t hp = ids[idx - 1] >> 32;
+        if (hp == hc) return;
+        const int64_t prev = tile_of(ids[idx - 1]);
+        for (int64_t t = max(prev + 1, int64_t(0)); t < cur + 1 && t < n_tiles; ++t) offsets[t] = int32_t(idx);
+    }
+}
+
+// counts[0] = the intersection total, counts[1] = min(total, cap): the
+// number of intersections written and sorted
+__global__ void clamp_count_kernel(const unsigned long long* __restrict__ total, int64_t cap,
+                                   int64_t* __restrict__ counts) {
+    const int64_t t = int64_t(*total);
+    counts[0] = t;
+    counts[1] = t < cap ? t : cap;
 }
 
 // ------------------------------------------------ spherical / lidar grid --
@@ -484,7 +523,7 @@ static int sort_isect_pairs_inplace(int64_t* ids, int32_t* flat, int64_t n, int 
 template <typename Emit>
 static int sorted_isects(const int32_t* counts, const float* depths, int64_t n, int64_t n_isects,
                          int64_t n_tiles, const IsectWs& w, int64_t* isect_ids, int32_t* flatten_ids,
-                         cudaStream_t st, Emit&& emit) {
+                         cudaStream_t st, Emit&& emit, const int64_t* n_isects_dev = nullptr) {
     // 1. compact visible Gaussians (count > 0); their number goes to scan_out[n]
     int rc = exclusive_scan<int32_t, true>(counts, n, w.scan_out, w.scan_out + n, w.scan_tmp, st);
     if (rc != XSG_OK) return rc;
@@ -503,7 +542,7 @@ static int sorted_isects(const int32_t* counts, const float* depths, int64_t n, 
     // 4. stable counting passes on the tile bits (up to 8 bits each), the
     //    last of which writes the outputs
     IsectEpilogue ep{depths, isect_ids, flatten_ids};
-    return counting_sort(w.bk, w.bv, w.bk2, w.bv2, n_isects, nullptr, tile_bits_for(n_tiles), 8, w, st, &ep,
+    return counting_sort(w.bk, w.bv, w.bk2, w.bv2, n_isects, n_isects_dev, tile_bits_for(n_tiles), 8, w, st, &ep,
                          nullptr, nullptr);
 }
 
@@ -561,7 +600,7 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
         if (rc != XSG_OK) return rc;
         launch(regular_emit_kernel<false>, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
             m2, r2, depths, n, ts, ntx, nty, 0, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
-            static_cast<const int64_t*>(nullptr));
+            static_cast<const int64_t*>(nullptr), INT64_MAX);
         return check_launch("isect_regular_emit");
     }
     const int64_t n_tiles = int64_t(ntx) * nty;
@@ -571,8 +610,53 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
                          [&](const uint32_t* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
                              launch(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st,
                                  m2, r2, depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv,
-                                 nullptr, nullptr, n_vis);
+                                 nullptr, nullptr, n_vis, INT64_MAX);
                          });
+}
+
+int xsg_isect_regular_tiles_async(const float* means2d, const float* radii, const float* depths, int64_t n, int W,
+                                  int H, int tsx, int tsy, int64_t capacity, int32_t* counts, int64_t* isect_ids,
+                                  int32_t* flatten_ids, int32_t* offsets, int64_t* n_isects_dev, void* workspace,
+                                  size_t ws_bytes, xsg_stream_t stream) {
+    XSG_REQUIRE(n >= 0 && W > 0 && H > 0 && tsx > 0 && tsy > 0 && capacity > 0 && capacity < (int64_t(1) << 31),
+                "isect_regular_tiles_async: bad arguments");
+    XSG_REQUIRE(offsets && n_isects_dev && isect_ids && flatten_ids && (n == 0 || (means2d && radii && depths && counts)),
+                "isect_regular_tiles_async: null argument");
+    cudaStream_t st = as_cuda(stream);
+    IsectWs w;
+    const size_t need = isect_ws_layout(n, capacity, workspace, ws_bytes, &w);
+    if (ws_bytes < need || !workspace) return set_error(XSG_ERR_WORKSPACE, "isect_regular_tiles_async: workspace too small");
+    const int ntx = (W + tsx - 1) / tsx, nty = (H + tsy - 1) / tsy;
+    const int64_t n_tiles = int64_t(ntx) * nty;
+    const float2 ts = make_float2(float(tsx), float(tsy));
+    auto* m2 = reinterpret_cast<const float2*>(means2d);
+    auto* r2 = reinterpret_cast<const float2*>(radii);
+    XSG_CUDA(cudaMemsetAsync(w.total, 0, sizeof(unsigned long long), st));
+    {
+        ScopedTimer tm("isect_count", st);
+        if (n > 0)
+            launch(regular_count_kernel, blocks_for(n, kTileThreads), kTileThreads, 0, st, m2, r2, n, ts, ntx, nty,
+                   counts, w.total);
+        launch(clamp_count_kernel, 1, 1, 0, st, static_cast<const unsigned long long*>(w.total), capacity,
+               n_isects_dev);
+    }
+    const int64_t* n_written = n_isects_dev + 1;
+    if (n > 0) {
+        const int bucket_neg = int((int64_t(1) << tile_bits_for(n_tiles)) - 1);
+        ScopedTimer tm("isect_emit_sort", st);
+        const int rc = sorted_isects(
+            counts, depths, n, capacity, n_tiles, w, isect_ids, flatten_ids, st,
+            [&](const uint32_t* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
+                launch(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st, m2, r2,
+                       depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv, nullptr, nullptr, n_vis,
+                       capacity);
+            },
+            n_written);
+        if (rc != XSG_OK) return rc;
+    }
+    launch(offset_encode_dev_kernel, blocks_for(capacity, 256), 256, 0, st, static_cast<const int64_t*>(isect_ids),
+           n_written, n_tiles, tile_bits_for(n_tiles), offsets);
+    return check_launch("isect_regular_tiles_async");
 }
 
 static SphTiling make_sph_tiling(int lidar, const float* elev_bounds, int n_elev, int tsx, int tsy, float W,

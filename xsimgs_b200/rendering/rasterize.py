@@ -12,7 +12,7 @@ from ..utils import apply_grad_mask
 class UTGSRasterize(torch.autograd.Function):
     @staticmethod
     def forward(ctx, positions, rotation, scale, density, colors, ray_o, ray_d,
-                isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int):
+                isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int, n_isects=None):
         height, width = ray_o.shape[:2]
         channels = colors.shape[-1] if colors is not None else 0
         ws = torch.empty(_C.rasterize_workspace_size(positions.shape[0], channels, n_isects=flatten_ids.numel(),
@@ -34,9 +34,11 @@ class UTGSRasterize(torch.autograd.Function):
             tile_offsets=isect_offsets,
             flatten_ids=flatten_ids,
             workspace=ws,
+            n_isects=n_isects,
         )
         # the backward reuses the forward's packed records and tile order
         ctx.workspace = ws
+        ctx.n_isects = n_isects
         ctx.tile_size_x = tile_size_x
         ctx.tile_size_y = tile_size_y
         ctx.save_for_backward(positions, rotation, scale, density, colors, ray_o, ray_d,
@@ -57,12 +59,15 @@ class UTGSRasterize(torch.autograd.Function):
             grad_depth.contiguous(),
             grad_alpha.contiguous(),
             forward_workspace=ctx.workspace,
+            n_isects=ctx.n_isects,
             ray_grads=bool(ctx.needs_input_grad[5] or ctx.needs_input_grad[6]),
         )
-        return apply_grad_mask(ctx, list(grads) + [None, None, None, None])
+        return apply_grad_mask(ctx, list(grads) + [None, None, None, None, None])
 
 
 def ut_gs_rasterize(positions, rotation, scale, density, colors, ray_o, ray_d,
-                    isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int):
+                    isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int, n_isects=None):
+    """`n_isects` (not in the reference): an int64 device tensor holding the
+    length of a capacity-sized `flatten_ids` (isect_regular_tiles_async)."""
     return UTGSRasterize.apply(positions, rotation, scale, density, colors, ray_o, ray_d,
-                               isect_offsets, flatten_ids, tile_size_x, tile_size_y)
+                               isect_offsets, flatten_ids, tile_size_x, tile_size_y, n_isects)

@@ -12,7 +12,7 @@ from ..utils import apply_grad_mask
 class UTGSDynamicRasterize(torch.autograd.Function):
     @staticmethod
     def forward(ctx, positions, velocity, rotation, scale, density, colors, ray_o, ray_d,
-                ray_time_delta, isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int):
+                ray_time_delta, isect_offsets, flatten_ids, tile_size_x: int, tile_size_y: int, n_isects=None):
         height, width = ray_o.shape[:2]
         channels = colors.shape[-1] if colors is not None else 0
         ws = torch.empty(_C.rasterize_workspace_size(positions.shape[0], channels, n_isects=flatten_ids.numel(),
@@ -36,9 +36,11 @@ class UTGSDynamicRasterize(torch.autograd.Function):
             tile_offsets=isect_offsets,
             flatten_ids=flatten_ids,
             workspace=ws,
+            n_isects=n_isects,
         )
         # the backward reuses the forward's packed records and tile order
         ctx.workspace = ws
+        ctx.n_isects = n_isects
         ctx.tile_size_x = tile_size_x
         ctx.tile_size_y = tile_size_y
         ctx.save_for_backward(positions, velocity, rotation, scale, density, colors,
@@ -60,14 +62,16 @@ class UTGSDynamicRasterize(torch.autograd.Function):
             grad_depth.contiguous(),
             grad_alpha.contiguous(),
             forward_workspace=ctx.workspace,
+            n_isects=ctx.n_isects,
             ray_grads=bool(ctx.needs_input_grad[6] or ctx.needs_input_grad[7] or ctx.needs_input_grad[8]),
         )
-        return apply_grad_mask(ctx, list(grads) + [None, None, None, None])
+        return apply_grad_mask(ctx, list(grads) + [None, None, None, None, None])
 
 
 def ut_gs_dynamic_rasterize(positions, velocity, rotation, scale, density, colors, ray_o, ray_d,
                             ray_time_delta, isect_offsets, flatten_ids, tile_size_x: int,
-                            tile_size_y: int):
+                            tile_size_y: int, n_isects=None):
+    """`n_isects` as in ut_gs_rasterize."""
     return UTGSDynamicRasterize.apply(positions, velocity, rotation, scale, density, colors,
                                       ray_o, ray_d, ray_time_delta, isect_offsets, flatten_ids,
-                                      tile_size_x, tile_size_y)
+                                      tile_size_x, tile_size_y, n_isects)
