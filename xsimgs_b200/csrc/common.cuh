@@ -39,6 +39,33 @@ inline void launch(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st
     kernel<<<grid, block, smem, st>>>(args...);
 }
 
+// Programmatic dependent launch (sm_90+): the kernel may be scheduled while
+// its predecessor in the stream is still finishing its last CTAs; it must
+// call pdl_wait() before its first global memory access (read or write), which
+// returns once the predecessor has completed and its writes are visible.
+// Chains of short dependent kernels (scans, sort passes) so lose the launch
+// gap and the predecessor's tail.  Kernels launched this way call
+// pdl_trigger() to let their own dependents be scheduled; the trigger takes
+// effect once every CTA of the grid has issued it or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... P, typename... A>
+inline void launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... args) {
+    count_launch();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    (void)cudaLaunchKernelEx(&cfg, kernel, static_cast<P>(args)...);  // errors surface in check_launch
+}
+
 // Optional per-kernel device timing (xsg_timing_enable): records a CUDA event
 // pair on `st` around the scope when enabled.
 struct ScopedTimer {

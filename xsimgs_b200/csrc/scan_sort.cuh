@@ -51,6 +51,8 @@ template <typename T, bool kPred>
 __global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(const T* __restrict__ in, int64_t n,
                                                                    int64_t* __restrict__ block_sums,
                                                                    const int64_t* __restrict__ n_dev) {
+    pdl_wait();
+    pdl_trigger();
     if (n_dev) n = *n_dev;
     const int64_t base = int64_t(blockIdx.x) * kScanChunk;
     int64_t s = 0;
@@ -72,6 +74,8 @@ template <typename T, bool kPred>
 __global__ void __launch_bounds__(kScanThreads)
     scan_apply_kernel(const T* __restrict__ in, int64_t n, const int64_t* __restrict__ block_offsets,
                       int64_t* __restrict__ out, int64_t* __restrict__ total, const int64_t* __restrict__ n_dev) {
+    pdl_wait();
+    pdl_trigger();
     if (n_dev) n = *n_dev;
     const int64_t base = int64_t(blockIdx.x) * kScanChunk + int64_t(threadIdx.x) * kScanItems;
     int64_t vals[kScanItems];
@@ -95,6 +99,8 @@ __global__ void __launch_bounds__(kScanThreads)
 
 // Single-block exclusive scan of up to any length (loops in chunks).
 __global__ void __launch_bounds__(1024) scan_small_kernel(int64_t* __restrict__ v, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int64_t carry;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
@@ -129,9 +135,9 @@ int exclusive_scan(const T* in, int64_t n, int64_t* out, int64_t* total, void* t
     }
     const int64_t nb = (n + kScanChunk - 1) / kScanChunk;
     int64_t* bs = static_cast<int64_t*>(tmp);
-    launch(scan_reduce_kernel<T, kPred>, unsigned(nb), kScanThreads, 0, st, in, n, bs, n_dev);
-    launch(scan_small_kernel, 1, 1024, 0, st, bs, nb);
-    launch(scan_apply_kernel<T, kPred>, unsigned(nb), kScanThreads, 0, st, in, n, static_cast<const int64_t*>(bs),
+    launch_pdl(scan_reduce_kernel<T, kPred>, unsigned(nb), kScanThreads, 0, st, in, n, bs, n_dev);
+    launch_pdl(scan_small_kernel, 1, 1024, 0, st, bs, nb);
+    launch_pdl(scan_apply_kernel<T, kPred>, unsigned(nb), kScanThreads, 0, st, in, n, static_cast<const int64_t*>(bs),
            out, total, n_dev);
     return check_launch("exclusive_scan");
 }
@@ -185,6 +191,8 @@ template <bool kBinMajor>
 __global__ void __launch_bounds__(32)
     cs_hist_kernel(const uint32_t* __restrict__ keys, int64_t n, const int64_t* __restrict__ n_dev, CsDigit dg,
                    int nbins, int32_t* __restrict__ counts) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ int32_t h[];
     const int lane = threadIdx.x;
     if (n_dev) n = *n_dev;
@@ -206,6 +214,8 @@ constexpr int kCsColRows = (4 * 148 + 31) / 32;
 __global__ void __launch_bounds__(1024)
     cs_colscan_kernel(const int32_t* __restrict__ counts, int G, int nbins, int32_t* __restrict__ offs,
                       int64_t* __restrict__ totals) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int32_t part[32][33];
     const int c = threadIdx.x & 31, g = threadIdx.x >> 5;
     const int b = blockIdx.x * 32 + c;
@@ -243,6 +253,8 @@ __global__ void __launch_bounds__(1024)
 // starts[b] = totals[< b]; one CTA.
 __global__ void __launch_bounds__(1024) cs_starts_kernel(const int64_t* __restrict__ totals, int nbins,
                                                          int64_t* __restrict__ starts) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int64_t carry;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
@@ -266,6 +278,8 @@ __global__ void __launch_bounds__(32)
                       const int64_t* __restrict__ n_dev, CsDigit dg, int nbins, const int64_t* __restrict__ pos0,
                       const int32_t* __restrict__ offs, const int64_t* __restrict__ starts,
                       uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, IsectEpilogue ep) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ int32_t cur[];  // positions < n < 2^31
     const int lane = threadIdx.x;
     if (n_dev) n = *n_dev;
@@ -366,15 +380,15 @@ inline int counting_pass(const uint32_t* keys, const uint32_t* vals, uint32_t* k
         int64_t* pos0 = a.take<int64_t>(size_t(mat + 1));
         void* stmp = a.take<char>(scan_workspace_bytes(mat));
         if (!counts || !pos0 || !stmp) return set_error(XSG_ERR_WORKSPACE, "counting pass: workspace too small");
-        launch(cs_hist_kernel<true>, G, 32, smem, st, keys, n, n_dev, dg, nbins, counts);
+        launch_pdl(cs_hist_kernel<true>, G, 32, smem, st, keys, n, n_dev, dg, nbins, counts);
         int rc = exclusive_scan<int32_t>(counts, mat, pos0, nullptr, stmp, st);
         if (rc != XSG_OK) return rc;
         const int64_t* p0 = pos0;
         if (ep)
-            launch(cs_scatter_kernel<true, true>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins, p0,
+            launch_pdl(cs_scatter_kernel<true, true>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins, p0,
                    static_cast<const int32_t*>(nullptr), static_cast<const int64_t*>(nullptr), nullptr, nullptr, e);
         else
-            launch(cs_scatter_kernel<true, false>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins, p0,
+            launch_pdl(cs_scatter_kernel<true, false>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins, p0,
                    static_cast<const int32_t*>(nullptr), static_cast<const int64_t*>(nullptr), keys_out, vals_out, e);
         return check_launch("counting_pass");
     }
@@ -382,17 +396,17 @@ inline int counting_pass(const uint32_t* keys, const uint32_t* vals, uint32_t* k
     int64_t* totals = a.take<int64_t>(size_t(nbins + 1));
     int64_t* starts = a.take<int64_t>(size_t(nbins + 1));
     if (!counts || !offs || !totals || !starts) return set_error(XSG_ERR_WORKSPACE, "counting pass: workspace too small");
-    launch(cs_hist_kernel<false>, G, 32, smem, st, keys, n, n_dev, dg, nbins, counts);
-    launch(cs_colscan_kernel, unsigned((nbins + 31) / 32), 1024, 0, st, static_cast<const int32_t*>(counts), G,
+    launch_pdl(cs_hist_kernel<false>, G, 32, smem, st, keys, n, n_dev, dg, nbins, counts);
+    launch_pdl(cs_colscan_kernel, unsigned((nbins + 31) / 32), 1024, 0, st, static_cast<const int32_t*>(counts), G,
            nbins, offs, totals);
-    launch(cs_starts_kernel, 1, 1024, 0, st, static_cast<const int64_t*>(totals), nbins, starts);
+    launch_pdl(cs_starts_kernel, 1, 1024, 0, st, static_cast<const int64_t*>(totals), nbins, starts);
     const int32_t* of = offs;
     const int64_t* sts = starts;
     if (ep)
-        launch(cs_scatter_kernel<false, true>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins,
+        launch_pdl(cs_scatter_kernel<false, true>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins,
                static_cast<const int64_t*>(nullptr), of, sts, nullptr, nullptr, e);
     else
-        launch(cs_scatter_kernel<false, false>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins,
+        launch_pdl(cs_scatter_kernel<false, false>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins,
                static_cast<const int64_t*>(nullptr), of, sts, keys_out, vals_out, e);
     return check_launch("counting_pass");
 }

@@ -77,6 +77,8 @@ __global__ void __launch_bounds__(kTileThreads)
     regular_count_kernel(const float2* __restrict__ means2d, const float2* __restrict__ radii, int64_t n,
                          float2 ts, int ntx, int nty, int32_t* __restrict__ counts,
                          unsigned long long* __restrict__ total) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     int c = 0;
     if (i < n) {
@@ -99,6 +101,8 @@ __global__ void __launch_bounds__(kTileThreads)
                         const int64_t* __restrict__ offsets, uint32_t* __restrict__ bucket_keys,
                         uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
                         int32_t* __restrict__ flatten_ids, const int64_t* __restrict__ n_dev, int64_t cap) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
     const bool in = p < (n_dev ? *n_dev : n_items);
@@ -153,6 +157,8 @@ __global__ void __launch_bounds__(kTileThreads)
 __global__ void compact_visible_kernel(const int32_t* __restrict__ counts, const int64_t* __restrict__ pos,
                                        const float* __restrict__ depths, int64_t n,
                                        uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n || counts[i] <= 0) return;
     const int64_t p = pos[i];
@@ -162,6 +168,8 @@ __global__ void compact_visible_kernel(const int32_t* __restrict__ counts, const
 
 __global__ void gather_counts_kernel(const int32_t* __restrict__ counts, const uint32_t* __restrict__ order,
                                      int64_t n, int32_t* __restrict__ out, const int64_t* __restrict__ n_dev) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i < (n_dev ? *n_dev : n)) out[i] = counts[order[i]];
 }
@@ -170,6 +178,8 @@ __global__ void gather_counts_kernel(const int32_t* __restrict__ counts, const u
 // is the first intersection index whose tile is >= t.
 __global__ void offset_encode_kernel(const int64_t* __restrict__ ids, int64_t n, int64_t n_tiles, int tb,
                                      int32_t* __restrict__ offsets) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= n) return;
     auto tile_of = [&](int64_t key) {
@@ -194,6 +204,8 @@ __global__ void offset_encode_kernel(const int64_t* __restrict__ ids, int64_t n,
 // capacity the grid is sized for); no intersections -> all offsets 0.
 __global__ void offset_encode_dev_kernel(const int64_t* __restrict__ ids, const int64_t* __restrict__ n_dev,
                                          int64_t n_tiles, int tb, int32_t* __restrict__ offsets) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t n = *n_dev;
     const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (n == 0) {
@@ -223,6 +235,8 @@ __global__ void offset_encode_dev_kernel(const int64_t* __restrict__ ids, const 
 // number of intersections written and sorted
 __global__ void clamp_count_kernel(const unsigned long long* __restrict__ total, int64_t cap,
                                    int64_t* __restrict__ counts) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t t = int64_t(*total);
     counts[0] = t;
     counts[1] = t < cap ? t : cap;
@@ -343,6 +357,8 @@ template <typename Cam>
 __global__ void __launch_bounds__(kTileThreads / 2)
     sph_count_kernel(SphInputs in, SphTiling T, UTParams up, int64_t n, int32_t* __restrict__ counts,
                      unsigned long long* __restrict__ total) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     int c = 0;
     if (i < n) {
@@ -366,6 +382,8 @@ __global__ void __launch_bounds__(kTileThreads / 2)
                     const int64_t* __restrict__ offsets, uint32_t* __restrict__ bucket_keys,
                     uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
                     int32_t* __restrict__ flatten_ids, int bucket_neg) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (p >= n_items) return;
     const uint32_t g = kSorted ? order[p] : uint32_t(p);
@@ -448,6 +466,8 @@ static size_t isect_ws_layout(int64_t n, int64_t m, void* base, size_t cap, Isec
 
 __global__ void split_key_kernel(const int64_t* __restrict__ ids, int64_t n, uint32_t* __restrict__ lo,
                                  uint32_t* __restrict__ idx) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
     lo[i] = uint32_t(uint64_t(ids[i]));
@@ -456,6 +476,8 @@ __global__ void split_key_kernel(const int64_t* __restrict__ ids, int64_t n, uin
 
 __global__ void gather_hi_kernel(const int64_t* __restrict__ ids, const uint32_t* __restrict__ perm, int64_t n,
                                  int tb, uint32_t* __restrict__ hi, uint32_t* __restrict__ idx) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (j >= n) return;
     const uint32_t p = perm[j];
@@ -466,6 +488,8 @@ __global__ void gather_hi_kernel(const int64_t* __restrict__ ids, const uint32_t
 __global__ void permute_isects_kernel(const int64_t* __restrict__ kin, const int32_t* __restrict__ fin,
                                       const uint32_t* __restrict__ perm, int64_t n, int64_t* __restrict__ kout,
                                       int32_t* __restrict__ fout) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (j >= n) return;
     const uint32_t p = perm[j];
@@ -500,18 +524,18 @@ static int counting_sort(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1,
 // [0, 32 + tb), in place: by the depth word, then stably by the tile bits.
 static int sort_isect_pairs_inplace(int64_t* ids, int32_t* flat, int64_t n, int tb, const struct IsectWs& w,
                                     cudaStream_t st) {
-    launch(split_key_kernel, blocks_for(n, 256), 256, 0, st, ids, n, w.bk, w.bv);
+    launch_pdl(split_key_kernel, blocks_for(n, 256), 256, 0, st, ids, n, w.bk, w.bv);
     uint32_t *ks, *vs;
     int rc = counting_sort(w.bk, w.bv, w.bk2, w.bv2, n, nullptr, 32, 11, w, st, nullptr, &ks, &vs);
     if (rc != XSG_OK) return rc;
     uint32_t* k2 = (ks == w.bk) ? w.bk2 : w.bk;
     uint32_t* v2 = (vs == w.bv) ? w.bv2 : w.bv;
-    launch(gather_hi_kernel, blocks_for(n, 256), 256, 0, st, ids, vs, n, tb, k2, v2);
+    launch_pdl(gather_hi_kernel, blocks_for(n, 256), 256, 0, st, ids, vs, n, tb, k2, v2);
     rc = counting_sort(k2, v2, ks, vs, n, nullptr, tb, 8, w, st, nullptr, &ks, &vs);
     if (rc != XSG_OK) return rc;
     XSG_CUDA(cudaMemcpyAsync(w.kcopy, ids, size_t(n) * 8, cudaMemcpyDeviceToDevice, st));
     XSG_CUDA(cudaMemcpyAsync(w.fcopy, flat, size_t(n) * 4, cudaMemcpyDeviceToDevice, st));
-    launch(permute_isects_kernel, blocks_for(n, 256), 256, 0, st, w.kcopy, w.fcopy, vs, n, ids, flat);
+    launch_pdl(permute_isects_kernel, blocks_for(n, 256), 256, 0, st, w.kcopy, w.fcopy, vs, n, ids, flat);
     return check_launch("sort_isect_pairs");
 }
 
@@ -528,14 +552,14 @@ static int sorted_isects(const int32_t* counts, const float* depths, int64_t n, 
     int rc = exclusive_scan<int32_t, true>(counts, n, w.scan_out, w.scan_out + n, w.scan_tmp, st);
     if (rc != XSG_OK) return rc;
     const int64_t* n_vis = w.scan_out + n;
-    launch(compact_visible_kernel, blocks_for(n, 256), 256, 0, st, counts, static_cast<const int64_t*>(w.scan_out),
+    launch_pdl(compact_visible_kernel, blocks_for(n, 256), 256, 0, st, counts, static_cast<const int64_t*>(w.scan_out),
            depths, n, w.gk, w.gv);
     // 2. stable sort by the 32 depth bits: three counting passes (11 + 11 + 10 bits)
     uint32_t* order = nullptr;
     rc = counting_sort(w.gk, w.gv, w.gk2, w.gv2, n, n_vis, 32, 11, w, st, nullptr, nullptr, &order);
     if (rc != XSG_OK) return rc;
     // 3. counts in depth order -> emission offsets
-    launch(gather_counts_kernel, blocks_for(n, 256), 256, 0, st, counts, order, n, w.cnt_sorted, n_vis);
+    launch_pdl(gather_counts_kernel, blocks_for(n, 256), 256, 0, st, counts, order, n, w.cnt_sorted, n_vis);
     rc = exclusive_scan<int32_t>(w.cnt_sorted, n, w.scan_out, nullptr, w.scan_tmp, st, n_vis);
     if (rc != XSG_OK) return rc;
     emit(order, static_cast<const int64_t*>(w.scan_out), n, n_vis);
@@ -569,7 +593,7 @@ int xsg_isect_regular_count(const float* means2d, const float* radii, int64_t n,
     const int ntx = (W + tsx - 1) / tsx, nty = (H + tsy - 1) / tsy;
     ScopedTimer tm("isect_count", st);
     if (n > 0)
-        launch(regular_count_kernel, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
+        launch_pdl(regular_count_kernel, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
             reinterpret_cast<const float2*>(means2d), reinterpret_cast<const float2*>(radii), n,
             make_float2(float(tsx), float(tsy)), ntx, nty, counts, w.total);
     unsigned long long tot = 0;
@@ -598,7 +622,7 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
     if (!sort) {
         int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
         if (rc != XSG_OK) return rc;
-        launch(regular_emit_kernel<false>, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
+        launch_pdl(regular_emit_kernel<false>, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
             m2, r2, depths, n, ts, ntx, nty, 0, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
             static_cast<const int64_t*>(nullptr), INT64_MAX);
         return check_launch("isect_regular_emit");
@@ -608,7 +632,7 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
     ScopedTimer tm("isect_emit_sort", st);
     return sorted_isects(counts, depths, n, n_isects, n_tiles, w, isect_ids, flatten_ids, st,
                          [&](const uint32_t* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
-                             launch(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st,
+                             launch_pdl(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st,
                                  m2, r2, depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv,
                                  nullptr, nullptr, n_vis, INT64_MAX);
                          });
@@ -635,9 +659,9 @@ int xsg_isect_regular_tiles_async(const float* means2d, const float* radii, cons
     {
         ScopedTimer tm("isect_count", st);
         if (n > 0)
-            launch(regular_count_kernel, blocks_for(n, kTileThreads), kTileThreads, 0, st, m2, r2, n, ts, ntx, nty,
+            launch_pdl(regular_count_kernel, blocks_for(n, kTileThreads), kTileThreads, 0, st, m2, r2, n, ts, ntx, nty,
                    counts, w.total);
-        launch(clamp_count_kernel, 1, 1, 0, st, static_cast<const unsigned long long*>(w.total), capacity,
+        launch_pdl(clamp_count_kernel, 1, 1, 0, st, static_cast<const unsigned long long*>(w.total), capacity,
                n_isects_dev);
     }
     const int64_t* n_written = n_isects_dev + 1;
@@ -647,14 +671,14 @@ int xsg_isect_regular_tiles_async(const float* means2d, const float* radii, cons
         const int rc = sorted_isects(
             counts, depths, n, capacity, n_tiles, w, isect_ids, flatten_ids, st,
             [&](const uint32_t* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
-                launch(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st, m2, r2,
+                launch_pdl(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st, m2, r2,
                        depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv, nullptr, nullptr, n_vis,
                        capacity);
             },
             n_written);
         if (rc != XSG_OK) return rc;
     }
-    launch(offset_encode_dev_kernel, blocks_for(capacity, 256), 256, 0, st, static_cast<const int64_t*>(isect_ids),
+    launch_pdl(offset_encode_dev_kernel, blocks_for(capacity, 256), 256, 0, st, static_cast<const int64_t*>(isect_ids),
            n_written, n_tiles, tile_bits_for(n_tiles), offsets);
     return check_launch("isect_regular_tiles_async");
 }
@@ -710,7 +734,7 @@ int xsg_isect_spherical_count(int lidar, const float* pack, const float* pts, co
     SphInputs in{pack, pts, vel, scales, reinterpret_cast<const float4*>(quats), opac, flags,
                  reinterpret_cast<const float2*>(means2d), reinterpret_cast<const float2*>(radii), depths};
     if (n > 0)
-        XSG_SPH_DISPATCH(lidar, (launch(sph_count_kernel<Cam>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
+        XSG_SPH_DISPATCH(lidar, (launch_pdl(sph_count_kernel<Cam>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
                                     in, T, up, n, counts, w.total)));
     unsigned long long tot = 0;
     XSG_CUDA(cudaMemcpyAsync(&tot, w.total, sizeof(tot), cudaMemcpyDeviceToHost, st));
@@ -745,7 +769,7 @@ int xsg_isect_spherical_emit(int lidar, const float* pack, const float* pts, con
     if (!sort) {
         int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
         if (rc != XSG_OK) return rc;
-        XSG_SPH_DISPATCH(lidar, (launch(sph_emit_kernel<Cam, false>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
+        XSG_SPH_DISPATCH(lidar, (launch_pdl(sph_emit_kernel<Cam, false>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
                                     in, T, up, n, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
                                     bucket_neg)));
         return check_launch("isect_spherical_emit");
@@ -756,7 +780,7 @@ int xsg_isect_spherical_emit(int lidar, const float* pack, const float* pts, con
     // (tile, depth bits) with two chained stable sorts instead.
     int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
     if (rc != XSG_OK) return rc;
-    XSG_SPH_DISPATCH(lidar, (launch(sph_emit_kernel<Cam, false>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
+    XSG_SPH_DISPATCH(lidar, (launch_pdl(sph_emit_kernel<Cam, false>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
                                 in, T, up, n, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
                                 bucket_neg)));
     return sort_isect_pairs_inplace(isect_ids, flatten_ids, n_isects, tile_bits_for(n_tiles), w, st);
@@ -772,7 +796,7 @@ int xsg_isect_offset_encode(const int64_t* isect_ids, int64_t n_isects, int tw, 
         return XSG_OK;
     }
     XSG_REQUIRE(isect_ids, "isect_offset_encode: null isect_ids");
-    launch(offset_encode_kernel, blocks_for(n_isects, 256), 256, 0, st, isect_ids, n_isects, n_tiles,
+    launch_pdl(offset_encode_kernel, blocks_for(n_isects, 256), 256, 0, st, isect_ids, n_isects, n_tiles,
                                                                    tile_bits_for(n_tiles), offsets);
     return check_launch("isect_offset_encode");
 }
