@@ -9,8 +9,9 @@ One step = SH colour forward -> ut_gs_render (UT projection, tile
 intersection + sort + offsets, rays, forward compositing) -> backward from
 N(0, 1) upstream gradients of the colour, depth and alpha images
 (compositing backward, SH backward) through the public API and autograd, and
-with N > 1 ranks the exchange of the Gaussian gradients over NCCL (views are
-sharded over the ranks).  Every rank holds the full scene.
+with N > 1 ranks the exchange of the Gaussian gradients over NVLink (views
+are sharded over the ranks; this package's NVSwitch multicast kernels, or
+NCCL with --exchange bucketed / per-leaf).  Every rank holds the full scene.
 
 value  : whole-job Mpix/s with inputs resident in HBM, device-timed with CUDA
          events (max over ranks).
@@ -65,8 +66,10 @@ def parse():
     p.add_argument("--no-rig", action="store_true", help="skip the C3 / C3-8 rig measurement")
     p.add_argument("--no-c5", action="store_true", help="skip the C5 skinned-actor measurement")
     p.add_argument("--gaussians", type=int, default=0, help="override the workload's Gaussian count")
-    p.add_argument("--exchange", default="bucketed", choices=["bucketed", "per-leaf"],
-                   help="geometry gradients ready together share one all-reduce (bucketed) or not")
+    p.add_argument("--exchange", default="nvls", choices=["nvls", "bucketed", "per-leaf"],
+                   help="gradient exchange at N > 1: this package's NVSwitch multicast kernels (nvls, the "
+                        "default; NCCL bucketed where NVLink multicast is unavailable), or NCCL with the "
+                        "geometry gradients ready together in one all-reduce (bucketed) or one per leaf")
     p.add_argument("--workload", default="c2", choices=["c2", "c3", "c3-8", "c5"],
                    help="c2: one C2 view per rank (weak scaling, the default); c3 / c3-8 / c5: the rig's views "
                         "sharded over the ranks (strong scaling)")
@@ -121,7 +124,7 @@ def workload_config(name: str, world: int, n_gauss: int) -> dict:
         views = [len(v) for v in assign_views([s.width * s.height for s in specs], world)]
     mvsh = world > 1 and name != "c5" and (scaling == "weak" or min(views) >= 1)
     cfg = {"workload": WORKLOAD_DESC[name], "views_per_gpu": views,
-           "parallelism": f"view-sharded dp{world} + NCCL gradient exchange",
+           "parallelism": f"view-sharded dp{world} + gradient exchange over NVLink",
            "gradient_exchange": ("all-reduce of the geometry gradients + all-gather of the per-view colour "
                                  "gradients, SH-coefficient gradient rebuilt on every rank") if mvsh else
                                 ("all-reduce of every Gaussian gradient" if world > 1 else "none"),
@@ -281,7 +284,7 @@ class Workload:
         import torch
         import xsimgs_b200 as X
         from xsimgs_b200 import scenes
-        from xsimgs_b200.multiview import GradientAllReduce, assign_views, multiview_colors
+        from xsimgs_b200.multiview import GradientAllReduce, assign_views, exchanged_leaves, multiview_colors
         self.X, self.torch, self.mvc = X, torch, multiview_colors
         self.name, self.world, self.rank, self.dev = name, world, rank, dev
         specs, n_default, self.scaling = workload_views(name)
@@ -307,13 +310,32 @@ class Workload:
         # below each keep one order on every rank and run side by side
         self.mvsh = world > 1 and name != "c5" and min(len(v) for v in self.assignment) >= 1
         import torch.distributed as dist
-        self.sh_group = dist.new_group(list(range(world))) if self.mvsh else None
-        order = ["quats", "scales", "opacities", "means"] + ([] if self.mvsh else ["sh"])
-        order += [k for k in self.leaves if k not in order]
-        # backward finishes the compositing's leaves first (quats, scales and
-        # opacities together: one bucket), then the SH backward's
-        buckets = ([3] + [1] * (len(order) - 3)) if exchange == "bucketed" else None
-        self.red = GradientAllReduce([self.leaves[k] for k in order], buckets=buckets)
+        order = exchanged_leaves(self.leaves, self.mvsh)
+        self.ex = None
+        self.sh_group = None
+        if exchange == "nvls" and world > 1:
+            # this package's NVSwitch kernels on the compute stream: the view
+            # exchange inside the SH backward, one all-reduce after backward
+            from xsimgs_b200.exchange import NvlsExchange, NvlsGradientSum
+            n_red = sum(self.leaves[k].numel() for k in order)
+            n_gat = self.k_max * self.n_gauss * 3 if self.mvsh else 0
+            try:
+                self.ex = NvlsExchange(None, n_red, n_gat, 3 * self.k_max if self.mvsh else 0, device=dev)
+            except RuntimeError as e:  # no NVLink multicast here: every rank finds the same
+                print(f"[bench] NVSwitch exchange unavailable ({e}); using NCCL", flush=True)
+                exchange = "bucketed"
+        self.exchange = exchange if world > 1 else "none"
+        if self.ex is not None:
+            self.red = NvlsGradientSum([self.leaves[k] for k in order], self.ex)
+        else:
+            # NCCL: the view exchange on a communicator of its own (its
+            # all-gathers and the all-reduces each keep one order on every
+            # rank and run side by side); backward finishes the compositing's
+            # leaves first (quats, scales and opacities together: one
+            # bucket), then the SH backward's
+            self.sh_group = dist.new_group(list(range(world))) if self.mvsh else None
+            buckets = ([3] + [1] * (len(order) - 3)) if exchange == "bucketed" else None
+            self.red = GradientAllReduce([self.leaves[k] for k in order], buckets=buckets)
         self.upstream = [tuple(t.to(dev) for t in scenes.upstream_grads(sp.height, sp.width, 3,
                                                                          seed=1 + rank * 16 + k))
                          for k, (sp, _) in enumerate(self.views)]
@@ -361,7 +383,7 @@ class Workload:
         means, quats, scales, opac, sh, vel = self._scene()
         if self.mvsh:
             cols = self.mvc(sh, means, torch.stack([cam.t0 for _, cam in self.views]), DEG, self.k_max,
-                            group=self.sh_group)
+                            group=self.sh_group, exchange=self.ex)
         outs, ups = [], []
         for v, ((sp, cam), g) in enumerate(zip(self.views, grads)):
             colors = cols[v] if self.mvsh else X.spherical_harmonics_fused(sh, means, cam.t0, DEG)
@@ -491,6 +513,30 @@ def exchange_probe(wl, world, dev, reps=10):
             x.wait()
 
     res = {}
+    if wl.ex is not None:
+        # this package's NVSwitch kernels: the view all-gather and one
+        # all-reduce of every exchanged gradient, as the step runs them
+        ex = wl.ex
+        dv = torch.zeros(ex.n_gather, device=dev)
+        ov = torch.zeros(ex.n_small, device=dev)
+        red = torch.zeros(ex.n_reduce, device=dev)
+
+        def run_nvls():
+            if ex.n_gather:
+                ex.all_gather(dv, ov)
+            ex.all_reduce_([red])
+
+        for _ in range(3):
+            run_nvls()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run_nvls()
+        e1.record()
+        barrier(world)
+        res["nvls"] = round(e0.elapsed_time(e1) / reps, 4)
+        ex.check()
     for split in (True, False):
         for _ in range(3):
             run(split)
@@ -626,6 +672,8 @@ def gpu_arm(args, world, rank, local):
         stages = stage_fields(wl, timed, n_isects)
 
     wl.red.remove()
+    if wl.ex is not None:
+        wl.ex.check()  # raises if a barrier of the exchange timed out
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -656,6 +704,7 @@ def gpu_arm(args, world, rank, local):
         "gpu_launches": int(launches), "gpu_launches_per_step": round(launches / args.steps, 1),
         "clocks": clk, "roofline": roof, "cpu_baseline": cpu, "phases": phases, "stages": stages,
         "exchange_alone_ms": xprobe,
+        "exchange": wl.exchange,
     }
     line.update(extra)
     print(json.dumps(line), flush=True)
@@ -709,6 +758,8 @@ def strong_leg(args, name, world, rank, dev, phases=True):
     ms = time_steps(wl, steps, max(3, args.warmup), world)
     ph = phase_times(wl, min(5, steps), world) if phases else None
     ms, = max_over_ranks([ms], world, dev)
+    if wl.ex is not None:
+        wl.ex.check()
     wl.red.remove()
     out = {"metric": f"Gaussian-render fwd+bwd Mpix/s ({name.upper()})", "unit": "Mpix/s", "scaling": "strong",
            "value": round(wl.px_per_step * steps / (ms * 1e-3) / 1e6, 2), "ms_per_step": round(ms / steps, 3),

@@ -502,6 +502,29 @@ int xsg_interpolate_smpl_poses_bwd(int64_t n_objects, int frames, int joints, co
                                    int64_t n_instances, const float* grad_out, float* d_poses, float* d_root_q,
                                    float* d_query_time, xsg_stream_t stream);
 
+/* ---- multi-GPU gradient exchange (no reference counterpart) ----
+ * Kernels for the sensor-sharded render step on NVSwitch systems.  Buffers
+ * are symmetric (same size on every rank, one multicast address for all
+ * copies, e.g. from torch's symmetric memory); `mc_addr` / `mc_dst` are
+ * multicast virtual addresses.
+ * xsg_exchange_barrier: peer_flags is a device array of `world` pointers, one
+ * per rank, to that rank's `world` uint32 flag words (zeroed once before the
+ * first barrier); every rank passes the same, strictly increasing `epoch` per
+ * barrier.  A rank that does not arrive within timeout_s sets *err (device
+ * int) to 1 + its rank and the barrier returns.
+ * xsg_nvls_allreduce_sum_f32: in-place sum over ranks of n floats (n a
+ * multiple of 4) at mc_addr; call between two barriers.
+ * xsg_nvls_broadcast_f32: writes the n local floats at src into every rank's
+ * copy at mc_dst (an all-gather when each rank writes its own slice); call
+ * between two barriers. */
+int xsg_exchange_barrier(uint32_t* const* peer_flags, int rank, int world, uint32_t epoch,
+                         double timeout_s, int* err, xsg_stream_t stream);
+int xsg_nvls_allreduce_sum_f32(uint64_t mc_addr, int64_t n, int rank, int world,
+                               xsg_stream_t stream);
+int xsg_nvls_broadcast_f32(const float* src, uint64_t mc_dst, int64_t n, xsg_stream_t stream);
+/* At most n CTAs per exchange kernel (0: four per SM, the default). */
+void xsg_exchange_set_max_ctas(int n);
+
 #ifdef __cplusplus
 }
 #endif

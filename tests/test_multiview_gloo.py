@@ -12,7 +12,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from xsimgs_b200.multiview import GradientAllReduce, assign_views
+from xsimgs_b200.multiview import GradientAllReduce, assign_views, exchanged_leaves
 
 
 def test_assign_views_balanced_and_deterministic():
@@ -26,6 +26,15 @@ def test_assign_views_balanced_and_deterministic():
     assert assign_views([1.0], 4) == [[0], [], [], []]
     with pytest.raises(ValueError):
         assign_views(costs, 0)
+
+
+def test_exchanged_leaves_order_and_multiview_sh():
+    names = ["means", "quats", "scales", "opacities", "sh", "local_q", "vertices"]
+    assert exchanged_leaves(names, multiview_sh=False) == ["quats", "scales", "opacities", "means", "sh",
+                                                           "local_q", "vertices"]
+    # the multi-view SH backward already returns the SH gradient summed over ranks
+    assert exchanged_leaves(names[:5], multiview_sh=True) == ["quats", "scales", "opacities", "means"]
+    assert exchanged_leaves(["sh", "means"], multiview_sh=False) == ["means", "sh"]
 
 
 def _plain(t):
@@ -257,7 +266,11 @@ def _worker_mvsh_gated(rank, world, port, q, own_group=False):
         for t in (means, sh, quats):
             t.requires_grad_(True)
         sh_group = dist.new_group([0, 1]) if own_group else None
-        red = GradientAllReduce([quats, means], gated=not own_group)
+        # the leaves a step exchanges, chosen as the bench chooses them: the
+        # SH gradient (already summed by the view exchange) is left out
+        leaves = {"means": means, "sh": sh, "quats": quats}
+        red = GradientAllReduce([leaves[k] for k in exchanged_leaves(leaves, multiview_sh=True)],
+                                gated=not own_group)
         for _ in range(2):  # hooks registered once, two passes
             for t in (means, sh, quats):
                 t.grad = None

@@ -601,6 +601,30 @@ BwdOut raster_bwd(const Tensor& points, const OptT& velocity, const Tensor& scal
     return o;
 }
 
+// ------------------------------------------------------------- exchange ---
+// Multi-GPU gradient exchange on symmetric buffers (no reference
+// counterpart); addresses are device / multicast virtual addresses as ints.
+void exchange_barrier(uint64_t peer_flags_dev, int64_t rank, int64_t world, int64_t epoch, double timeout_s,
+                      const Tensor& err) {
+    TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt && err.numel() >= 1, "err must be a CUDA int32 tensor");
+    c10::cuda::CUDAGuard g(err.device());
+    check(xsg_exchange_barrier(reinterpret_cast<uint32_t* const*>(peer_flags_dev), int(rank), int(world),
+                               uint32_t(epoch), timeout_s, err.data_ptr<int32_t>(), stream()));
+}
+
+void nvls_allreduce_sum(uint64_t mc_addr, int64_t n, int64_t rank, int64_t world, const Tensor& like) {
+    TORCH_CHECK(like.is_cuda(), "nvls_allreduce: a CUDA tensor names the device");
+    c10::cuda::CUDAGuard g(like.device());
+    check(xsg_nvls_allreduce_sum_f32(mc_addr, n, int(rank), int(world), stream()));
+}
+
+void nvls_broadcast(const Tensor& src, uint64_t mc_dst) {
+    check_tensor(src, "src", src);
+    TORCH_CHECK(src.scalar_type() == at::kFloat, "nvls_broadcast: float32 source");
+    c10::cuda::CUDAGuard g(src.device());
+    check(xsg_nvls_broadcast_f32(fptr(src), mc_dst, src.numel(), stream()));
+}
+
 // ------------------------------------------------------------------ SH ---
 Tensor sh_fwd(int64_t degree, const Tensor& origin, const Tensor& positions, const Tensor& coeffs, const OptT& mask,
               bool layout_3kn, const OptT& coeffs_dc, const OptT& output) {
@@ -1029,6 +1053,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("v_render_alpha"), py::arg("ray_grads") = true, py::arg("forward_workspace") = py::none(),
           py::arg("n_isects") = py::none());
 
+    m.def("exchange_barrier", &exchange_barrier, py::arg("peer_flags"), py::arg("rank"), py::arg("world"),
+          py::arg("epoch"), py::arg("timeout_s"), py::arg("err"));
+    m.def("nvls_allreduce_sum", &nvls_allreduce_sum, py::arg("mc_addr"), py::arg("n"), py::arg("rank"),
+          py::arg("world"), py::arg("like"));
+    m.def("nvls_broadcast", &nvls_broadcast, py::arg("src"), py::arg("mc_dst"));
+    m.def("exchange_set_max_ctas", [](int64_t n) { xsg_exchange_set_max_ctas(int(n)); }, py::arg("n"));
     m.def("spherical_harmonics_fused_fwd", &sh_fwd, py::arg("degree_to_use"), py::arg("origin"),
           py::arg("positions"), py::arg("coeffs"), py::arg("mask"), py::arg("layout_3kn"),
           py::arg("coeffs_dc") = py::none(), py::arg("output") = py::none());

@@ -189,7 +189,7 @@ __device__ __forceinline__ void cs_range(int64_t n, int64_t& i0, int64_t& i1) {
 // counts[b * G + w] (bin-major) or counts[w * nbins + b] (warp-major)
 template <bool kBinMajor>
 __global__ void __launch_bounds__(32)
-    cs_hist_kernel(const uint32_t* __restrict__ keys, int64_t n, const int64_t* __restrict__ n_dev, CsDigit dg,
+    cs_hist_kernel(const uint2* __restrict__ kv, int64_t n, const int64_t* __restrict__ n_dev, CsDigit dg,
                    int nbins, int32_t* __restrict__ counts) {
     pdl_wait();
     pdl_trigger();
@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(32)
     __syncwarp();
     int64_t i0, i1;
     cs_range(n, i0, i1);
-    for (int64_t i = i0 + lane; i < i1; i += 32) atomicAdd(h + dg(keys[i]), 1);
+    for (int64_t i = i0 + lane; i < i1; i += 32) atomicAdd(h + dg(kv[i].x), 1);
     __syncwarp();
     for (int b = lane; b < nbins; b += 32)
         counts[kBinMajor ? int64_t(b) * gridDim.x + blockIdx.x : int64_t(blockIdx.x) * nbins + b] = h[b];
@@ -274,10 +274,9 @@ __global__ void __launch_bounds__(1024) cs_starts_kernel(const int64_t* __restri
 // starts[b] + offs[w * nbins + b] (wide digits).
 template <bool kBinMajor, bool kIsect>
 __global__ void __launch_bounds__(32)
-    cs_scatter_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int64_t n,
-                      const int64_t* __restrict__ n_dev, CsDigit dg, int nbins, const int64_t* __restrict__ pos0,
-                      const int32_t* __restrict__ offs, const int64_t* __restrict__ starts,
-                      uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, IsectEpilogue ep) {
+    cs_scatter_kernel(const uint2* __restrict__ kv, int64_t n, const int64_t* __restrict__ n_dev, CsDigit dg,
+                      int nbins, const int64_t* __restrict__ pos0, const int32_t* __restrict__ offs,
+                      const int64_t* __restrict__ starts, uint2* __restrict__ kv_out, IsectEpilogue ep) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ int32_t cur[];  // positions < n < 2^31
@@ -297,9 +296,9 @@ __global__ void __launch_bounds__(32)
 #pragma unroll
         for (int r = 0; r < kB; ++r) {
             const int64_t i = base + 32 * r + lane;
-            const bool ok = i < i1;
-            kk[r] = ok ? keys[i] : 0u;
-            vv[r] = ok ? vals[i] : 0u;
+            const uint2 e = i < i1 ? kv[i] : make_uint2(0u, 0u);
+            kk[r] = e.x;
+            vv[r] = e.y;
         }
         if constexpr (kIsect) {
 #pragma unroll
@@ -326,8 +325,7 @@ __global__ void __launch_bounds__(32)
                     ep.isect_ids[pos] = int64_t(hi | uint64_t(uint32_t(bits)));
                     ep.flatten_ids[pos] = int32_t(vv[r]);
                 } else {
-                    keys_out[pos] = kk[r];
-                    vals_out[pos] = vv[r];
+                    kv_out[pos] = make_uint2(kk[r], vv[r]);
                 }
             }
         }
@@ -350,11 +348,11 @@ inline size_t cs_workspace_bytes(int64_t n, int nbins) {
 }
 
 // One stable pass of `n` (upper bound; the count itself at n_dev when given)
-// pairs on digit dg with nbins values into keys_out / vals_out, or with `ep`
-// into the 64-bit isect ids and flatten ids.
-inline int counting_pass(const uint32_t* keys, const uint32_t* vals, uint32_t* keys_out, uint32_t* vals_out,
-                         int64_t n, const int64_t* n_dev, CsDigit dg, int nbins, void* tmp, size_t tmp_bytes,
-                         cudaStream_t st, const IsectEpilogue* ep) {
+// (key, value) pairs, stored interleaved (one 8-byte word each, so a scatter
+// is one store per pair), on digit dg with nbins values into kv_out, or with
+// `ep` into the 64-bit isect ids and flatten ids.
+inline int counting_pass(const uint2* kv, uint2* kv_out, int64_t n, const int64_t* n_dev, CsDigit dg, int nbins,
+                         void* tmp, size_t tmp_bytes, cudaStream_t st, const IsectEpilogue* ep) {
     if (n <= 0) return XSG_OK;
     if (nbins > kCsMaxBins) return set_error(XSG_ERR_UNSUPPORTED, "counting pass: too many bins");
     static bool attrs_set[64] = {};
@@ -380,34 +378,27 @@ inline int counting_pass(const uint32_t* keys, const uint32_t* vals, uint32_t* k
         int64_t* pos0 = a.take<int64_t>(size_t(mat + 1));
         void* stmp = a.take<char>(scan_workspace_bytes(mat));
         if (!counts || !pos0 || !stmp) return set_error(XSG_ERR_WORKSPACE, "counting pass: workspace too small");
-        launch_pdl(cs_hist_kernel<true>, G, 32, smem, st, keys, n, n_dev, dg, nbins, counts);
+        launch_pdl(cs_hist_kernel<true>, G, 32, smem, st, kv, n, n_dev, dg, nbins, counts);
         int rc = exclusive_scan<int32_t>(counts, mat, pos0, nullptr, stmp, st);
         if (rc != XSG_OK) return rc;
         const int64_t* p0 = pos0;
-        if (ep)
-            launch_pdl(cs_scatter_kernel<true, true>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins, p0,
-                   static_cast<const int32_t*>(nullptr), static_cast<const int64_t*>(nullptr), nullptr, nullptr, e);
-        else
-            launch_pdl(cs_scatter_kernel<true, false>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins, p0,
-                   static_cast<const int32_t*>(nullptr), static_cast<const int64_t*>(nullptr), keys_out, vals_out, e);
+        launch_pdl(ep ? cs_scatter_kernel<true, true> : cs_scatter_kernel<true, false>, G, 32, smem, st, kv, n,
+                   n_dev, dg, nbins, p0, static_cast<const int32_t*>(nullptr), static_cast<const int64_t*>(nullptr),
+                   ep ? nullptr : kv_out, e);
         return check_launch("counting_pass");
     }
     int32_t* offs = a.take<int32_t>(size_t(mat));
     int64_t* totals = a.take<int64_t>(size_t(nbins + 1));
     int64_t* starts = a.take<int64_t>(size_t(nbins + 1));
     if (!counts || !offs || !totals || !starts) return set_error(XSG_ERR_WORKSPACE, "counting pass: workspace too small");
-    launch_pdl(cs_hist_kernel<false>, G, 32, smem, st, keys, n, n_dev, dg, nbins, counts);
+    launch_pdl(cs_hist_kernel<false>, G, 32, smem, st, kv, n, n_dev, dg, nbins, counts);
     launch_pdl(cs_colscan_kernel, unsigned((nbins + 31) / 32), 1024, 0, st, static_cast<const int32_t*>(counts), G,
            nbins, offs, totals);
     launch_pdl(cs_starts_kernel, 1, 1024, 0, st, static_cast<const int64_t*>(totals), nbins, starts);
     const int32_t* of = offs;
     const int64_t* sts = starts;
-    if (ep)
-        launch_pdl(cs_scatter_kernel<false, true>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins,
-               static_cast<const int64_t*>(nullptr), of, sts, nullptr, nullptr, e);
-    else
-        launch_pdl(cs_scatter_kernel<false, false>, G, 32, smem, st, keys, vals, n, n_dev, dg, nbins,
-               static_cast<const int64_t*>(nullptr), of, sts, keys_out, vals_out, e);
+    launch_pdl(ep ? cs_scatter_kernel<false, true> : cs_scatter_kernel<false, false>, G, 32, smem, st, kv, n, n_dev,
+               dg, nbins, static_cast<const int64_t*>(nullptr), of, sts, ep ? nullptr : kv_out, e);
     return check_launch("counting_pass");
 }
 

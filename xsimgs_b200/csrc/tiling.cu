@@ -97,9 +97,8 @@ template <bool kSorted>
 __global__ void __launch_bounds__(kTileThreads)
     regular_emit_kernel(const float2* __restrict__ means2d, const float2* __restrict__ radii,
                         const float* __restrict__ depths, int64_t n_items, float2 ts, int ntx, int nty,
-                        int bucket_neg, const uint32_t* __restrict__ order,
-                        const int64_t* __restrict__ offsets, uint32_t* __restrict__ bucket_keys,
-                        uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
+                        int bucket_neg, const uint2* __restrict__ order, const int64_t* __restrict__ offsets,
+                        uint2* __restrict__ buckets, int64_t* __restrict__ isect_ids,
                         int32_t* __restrict__ flatten_ids, const int64_t* __restrict__ n_dev, int64_t cap) {
     pdl_wait();
     pdl_trigger();
@@ -110,7 +109,7 @@ __global__ void __launch_bounds__(kTileThreads)
     Rect rc{0, 0, 0, 0};
     bool has = false;
     if (in) {
-        g = kSorted ? order[p] : uint32_t(p);
+        g = kSorted ? order[p].y : uint32_t(p);
         has = regular_rect(means2d[g], radii[g], ts, ntx, nty, rc);
     }
     const int cnt = has ? rc.count() : 0;
@@ -120,8 +119,7 @@ __global__ void __launch_bounds__(kTileThreads)
         if (off >= cap) return;  // capacity-bounded output: the rest is dropped, the count says so
         const uint32_t tile = uint32_t(y) * uint32_t(ntx) + uint32_t(x);
         if constexpr (kSorted) {
-            bucket_keys[off] = b < 0 ? uint32_t(bucket_neg) : tile;
-            bucket_vals[off] = gg;
+            buckets[off] = make_uint2(b < 0 ? uint32_t(bucket_neg) : tile, gg);
         } else {
             const uint64_t hi = b < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(tile) << 32);
             isect_ids[off] = int64_t(hi | uint64_t(uint32_t(b)));
@@ -155,23 +153,20 @@ __global__ void __launch_bounds__(kTileThreads)
 
 // Visible (count > 0) Gaussians -> (depth bits, index) pairs, in index order.
 __global__ void compact_visible_kernel(const int32_t* __restrict__ counts, const int64_t* __restrict__ pos,
-                                       const float* __restrict__ depths, int64_t n,
-                                       uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+                                       const float* __restrict__ depths, int64_t n, uint2* __restrict__ kv) {
     pdl_wait();
     pdl_trigger();
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n || counts[i] <= 0) return;
-    const int64_t p = pos[i];
-    keys[p] = __float_as_uint(depths[i]);
-    vals[p] = uint32_t(i);
+    kv[pos[i]] = make_uint2(__float_as_uint(depths[i]), uint32_t(i));
 }
 
-__global__ void gather_counts_kernel(const int32_t* __restrict__ counts, const uint32_t* __restrict__ order,
+__global__ void gather_counts_kernel(const int32_t* __restrict__ counts, const uint2* __restrict__ order,
                                      int64_t n, int32_t* __restrict__ out, const int64_t* __restrict__ n_dev) {
     pdl_wait();
     pdl_trigger();
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < (n_dev ? *n_dev : n)) out[i] = counts[order[i]];
+    if (i < (n_dev ? *n_dev : n)) out[i] = counts[order[i].y];
 }
 
 // isect_offset_encode_kernel semantics (tiling_common.cu:25-71): offsets[t]
@@ -378,15 +373,14 @@ __global__ void __launch_bounds__(kTileThreads / 2)
 // intersections by a per-intersection depth kept in `isect_depth`.
 template <typename Cam, bool kSorted>
 __global__ void __launch_bounds__(kTileThreads / 2)
-    sph_emit_kernel(SphInputs in, SphTiling T, UTParams up, int64_t n_items, const uint32_t* __restrict__ order,
-                    const int64_t* __restrict__ offsets, uint32_t* __restrict__ bucket_keys,
-                    uint32_t* __restrict__ bucket_vals, int64_t* __restrict__ isect_ids,
-                    int32_t* __restrict__ flatten_ids, int bucket_neg) {
+    sph_emit_kernel(SphInputs in, SphTiling T, UTParams up, int64_t n_items, const uint2* __restrict__ order,
+                    const int64_t* __restrict__ offsets, uint2* __restrict__ buckets,
+                    int64_t* __restrict__ isect_ids, int32_t* __restrict__ flatten_ids, int bucket_neg) {
     pdl_wait();
     pdl_trigger();
     const int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (p >= n_items) return;
-    const uint32_t g = kSorted ? order[p] : uint32_t(p);
+    const uint32_t g = kSorted ? order[p].y : uint32_t(p);
     Cam k;
     k.load(in.pack);
     Rect r1, r2;
@@ -402,8 +396,7 @@ __global__ void __launch_bounds__(kTileThreads / 2)
             for (int x = rc.x0; x < rc.x1; ++x) {
                 const uint32_t tile = uint32_t(int64_t(y) * T.n_az + x);
                 if constexpr (kSorted) {
-                    bucket_keys[off] = bits < 0 ? uint32_t(bucket_neg) : tile;
-                    bucket_vals[off] = g;
+                    buckets[off] = make_uint2(bits < 0 ? uint32_t(bucket_neg) : tile, g);
                 } else {
                     const uint64_t hi = bits < 0 ? 0xFFFFFFFF00000000ull : (uint64_t(tile) << 32);
                     isect_ids[off] = int64_t(hi | uint64_t(uint32_t(bits)));
@@ -422,9 +415,9 @@ struct IsectWs {
     unsigned long long* total;
     int64_t* scan_out;      // n + 1
     void* scan_tmp;
-    uint32_t *gk, *gv, *gk2, *gv2;  // Gaussian presort, n each
+    uint2 *g0, *g1;         // Gaussian presort (depth bits, index), n each
     int32_t* cnt_sorted;    // n
-    uint32_t *bk, *bv, *bk2, *bv2;  // tile sort, max_isects each
+    uint2 *b0, *b1;         // tile sort (bucket, index or position), max_isects each
     void* sort_tmp;
     size_t sort_tmp_bytes;
     int64_t* kcopy;         // max_isects (generic 64-bit key sort)
@@ -445,11 +438,11 @@ static size_t isect_ws_layout(int64_t n, int64_t m, void* base, size_t cap, Isec
     w.total = a.take<unsigned long long>(1);
     w.scan_out = a.take<int64_t>(size_t(n + 1));
     w.scan_tmp = a.take<char>(scan_workspace_bytes(big + 1));
-    w.gk = a.take<uint32_t>(size_t(n)); w.gv = a.take<uint32_t>(size_t(n));
-    w.gk2 = a.take<uint32_t>(size_t(n)); w.gv2 = a.take<uint32_t>(size_t(n));
+    w.g0 = a.take<uint2>(size_t(n));
+    w.g1 = a.take<uint2>(size_t(n));
     w.cnt_sorted = a.take<int32_t>(size_t(n));
-    w.bk = a.take<uint32_t>(size_t(m)); w.bv = a.take<uint32_t>(size_t(m));
-    w.bk2 = a.take<uint32_t>(size_t(m)); w.bv2 = a.take<uint32_t>(size_t(m));
+    w.b0 = a.take<uint2>(size_t(m));
+    w.b1 = a.take<uint2>(size_t(m));
     w.sort_tmp_bytes = sort_scratch_bytes(n, m);
     w.sort_tmp = a.take<char>(w.sort_tmp_bytes);
     w.kcopy = a.take<int64_t>(size_t(m));
@@ -458,65 +451,59 @@ static size_t isect_ws_layout(int64_t n, int64_t m, void* base, size_t cap, Isec
     // `used` is what the layout needs even when cap was too small
     size_t need = 0;
     need += Arena::round(8) + Arena::round(size_t(n + 1) * 8) + scan_workspace_bytes(big + 1);
-    need += 4 * Arena::round(size_t(n) * 4) + Arena::round(size_t(n) * 4);
-    need += 4 * Arena::round(size_t(m) * 4) + sort_scratch_bytes(n, m);
+    need += 2 * Arena::round(size_t(n) * 8) + Arena::round(size_t(n) * 4);
+    need += 2 * Arena::round(size_t(m) * 8) + sort_scratch_bytes(n, m);
     need += Arena::round(size_t(m) * 8) + Arena::round(size_t(m) * 4);
     return need;
 }
 
-__global__ void split_key_kernel(const int64_t* __restrict__ ids, int64_t n, uint32_t* __restrict__ lo,
-                                 uint32_t* __restrict__ idx) {
+__global__ void split_key_kernel(const int64_t* __restrict__ ids, int64_t n, uint2* __restrict__ kv) {
     pdl_wait();
     pdl_trigger();
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    lo[i] = uint32_t(uint64_t(ids[i]));
-    idx[i] = uint32_t(i);
+    kv[i] = make_uint2(uint32_t(uint64_t(ids[i])), uint32_t(i));
 }
 
-__global__ void gather_hi_kernel(const int64_t* __restrict__ ids, const uint32_t* __restrict__ perm, int64_t n,
-                                 int tb, uint32_t* __restrict__ hi, uint32_t* __restrict__ idx) {
+__global__ void gather_hi_kernel(const int64_t* __restrict__ ids, const uint2* __restrict__ perm, int64_t n,
+                                 int tb, uint2* __restrict__ kv) {
     pdl_wait();
     pdl_trigger();
     const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (j >= n) return;
-    const uint32_t p = perm[j];
-    hi[j] = uint32_t((uint64_t(ids[p]) >> 32) & ((uint64_t(1) << tb) - 1));
-    idx[j] = p;
+    const uint32_t p = perm[j].y;
+    kv[j] = make_uint2(uint32_t((uint64_t(ids[p]) >> 32) & ((uint64_t(1) << tb) - 1)), p);
 }
 
 __global__ void permute_isects_kernel(const int64_t* __restrict__ kin, const int32_t* __restrict__ fin,
-                                      const uint32_t* __restrict__ perm, int64_t n, int64_t* __restrict__ kout,
+                                      const uint2* __restrict__ perm, int64_t n, int64_t* __restrict__ kout,
                                       int32_t* __restrict__ fout) {
     pdl_wait();
     pdl_trigger();
     const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (j >= n) return;
-    const uint32_t p = perm[j];
+    const uint32_t p = perm[j].y;
     kout[j] = kin[p];
     fout[j] = fin[p];
 }
 
-// Stable LSD sort of (u32 key, u32 value) pairs on key bits [0, bits) with
-// counting passes of up to `digit` bits; the result is returned in *keys_res /
-// *vals_res (one of the two buffer pairs).  With `ep` the last pass writes the
-// 64-bit isect ids and flatten ids instead.
-static int counting_sort(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int64_t n, const int64_t* n_dev,
-                         int bits, int digit, const IsectWs& w, cudaStream_t st, const IsectEpilogue* ep,
-                         uint32_t** keys_res, uint32_t** vals_res) {
+// Stable LSD sort of interleaved (u32 key, u32 value) pairs on key bits
+// [0, bits) with counting passes of up to `digit` bits, ping-ponging between
+// kv0 and kv1; the result is returned in *res (one of the two).  With `ep` the
+// last pass writes the 64-bit isect ids and flatten ids instead.
+static int counting_sort(uint2* kv0, uint2* kv1, int64_t n, const int64_t* n_dev, int bits, int digit,
+                         const IsectWs& w, cudaStream_t st, const IsectEpilogue* ep, uint2** res) {
     const int np = (bits + digit - 1) / digit;
     const int per = (bits + np - 1) / np;
     for (int p = 0; p < np; ++p) {
         const int lo = p * per, b = std::min(per, bits - lo);
         const bool last = p == np - 1;
-        const int rc = counting_pass(k0, v0, k1, v1, n, n_dev, CsDigit{lo, uint32_t((uint64_t(1) << b) - 1)}, 1 << b,
+        const int rc = counting_pass(kv0, kv1, n, n_dev, CsDigit{lo, uint32_t((uint64_t(1) << b) - 1)}, 1 << b,
                                      w.sort_tmp, w.sort_tmp_bytes, st, last ? ep : nullptr);
         if (rc != XSG_OK) return rc;
-        std::swap(k0, k1);
-        std::swap(v0, v1);
+        std::swap(kv0, kv1);
     }
-    if (keys_res) *keys_res = k0;
-    if (vals_res) *vals_res = v0;
+    if (res) *res = kv0;
     return XSG_OK;
 }
 
@@ -524,18 +511,18 @@ static int counting_sort(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1,
 // [0, 32 + tb), in place: by the depth word, then stably by the tile bits.
 static int sort_isect_pairs_inplace(int64_t* ids, int32_t* flat, int64_t n, int tb, const struct IsectWs& w,
                                     cudaStream_t st) {
-    launch_pdl(split_key_kernel, blocks_for(n, 256), 256, 0, st, ids, n, w.bk, w.bv);
-    uint32_t *ks, *vs;
-    int rc = counting_sort(w.bk, w.bv, w.bk2, w.bv2, n, nullptr, 32, 11, w, st, nullptr, &ks, &vs);
+    launch_pdl(split_key_kernel, blocks_for(n, 256), 256, 0, st, ids, n, w.b0);
+    uint2* res;
+    int rc = counting_sort(w.b0, w.b1, n, nullptr, 32, 11, w, st, nullptr, &res);
     if (rc != XSG_OK) return rc;
-    uint32_t* k2 = (ks == w.bk) ? w.bk2 : w.bk;
-    uint32_t* v2 = (vs == w.bv) ? w.bv2 : w.bv;
-    launch_pdl(gather_hi_kernel, blocks_for(n, 256), 256, 0, st, ids, vs, n, tb, k2, v2);
-    rc = counting_sort(k2, v2, ks, vs, n, nullptr, tb, 8, w, st, nullptr, &ks, &vs);
+    uint2* other = (res == w.b0) ? w.b1 : w.b0;
+    launch_pdl(gather_hi_kernel, blocks_for(n, 256), 256, 0, st, ids, static_cast<const uint2*>(res), n, tb, other);
+    rc = counting_sort(other, res, n, nullptr, tb, 8, w, st, nullptr, &res);
     if (rc != XSG_OK) return rc;
     XSG_CUDA(cudaMemcpyAsync(w.kcopy, ids, size_t(n) * 8, cudaMemcpyDeviceToDevice, st));
     XSG_CUDA(cudaMemcpyAsync(w.fcopy, flat, size_t(n) * 4, cudaMemcpyDeviceToDevice, st));
-    launch_pdl(permute_isects_kernel, blocks_for(n, 256), 256, 0, st, w.kcopy, w.fcopy, vs, n, ids, flat);
+    launch_pdl(permute_isects_kernel, blocks_for(n, 256), 256, 0, st, w.kcopy, w.fcopy, static_cast<const uint2*>(res),
+               n, ids, flat);
     return check_launch("sort_isect_pairs");
 }
 
@@ -553,21 +540,21 @@ static int sorted_isects(const int32_t* counts, const float* depths, int64_t n, 
     if (rc != XSG_OK) return rc;
     const int64_t* n_vis = w.scan_out + n;
     launch_pdl(compact_visible_kernel, blocks_for(n, 256), 256, 0, st, counts, static_cast<const int64_t*>(w.scan_out),
-           depths, n, w.gk, w.gv);
+           depths, n, w.g0);
     // 2. stable sort by the 32 depth bits: three counting passes (11 + 11 + 10 bits)
-    uint32_t* order = nullptr;
-    rc = counting_sort(w.gk, w.gv, w.gk2, w.gv2, n, n_vis, 32, 11, w, st, nullptr, nullptr, &order);
+    uint2* order = nullptr;
+    rc = counting_sort(w.g0, w.g1, n, n_vis, 32, 11, w, st, nullptr, &order);
     if (rc != XSG_OK) return rc;
     // 3. counts in depth order -> emission offsets
-    launch_pdl(gather_counts_kernel, blocks_for(n, 256), 256, 0, st, counts, order, n, w.cnt_sorted, n_vis);
+    launch_pdl(gather_counts_kernel, blocks_for(n, 256), 256, 0, st, counts, static_cast<const uint2*>(order), n,
+               w.cnt_sorted, n_vis);
     rc = exclusive_scan<int32_t>(w.cnt_sorted, n, w.scan_out, nullptr, w.scan_tmp, st, n_vis);
     if (rc != XSG_OK) return rc;
-    emit(order, static_cast<const int64_t*>(w.scan_out), n, n_vis);
+    emit(static_cast<const uint2*>(order), static_cast<const int64_t*>(w.scan_out), n, n_vis);
     // 4. stable counting passes on the tile bits (up to 8 bits each), the
     //    last of which writes the outputs
     IsectEpilogue ep{depths, isect_ids, flatten_ids};
-    return counting_sort(w.bk, w.bv, w.bk2, w.bv2, n_isects, n_isects_dev, tile_bits_for(n_tiles), 8, w, st, &ep,
-                         nullptr, nullptr);
+    return counting_sort(w.b0, w.b1, n_isects, n_isects_dev, tile_bits_for(n_tiles), 8, w, st, &ep, nullptr);
 }
 
 }  // namespace xsg
@@ -623,7 +610,7 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
         int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
         if (rc != XSG_OK) return rc;
         launch_pdl(regular_emit_kernel<false>, blocks_for(n, kTileThreads), kTileThreads, 0, st, 
-            m2, r2, depths, n, ts, ntx, nty, 0, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
+            m2, r2, depths, n, ts, ntx, nty, 0, nullptr, w.scan_out, nullptr, isect_ids, flatten_ids,
             static_cast<const int64_t*>(nullptr), INT64_MAX);
         return check_launch("isect_regular_emit");
     }
@@ -631,9 +618,9 @@ int xsg_isect_regular_emit(const float* means2d, const float* radii, const float
     const int bucket_neg = int((int64_t(1) << tile_bits_for(n_tiles)) - 1);
     ScopedTimer tm("isect_emit_sort", st);
     return sorted_isects(counts, depths, n, n_isects, n_tiles, w, isect_ids, flatten_ids, st,
-                         [&](const uint32_t* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
+                         [&](const uint2* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
                              launch_pdl(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st,
-                                 m2, r2, depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv,
+                                 m2, r2, depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.b0,
                                  nullptr, nullptr, n_vis, INT64_MAX);
                          });
 }
@@ -670,9 +657,9 @@ int xsg_isect_regular_tiles_async(const float* means2d, const float* radii, cons
         ScopedTimer tm("isect_emit_sort", st);
         const int rc = sorted_isects(
             counts, depths, n, capacity, n_tiles, w, isect_ids, flatten_ids, st,
-            [&](const uint32_t* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
+            [&](const uint2* order, const int64_t* offs, int64_t n_up, const int64_t* n_vis) {
                 launch_pdl(regular_emit_kernel<true>, blocks_for(n_up, kTileThreads), kTileThreads, 0, st, m2, r2,
-                       depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.bk, w.bv, nullptr, nullptr, n_vis,
+                       depths, n_up, ts, ntx, nty, bucket_neg, order, offs, w.b0, nullptr, nullptr, n_vis,
                        capacity);
             },
             n_written);
@@ -770,7 +757,7 @@ int xsg_isect_spherical_emit(int lidar, const float* pack, const float* pts, con
         int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
         if (rc != XSG_OK) return rc;
         XSG_SPH_DISPATCH(lidar, (launch_pdl(sph_emit_kernel<Cam, false>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
-                                    in, T, up, n, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
+                                    in, T, up, n, nullptr, w.scan_out, nullptr, isect_ids, flatten_ids,
                                     bucket_neg)));
         return check_launch("isect_spherical_emit");
     }
@@ -781,7 +768,7 @@ int xsg_isect_spherical_emit(int lidar, const float* pack, const float* pts, con
     int rc = exclusive_scan<int32_t>(counts, n, w.scan_out, nullptr, w.scan_tmp, st);
     if (rc != XSG_OK) return rc;
     XSG_SPH_DISPATCH(lidar, (launch_pdl(sph_emit_kernel<Cam, false>, blocks_for(n, kTileThreads / 2), kTileThreads / 2, 0, st, 
-                                in, T, up, n, nullptr, w.scan_out, nullptr, nullptr, isect_ids, flatten_ids,
+                                in, T, up, n, nullptr, w.scan_out, nullptr, isect_ids, flatten_ids,
                                 bucket_neg)));
     return sort_isect_pairs_inplace(isect_ids, flatten_ids, n_isects, tile_bits_for(n_tiles), w, st);
 }

@@ -3,8 +3,8 @@ rendering its share of the sensor views against a full replica of the
 Gaussians, then one exchange — the sum of the per-Gaussian gradients over
 ranks (NCCL all-reduce on NVLink / NVSwitch; gloo on CPU for tests).
 
-No kernel reads another GPU's memory: the only remote data is what the
-collective delivers into local buffers.
+With NCCL no kernel of this package touches another GPU's memory; the
+alternative exchange in exchange.py does it with its own NVSwitch kernels.
 """
 from __future__ import annotations
 
@@ -31,6 +31,19 @@ def assign_views(costs: Sequence[float], world: int) -> list[list[int]]:
     for v in out:
         v.sort()
     return out
+
+
+def exchanged_leaves(names: Iterable[str], multiview_sh: bool) -> list[str]:
+    """The leaves whose gradients a step sums over ranks, in the order the
+    backward finishes them: the compositing's (quats, scales, opacities),
+    then means, then the SH coefficients and any other leaf (skinning
+    parameters ...).  With the multi-view SH exchange (MultiViewSH) the SH
+    gradient comes out of the backward already summed over ranks and is not
+    exchanged again."""
+    names = list(names)
+    order = [k for k in ("quats", "scales", "opacities", "means") if k in names]
+    order += [k for k in names if k not in order and not (multiview_sh and k == "sh")]
+    return order
 
 
 class GradientAllReduce:
@@ -183,11 +196,11 @@ class MultiViewSH(torch.autograd.Function):
     Coefficients [N, K, 3] with band 0 included; no mask."""
 
     @staticmethod
-    def forward(ctx, sh, means, origins, degree: int, k_max: int, group=None, reducer=None):
+    def forward(ctx, sh, means, origins, degree: int, k_max: int, group=None, reducer=None, exchange=None):
         from ._native import _C
         cols = torch.stack([_C.spherical_harmonics_fused_fwd(degree, origins[v].contiguous(), means, sh, None, False)
                             for v in range(origins.shape[0])])
-        ctx.degree, ctx.k_max, ctx.group, ctx.reducer = degree, k_max, group, reducer
+        ctx.degree, ctx.k_max, ctx.group, ctx.reducer, ctx.exchange = degree, k_max, group, reducer, exchange
         ctx.save_for_backward(sh, means, origins)
         return cols
 
@@ -197,6 +210,8 @@ class MultiViewSH(torch.autograd.Function):
         sh, means, origins = ctx.saved_tensors
         d_cols = d_cols.contiguous()
         k, n = origins.shape[0], means.shape[0]
+        if ctx.exchange is not None:
+            return MultiViewSH._backward_nvls(ctx, sh, means, origins, d_cols)
         distributed = dist.is_available() and dist.is_initialized() and dist.get_world_size(ctx.group) > 1
         if distributed:
             world = dist.get_world_size(ctx.group)
@@ -222,13 +237,41 @@ class MultiViewSH(torch.autograd.Function):
         timeline.mark("sh_gathered")
         d_sh = _C.spherical_harmonics_coeffs_bwd_multi(ctx.degree, all_o, means, all_d, sh.shape[1])
         timeline.mark("sh_bwd_end")
-        return d_sh, d_means, None, None, None, None, None
+        return d_sh, d_means, None, None, None, None, None, None
+
+    @staticmethod
+    def _backward_nvls(ctx, sh, means, origins, d_cols):
+        """The same with the view exchange on this package's NVSwitch kernels
+        (exchange.NvlsExchange.all_gather) on the compute stream."""
+        from ._native import _C
+        ex = ctx.exchange
+        k, n, kmax = origins.shape[0], means.shape[0], ctx.k_max
+        timeline.mark("sh_bwd_start")
+        d_means = _C.spherical_harmonics_positions_bwd(ctx.degree, origins, means, sh, d_cols)
+        if k < kmax:
+            pad_d = torch.zeros(kmax, n, 3, device=d_cols.device, dtype=d_cols.dtype)
+            pad_d[:k] = d_cols
+            pad_o = origins[:1].expand(kmax, 3).clone()
+            pad_o[:k] = origins
+        else:
+            pad_d, pad_o = d_cols, origins
+        all_d, all_o = ex.all_gather(pad_d, pad_o)
+        all_d = all_d.reshape(ex.world * kmax, n, 3)
+        all_o = all_o.reshape(ex.world * kmax, 3)
+        timeline.mark("sh_gathered")
+        d_sh = _C.spherical_harmonics_coeffs_bwd_multi(ctx.degree, all_o.contiguous(), means, all_d.contiguous(),
+                                                       sh.shape[1])
+        timeline.mark("sh_bwd_end")
+        return d_sh, d_means, None, None, None, None, None, None
 
 
-def multiview_colors(sh, means, origins, degree: int, k_max: int, group=None, reducer=None):
-    """[k, N, 3] colours of this rank's k views (see MultiViewSH)."""
+def multiview_colors(sh, means, origins, degree: int, k_max: int, group=None, reducer=None, exchange=None):
+    """[k, N, 3] colours of this rank's k views (see MultiViewSH); with
+    `exchange` (an exchange.NvlsExchange made for k_max * N * 3 and
+    k_max * 3 gathered floats) the backward gathers the views over NVSwitch
+    with this package's kernels instead of NCCL."""
     return MultiViewSH.apply(sh.contiguous(), means.contiguous(), origins.contiguous(), degree, k_max, group,
-                             reducer)
+                             reducer, exchange)
 
 
 class Timeline:
