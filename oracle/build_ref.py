@@ -138,6 +138,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         return out if os.path.exists(out) else None
     import torch
     os.makedirs(OBJ_DIR, exist_ok=True)
+    os.makedirs(OUT_DIR, exist_ok=True)
     nvcc, cxx = _flags()
     compat_headers = [os.path.join(dp, f) for dp, _, fs in os.walk(COMPAT) for f in fs]
     jobs_list, objs = [], []
