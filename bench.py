@@ -326,7 +326,9 @@ class Workload:
                 exchange = "bucketed"
         self.exchange = exchange if world > 1 else "none"
         if self.ex is not None:
-            self.red = NvlsGradientSum([self.leaves[k] for k in order], self.ex)
+            # the view gather joins the all-reduce's window (one barrier pair)
+            self.red = NvlsGradientSum([self.leaves[k] for k in order], self.ex,
+                                       sh_leaf=self.leaves["sh"] if self.mvsh else None)
         else:
             # NCCL: the view exchange on a communicator of its own (its
             # all-gathers and the all-reduces each keep one order on every
@@ -447,11 +449,16 @@ def time_steps(wl, steps, warmup, world):
     return e0.elapsed_time(e1)
 
 
+PHASE_NAMES = {"fwd_end": "forward", "sh_bwd_start": "backward_compute", "sh_gathered": "sh_bwd_exchange_wait",
+               "sh_bwd_end": "sh_coeff_rebuild", "bwd_end": "backward_rest", "exchange_end": "exchange"}
+
+
 def phase_times(wl, steps, world):
-    """Mean per-phase device times (ms) of a step: forward (everything
-    queued before backward), backward compute up to the view exchange, the
-    SH backward with the all-gather wait, the SH-coefficient rebuild, and
-    the all-reduce tail after the last backward kernel."""
+    """Mean per-phase device times (ms) of a step, each from the previous
+    mark: forward (everything queued before backward), backward compute up
+    to the SH backward, the view all-gather wait (NCCL path), the
+    SH-coefficient rebuild, the rest of backward, and the gradient exchange
+    (all-reduce; with the NVSwitch kernels also the view gather)."""
     from xsimgs_b200.multiview import timeline
     acc = {}
     barrier(world)
@@ -463,14 +470,14 @@ def phase_times(wl, steps, world):
         marks += timeline.take()
         barrier(world)
         ev = dict(marks)
-        order = ["start", "fwd_end", "sh_bwd_start", "sh_gathered", "sh_bwd_end", "bwd_end", "exchange_end"]
-        names = {"fwd_end": "forward", "sh_bwd_start": "backward_compute", "sh_gathered": "sh_bwd_exchange_wait",
-                 "sh_bwd_end": "sh_coeff_rebuild", "bwd_end": "backward_rest", "exchange_end": "allreduce_tail"}
-        prev = ev["start"]
-        for k in order[1:]:
-            if k in ev:
-                acc[names[k]] = acc.get(names[k], 0.0) + prev.elapsed_time(ev[k])
-                prev = ev[k]
+        # each phase ends at a mark and starts at the one before it in time
+        # (the NVSwitch exchange rebuilds the SH gradient after the exchange
+        # window, the NCCL path inside backward)
+        t_of = sorted((ev["start"].elapsed_time(e), k) for k, e in ev.items() if k != "start")
+        prev = 0.0
+        for t, k in t_of:
+            acc[PHASE_NAMES[k]] = acc.get(PHASE_NAMES[k], 0.0) + (t - prev)
+            prev = t
     timeline.enabled = False
     mine = {k: v / steps for k, v in acc.items()}
     if world == 1:
@@ -479,8 +486,7 @@ def phase_times(wl, steps, world):
     # collectives wait out
     import torch
     import torch.distributed as dist
-    keys = ["forward", "backward_compute", "sh_bwd_exchange_wait", "sh_coeff_rebuild", "backward_rest",
-            "allreduce_tail"]
+    keys = list(PHASE_NAMES.values())
     t = torch.tensor([mine.get(k, 0.0) for k in keys], dtype=torch.float64, device=torch.device("cuda"))
     all_t = [torch.empty_like(t) for _ in range(world)]
     dist.all_gather(all_t, t)
@@ -514,17 +520,16 @@ def exchange_probe(wl, world, dev, reps=10):
 
     res = {}
     if wl.ex is not None:
-        # this package's NVSwitch kernels: the view all-gather and one
-        # all-reduce of every exchanged gradient, as the step runs them
+        # this package's NVSwitch kernels: the view all-gather and the
+        # all-reduce of every exchanged gradient in one window, as the step
+        # runs them
         ex = wl.ex
         dv = torch.zeros(ex.n_gather, device=dev)
         ov = torch.zeros(ex.n_small, device=dev)
         red = torch.zeros(ex.n_reduce, device=dev)
 
         def run_nvls():
-            if ex.n_gather:
-                ex.all_gather(dv, ov)
-            ex.all_reduce_([red])
+            ex.exchange([red], *((dv, ov) if ex.n_gather else ()))
 
         for _ in range(3):
             run_nvls()

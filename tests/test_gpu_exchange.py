@@ -5,8 +5,9 @@
     error word (the context stays usable); a peer that did arrive does not.
   * With two or more GPUs, two NCCL ranks: the all-gather returns every
     rank's slice bit for bit, the in-switch all-reduce returns the exact sum
-    of two ranks' values, and MultiViewSH's NVSwitch backward equals its NCCL
-    backward.
+    of two ranks' values, and a render-shaped step exchanged in one NVSwitch
+    window (NvlsGradientSum with the SH leaf, MultiViewSH leaving its view
+    gradients to it) ends with the same gradients as the NCCL exchange.
 """
 import os
 
@@ -36,6 +37,51 @@ def test_barrier_times_out_when_a_peer_never_arrives(cuda):
     assert float(torch.ones(8, device=cuda).sum()) == 8.0
 
 
+def _multiview_step_both_ways(rank, world, dev):
+    """A render-shaped step (a colour per view from the SH coefficients, the
+    means feeding the colours and the 'compositing', quaternions only the
+    latter) backpropagated and exchanged twice: NCCL (GradientAllReduce +
+    MultiViewSH gathering inside backward) and this package's NVSwitch window
+    (NvlsGradientSum with the SH leaf).  Gradients must agree."""
+    import torch.distributed as dist
+    from xsimgs_b200.exchange import NvlsExchange, NvlsGradientSum
+    from xsimgs_b200.multiview import GradientAllReduce, exchanged_leaves, multiview_colors
+    n, K = 2000, 16
+    g = torch.Generator().manual_seed(100 + rank)
+    means = (torch.randn(n, 3, generator=g) * 3).to(dev).requires_grad_(True)
+    sh = (torch.randn(n, K, 3, generator=g) * 0.3).to(dev).requires_grad_(True)
+    quats = torch.randn(n, 4, generator=g).to(dev).requires_grad_(True)
+    origins = torch.randn(1, 3, generator=g).to(dev)
+    d_cols = torch.randn(1, n, 3, generator=g).to(dev)
+    w_q, w_m = torch.randn(n, 4, generator=g).to(dev), torch.randn(n, 3, generator=g).to(dev)
+    leaves = {"means": means, "sh": sh, "quats": quats}
+    order = exchanged_leaves(leaves, multiview_sh=True)
+
+    def step(red, **kw):
+        for t in leaves.values():
+            t.grad = None
+        cols = multiview_colors(sh, means, origins, 3, k_max=1, **kw)
+        loss = (cols * d_cols).sum() + (quats * w_q).sum() + (means * w_m).sum()
+        loss.backward()
+        red.wait()
+        return {k: t.grad.detach().clone() for k, t in leaves.items()}
+
+    grp = dist.new_group([0, 1])
+    red_nccl = GradientAllReduce([leaves[k] for k in order])
+    nccl = step(red_nccl, group=grp)
+    red_nccl.remove()  # its hooks would otherwise all-reduce the next pass too
+    ex = NvlsExchange(None, sum(leaves[k].numel() for k in order), n * 3, 3, device=dev)
+    red = NvlsGradientSum([leaves[k] for k in order], ex, sh_leaf=sh)
+    out = {}
+    for it in range(2):
+        mine = step(red, exchange=ex)
+        for k in leaves:
+            out[f"mv_{k}_{it}"] = bool(torch.allclose(mine[k], nccl[k], rtol=1e-5, atol=1e-5))
+    torch.cuda.synchronize()
+    ex.check()
+    return out
+
+
 def _two_rank_worker(rank, world, port, out_q):
     import torch.distributed as dist
     from xsimgs_b200.exchange import NvlsExchange
@@ -61,6 +107,7 @@ def _two_rank_worker(rank, world, port, out_q):
                                              torch.equal(s.cpu(), torch.stack(small)))
         torch.cuda.synchronize()
         ex.check()
+        res.update(_multiview_step_both_ways(rank, world, dev))
         res["ok"] = True
     except Exception as e:  # noqa: BLE001
         res["error"] = repr(e)[:300]
@@ -86,4 +133,6 @@ def test_nvls_exchange_two_ranks():
         if "error" in res and "multicast" in res["error"]:
             pytest.skip(f"no NVLink multicast here: {res['error']}")
         assert res.get("ok"), (r, res)
-        assert all(v for k, v in res.items() if k.endswith(tuple("012"))), (r, res)
+        bad = [k for k, v in res.items() if k.endswith(tuple("012")) and not v]
+        assert not bad, (r, bad)
+        assert sum(k.startswith("mv_") for k in res) == 6, res

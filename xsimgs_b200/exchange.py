@@ -49,6 +49,10 @@ class NvlsExchange:
     `n_gather_small`) to all-gather."""
 
     TIMEOUT_S = 10.0
+    # set by NvlsGradientSum(sh_leaf=...): MultiViewSH leaves its view
+    # gradients here for the step's single exchange window
+    defer_views = False
+    pending_views = None
 
     @staticmethod
     def supported(group=None) -> tuple[bool, str]:
@@ -96,6 +100,7 @@ class NvlsExchange:
             self.small_mc = _multicast_address(self.gat_small, hs)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.epoch = 0
+        self._side = None
         # every rank's flags are zero before any rank's first barrier
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
@@ -121,6 +126,50 @@ class NvlsExchange:
             t.copy_(self.red[off:off + t.numel()].view_as(t))
             off += t.numel()
 
+    def exchange(self, tensors, d: torch.Tensor | None = None, small: torch.Tensor | None = None):
+        """all_reduce_(tensors) and, when `d` is given, all_gather(d, small)
+        inside ONE pair of barriers (the two kinds of traffic share the
+        window instead of each waiting out its own pair); returns the
+        gathered views as all_gather does (None, None without `d`)."""
+        tensors = list(tensors)
+        total = sum(t.numel() for t in tensors)
+        if total > self.n_reduce:
+            raise ValueError(f"exchange: {total} floats exceed the reduce buffer ({self.n_reduce})")
+        if d is not None and (d.numel() != self.n_gather or (small is not None and small.numel() != self.n_small)):
+            raise ValueError("exchange: gather sizes differ from the ones the buffers were made for")
+        if total:
+            torch.cat([t.reshape(-1) for t in tensors], out=self.red[:total])
+        if d is not None:
+            d, small = d.contiguous(), (small.contiguous() if small is not None else None)
+        self.barrier()  # inputs written everywhere, previous contents read everywhere
+        main = torch.cuda.current_stream(self.device)
+        if d is not None:
+            # the gather's stores on a side stream, beside the all-reduce
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=self.device)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                _C.nvls_broadcast(d.reshape(-1), self.gat_mc + 4 * self.rank * self.slice)
+                if small is not None:
+                    _C.nvls_broadcast(small.reshape(-1), self.small_mc + 4 * self.rank * self.slice_small)
+            d.record_stream(self._side)
+            if small is not None:
+                small.record_stream(self._side)
+        if total:
+            _C.nvls_allreduce_sum(self.red_mc, self.n_reduce, self.rank, self.world, self.red)
+        if d is not None:
+            main.wait_stream(self._side)
+        self.barrier()  # every store has landed
+        off = 0
+        for t in tensors:
+            t.copy_(self.red[off:off + t.numel()].view_as(t))
+            off += t.numel()
+        if d is None:
+            return None, None
+        out_d = self.gat.view(self.world, self.slice)[:, :self.n_gather]
+        out_s = self.gat_small.view(self.world, self.slice_small)[:, :self.n_small] if small is not None else None
+        return out_d, out_s
+
     def all_gather(self, d: torch.Tensor, small: torch.Tensor | None = None):
         """Every rank's `d` (n_gather floats) and `small` (n_gather_small
         floats): ([world, n_gather], [world, n_gather_small]) views of the
@@ -145,21 +194,45 @@ class NvlsExchange:
 
 class NvlsGradientSum:
     """After a rank's backward pass, sums the gradients of `leaves` over the
-    ranks with one NvlsExchange.all_reduce_ (a zero gradient for a leaf this
-    rank did not reach).  Same `wait()` contract as
-    multiview.GradientAllReduce."""
+    ranks (a zero gradient for a leaf this rank did not reach) with one
+    NvlsExchange window.  Same `wait()` contract as
+    multiview.GradientAllReduce.
 
-    def __init__(self, leaves, exchange: NvlsExchange):
+    With `sh_leaf`, the multi-view SH exchange joins the same window:
+    MultiViewSH (given this exchange) then leaves its view gradients with the
+    exchange instead of gathering them inside backward, and wait() gathers
+    them together with the all-reduce and adds the rebuilt SH-coefficient
+    gradient (summed over every view of every rank) to `sh_leaf.grad`.  So
+    `sh_leaf.grad` is complete only after wait(), like every other exchanged
+    gradient."""
+
+    def __init__(self, leaves, exchange: NvlsExchange, sh_leaf: torch.Tensor | None = None):
         self.leaves = list(leaves)
         self.exchange = exchange
+        self.sh_leaf = sh_leaf
+        exchange.defer_views = sh_leaf is not None
+        exchange.pending_views = None
 
     def wait(self) -> int:
         from .multiview import timeline
+        from ._native import _C
+        ex = self.exchange
         for t in self.leaves:
             if t.grad is None:
                 t.grad = torch.zeros_like(t)
-        self.exchange.all_reduce_([t.grad for t in self.leaves])
+        pend, ex.pending_views = ex.pending_views, None
+        if self.sh_leaf is not None and pend is None:
+            raise RuntimeError("NvlsGradientSum.wait: no view gradients were left by MultiViewSH in this pass")
+        all_d, all_o = ex.exchange([t.grad for t in self.leaves], *((pend["d"], pend["o"]) if pend else ()))
         timeline.mark("exchange_end")
+        if pend is not None:
+            kmax, n = pend["k_max"], pend["means"].shape[0]
+            d_sh = _C.spherical_harmonics_coeffs_bwd_multi(
+                pend["degree"], all_o.reshape(ex.world * kmax, 3).contiguous(), pend["means"],
+                all_d.reshape(ex.world * kmax, n, 3).contiguous(), pend["K"])
+            g = self.sh_leaf
+            g.grad = d_sh.view_as(g) if g.grad is None else g.grad + d_sh.view_as(g)
+            timeline.mark("sh_bwd_end")
         return 1
 
     def remove(self):

@@ -255,6 +255,12 @@ class MultiViewSH(torch.autograd.Function):
             pad_o[:k] = origins
         else:
             pad_d, pad_o = d_cols, origins
+        if ex.defer_views:
+            # the step's NvlsGradientSum gathers these with its all-reduce and
+            # adds the rebuilt SH gradient to the SH leaf after backward
+            ex.pending_views = {"d": pad_d, "o": pad_o, "means": means, "degree": ctx.degree, "k_max": kmax,
+                                "K": sh.shape[1]}
+            return None, d_means, None, None, None, None, None, None
         all_d, all_o = ex.all_gather(pad_d, pad_o)
         all_d = all_d.reshape(ex.world * kmax, n, 3)
         all_o = all_o.reshape(ex.world * kmax, 3)

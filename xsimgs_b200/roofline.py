@@ -52,9 +52,9 @@ def bwd_flops(n_eval_bwd: int, n_contrib: int, cdim: int, ray_grads: bool = True
 # gradients, two pixels a lane, the forward's contributor masks) on the C2
 # view (1M Gaussians, 1920x1080, 16x16 tiles), dram__bytes_read.sum +
 # dram__bytes_write.sum from one capture:
-#   ncu --set full --clock-control none -k regex:raster_bwd_px2 -s 1 -c 1 \
-#       python bench.py --steps 2 --warmup 1 --no-cpu-baseline --no-lidar
-BWD_DRAM_BYTES_C2 = 269.33e6 + 35.51e6
+#   ncu --set full --clock-control none -k "regex:raster_(fwd|bwd_px2)" -s 2 -c 2 \
+#       python bench.py --steps 2 --warmup 1 --no-cpu-baseline --no-lidar --no-rig --no-c5
+BWD_DRAM_BYTES_C2 = 270.41e6 + 35.77e6
 
 
 # The quaternion / scale part of the backward (quat_scale_to_preci_half_vjp,
