@@ -664,7 +664,7 @@ def gpu_arm(args, world, rank, local):
         extra["rig"] = strong_leg(args, "c3-8", world, rank, dev)
         extra["rig"]["c3"] = strong_leg(args, "c3", world, rank, dev, phases=False)
     if main_default and not args.no_c5:
-        extra["c5"] = strong_leg(args, "c5", world, rank, dev)
+        extra["c5"] = strong_leg(args, "c5", world, rank, dev, roofline=False)
 
     clk = clocks.stop()
 
@@ -754,15 +754,36 @@ def lidar_leg(args, wl, world, rank, dev):
             "phm": {"value": round(rays / (p * 1e-3)), "ms_per_step": round(p / args.steps, 3)}}
 
 
-def strong_leg(args, name, world, rank, dev, phases=True):
+def strong_leg(args, name, world, rank, dev, phases=True, roofline=True):
     """A strong-scaling workload (all views of the rig per step, sharded over
-    the ranks) timed like the main line; Mpix/s of the whole job."""
+    the ranks) timed like the main line; Mpix/s of the whole job, and the
+    compositing kernels' FP32 fractions on rank 0's views."""
     import torch
+    from xsimgs_b200 import capi
     wl = Workload(name, world, rank, dev, exchange=args.exchange)
     steps = max(3, min(args.steps, 20))
     ms = time_steps(wl, steps, max(3, args.warmup), world)
     ph = phase_times(wl, min(5, steps), world) if phases else None
     ms, = max_over_ranks([ms], world, dev)
+    roof = None
+    if roofline:
+        # a few more steps with the library's timed scopes on (every rank
+        # steps: the exchange is collective); the pair counts on rank 0
+        capi.timing_reset()
+        capi.timing_enable(True)
+        time_steps(wl, 3, 0, world)
+        capi.timing_enable(False)
+        timed = {}
+        for kname in ("rasterize_fwd", "rasterize_bwd"):
+            t, n = capi.timing_query(kname)
+            if n:
+                timed[kname] = (t, n)
+        capi.timing_reset()
+        if rank == 0 and wl.views and timed:
+            r, _ = roofline_fields(wl, timed, 3, dev)
+            roof = {"bwd": {k: r[k] for k in ("achieved", "frac", "avg_launch_ms")},
+                    "bwd_executed_frac": r["executed"]["frac"], "fwd": r["fwd"], "peak": r["peak"],
+                    "unit": r["unit"], "views": len(wl.views)}
     if wl.ex is not None:
         wl.ex.check()
     wl.red.remove()
@@ -771,6 +792,8 @@ def strong_leg(args, name, world, rank, dev, phases=True):
            "steps": steps, "config": workload_config(name, world, wl.n_gauss)}
     if ph is not None:
         out["phases_rank0"] = ph
+    if roof is not None:
+        out["roofline_rank0"] = roof
     del wl
     torch.cuda.empty_cache()
     return out
