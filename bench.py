@@ -783,7 +783,8 @@ def strong_leg(args, name, world, rank, dev, phases=True, roofline=True):
             r, _ = roofline_fields(wl, timed, 3, dev)
             roof = {"bwd": {k: r[k] for k in ("achieved", "frac", "avg_launch_ms")},
                     "bwd_executed_frac": r["executed"]["frac"], "fwd": r["fwd"], "peak": r["peak"],
-                    "unit": r["unit"], "views": len(wl.views)}
+                    "unit": r["unit"], "views": len(wl.views), "pairs": r["pairs"],
+                    "fwd_warp_entries": r["fwd_warp_entries"]}
     if wl.ex is not None:
         wl.ex.check()
     wl.red.remove()
@@ -807,6 +808,9 @@ def roofline_fields(wl, timed, steps, dev):
     from xsimgs_b200 import capi, roofline
     fl_b = fl_bx = fl_f = 0.0
     pairs = {"evaluated_fwd": 0, "evaluated_bwd": 0, "contributing": 0}
+    # the forward's (warp, list entry) work: staged, passing the warp's cone
+    # test, passing the per-lane quadric test, evaluated (pair counters 2-5)
+    warp_work = {"staged": 0, "cone_passed": 0, "quadric_passed": 0, "evaluated": 0}
     n_isects = 0
     L = wl.leaves
     for sp, cam in wl.views:
@@ -824,7 +828,10 @@ def roofline_fields(wl, timed, steps, dev):
                 flatten_ids=td["flatten_ids"])
         torch.cuda.synchronize()
         capi.set_pair_counters(None)
-        n_eval_f, n_contrib = (int(x) for x in cnt.tolist()[:2])
+        cl = cnt.tolist()
+        n_eval_f, n_contrib = int(cl[0]), int(cl[1])
+        for key, i in (("staged", 2), ("cone_passed", 3), ("quadric_passed", 4), ("evaluated", 5)):
+            warp_work[key] += int(cl[i])
         n_isects += int(td["flatten_ids"].numel())
         touched = int((td["radii"] > 0).all(-1).sum())
         # backward replays every pair up to each pixel's last contributor
@@ -860,7 +867,7 @@ def roofline_fields(wl, timed, steps, dev):
                                "on this workload (bytes per launch)") if c2_full else None,
             "peak_source": "measured: FP32 FMA probe in this run (MEASURED_PEAKS.json has only HBM and bf16)",
             "avg_launch_ms": round(bwd_ms / max(1, bwd_n), 4),
-            "flops_per_launch": fl_b / len(wl.views), "pairs": pairs,
+            "flops_per_launch": fl_b / len(wl.views), "pairs": pairs, "fwd_warp_entries": warp_work,
             "fwd": {"achieved": round(ach_f, 2), "avg_launch_ms": round(fwd_ms / max(1, fwd_n), 4),
                     "frac": round(ach_f / pk, 3)}}
     return roof, n_isects
