@@ -112,7 +112,13 @@ def workload_views(name: str):
     raise ValueError(name)
 
 
-def workload_config(name: str, world: int, n_gauss: int) -> dict:
+def mvsh_enabled(name: str, world: int, views_everywhere: bool, exchange: str) -> bool:
+    """Whether a step exchanges per-view colour gradients (MultiViewSH)
+    instead of all-reducing the SH gradient."""
+    return world > 1 and name != "c5" and (views_everywhere or exchange == "nvls")
+
+
+def workload_config(name: str, world: int, n_gauss: int, exchange: str = "nvls") -> dict:
     """The `config` dict of a workload at `world` ranks; both arms print it."""
     from xsimgs_b200.multiview import assign_views
     specs, _, scaling = workload_views(name)
@@ -122,7 +128,7 @@ def workload_config(name: str, world: int, n_gauss: int) -> dict:
     else:
         px = sum(s.width * s.height for s in specs)
         views = [len(v) for v in assign_views([s.width * s.height for s in specs], world)]
-    mvsh = world > 1 and name != "c5" and (scaling == "weak" or min(views) >= 1)
+    mvsh = mvsh_enabled(name, world, scaling == "weak" or min(views) >= 1, exchange)
     cfg = {"workload": WORKLOAD_DESC[name], "views_per_gpu": views,
            "parallelism": f"view-sharded dp{world} + gradient exchange over NVLink",
            "gradient_exchange": ("all-reduce of the geometry gradients + all-gather of the per-view colour "
@@ -219,7 +225,7 @@ def reference_arm(args, world, rank):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1000 * tot_t / args.steps, 2), "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "f32", "data": f"synthetic (seeded {args.workload.upper()} scene)",
-        "config": workload_config(args.workload, world, n_gauss),
+        "config": workload_config(args.workload, world, n_gauss, args.exchange),
         "cpu_baseline": {"value": round(value, 4), "unit": "Mpix/s", "cores": cores, "kind": "port",
                          "sample": sample,
                          "implementation": "CPU oracle restatement of the reference (oracle/xsg_oracle.cpp)"},
@@ -308,8 +314,12 @@ class Workload:
         # and rebuild the SH-coefficient gradient locally (MultiViewSH), on a
         # communicator of their own: its all-gathers and the all-reduces
         # below each keep one order on every rank and run side by side
-        self.mvsh = world > 1 and name != "c5" and min(len(v) for v in self.assignment) >= 1
         import torch.distributed as dist
+        views_everywhere = min(len(v) for v in self.assignment) >= 1
+        # the NVSwitch window lets a rank without views join the view gather
+        # with zero gradients; NCCL's gather inside backward needs a view on
+        # every rank
+        self.mvsh = mvsh_enabled(name, world, views_everywhere, exchange)
         order = exchanged_leaves(self.leaves, self.mvsh)
         self.ex = None
         self.sh_group = None
@@ -324,6 +334,8 @@ class Workload:
             except RuntimeError as e:  # no NVLink multicast here: every rank finds the same
                 print(f"[bench] NVSwitch exchange unavailable ({e}); using NCCL", flush=True)
                 exchange = "bucketed"
+                self.mvsh = mvsh_enabled(name, world, views_everywhere, exchange)
+                order = exchanged_leaves(self.leaves, self.mvsh)
         self.exchange = exchange if world > 1 else "none"
         if self.ex is not None:
             # the view gather joins the all-reduce's window (one barrier pair)
@@ -383,9 +395,11 @@ class Workload:
         for v in self.leaves.values():
             v.grad = None
         means, quats, scales, opac, sh, vel = self._scene()
-        if self.mvsh:
+        if self.mvsh and self.views:
             cols = self.mvc(sh, means, torch.stack([cam.t0 for _, cam in self.views]), DEG, self.k_max,
                             group=self.sh_group, exchange=self.ex)
+        elif self.mvsh:
+            self.ex.leave_no_views(means, DEG, sh.shape[1], self.k_max)
         outs, ups = [], []
         for v, ((sp, cam), g) in enumerate(zip(self.views, grads)):
             colors = cols[v] if self.mvsh else X.spherical_harmonics_fused(sh, means, cam.t0, DEG)
@@ -701,7 +715,7 @@ def gpu_arm(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 3), "higher_is_better": True,
         "scaling": wl.scaling, "vs_baseline": None, "dtype": "f32",
         "data": f"synthetic (seeded {args.workload.upper()} scene)",
-        "config": workload_config(args.workload, world, wl.n_gauss),
+        "config": workload_config(args.workload, world, wl.n_gauss, wl.exchange),
         "e2e": {"value": round(e2e, 2), "unit": "Mpix/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                 "note": "per step: the upstream gradient images in (pinned host -> device), the step's scalar "
                         "result (mean alpha) out; rendered images and parameter gradients stay on the device, "
@@ -790,7 +804,7 @@ def strong_leg(args, name, world, rank, dev, phases=True, roofline=True):
     wl.red.remove()
     out = {"metric": f"Gaussian-render fwd+bwd Mpix/s ({name.upper()})", "unit": "Mpix/s", "scaling": "strong",
            "value": round(wl.px_per_step * steps / (ms * 1e-3) / 1e6, 2), "ms_per_step": round(ms / steps, 3),
-           "steps": steps, "config": workload_config(name, world, wl.n_gauss)}
+           "steps": steps, "config": workload_config(name, world, wl.n_gauss, wl.exchange)}
     if ph is not None:
         out["phases_rank0"] = ph
     if roof is not None:

@@ -7,7 +7,8 @@
     rank's slice bit for bit, the in-switch all-reduce returns the exact sum
     of two ranks' values, and a render-shaped step exchanged in one NVSwitch
     window (NvlsGradientSum with the SH leaf, MultiViewSH leaving its view
-    gradients to it) ends with the same gradients as the NCCL exchange.
+    gradients to it) ends with the same gradients as the NCCL exchange, also
+    when one rank renders no view (it gathers zero view gradients).
 """
 import os
 
@@ -77,6 +78,29 @@ def _multiview_step_both_ways(rank, world, dev):
         mine = step(red, exchange=ex)
         for k in leaves:
             out[f"mv_{k}_{it}"] = bool(torch.allclose(mine[k], nccl[k], rtol=1e-5, atol=1e-5))
+    # rank 1 renders no view: in the NVSwitch window it gathers k_max views of
+    # zero colour gradient (leave_no_views); the NCCL reference for that is
+    # rank 1 rendering its view with a zero upstream colour gradient
+    def step_viewless(red, nvls):
+        for t in leaves.values():
+            t.grad = None
+        loss = (quats * w_q).sum() + (means * w_m).sum()
+        if rank == 0 or not nvls:
+            cols = multiview_colors(sh, means, origins, 3, k_max=1,
+                                    **({"exchange": ex} if nvls else {"group": grp}))
+            loss = loss + (cols * (d_cols if rank == 0 else torch.zeros_like(d_cols))).sum()
+        else:
+            ex.leave_no_views(means, 3, K, 1)
+        loss.backward()
+        red.wait()
+        return {k: t.grad.detach().clone() for k, t in leaves.items()}
+
+    red_nccl = GradientAllReduce([leaves[k] for k in order])
+    want = step_viewless(red_nccl, nvls=False)
+    red_nccl.remove()
+    got = step_viewless(red, nvls=True)
+    for k in leaves:
+        out[f"mv_viewless_{k}_0"] = bool(torch.allclose(got[k], want[k], rtol=1e-5, atol=1e-5))
     torch.cuda.synchronize()
     ex.check()
     return out
@@ -135,4 +159,4 @@ def test_nvls_exchange_two_ranks():
         assert res.get("ok"), (r, res)
         bad = [k for k, v in res.items() if k.endswith(tuple("012")) and not v]
         assert not bad, (r, bad)
-        assert sum(k.startswith("mv_") for k in res) == 6, res
+        assert sum(k.startswith("mv_") for k in res) == 9, res

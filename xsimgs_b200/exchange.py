@@ -170,6 +170,17 @@ class NvlsExchange:
         out_s = self.gat_small.view(self.world, self.slice_small)[:, :self.n_small] if small is not None else None
         return out_d, out_s
 
+    def leave_no_views(self, means: torch.Tensor, degree: int, n_coeffs: int, k_max: int) -> None:
+        """For a rank that renders no view in this pass while the others run
+        MultiViewSH: its share of the view gather is k_max views of zero
+        colour gradient (from an origin outside the Gaussians' bounding box,
+        so every SH basis value stays finite), which add nothing to the
+        rebuilt SH gradient.  Call it where MultiViewSH would have run."""
+        n = means.shape[0]
+        o = (means.detach().amax(0) + 1.0).reshape(1, 3).expand(k_max, 3).contiguous()
+        self.pending_views = {"d": torch.zeros(k_max, n, 3, device=means.device, dtype=means.dtype), "o": o,
+                              "means": means.detach(), "degree": degree, "k_max": k_max, "K": n_coeffs}
+
     def all_gather(self, d: torch.Tensor, small: torch.Tensor | None = None):
         """Every rank's `d` (n_gather floats) and `small` (n_gather_small
         floats): ([world, n_gather], [world, n_gather_small]) views of the
